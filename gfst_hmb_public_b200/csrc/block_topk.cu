@@ -1,0 +1,18 @@
+// C-ABI entry of the coarse block retrieval (score + top-k).
+#include "block_topk.cuh"
+
+extern "C" int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_streams, int n_queries, int n_blocks,
+                               int n_blocks_stride, int d, int k, int dtype, float* top_scores, int32_t* top_idx,
+                               cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(n_streams >= 0 && n_queries >= 0 && n_blocks >= 0, GFST_ERR_ARG, "negative size");
+  GFST_REQUIRE(n_blocks_stride >= n_blocks, GFST_ERR_ARG, "n_blocks_stride %d < n_blocks %d", n_blocks_stride,
+               n_blocks);
+  GFST_REQUIRE(k >= 1 && k <= 32, GFST_ERR_SHAPE, "k=%d outside [1, 32]", k);
+  GFST_REQUIRE(d >= 1 && d <= 256, GFST_ERR_SHAPE, "d=%d outside [1, 256]", d);
+  GFST_REQUIRE(dtype == GFST_F32 || dtype == GFST_BF16, GFST_ERR_DTYPE, "unsupported dtype %d", dtype);
+  if (n_streams == 0 || n_queries == 0) return GFST_OK;
+  GFST_REQUIRE(Q && top_scores && top_idx && (Ksum || n_blocks == 0), GFST_ERR_ARG, "null buffer");
+  return block_topk_simt(Q, Ksum, n_streams, n_queries, n_blocks, n_blocks_stride, d, k, dtype, top_scores,
+                         top_idx, stream);
+}

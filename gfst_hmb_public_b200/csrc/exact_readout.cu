@@ -1,0 +1,185 @@
+// Exact-token readout: inside the k blocks selected for a query, score every
+// token key against the query, take the best token in the total order
+// (score descending, token index ascending; token index = block * L + position)
+// and copy that token's value row out.
+//
+// Reference (pkhairkh/gfst-hmb-public): ExactRecallReadout._score_block_tokens
+// scores each retrieved block's tokens against the query
+// (src/gfst_hmb_mpuc/modeling.py:599-657); the collapsed scores are sorted
+// descending and the first token is the copy target (modeling.py:1151-1169).
+//
+// HBM-bound gather.  One CTA per (stream, query); its warps take the selected
+// blocks round robin and each lane scores whole token rows with 16-byte loads
+// (a sequential fp32 FMA chain over d; bf16 products are exact in fp32).
+// Consecutive CTAs are consecutive queries of one stream, so blocks picked by
+// several queries of a stream are served from L2.
+#include "gfst_common.cuh"
+
+namespace gfst {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+
+template <typename T>
+struct Elems16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+__device__ __forceinline__ float dot16(const uint4& v, const float* q, float acc, float) {
+  acc = fmaf(__uint_as_float(v.x), q[0], acc);
+  acc = fmaf(__uint_as_float(v.y), q[1], acc);
+  acc = fmaf(__uint_as_float(v.z), q[2], acc);
+  acc = fmaf(__uint_as_float(v.w), q[3], acc);
+  return acc;
+}
+__device__ __forceinline__ float dot16(const uint4& v, const float* q, float acc, __nv_bfloat16) {
+  acc = fmaf(bf16_lo(v.x), q[0], acc);
+  acc = fmaf(bf16_hi(v.x), q[1], acc);
+  acc = fmaf(bf16_lo(v.y), q[2], acc);
+  acc = fmaf(bf16_hi(v.y), q[3], acc);
+  acc = fmaf(bf16_lo(v.z), q[4], acc);
+  acc = fmaf(bf16_hi(v.z), q[5], acc);
+  acc = fmaf(bf16_lo(v.w), q[6], acc);
+  acc = fmaf(bf16_hi(v.w), q[7], acc);
+  return acc;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return bf16_to_f32(v); }
+
+__device__ __forceinline__ void warp_best(float& s, int& i) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float so = __shfl_xor_sync(0xffffffffu, s, o);
+    const int io = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(so, io, s, i)) {
+      s = so;
+      i = io;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) exact_readout_kernel(
+    const T* __restrict__ Q, const T* __restrict__ pool_K, const T* __restrict__ pool_V,
+    const int32_t* __restrict__ top_idx, int n_queries, int n_slots, int L, int d, int dv, int k,
+    int32_t* __restrict__ best_tok, float* __restrict__ best_score, T* __restrict__ out_V) {
+  constexpr int N = Elems16<T>::N;
+  extern __shared__ __align__(16) float qs[];  // [d] query in fp32
+  __shared__ float red_s[kWarps];
+  __shared__ int red_i[kWarps];
+  const int64_t sq = blockIdx.x;  // stream * n_queries + query
+  const int64_t s = sq / n_queries;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  for (int c = tid; c < d; c += kThreads) qs[c] = to_f32(Q[sq * d + c]);
+  __syncthreads();
+
+  const int32_t* sel = top_idx + sq * k;
+  const int vecs = d / N;
+  float bs = __int_as_float(0x7fc00000);  // NaN sentinel ranks last
+  int bi = 0x7fffffff;
+  for (int j = warp; j < k; j += kWarps) {
+    const int b = __ldg(sel + j);
+    if (b < 0 || b >= n_slots) continue;
+    const uint4* blk = reinterpret_cast<const uint4*>(pool_K + ((size_t)s * n_slots + b) * L * d);
+    for (int p = lane; p < L; p += 32) {
+      const uint4* row = blk + (size_t)p * vecs;
+      float acc = 0.f;
+      for (int c = 0; c < vecs; c += 4) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = (c + u < vecs) ? __ldg(row + c + u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c + u < vecs) acc = dot16(v[u], qs + (c + u) * N, acc, T());
+      }
+      const int tok = b * L + p;
+      if (better(acc, tok, bs, bi)) {
+        bs = acc;
+        bi = tok;
+      }
+    }
+  }
+  warp_best(bs, bi);
+  if (lane == 0) {
+    red_s[warp] = bs;
+    red_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bs = lane < kWarps ? red_s[lane] : __int_as_float(0x7fc00000);
+    bi = lane < kWarps ? red_i[lane] : 0x7fffffff;
+    warp_best(bs, bi);
+    if (lane == 0) {
+      red_s[0] = bs;
+      red_i[0] = bi;
+    }
+  }
+  __syncthreads();
+  bs = red_s[0];
+  bi = red_i[0];
+  const bool found = bi != 0x7fffffff;
+  if (tid == 0) {
+    best_tok[sq] = found ? bi : -1;
+    best_score[sq] = found ? bs : -INFINITY;
+  }
+  if (out_V != nullptr) {
+    const int vv = dv / N;
+    uint4* dst = reinterpret_cast<uint4*>(out_V + sq * dv);
+    if (found) {
+      const int b = bi / L, p = bi % L;
+      const uint4* src = reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + b) * L + p) * dv);
+      for (int c = tid; c < vv; c += kThreads) dst[c] = __ldg(src + c);
+    } else {
+      for (int c = tid; c < vv; c += kThreads) dst[c] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <typename T>
+int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t* top_idx, int64_t S, int Nq,
+           int NS, int L, int d, int dv, int k, int32_t* best_tok, float* best_score, void* out_V,
+           cudaStream_t stream) {
+  constexpr int N = Elems16<T>::N;
+  GFST_REQUIRE(d % N == 0, GFST_ERR_ALIGN, "d=%d must be a multiple of %d", d, N);
+  GFST_REQUIRE(out_V == nullptr || dv % N == 0, GFST_ERR_ALIGN, "dv=%d must be a multiple of %d", dv, N);
+  const int64_t grid = S * (int64_t)Nq;
+  GFST_REQUIRE(grid <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many queries");
+  exact_readout_kernel<T><<<(unsigned)grid, kThreads, (size_t)d * sizeof(float), stream>>>(
+      static_cast<const T*>(Q), static_cast<const T*>(pool_K), static_cast<const T*>(pool_V), top_idx, Nq, NS, L,
+      d, dv, k, best_tok, best_score, static_cast<T*>(out_V));
+  return check_launch("exact_readout_kernel");
+}
+
+}  // namespace
+}  // namespace gfst
+
+extern "C" int gfst_exact_readout(const void* Q, const void* pool_K, const void* pool_V, const int32_t* top_idx,
+                                  int64_t n_streams, int n_queries, int n_slots, int L, int d, int dv, int k,
+                                  int dtype, int32_t* best_tok, float* best_score, void* out_V,
+                                  cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(n_streams >= 0 && n_queries >= 0 && n_slots >= 1 && L >= 1, GFST_ERR_ARG, "bad sizes");
+  GFST_REQUIRE(k >= 1 && k <= 32, GFST_ERR_SHAPE, "k=%d outside [1, 32]", k);
+  GFST_REQUIRE(d >= 1 && d <= 256, GFST_ERR_SHAPE, "d=%d outside [1, 256]", d);
+  GFST_REQUIRE((pool_V == nullptr) == (out_V == nullptr), GFST_ERR_ARG, "pool_V and out_V go together");
+  GFST_REQUIRE((int64_t)n_slots * L <= 0x7fffffffLL, GFST_ERR_SHAPE, "token index overflows int32");
+  if (n_streams == 0 || n_queries == 0) return GFST_OK;
+  GFST_REQUIRE(Q && pool_K && top_idx && best_tok && best_score, GFST_ERR_ARG, "null buffer");
+  GFST_REQUIRE(aligned16(pool_K) && aligned16(pool_V) && aligned16(out_V), GFST_ERR_ALIGN,
+               "pool and output buffers must be 16-byte aligned");
+  if (dtype == GFST_F32)
+    return launch<float>(Q, pool_K, pool_V, top_idx, n_streams, n_queries, n_slots, L, d, dv, k, best_tok,
+                         best_score, out_V, stream);
+  if (dtype == GFST_BF16)
+    return launch<__nv_bfloat16>(Q, pool_K, pool_V, top_idx, n_streams, n_queries, n_slots, L, d, dv, k, best_tok,
+                                 best_score, out_V, stream);
+  set_last_error("unsupported dtype %d", dtype);
+  return GFST_ERR_DTYPE;
+}

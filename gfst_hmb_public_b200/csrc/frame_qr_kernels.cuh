@@ -1,0 +1,205 @@
+// Frame kernels: one-step rank-m update + thin QR, and the T-token streaming
+// pass that keeps every frame in registers across tokens.  Templated on the
+// capacity class (DMAX, RMAX, TPF); the classes are instantiated in
+// frame_qr_r8.cu / frame_qr_r16.cu / frame_qr_r32.cu and dispatched in frame_qr.cu.
+//
+// Reference behaviour (paths relative to pkhairkh/gfst-hmb-public):
+//   src/gfst_hmb_mpuc/gfst.py:26-46      canonical_qr_batched + canonicalize_qr_column_signs
+//   src/gfst_hmb_mpuc/gfst.py:115-140    update_basis_candidate_batched (beta*U + A B^T form)
+//   src/gfst_hmb_mpuc/modeling.py:2299-2423  per-token largest-level tracker update
+#pragma once
+#include "frame_qr.cuh"
+#include "frame_qr_launch.h"
+
+namespace gfst {
+
+
+constexpr int kWarps = 4;  // warps per CTA
+
+// Register budget per capacity class: frames holding >= 128 values per lane get
+// the whole register file share of 3 CTAs per SM; smaller ones pack 4.
+template <int DMAX, int RMAX, int TPF>
+constexpr int min_blocks() {
+  return (DMAX / TPF) * RMAX >= 128 ? 3 : 4;
+}
+
+// ---------------------------------------------------------------------------
+// one step: Uout = QR(beta * U + A B^T)
+// ---------------------------------------------------------------------------
+template <int DMAX, int RMAX, int TPF, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
+    frame_update_qr_kernel(const float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
+                           float beta, float* __restrict__ Uout, int64_t n_frames, int d, int r, int m,
+                           float eps_sign, int sign_mode, bool vec4) {
+  using QR = FrameQR<DMAX, RMAX, TPF>;
+  constexpr int GPW = 32 / TPF;
+  __shared__ typename QR::Smem qsm[WARPS * GPW];
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t = lane % TPF;
+  const int g = warp * GPW + lane / TPF;
+  const int64_t f = (int64_t)blockIdx.x * (WARPS * GPW) + g;
+  const bool valid = f < n_frames;
+  const size_t frame_elems = (size_t)d * r;
+
+  float a[QR::RPT][RMAX];
+  QR::load(a, U + (valid ? f : 0) * frame_elems, t, d, r, valid, vec4);
+
+  if (beta != 1.f) {
+#pragma unroll
+    for (int s = 0; s < QR::RPT; ++s)
+#pragma unroll
+      for (int j = 0; j < RMAX; ++j) a[s][j] *= beta;
+  }
+  if (m > 0 && valid) {
+    const float* Af = A + f * (size_t)d * m;
+    const float* Bf = B + f * (size_t)r * m;
+    for (int mm = 0; mm < m; ++mm) {
+      float bcol[RMAX];
+#pragma unroll
+      for (int j = 0; j < RMAX; ++j) bcol[j] = j < r ? __ldg(Bf + (size_t)j * m + mm) : 0.f;
+#pragma unroll
+      for (int s = 0; s < QR::RPT; ++s) {
+        const int row = t + s * TPF;
+        const float av = row < d ? __ldg(Af + (size_t)row * m + mm) : 0.f;
+#pragma unroll
+        for (int j = 0; j < RMAX; ++j) a[s][j] = fmaf(av, bcol[j], a[s][j]);
+      }
+    }
+  }
+
+  const uint32_t cols_mask = r >= 32 ? 0xffffffffu : ((1u << r) - 1u);
+  QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, cols_mask);
+  QR::store(a, Uout + (valid ? f : 0) * frame_elems, t, d, r, valid, vec4);
+}
+
+// ---------------------------------------------------------------------------
+// streaming: for t in [0, T): U <- QR(beta * U + A_t B_t^T)
+// A_t and B_t are staged per frame group in shared memory with cp.async,
+// double-buffered so token t+1's inputs load while token t factorises.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all_but_one() {
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+}
+
+template <int DMAX, int RMAX, int TPF, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
+    frame_stream_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B, float beta,
+                        int64_t n_frames, int T, int d, int r, int m, float eps_sign, int sign_mode,
+                        float* __restrict__ frames_out, int out_every, bool vec4) {
+  using QR = FrameQR<DMAX, RMAX, TPF>;
+  constexpr int GPW = 32 / TPF;
+  __shared__ typename QR::Smem qsm[WARPS * GPW];
+  extern __shared__ __align__(16) float stage[];  // [WARPS*GPW][2][d*m + r*m]
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t = lane % TPF;
+  const int g = warp * GPW + lane / TPF;
+  const int64_t f = (int64_t)blockIdx.x * (WARPS * GPW) + g;
+  const bool valid = f < n_frames;
+  const int64_t fs = valid ? f : 0;
+  const size_t frame_elems = (size_t)d * r;
+  const int a_elems = d * m, b_elems = r * m;
+  const int tok_elems = a_elems + b_elems;  // multiple of 4 (host-checked)
+  float* my_stage = stage + (size_t)g * 2 * tok_elems;
+
+  const float* Af = A + fs * (size_t)T * a_elems;
+  const float* Bf = B + fs * (size_t)T * b_elems;
+
+  auto issue = [&](int tok) {
+    if (valid && tok < T) {
+      float* dst = my_stage + (tok & 1) * tok_elems;
+      const float* srcA = Af + (size_t)tok * a_elems;
+      const float* srcB = Bf + (size_t)tok * b_elems;
+      for (int c = t; c < a_elems / 4; c += TPF) cp_async16(dst + 4 * c, srcA + 4 * c);
+      for (int c = t; c < b_elems / 4; c += TPF) cp_async16(dst + a_elems + 4 * c, srcB + 4 * c);
+    }
+    cp_async_commit();
+  };
+
+  float a[QR::RPT][RMAX];
+  QR::load(a, U + fs * frame_elems, t, d, r, valid, vec4);
+  const uint32_t cols_mask = r >= 32 ? 0xffffffffu : ((1u << r) - 1u);
+
+  issue(0);
+  for (int tok = 0; tok < T; ++tok) {
+    issue(tok + 1);
+    cp_async_wait_all_but_one();
+    __syncwarp();
+    const float* sA = my_stage + (tok & 1) * tok_elems;
+    const float* sB = sA + a_elems;
+    if (beta != 1.f) {
+#pragma unroll
+      for (int s = 0; s < QR::RPT; ++s)
+#pragma unroll
+        for (int j = 0; j < RMAX; ++j) a[s][j] *= beta;
+    }
+    if (valid) {
+      for (int mm = 0; mm < m; ++mm) {
+        float bcol[RMAX];
+#pragma unroll
+        for (int j = 0; j < RMAX; ++j) bcol[j] = j < r ? sB[j * m + mm] : 0.f;
+#pragma unroll
+        for (int s = 0; s < QR::RPT; ++s) {
+          const int row = t + s * TPF;
+          const float av = row < d ? sA[row * m + mm] : 0.f;
+#pragma unroll
+          for (int j = 0; j < RMAX; ++j) a[s][j] = fmaf(av, bcol[j], a[s][j]);
+        }
+      }
+    }
+    QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, cols_mask);
+    if (frames_out != nullptr && ((tok + 1) % out_every) == 0) {
+      const int64_t snap = (tok + 1) / out_every - 1;
+      QR::store(a, frames_out + (snap * n_frames + fs) * frame_elems, t, d, r, valid, vec4);
+    }
+    __syncwarp();  // every lane is done with this stage buffer before it is refilled
+  }
+  QR::store(a, U + fs * frame_elems, t, d, r, valid, vec4);
+}
+
+// ---------------------------------------------------------------------------
+// launchers (host)
+// ---------------------------------------------------------------------------
+
+template <int DMAX, int RMAX, int TPF>
+int launch_update(const float* U, const float* A, const float* B, float beta, float* Uout, int64_t n, int d, int r,
+                  int m, float eps_sign, int sign_mode, cudaStream_t stream) {
+  constexpr int GPW = 32 / TPF;
+  const int64_t per_block = kWarps * GPW;
+  const int64_t blocks = (n + per_block - 1) / per_block;
+  GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
+  const bool vec4 = (r == RMAX) && (RMAX % 4 == 0) && aligned16(U) && aligned16(Uout);
+  frame_update_qr_kernel<DMAX, RMAX, TPF, kWarps><<<(unsigned)blocks, kWarps * 32, 0, stream>>>(
+      U, A, B, beta, Uout, n, d, r, m, eps_sign, sign_mode, vec4);
+  return check_launch("frame_update_qr_kernel");
+}
+
+template <int DMAX, int RMAX, int TPF>
+int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
+                  float eps_sign, int sign_mode, float* frames_out, int out_every, cudaStream_t stream) {
+  constexpr int GPW = 32 / TPF;
+  const int64_t per_block = kWarps * GPW;
+  const int64_t blocks = (n + per_block - 1) / per_block;
+  GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
+  const bool vec4 = (r == RMAX) && (RMAX % 4 == 0) && aligned16(U) &&
+                    (frames_out == nullptr || aligned16(frames_out));
+  const size_t smem = (size_t)per_block * 2 * (size_t)(d * m + r * m) * sizeof(float);
+  auto kern = frame_stream_kernel<DMAX, RMAX, TPF, kWarps>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  kern<<<(unsigned)blocks, kWarps * 32, smem, stream>>>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode,
+                                                         frames_out, out_every, vec4);
+  return check_launch("frame_stream_kernel");
+}
+
+}  // namespace gfst

@@ -1,0 +1,151 @@
+/*
+ * gfst_b200.h -- C ABI of the B200 (sm_100a) GFST-HMB streaming hot path.
+ *
+ * Every entry point takes raw device pointers, plain sizes and a cudaStream_t,
+ * returns an int status (GFST_OK == 0), allocates nothing unless stated, and
+ * never synchronises the host.  Work is enqueued on `stream`; results are
+ * valid once that stream has reached the enqueued work.  Callers own every
+ * buffer.  Layouts are dense row-major (C order) unless stated.
+ *
+ * The entry points replace these reference interfaces (paths are relative to
+ * the reference project pkhairkh/gfst-hmb-public):
+ *   gfst_frame_update_qr   <- gfst_local_qr_sm120_forward(candidate[B,m,n], eps_sign)
+ *                             src/gfst_hmb_mpuc/csrc/mathdx/mathdx_extension.cpp:20-22,
+ *                             src/gfst_hmb_mpuc/csrc/mathdx/mathdx_runtime.cu:665-671, and the
+ *                             torch path gfst.canonical_qr_batched / update_basis_candidate_batched
+ *                             src/gfst_hmb_mpuc/gfst.py:26-46, 115-140
+ *   gfst_frame_stream      <- the per-token loop GfstHmbSublayer._update_local_bases
+ *                             src/gfst_hmb_mpuc/modeling.py:2299-2423 (largest level), with the
+ *                             frame kept on chip across tokens
+ *   gfst_block_commit_mean <- GfstDecodeState.append_exact_token block commit
+ *                             src/gfst_hmb_mpuc/state.py:651-815 and the block summary of
+ *                             GfstHmbSublayer._update_block_memory modeling.py:3482-3535
+ *                             (summary key = mean of the block's token keys)
+ *   gfst_block_topk        <- FaissGpuRetriever.search / exact_topk
+ *                             src/gfst_hmb_mpuc/retrieval.py:136-172
+ *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
+ *                             src/gfst_hmb_mpuc/modeling.py:599-657, 1151-1169
+ */
+#ifndef GFST_B200_H_
+#define GFST_B200_H_
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define GFST_API __attribute__((visibility("default")))
+#else
+#define GFST_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+enum gfst_status {
+  GFST_OK = 0,
+  GFST_ERR_ARG = 1,         /* null pointer or negative size                          */
+  GFST_ERR_SHAPE = 2,       /* shape outside what the kernels support                 */
+  GFST_ERR_ALIGN = 3,       /* pointer or row pitch not aligned as required           */
+  GFST_ERR_LAUNCH = 4,      /* the CUDA launch itself failed (cudaGetLastError)       */
+  GFST_ERR_DEVICE = 5,      /* device is not sm_100 or a CUDA runtime call failed     */
+  GFST_ERR_TIMEOUT = 6,     /* a bounded device-side wait gave up                     */
+  GFST_ERR_DTYPE = 7        /* unsupported element type                               */
+};
+
+/* Sign convention applied to every column of a thin-QR factor Q. */
+enum gfst_sign_mode {
+  /* Reference rule (gfst.py:35-46): find the first row whose |q| > eps_sign;
+   * if that entry is negative, negate the column.  Columns with no such entry
+   * are left as they are. */
+  GFST_SIGN_FIRST_SIGNIFICANT = 0,
+  /* Q * sign(diag(R)) with sign(0) = +1: every R_jj >= 0. */
+  GFST_SIGN_R_DIAG_POSITIVE = 1
+};
+
+/* Element types of key / value / query / summary buffers. */
+enum gfst_dtype { GFST_F32 = 0, GFST_BF16 = 1 };
+
+/* Human-readable text of a status code (static storage). */
+GFST_API const char* gfst_status_string(int status);
+/* ABI version of this library, (major << 16) | minor. */
+GFST_API int gfst_abi_version(void);
+/* Detail text of the last non-OK status returned on the calling host thread
+ * (empty string if none). */
+GFST_API const char* gfst_last_error(void);
+
+/* ---- frames: rank-m update + Householder thin QR ---------------------- *
+ * For every frame f in [0, n_frames):
+ *     C   = beta * U[f] + A[f] * B[f]^T        (U: d x r, A: d x m, B: r x m)
+ *     Q   = thin Q of Householder QR(C) (LAPACK geqrf/orgqr order), sign-fixed
+ *     Uout[f] = Q                               (d x r)
+ * m == 0 is a plain batched QR of U (A and B may be NULL).  U and Uout may alias.
+ * Limits: 1 <= r <= d, r <= 32, d <= 128 (d <= 256 when r <= 16), 0 <= m <= 8.
+ * fp32 throughout; no fast-math.                                            */
+GFST_API int gfst_frame_update_qr(const float* U, const float* A, const float* B, float beta,
+                         float* Uout, int64_t n_frames, int d, int r, int m,
+                         float eps_sign, int sign_mode, cudaStream_t stream);
+
+/* ---- frames: T-token streaming pass, frame resident on chip ---------------
+ * For t in [0, T):  U[f] <- QR_signfixed(beta * U[f] + A[f,t] * B[f,t]^T)
+ * U: [n_frames, d, r] (in/out), A: [n_frames, T, d, m], B: [n_frames, T, r, m].
+ * If frames_out != NULL and out_every > 0, the frame after token t is written
+ * to frames_out[(t+1)/out_every - 1] (layout [T/out_every, n_frames, d, r])
+ * whenever (t+1) % out_every == 0.  Same shape limits as gfst_frame_update_qr;
+ * m >= 1; A and B rows need 16-byte alignment (d*m and r*m multiples of 4).  */
+GFST_API int gfst_frame_stream(float* U, const float* A, const float* B, float beta,
+                      int64_t n_frames, int T, int d, int r, int m,
+                      float eps_sign, int sign_mode,
+                      float* frames_out, int out_every, cudaStream_t stream);
+
+/* ---- block commit ----------------------------------------------------------
+ * For every stream s in [0, n_streams):
+ *   pool_K[s, slot] = K[s]   (L x d),  pool_V[s, slot] = V[s]   (L x dv)
+ *   summary[s, slot, :] = mean over the L rows of K[s]   (fp32 sum in token
+ *                         order, divided by L, rounded once to `dtype`)
+ * K: [n_streams, L, d], V: [n_streams, L, dv]; pool_K: [n_streams, n_slots, L, d];
+ * pool_V: [n_streams, n_slots, L, dv]; summary: [n_streams, n_slots, d].
+ * V / pool_V may be NULL (keys only).  dtype is GFST_F32 or GFST_BF16 for all
+ * five buffers.  Rows need 16-byte alignment.                               */
+GFST_API int gfst_block_commit_mean(const void* K, const void* V, void* pool_K, void* pool_V,
+                           void* summary, int64_t n_streams, int n_slots, int slot,
+                           int L, int d, int dv, int dtype, cudaStream_t stream);
+
+/* ---- coarse block retrieval: score + top-k ---------------------------------
+ * For every stream s and query q:
+ *   score[b] = Q[s,q,:] . Ksum[s,b,:]   for b in [0, n_blocks)   (fp32 accumulate)
+ *   top_idx[s,q,0..k) / top_scores[s,q,0..k) = the k best blocks in the total
+ *   order (score descending, block index ascending).  Slots past n_blocks are
+ *   filled with index -1 and score -inf.
+ * Q: [n_streams, n_queries, d]; Ksum: [n_streams, n_blocks_stride, d] of which the
+ * first n_blocks rows are scored.  dtype GFST_F32 computes with fp32 FMAs;
+ * GFST_BF16 runs the tcgen05 tensor-core path (bf16 operands, fp32 accumulate).
+ * Limits: 1 <= k <= 32; d a multiple of 8 (bf16) or 4 (f32), d <= 256.     */
+GFST_API int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_streams, int n_queries,
+                    int n_blocks, int n_blocks_stride, int d, int k, int dtype,
+                    float* top_scores, int32_t* top_idx, cudaStream_t stream);
+
+/* ---- exact-token readout ------------------------------------------------------
+ * For every stream s and query q, over the tokens of the k blocks top_idx[s,q,:]
+ * (entries < 0 or >= n_slots are skipped; a block listed twice counts once):
+ *   score(b, p) = Q[s,q,:] . pool_K[s,b,p,:]        (fp32 accumulate)
+ *   best = argmax in the total order (score descending, token index ascending),
+ *          token index = b * L + p
+ *   best_tok[s,q] = best (or -1 when no block is valid), best_score[s,q] = its score,
+ *   out_V[s,q,:] = pool_V[s,best_b,best_p,:] (zeros when no block is valid)
+ * Q: [n_streams, n_queries, d]; pool_K: [n_streams, n_slots, L, d];
+ * pool_V: [n_streams, n_slots, L, dv] (may be NULL together with out_V);
+ * top_idx: [n_streams, n_queries, k].  dtype applies to Q, pool_K, pool_V, out_V.
+ * Limits: 1 <= k <= 32, d a multiple of 8, d <= 256, L >= 1.                     */
+GFST_API int gfst_exact_readout(const void* Q, const void* pool_K, const void* pool_V,
+                       const int32_t* top_idx, int64_t n_streams, int n_queries,
+                       int n_slots, int L, int d, int dv, int k, int dtype,
+                       int32_t* best_tok, float* best_score, void* out_V,
+                       cudaStream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* GFST_B200_H_ */

@@ -1,0 +1,244 @@
+"""CPU restatement of the reference's GFST-HMB hot path -- TEST INFRASTRUCTURE ONLY.
+
+Imported only by tests/, __graft_entry__.smoke() and bench.py's CPU baseline /
+reference arm, never by the product package.  Every function names the
+reference file:line (pkhairkh/gfst-hmb-public) it restates.  Arrays are numpy;
+the QR uses torch's CPU LAPACK binding, which is the exact call the reference
+makes (``torch.linalg.qr(..., mode="reduced")``, src/gfst_hmb_mpuc/gfst.py:29).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+SIGN_FIRST_SIGNIFICANT = 0
+SIGN_R_DIAG_POSITIVE = 1
+
+
+# ---------------------------------------------------------------------------
+# bf16 helpers (round to nearest even, as torch / CUDA do)
+# ---------------------------------------------------------------------------
+def to_bf16_f32(x: np.ndarray) -> np.ndarray:
+    """Round float32 values to bf16 and widen back to float32."""
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    return t.to(torch.bfloat16).to(torch.float32).numpy()
+
+
+def as_f32(x) -> np.ndarray:
+    if isinstance(x, torch.Tensor):
+        return x.detach().to("cpu", torch.float32).numpy()
+    return np.asarray(x, dtype=np.float32)
+
+
+# ---------------------------------------------------------------------------
+# frames
+# ---------------------------------------------------------------------------
+def canonicalize_qr_column_signs(q: np.ndarray, eps_sign: float = 1e-8) -> np.ndarray:
+    """gfst.py:35-46: per column, the first row with |q| > eps_sign decides the
+    sign; a negative entry flips the column; columns without one stay."""
+    q = np.asarray(q)
+    mask = np.abs(q) > np.float32(eps_sign)
+    first = np.argmax(mask, axis=-2)  # first True row (0 if none)
+    first_vals = np.take_along_axis(q, first[..., None, :], axis=-2)[..., 0, :]
+    flip = mask.any(axis=-2) & (first_vals < 0)
+    sign = np.where(flip, -1.0, 1.0).astype(q.dtype)
+    return q * sign[..., None, :]
+
+
+def qr_reference(matrices: np.ndarray, eps_sign: float = 1e-8,
+                 sign_mode: int = SIGN_FIRST_SIGNIFICANT) -> np.ndarray:
+    """gfst.py:26-32 (canonical_qr_batched): reduced Householder QR in float32
+    through LAPACK, then the sign rule.  ``SIGN_R_DIAG_POSITIVE`` multiplies each
+    column by sign(R_jj) (sign(0) = +1) instead."""
+    a = torch.from_numpy(np.ascontiguousarray(matrices, dtype=np.float32))
+    if a.numel() == 0:
+        return np.zeros(matrices.shape, dtype=np.float32)
+    q, r = torch.linalg.qr(a, mode="reduced")
+    q = q.numpy()
+    if sign_mode == SIGN_R_DIAG_POSITIVE:
+        diag = np.diagonal(r.numpy(), axis1=-2, axis2=-1)
+        return q * np.where(diag < 0, -1.0, 1.0).astype(np.float32)[..., None, :]
+    return canonicalize_qr_column_signs(q, eps_sign)
+
+
+def qr_fp64(matrices: np.ndarray, eps_sign: float = 1e-8, sign_mode: int = SIGN_FIRST_SIGNIFICANT) -> np.ndarray:
+    """Same as qr_reference in float64 (error analysis: distance to the exact Q)."""
+    a = torch.from_numpy(np.ascontiguousarray(matrices, dtype=np.float64))
+    q, r = torch.linalg.qr(a, mode="reduced")
+    q = q.numpy()
+    if sign_mode == SIGN_R_DIAG_POSITIVE:
+        diag = np.diagonal(r.numpy(), axis1=-2, axis2=-1)
+        return q * np.where(diag < 0, -1.0, 1.0)[..., None, :]
+    return canonicalize_qr_column_signs(q, eps_sign)
+
+
+def frame_candidate(U: np.ndarray, A: np.ndarray | None, B: np.ndarray | None, beta: float = 1.0) -> np.ndarray:
+    """beta*U + A B^T in float32: the candidate form of gfst.py:136-140, which
+    also covers the plain rank-m update U + sum_i u_i v_i^T of the streaming
+    workloads (beta = 1)."""
+    U = np.asarray(U, dtype=np.float32)
+    c = (np.float32(beta) * U) if beta != 1.0 else U.copy()
+    if A is not None:
+        c = c + np.matmul(np.asarray(A, np.float32), np.swapaxes(np.asarray(B, np.float32), -1, -2))
+    return c.astype(np.float32)
+
+
+def residual_rank_one_candidate(U: np.ndarray, x: np.ndarray, alpha: float, eps_update: float = 1e-6) -> np.ndarray:
+    """gfst.py:115-140 (update_basis_candidate_batched, rule residual_rank_one_v1)."""
+    Ut = torch.from_numpy(np.asarray(U, np.float32))
+    xt = torch.from_numpy(np.asarray(x, np.float32))
+    weights = torch.matmul(Ut.transpose(-2, -1), xt.unsqueeze(-1)).squeeze(-1)
+    projection = torch.matmul(Ut, weights.unsqueeze(-1)).squeeze(-1)
+    residual = xt - projection
+    norm = torch.linalg.vector_norm(xt, dim=-1, keepdim=True)
+    scaled = residual / torch.sqrt(norm.square() + float(eps_update) ** 2)
+    novelty = torch.zeros_like(weights)
+    novelty[..., -1] = 1.0
+    out = (1.0 - alpha) * Ut + alpha * xt.unsqueeze(-1) * weights.unsqueeze(-2) \
+        + alpha * scaled.unsqueeze(-1) * novelty.unsqueeze(-2)
+    return out.numpy()
+
+
+def stream_frames(U0: np.ndarray, A: np.ndarray, B: np.ndarray, beta: float = 1.0, eps_sign: float = 1e-8,
+                  sign_mode: int = SIGN_FIRST_SIGNIFICANT, out_every: int = 0):
+    """Per-token loop of modeling.py:2355-2374 (update candidate, canonical QR)
+    over frames [F, d, r] with inputs A [F, T, d, m], B [F, T, r, m].
+    Returns (final frames, snapshots [T//out_every, F, d, r] or None)."""
+    U = np.array(U0, dtype=np.float32, copy=True)
+    T = A.shape[1]
+    snaps = []
+    for t in range(T):
+        U = qr_reference(frame_candidate(U, A[:, t], B[:, t], beta), eps_sign, sign_mode)
+        if out_every and (t + 1) % out_every == 0:
+            snaps.append(U.copy())
+    return U, (np.stack(snaps) if snaps else None)
+
+
+# frame metrics ---------------------------------------------------------------
+def orthogonality_error(Q: np.ndarray) -> np.ndarray:
+    """max |Q^T Q - I| per frame (float64 arithmetic)."""
+    Q = np.asarray(Q, np.float64)
+    g = np.matmul(np.swapaxes(Q, -1, -2), Q)
+    eye = np.eye(Q.shape[-1])
+    return np.abs(g - eye).max(axis=(-1, -2))
+
+
+def subspace_distance(Q1: np.ndarray, Q2: np.ndarray, prefix: int | None = None) -> np.ndarray:
+    """Principal-angle distance max sin(theta) between span(Q1[:, :p]) and
+    span(Q2[:, :p]) per frame, in float64.  Both bases are re-orthonormalised in
+    float64 first (so fp32 orthogonality error does not masquerade as angle),
+    then sin(theta_max) = ||(I - Q2 Q2^T) Q1||_2, which has no cancellation for
+    small angles."""
+    Q1 = np.asarray(Q1, np.float64)
+    Q2 = np.asarray(Q2, np.float64)
+    if prefix is not None:
+        Q1 = Q1[..., :prefix]
+        Q2 = Q2[..., :prefix]
+    Q1 = np.linalg.qr(Q1)[0]
+    Q2 = np.linalg.qr(Q2)[0]
+    resid = Q1 - np.matmul(Q2, np.matmul(np.swapaxes(Q2, -1, -2), Q1))
+    return np.linalg.svd(resid, compute_uv=False).max(axis=-1)
+
+
+def max_prefix_subspace_distance(Q1: np.ndarray, Q2: np.ndarray) -> np.ndarray:
+    """Largest principal-angle distance over every leading-column prefix 1..r
+    (the nested flag subspaces of modeling.py:2380-2417)."""
+    r = Q1.shape[-1]
+    return np.max(np.stack([subspace_distance(Q1, Q2, p) for p in range(1, r + 1)]), axis=0)
+
+
+# ---------------------------------------------------------------------------
+# block commit
+# ---------------------------------------------------------------------------
+def block_commit_mean(K_block: np.ndarray, bf16: bool) -> np.ndarray:
+    """Summary key of a block = mean of its L token keys (the mean-of-keys summary
+    of the streaming workloads; the reference's eigen-based block summary is
+    modeling.py:3496-3507).  Sum in token
+    order in float32, divide by L in float32, round once to bf16 when the memory
+    is bf16.  K_block: [..., L, d] float32 (bf16-representable for bf16 memory)."""
+    K = np.asarray(K_block, np.float32)
+    acc = np.zeros(K.shape[:-2] + K.shape[-1:], np.float32)
+    for t in range(K.shape[-2]):
+        acc = (acc + K[..., t, :]).astype(np.float32)
+    mean = (acc / np.float32(K.shape[-2])).astype(np.float32)
+    return to_bf16_f32(mean) if bf16 else mean
+
+
+# ---------------------------------------------------------------------------
+# top-k block select
+# ---------------------------------------------------------------------------
+def _order_desc_idx_asc(scores: np.ndarray) -> np.ndarray:
+    """Indices sorting the last axis by (score desc, index asc); NaN last."""
+    s = np.where(np.isnan(scores), -np.inf, scores)
+    n = s.shape[-1]
+    idx = np.broadcast_to(np.arange(n), s.shape)
+    # lexsort: last key is primary
+    order = np.lexsort((idx, -s), axis=-1)
+    return order
+
+
+def block_scores(Q: np.ndarray, Ksum: np.ndarray) -> np.ndarray:
+    """scores[s, q, b] = Q[s,q] . Ksum[s,b] in float64 (exact enough to rank
+    bf16/fp32 inputs; retrieval.py:165-172 computes keys @ q)."""
+    return np.matmul(np.asarray(Q, np.float64), np.swapaxes(np.asarray(Ksum, np.float64), -1, -2))
+
+
+def block_topk(Q: np.ndarray, Ksum: np.ndarray, k: int):
+    """retrieval.py:165-172 (exact_topk) batched over streams and queries, with
+    the deterministic total order (score desc, block index asc).  Returns
+    (top_scores f32 [S,Nq,k], top_idx int32 [S,Nq,k], margin_ok bool [S,Nq]);
+    slots past the block count hold (-inf, -1).  margin_ok is False when the
+    k-th and (k+1)-th scores are within 1e-3 relative, where any order of the
+    boundary is acceptable."""
+    scores = block_scores(Q, Ksum)
+    nb = scores.shape[-1]
+    order = _order_desc_idx_asc(scores)
+    kk = min(k, nb)
+    top_idx = np.full(scores.shape[:-1] + (k,), -1, np.int32)
+    top_sc = np.full(scores.shape[:-1] + (k,), -np.inf, np.float32)
+    top_idx[..., :kk] = order[..., :kk]
+    top_sc[..., :kk] = np.take_along_axis(scores, order[..., :kk], axis=-1).astype(np.float32)
+    margin_ok = np.ones(scores.shape[:-1], bool)
+    if nb > kk:
+        sk = np.take_along_axis(scores, order[..., kk - 1:kk], axis=-1)[..., 0]
+        sn = np.take_along_axis(scores, order[..., kk:kk + 1], axis=-1)[..., 0]
+        margin_ok = np.abs(sk - sn) > 1e-3 * np.maximum(np.abs(sk), 1e-30)
+    return top_sc, top_idx, margin_ok
+
+
+# ---------------------------------------------------------------------------
+# exact-token readout
+# ---------------------------------------------------------------------------
+def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, top_idx: np.ndarray):
+    """modeling.py:599-657 (_score_block_tokens: token score = key . query) and
+    modeling.py:1151-1169 (best token = first of the scores sorted descending),
+    with token index b*L + p and the total order (score desc, index asc).
+    Q [S,Nq,d]; pool_K [S,NB,L,d]; pool_V [S,NB,L,dv]; top_idx [S,Nq,k] int.
+    Returns (best_tok int32 [S,Nq], best_score f32 [S,Nq], out_V [S,Nq,dv] or None,
+    margin_ok bool [S,Nq] -- False when the runner-up is within 1e-3 relative)."""
+    S, Nq, _ = Q.shape
+    L = pool_K.shape[2]
+    best_tok = np.full((S, Nq), -1, np.int32)
+    best_score = np.full((S, Nq), -np.inf, np.float32)
+    margin_ok = np.ones((S, Nq), bool)
+    dv = pool_V.shape[-1] if pool_V is not None else 0
+    out_V = np.zeros((S, Nq, dv), np.float32) if pool_V is not None else None
+    for s in range(S):
+        for q in range(Nq):
+            blocks = [int(b) for b in top_idx[s, q] if b >= 0]
+            blocks = sorted(set(blocks))
+            if not blocks:
+                continue
+            keys = np.concatenate([pool_K[s, b] for b in blocks], axis=0).astype(np.float64)
+            toks = np.concatenate([b * L + np.arange(L) for b in blocks])
+            sc = keys @ np.asarray(Q[s, q], np.float64)
+            order = np.lexsort((toks, -np.where(np.isnan(sc), -np.inf, sc)))
+            w = order[0]
+            best_tok[s, q] = toks[w]
+            best_score[s, q] = np.float32(sc[w])
+            if len(order) > 1:
+                s1, s2 = sc[order[0]], sc[order[1]]
+                margin_ok[s, q] = abs(s1 - s2) > 1e-3 * max(abs(s1), 1e-30)
+            if pool_V is not None:
+                out_V[s, q] = pool_V[s, toks[w] // L, toks[w] % L]
+    return best_tok, best_score, out_V, margin_ok

@@ -1,0 +1,177 @@
+"""Generate the golden vectors in tests/golden/*.npz from the reference's own code.
+
+Run in the build container only (it needs the read-only reference checkout):
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+The reference package cannot be imported as shipped (its __init__ pulls in
+modules that were left out of the public release), so this script registers
+namespace modules pointing into the reference's source tree, plus a stub for
+the missing sm120 runtime loader whose accelerated ops report "unavailable",
+which sends the reference down its own torch code paths.  Nothing is copied.
+
+Every fixture stores the inputs and the reference outputs.  The CPU tests pin
+the oracle against them; the GPU tests pin the kernels against the oracle.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+REPO = OUT.parents[1]
+
+
+def install_reference(root: Path):
+    src = root / "src" / "gfst_hmb_mpuc"
+    pkg = types.ModuleType("gfst_hmb_mpuc")
+    pkg.__path__ = [str(src)]
+    sys.modules["gfst_hmb_mpuc"] = pkg
+    for sub in ("diagnostics", "training"):
+        m = types.ModuleType(f"gfst_hmb_mpuc.{sub}")
+        m.__path__ = [str(src / sub)]
+        sys.modules[f"gfst_hmb_mpuc.{sub}"] = m
+    # runtime_backends: the public release lacks sm120.py; every accelerated op
+    # reports unavailable so callers take their native torch branch
+    rb = types.ModuleType("gfst_hmb_mpuc.runtime_backends")
+    rb.__path__ = [str(src / "runtime_backends")]
+    sm = types.ModuleType("gfst_hmb_mpuc.runtime_backends.sm120")
+
+    def _none(*args, **kwargs):
+        return None
+
+    def _false(*args, **kwargs):
+        return False
+
+    for name in ("exact_block_score", "exact_block_materialize", "gfst_block_commit", "gfst_heev",
+                 "gfst_reference_block_average", "gfst_reference_global_sketch", "gfst_local_qr",
+                 "gfst_global_sketch", "gfst_canonical_summary_from_eigpairs", "gfst_summary_from_sketch",
+                 "gfst_summary_from_sketch_batched", "load_sm120_extension", "load_mathdx_extension",
+                 "mathdx_extension_dependency_report", "mathdx_runtime_dependency_report", "mpuc_recurrent_scan",
+                 "segmented_logsumexp_occurrence", "segmented_max_by_group"):
+        setattr(sm, name, _none)
+    for name in ("exact_readout_score_available", "experimental_canonical_summary_enabled",
+                 "mathdx_extension_available", "mpuc_recurrent_scan_available", "segmented_reduction_available",
+                 "sm120_exact_math_kernels_available"):
+        setattr(sm, name, _false)
+    sys.modules["gfst_hmb_mpuc.runtime_backends.sm120"] = sm
+    for name in dir(sm):
+        if not name.startswith("_"):
+            setattr(rb, name, getattr(sm, name))
+    rb.sm120 = sm
+    sys.modules["gfst_hmb_mpuc.runtime_backends"] = rb
+    return importlib
+
+
+def batched_qr_inputs(n, d, r, seed):
+    sys.path.insert(0, str(REPO))
+    from gfst_hmb_public_b200 import workloads as wl
+
+    return wl.batched_qr_inputs(n, d, r, seed=seed)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", default="/root/reference")
+    args = parser.parse_args()
+    install_reference(Path(args.reference))
+    gfst = importlib.import_module("gfst_hmb_mpuc.gfst")
+    retrieval = importlib.import_module("gfst_hmb_mpuc.retrieval")
+    hh = importlib.import_module("gfst_hmb_mpuc.diagnostics.temp_local_qr_householder_vs_mgs_dataset")
+    sign = importlib.import_module("gfst_hmb_mpuc.diagnostics.temp_local_qr_sign_problem_analysis")
+    bcr = importlib.import_module("gfst_hmb_mpuc.diagnostics.block_commit_replay")
+    perf = importlib.import_module("gfst_hmb_mpuc.perf")
+    torch.manual_seed(0)
+
+    # 1. the 4 x 2 known-answer candidate of the reference's QR tests
+    #    (tests/test_temp_local_qr_householder_vs_mgs_dataset.py:54-70)
+    cand = torch.tensor([[1.0, 0.2], [0.1, 0.95], [0.3, 0.1], [0.2, -0.05]], dtype=torch.float32)
+    traced = hh.householder_reduced_q_with_trace(cand, eps_sign=1e-8)
+    np.savez(OUT / "qr_known_answer.npz",
+             candidate=cand.numpy(),
+             canonical_q=gfst.canonical_qr(cand, eps_sign=1e-8).numpy(),
+             householder_signfixed_q=traced["signfixed_q"].detach().numpy(),
+             mgs_q=hh.modified_gram_schmidt_q(cand, eps_sign=1e-8, reorthogonalize=True).numpy())
+
+    # 2. seeded sign-problem families of the reference's QR diagnostics
+    #    (diagnostics/temp_local_qr_sign_problem_analysis.py:249-301)
+    cases = sign.generate_random_sign_problem_cases(num_cases=20, seed=1234, rows=64, cols=32)
+    mats = torch.stack([c["matrix"] for c in cases])
+    np.savez(OUT / "qr_sign_problem_cases.npz",
+             matrices=mats.numpy(),
+             families=np.array([c["family"] for c in cases]),
+             canonical_q=gfst.canonical_qr_batched(mats, eps_sign=1e-8).numpy())
+
+    # 3. batched-QR workload sample through canonical_qr_batched (gfst.py:26-32)
+    x = batched_qr_inputs(512, 64, 8, seed=20261201 + 1)
+    np.savez(OUT / "qr_batched_sample.npz", matrices=x.numpy(),
+             canonical_q=gfst.canonical_qr_batched(x, eps_sign=1e-8).numpy())
+
+    # 4. reference update rule residual_rank_one_v1 over 16 tokens (gfst.py:73-140)
+    g = torch.Generator().manual_seed(5)
+    U = gfst.canonical_qr_batched(torch.randn((4, 64, 32), generator=g), eps_sign=1e-8)
+    xs = torch.randn((16, 4, 64), generator=g)
+    traj = []
+    cands = []
+    Ut = U
+    for t in range(16):
+        cands.append(gfst.update_basis_candidate_batched(Ut, xs[t], 0.2, eps_update=1e-6))
+        Ut = gfst.update_basis_batched(Ut, xs[t], 0.2, eps_update=1e-6, eps_sign=1e-8)
+        traj.append(Ut)
+    np.savez(OUT / "update_rule_trajectory.npz", U0=U.numpy(), values=xs.numpy(), alpha=np.float32(0.2),
+             candidates=torch.stack(cands).numpy(), frames=torch.stack(traj).numpy())
+
+    # 5. retrieval: exact_topk (retrieval.py:165-172) on seeded banks, and the
+    #    small bank of tests/test_retrieval.py:14-52
+    g = torch.Generator().manual_seed(9)
+    keys = torch.randn((64, 32), generator=g)
+    queries = torch.randn((8, 32), generator=g)
+    idx, vals = zip(*[retrieval.FaissGpuRetriever.exact_topk(keys, q, 5) for q in queries])
+    small = torch.tensor([[1.0, 0.0, 0.0, 0.0], [0.0, 1.0, 0.0, 0.0], [0.5, 0.5, 0.0, 0.0],
+                          [0.0, 0.0, 1.0, 0.0], [0.0, 0.0, 0.0, 1.0], [0.8, 0.2, 0.0, 0.0]])
+    sq = torch.tensor([1.0, 0.0, 0.0, 0.0])
+    si, sv = retrieval.FaissGpuRetriever.exact_topk(small, sq, 3)
+    np.savez(OUT / "retrieval_exact_topk.npz", keys=keys.numpy(), queries=queries.numpy(),
+             top_idx=torch.stack(idx).numpy(), top_scores=torch.stack(vals).numpy(),
+             small_keys=small.numpy(), small_query=sq.numpy(), small_idx=si.numpy(), small_scores=sv.numpy())
+
+    # 6. reference block commit replay, native path (block_commit_replay.py:97-139)
+    g = torch.Generator().manual_seed(13)
+    frames = gfst.canonical_qr_batched(torch.randn((16, 8, 4), generator=g), eps_sign=1e-8)
+    proj_sum = sum(gfst.basis_projector(f) for f in frames)
+    red_sum = torch.randn((8,), generator=g) * 3.0
+    weight = torch.randn((6, 16), generator=g)
+    bundle = {"projector_sum": proj_sum, "reduced_sum": red_sum, "token_count": 16, "max_flag_dim": 4,
+              "flag_dims": (2, 4), "eps": 1e-6, "eps_sign": 1e-8, "block_key_proj_weight": weight,
+              "prefix_dims": (2, 4)}
+    rep = bcr.replay_block_commit_bundle(bundle, implementation="native")
+    np.savez(OUT / "block_commit_replay.npz", projector_sum=proj_sum.numpy(), reduced_sum=red_sum.numpy(),
+             token_count=16, flag_dims=np.array([2, 4]), weight=weight.numpy(),
+             average_projector=rep["average_projector"].numpy(), summary_basis=rep["summary_basis"].numpy(),
+             reduced_mean=rep["reduced_mean"].numpy(), top_vector=rep["top_vector"].numpy(),
+             block_key=rep["block_key"].numpy())
+
+    # 7. exact-token collapse + select (perf.py:164-229, modeling.py:1151-1169)
+    g = torch.Generator().manual_seed(17)
+    scores = torch.randn((48,), generator=g)
+    token_ids = torch.randint(0, 20, (48,), generator=g)
+    blocks = torch.arange(48) // 16
+    positions = torch.arange(48) % 16
+    uid, gsc, gbl, gpo = perf.collapse_logsumexp_scores_and_occurrence(scores, token_ids, blocks, positions)
+    order = torch.argsort(gsc, descending=True)
+    np.savez(OUT / "readout_collapse.npz", scores=scores.numpy(), token_ids=token_ids.numpy(),
+             blocks=blocks.numpy(), positions=positions.numpy(), unique_ids=uid.numpy(),
+             grouped_scores=gsc.numpy(), grouped_blocks=gbl.numpy(), grouped_positions=gpo.numpy(),
+             selected_token=int(uid[order[0]]))
+    for p in sorted(OUT.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,73 @@
+"""The C-ABI library loads without a GPU, exports every symbol declared in
+include/gfst_b200.h, and rejects bad arguments on the host before touching
+the device (no kernel is launched by these calls)."""
+import re
+from pathlib import Path
+
+import pytest
+
+from gfst_hmb_public_b200 import _native as nat
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "gfst_b200.h"
+
+
+def declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"GFST_API\s+[\w\s\*]+?\b(gfst_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = nat.load()
+    names = declared()
+    assert len(names) >= 8
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(nat.exported_symbols())
+
+
+def test_status_strings_and_version():
+    lib = nat.load()
+    assert lib.gfst_status_string(0) == b"ok"
+    assert lib.gfst_status_string(2) == b"unsupported shape"
+    assert lib.gfst_abi_version() >> 16 == 1
+
+
+def test_host_validation_rejects_without_launching():
+    lib = nat.load()
+    # r > 32
+    assert lib.gfst_frame_update_qr(None, None, None, 1.0, None, 4, 64, 40, 0, 1e-8, 0, None) == 2
+    assert b"r=40" in lib.gfst_last_error()
+    # r > d
+    assert lib.gfst_frame_update_qr(None, None, None, 1.0, None, 4, 4, 8, 0, 1e-8, 0, None) == 2
+    # unknown sign mode
+    assert lib.gfst_frame_update_qr(None, None, None, 1.0, None, 4, 64, 8, 0, 1e-8, 7, None) == 1
+    # rank too large
+    assert lib.gfst_frame_update_qr(None, None, None, 1.0, None, 4, 64, 8, 9, 1e-8, 0, None) == 2
+    # null buffers with work to do
+    assert lib.gfst_frame_update_qr(None, None, None, 1.0, None, 4, 64, 8, 0, 1e-8, 0, None) == 1
+    # empty batch is a no-op
+    assert lib.gfst_frame_update_qr(None, None, None, 1.0, None, 0, 64, 8, 0, 1e-8, 0, None) == 0
+    # streaming alignment rule: d*m, r*m multiples of 4
+    assert lib.gfst_frame_stream(None, None, None, 1.0, 4, 8, 6, 3, 1, 1e-8, 0, None, 0, None) in (1, 3)
+    # commit: slot out of range, bad dtype
+    assert lib.gfst_block_commit_mean(None, None, None, None, None, 2, 4, 4, 16, 64, 64, 1, None) == 1
+    assert lib.gfst_block_topk(None, None, 1, 1, 4, 4, 64, 33, 0, None, None, None) == 2
+    assert lib.gfst_block_topk(None, None, 1, 1, 4, 4, 64, 2, 5, None, None, None) == 7
+    assert lib.gfst_exact_readout(None, None, None, None, 1, 1, 4, 16, 64, 64, 0, 1, None, None, None, None) == 2
+
+
+def test_python_ops_reject_cpu_tensors():
+    import torch
+
+    from gfst_hmb_public_b200 import gfst, readout, retrieval
+
+    with pytest.raises(RuntimeError):
+        gfst.canonical_qr_batched(torch.randn(2, 8, 4))
+    with pytest.raises(RuntimeError):
+        retrieval.block_topk(torch.randn(1, 2, 8), torch.randn(1, 4, 8), 2)
+    with pytest.raises(RuntimeError):
+        readout.exact_readout(torch.randn(1, 2, 8), torch.randn(1, 2, 4, 8), None,
+                              torch.zeros(1, 2, 2, dtype=torch.int32))
+    with pytest.raises(RuntimeError):
+        retrieval.BlockRetriever().search(state=object(), layer_idx=0, batch_idx=0, keys_tensor=torch.eye(4),
+                                          query_tensor=torch.ones(4), top_k=2)

@@ -1,0 +1,170 @@
+"""Parity of the sm_100a frame kernels (update + Householder thin QR, streaming
+pass) against the CPU oracle, through the C ABI.
+
+Tolerances (the parity bar for frames): orthogonality max|Q^T Q - I| <= 1e-5,
+principal-angle distance of every leading-column prefix <= 1e-4, and
+elementwise |Q - Q_oracle| <= 1e-4 (two correct fp32 Householder codes differ by
+up to ~5e-5 on the near-collinear frames).
+"""
+import numpy as np
+import pytest
+import torch
+
+from gfst_hmb_public_b200 import gfst, workloads as wl
+from oracle import gfst_oracle as go
+
+pytestmark = pytest.mark.gpu
+
+ORTH_TOL = 1e-5
+SUBSPACE_TOL = 1e-4
+ELEM_TOL = 1e-4
+MODES = [go.SIGN_FIRST_SIGNIFICANT, go.SIGN_R_DIAG_POSITIVE]
+
+
+def _check_frames(q_dev: torch.Tensor, q_ref: np.ndarray, elem_tol: float = ELEM_TOL):
+    q = q_dev.detach().cpu().numpy()
+    assert q.shape == q_ref.shape
+    assert np.isfinite(q).all()
+    assert go.orthogonality_error(q).max() <= ORTH_TOL
+    assert go.max_prefix_subspace_distance(q, q_ref).max() <= SUBSPACE_TOL
+    assert np.abs(q - q_ref).max() <= elem_tol
+
+
+def test_reference_golden_candidate(cuda_device):
+    # 4 x 2 candidate of tests/test_temp_local_qr_householder_vs_mgs_dataset.py:54-70
+    cand = np.array([[1.0, 0.2], [0.1, 0.95], [0.3, 0.1], [0.2, -0.05]], np.float32)
+    q = gfst.gfst_local_qr(torch.from_numpy(cand).to(cuda_device), 1e-8)
+    _check_frames(q.unsqueeze(0), go.qr_reference(cand[None], 1e-8)[0][None])
+
+
+@pytest.mark.parametrize("sign_mode", MODES)
+def test_batched_qr_workload_sample(cuda_device, sign_mode):
+    spec = wl.BATCHED_QR
+    x = wl.batched_qr_inputs(8192, spec["d"], spec["r"], seed=spec["seed"])
+    q = gfst.frame_update_qr(x.to(cuda_device), sign_mode=sign_mode)
+    _check_frames(q, go.qr_reference(x.numpy(), 1e-8, sign_mode))
+
+
+@pytest.mark.parametrize(
+    "d,r",
+    [(4, 2), (5, 3), (7, 1), (8, 8), (16, 4), (33, 17), (64, 8), (64, 32), (100, 20), (128, 16), (128, 32),
+     (200, 8), (256, 16), (9, 9)],
+)
+def test_every_shape_class(cuda_device, d, r):
+    g = torch.Generator().manual_seed(d * 1000 + r)
+    x = torch.randn((37, d, r), generator=g)
+    for mode in MODES:
+        q = gfst.frame_update_qr(x.to(cuda_device), sign_mode=mode)
+        _check_frames(q, go.qr_reference(x.numpy(), 1e-8, mode))
+
+
+@pytest.mark.parametrize("m,beta", [(1, 1.0), (2, 0.8), (4, 1.0), (8, 0.5)])
+def test_rank_m_update_then_qr(cuda_device, m, beta):
+    g = torch.Generator().manual_seed(100 + m)
+    U = wl.random_orthonormal_frames(64, 128, 32, seed=7)
+    A = torch.randn((64, 128, m), generator=g) / 11.3
+    B = torch.randn((64, 32, m), generator=g) / 11.3
+    q = gfst.frame_update_qr(U.to(cuda_device), A.to(cuda_device), B.to(cuda_device), beta=beta,
+                             sign_mode="r_diag_positive")
+    ref = go.qr_reference(go.frame_candidate(U.numpy(), A.numpy(), B.numpy(), beta), 1e-8,
+                          go.SIGN_R_DIAG_POSITIVE)
+    _check_frames(q, ref)
+
+
+def test_reference_update_rule(cuda_device):
+    # residual_rank_one_v1 (gfst.py:115-140) folded into beta*U + A B^T
+    g = torch.Generator().manual_seed(3)
+    U = wl.random_orthonormal_frames(16, 64, 32, seed=11)
+    x = torch.randn((16, 64), generator=g)
+    q = gfst.update_basis_batched(U.to(cuda_device), x.to(cuda_device), 0.2)
+    ref = go.qr_reference(go.residual_rank_one_candidate(U.numpy(), x.numpy(), 0.2), 1e-8)
+    _check_frames(q, ref)
+
+
+def test_degenerate_frames(cuda_device):
+    x = torch.zeros((3, 16, 4))
+    x[1, :, 0] = 1.0            # rank one, repeated column
+    x[1, :, 1] = 1.0
+    x[2] = torch.eye(16, 4) * -2.0  # negative diagonal
+    for mode in MODES:
+        q = gfst.frame_update_qr(x.to(cuda_device), sign_mode=mode).cpu().numpy()
+        ref = go.qr_reference(x.numpy(), 1e-8, mode)
+        assert np.isfinite(q).all()
+        # zero frame -> identity columns, like LAPACK
+        assert np.abs(q[0] - ref[0]).max() <= 1e-6
+        assert np.abs(q[2] - ref[2]).max() <= 1e-6
+        # rank-deficient frame: the leading column is determined
+        assert np.abs(q[1][:, 0] - ref[1][:, 0]).max() <= 1e-6
+
+
+def test_deterministic(cuda_device):
+    x = wl.batched_qr_inputs(4096, 64, 8, seed=5).to(cuda_device)
+    a = gfst.frame_update_qr(x)
+    b = gfst.frame_update_qr(x)
+    assert torch.equal(a, b)
+
+
+def test_in_place_alias(cuda_device):
+    x = wl.batched_qr_inputs(512, 64, 8, seed=6).to(cuda_device)
+    ref = gfst.frame_update_qr(x)
+    gfst.frame_update_qr(x, out=x)
+    assert torch.equal(ref, x)
+
+
+def test_nan_input_returns(cuda_device):
+    x = torch.randn((8, 64, 8))
+    x[3, 5, 2] = float("nan")
+    q = gfst.frame_update_qr(x.to(cuda_device)).cpu()
+    assert torch.isfinite(q[0]).all() and not torch.isfinite(q[3]).all()
+
+
+@pytest.mark.parametrize("sign_mode", MODES)
+def test_stream_small_trajectory(cuda_device, sign_mode):
+    spec = wl.STREAM_SMALL
+    F = spec.streams
+    U0 = wl.random_orthonormal_frames(F, spec.d, spec.r, seed=spec.seed)
+    A, B = wl.stream_update_factors(F, spec.tokens, spec.d, spec.r, spec.m, seed=spec.seed + 100)
+    U = U0.to(cuda_device).clone()
+    snaps = gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), sign_mode=sign_mode, out_every=16)
+    ref_final, ref_snaps = go.stream_frames(U0.numpy(), A.numpy(), B.numpy(), 1.0, 1e-8, sign_mode, 16)
+    _check_frames(U, ref_final)
+    assert snaps.shape == ref_snaps.shape
+    for i in range(snaps.shape[0]):
+        _check_frames(snaps[i], ref_snaps[i])
+
+
+@pytest.mark.parametrize("d,r,m,T", [(128, 16, 2, 256), (128, 32, 4, 96), (64, 32, 4, 64)])
+def test_stream_mid_and_full_frames(cuda_device, d, r, m, T):
+    F = 12
+    U0 = wl.random_orthonormal_frames(F, d, r, seed=d + r)
+    A, B = wl.stream_update_factors(F, T, d, r, m, seed=d * r)
+    U = U0.to(cuda_device).clone()
+    gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), sign_mode="r_diag_positive")
+    ref, _ = go.stream_frames(U0.numpy(), A.numpy(), B.numpy(), 1.0, 1e-8, go.SIGN_R_DIAG_POSITIVE)
+    _check_frames(U, ref)
+
+
+def test_stream_matches_repeated_single_steps(cuda_device):
+    F, d, r, m, T = 40, 128, 16, 2, 24
+    U0 = wl.random_orthonormal_frames(F, d, r, seed=1).to(cuda_device)
+    A, B = wl.stream_update_factors(F, T, d, r, m, seed=2, device="cpu")
+    A, B = A.to(cuda_device), B.to(cuda_device)
+    U = U0.clone()
+    gfst.stream_frames(U, A, B)
+    V = U0.clone()
+    for t in range(T):
+        V = gfst.frame_update_qr(V, A[:, t].contiguous(), B[:, t].contiguous())
+    # same kernels, same arithmetic order -> bitwise identical
+    assert torch.equal(U, V)
+
+
+def test_cpu_tensors_rejected():
+    with pytest.raises(RuntimeError):
+        gfst.canonical_qr_batched(torch.randn(2, 8, 4))
+
+
+def test_unsupported_shape_rejected(cuda_device):
+    with pytest.raises(RuntimeError):
+        gfst.frame_update_qr(torch.randn(2, 64, 33, device=cuda_device))
+    with pytest.raises(RuntimeError):
+        gfst.frame_update_qr(torch.randn(2, 300, 8, device=cuda_device))

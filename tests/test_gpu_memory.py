@@ -1,0 +1,175 @@
+"""Parity of block commit, coarse top-k and exact readout kernels against the
+CPU oracle, through the C ABI.
+
+Bar: commit summaries bit-exact (same fp32 token-order sum and rounding);
+selected block indices and exact-token argmax bit-exact wherever the oracle's
+margin to the runner-up exceeds 1e-3 relative; readout values exact copies;
+scores within 1e-5 relative (fp32 accumulation order only).
+"""
+import numpy as np
+import pytest
+import torch
+
+from gfst_hmb_public_b200 import memory, readout, retrieval, workloads as wl
+from oracle import gfst_oracle as go
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.float32, torch.bfloat16]
+
+
+def _np(t):
+    return t.detach().to("cpu", torch.float32).numpy()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("L,d,dv", [(16, 64, 64), (64, 128, 128), (7, 24, 40), (128, 128, 64)])
+def test_block_commit_mean_bit_exact(cuda_device, dtype, L, d, dv):
+    S, n_slots = 9, 5
+    g = torch.Generator().manual_seed(L * d)
+    K = torch.randn((S, L, d), generator=g).to(dtype)
+    V = torch.randn((S, L, dv), generator=g).to(dtype)
+    mem = memory.BlockMemory(S, n_slots, L, d, dv, dtype=dtype, device=cuda_device)
+    for _ in range(3):
+        mem.commit(K.to(cuda_device), V.to(cuda_device))
+    slot = 2
+    assert torch.equal(mem.pool_K[:, slot].cpu(), K)
+    assert torch.equal(mem.pool_V[:, slot].cpu(), V)
+    ref = go.block_commit_mean(_np(K), bf16=dtype == torch.bfloat16)
+    assert np.array_equal(_np(mem.summary[:, slot]), ref)
+    assert mem.state_version == 3 and mem.next_slot() == 3
+    # untouched slots stay zero
+    assert torch.count_nonzero(mem.pool_K[:, 4]).item() == 0
+
+
+def test_block_commit_ring_wraps(cuda_device):
+    mem = memory.BlockMemory(2, 3, 4, 8, dtype=torch.float32, device=cuda_device)
+    for b in range(5):
+        K = torch.full((2, 4, 8), float(b), device=cuda_device)
+        mem.commit(K, K)
+    assert mem.slot_block_index().tolist() == [3, 4, 2]
+    assert mem.summary[:, 0, 0].tolist() == [3.0, 3.0]
+
+
+def _check_topk(scores, idx, Q, Ksum, k):
+    ref_s, ref_i, ok = go.block_topk(_np(Q), _np(Ksum), k)
+    got_i = idx.cpu().numpy()
+    got_s = scores.cpu().numpy()
+    assert ok.mean() > 0.5  # the cases are not degenerate
+    assert np.array_equal(got_i[ok], ref_i[ok])
+    fin = np.isfinite(ref_s)
+    np.testing.assert_allclose(got_s[fin & ok[..., None]], ref_s[fin & ok[..., None]], rtol=1e-5, atol=1e-5)
+    assert np.array_equal(fin, np.isfinite(got_s))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("S,Nq,NB,d,k", [(4, 64, 16, 64, 2), (3, 200, 64, 128, 4), (2, 130, 512, 128, 16),
+                                          (1, 1, 5, 32, 8), (2, 17, 33, 96, 32)])
+def test_block_topk_matches_oracle(cuda_device, dtype, S, Nq, NB, d, k):
+    g = torch.Generator().manual_seed(S * Nq + NB)
+    Q = torch.randn((S, Nq, d), generator=g).to(dtype)
+    Ksum = torch.randn((S, NB, d), generator=g).to(dtype)
+    scores, idx = retrieval.block_topk(Q.to(cuda_device), Ksum.to(cuda_device), k)
+    _check_topk(scores, idx, Q, Ksum, k)
+
+
+def test_block_topk_ties_pick_lowest_index(cuda_device):
+    Ksum = torch.zeros((1, 10, 8))
+    Ksum[0, [2, 5, 7], 0] = 1.0  # three equal best scores
+    Q = torch.zeros((1, 1, 8))
+    Q[0, 0, 0] = 1.0
+    scores, idx = retrieval.block_topk(Q.to(cuda_device), Ksum.to(cuda_device), 4)
+    assert idx.cpu().tolist() == [[[2, 5, 7, 0]]]
+
+
+def test_block_topk_partial_bank(cuda_device):
+    Q = torch.randn((2, 3, 16), device=cuda_device)
+    Ksum = torch.randn((2, 8, 16), device=cuda_device)
+    scores, idx = retrieval.block_topk(Q, Ksum, 6, n_blocks=4)
+    assert (idx[..., 4:] == -1).all() and torch.isinf(scores[..., 4:]).all()
+    assert (idx[..., :4] >= 0).all() and (idx[..., :4] < 4).all()
+
+
+def test_retriever_matches_exact_oracle_on_small_bank(cuda_device):
+    # the small bank of tests/test_retrieval.py:14-52 in the reference
+    keys = torch.tensor([[1.0, 0.0, 0.0, 0.0], [0.0, 1.0, 0.0, 0.0], [0.5, 0.5, 0.0, 0.0],
+                         [0.0, 0.0, 1.0, 0.0], [0.0, 0.0, 0.0, 1.0], [0.8, 0.2, 0.0, 0.0]], device=cuda_device)
+    query = torch.tensor([1.0, 0.0, 0.0, 0.0], device=cuda_device)
+
+    class State:
+        state_version = 0
+
+    state = State()
+    r = retrieval.BlockRetriever()
+    indices, scores = r.search(state=state, layer_idx=0, batch_idx=0, keys_tensor=keys, query_tensor=query, top_k=3)
+    assert indices.tolist() == [0, 5, 2]
+    assert torch.allclose(scores.cpu(), torch.tensor([1.0, 0.8, 0.5]), atol=1e-5)
+    assert r._index_cache[(id(state), 0, 0)].device_index == 0
+    before = r._index_cache[(id(state), 0, 0)].state_version
+    state.state_version += 1
+    r.search(state=state, layer_idx=0, batch_idx=0, keys_tensor=keys, query_tensor=query, top_k=2)
+    assert r._index_cache[(id(state), 0, 0)].state_version > before
+    empty_i, empty_s = r.search(state=state, layer_idx=0, batch_idx=0, keys_tensor=keys[:0], query_tensor=query,
+                                top_k=2)
+    assert empty_i.numel() == 0 and empty_s.numel() == 0
+
+
+def test_retriever_rejects_cpu_and_wrong_device(cuda_device):
+    r = retrieval.BlockRetriever()
+
+    class State:
+        state_version = 0
+
+    with pytest.raises(RuntimeError):
+        r.search(state=State(), layer_idx=0, batch_idx=0, keys_tensor=torch.eye(4), query_tensor=torch.ones(4),
+                 top_k=2)
+    if torch.cuda.device_count() > 1:
+        with pytest.raises(RuntimeError):
+            r.search(state=State(), layer_idx=0, batch_idx=0, keys_tensor=torch.eye(4, device="cuda:1"),
+                     query_tensor=torch.ones(4, device="cuda:1"), top_k=2)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("S,Nq,NS,L,d,dv,k", [(3, 40, 16, 16, 64, 64, 2), (2, 33, 64, 64, 128, 128, 4),
+                                               (2, 9, 9, 128, 128, 64, 8), (1, 5, 4, 5, 16, 24, 3)])
+def test_exact_readout_matches_oracle(cuda_device, dtype, S, Nq, NS, L, d, dv, k):
+    g = torch.Generator().manual_seed(S * 100 + Nq)
+    pool_K = torch.randn((S, NS, L, d), generator=g).to(dtype)
+    pool_V = torch.randn((S, NS, L, dv), generator=g).to(dtype)
+    Q = torch.randn((S, Nq, d), generator=g).to(dtype)
+    sel = torch.stack([torch.stack([torch.randperm(NS, generator=g)[:k] for _ in range(Nq)]) for _ in range(S)])
+    sel = sel.to(torch.int32)
+    sel[0, 0, -1] = -1  # a skipped entry
+    best_tok, best_score, out_V = readout.exact_readout(Q.to(cuda_device), pool_K.to(cuda_device),
+                                                        pool_V.to(cuda_device), sel.to(cuda_device))
+    ref_tok, ref_score, ref_V, ok = go.exact_readout(_np(Q), _np(pool_K), _np(pool_V), sel.numpy())
+    got_tok = best_tok.cpu().numpy()
+    assert ok.mean() > 0.5
+    assert np.array_equal(got_tok[ok], ref_tok[ok])
+    np.testing.assert_allclose(best_score.cpu().numpy()[ok], ref_score[ok], rtol=1e-5, atol=1e-5)
+    assert np.array_equal(_np(out_V)[ok], ref_V[ok])
+
+
+def test_exact_readout_no_valid_block(cuda_device):
+    pool = torch.randn((1, 4, 8, 16), device=cuda_device)
+    sel = torch.full((1, 2, 3), -1, dtype=torch.int32, device=cuda_device)
+    tok, score, v = readout.exact_readout(torch.randn(1, 2, 16, device=cuda_device), pool, pool, sel)
+    assert tok.tolist() == [[-1, -1]] and torch.isinf(score).all() and (v == 0).all()
+
+
+def test_needle_queries_recover_the_needle(cuda_device):
+    # long-memory readout in miniature: query = key[needle] + N(0, 0.1^2)
+    S, NB, L, d, Nq, k = 4, 256, 128, 128, 64, 8
+    g = torch.Generator().manual_seed(77)
+    pool_K = torch.randn((S, NB, L, d), generator=g).to(torch.bfloat16)
+    needles = torch.randint(0, NB * L, (S, Nq), generator=g)
+    keys_flat = pool_K.reshape(S, NB * L, d).float()
+    Q = (keys_flat[torch.arange(S)[:, None], needles] + 0.1 * torch.randn((S, Nq, d), generator=g)).to(torch.bfloat16)
+    mem_summary = torch.from_numpy(go.block_commit_mean(_np(pool_K), bf16=True)).to(torch.bfloat16)
+    scores, idx = retrieval.block_topk(Q.to(cuda_device), mem_summary.to(cuda_device), k)
+    tok, _, _ = readout.exact_readout(Q.to(cuda_device), pool_K.to(cuda_device), None, idx)
+    ref_s, ref_i, ok = go.block_topk(_np(Q), _np(mem_summary), k)
+    got_i = idx.cpu().numpy()
+    assert np.array_equal(got_i[ok], ref_i[ok])
+    ref_tok, _, _, ok2 = go.exact_readout(_np(Q), _np(pool_K), None, got_i)
+    assert np.array_equal(tok.cpu().numpy()[ok2], ref_tok[ok2])
