@@ -278,6 +278,9 @@ struct FrameQR {
                                             int sign_mode, uint32_t cols_mask) {
     uint32_t rneg = 0u;
     static_for<0, RMAX>([&](auto kc) { geqrf_step<decltype(kc)::value>(a, t, sm, rneg); });
+    // tau[RMAX-1] is written by one lane in the last step, which has no
+    // reduction (and so no __syncwarp) after it; order it before any reader.
+    __syncwarp();
     static_for_down<0, RMAX>([&](auto kc) { orgqr_step<decltype(kc)::value>(a, t, sm); });
     const uint32_t flip = (sign_mode == GFST_SIGN_R_DIAG_POSITIVE)
                               ? rneg

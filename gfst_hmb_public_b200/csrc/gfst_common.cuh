@@ -7,7 +7,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
-#include "../../include/gfst_b200.h"
+#include "gfst_b200.h"
 
 namespace gfst {
 
