@@ -8,15 +8,16 @@ namespace gfst {
 // shape dispatch
 // ---------------------------------------------------------------------------
 struct Shape {
-  int dmax, rmax, tpf;
+  int dmax, rmax;
 };
 
-// Capacity classes, smallest first.  A frame runs in the first class with
-// dmax >= d and rmax >= r.
+// Capacity classes (rows x columns), smallest first.  A frame runs in the
+// first class with dmax >= d and rmax >= r.  Each class fixes the lane grid
+// (row groups x column groups) in GFST_SHAPE_CASES below.
 constexpr Shape kShapes[] = {
-    {8, 8, 8},     {32, 8, 8},    {64, 8, 8},    {128, 8, 16},  {256, 8, 32},
-    {16, 16, 16},  {32, 16, 16},  {64, 16, 16},  {128, 16, 32}, {256, 16, 32},
-    {32, 32, 32},  {64, 32, 32},  {128, 32, 32},
+    {8, 8},   {32, 8},   {64, 8},   {128, 8},   {256, 8},
+    {16, 16}, {32, 16},  {64, 16},  {128, 16},  {256, 16},
+    {32, 32}, {64, 32},  {128, 32},
 };
 
 int pick_shape(int d, int r) {
@@ -27,20 +28,21 @@ int pick_shape(int d, int r) {
   return -1;
 }
 
-#define GFST_SHAPE_CASES(X)  \
-  X(0, 8, 8, 8)              \
-  X(1, 32, 8, 8)             \
-  X(2, 64, 8, 8)             \
-  X(3, 128, 8, 16)           \
-  X(4, 256, 8, 32)           \
-  X(5, 16, 16, 16)           \
-  X(6, 32, 16, 16)           \
-  X(7, 64, 16, 16)           \
-  X(8, 128, 16, 32)          \
-  X(9, 256, 16, 32)          \
-  X(10, 32, 32, 32)          \
-  X(11, 64, 32, 32)          \
-  X(12, 128, 32, 32)
+// (index, DMAX, RMAX, RG, CG): RG row groups x CG column groups of lanes per frame
+#define GFST_SHAPE_CASES(X) \
+  X(0, 8, 8, 4, 2)          \
+  X(1, 32, 8, 8, 1)         \
+  X(2, 64, 8, 8, 1)         \
+  X(3, 128, 8, 16, 1)       \
+  X(4, 256, 8, 32, 1)       \
+  X(5, 16, 16, 8, 2)        \
+  X(6, 32, 16, 8, 2)        \
+  X(7, 64, 16, 8, 4)        \
+  X(8, 128, 16, 8, 4)       \
+  X(9, 256, 16, 16, 2)      \
+  X(10, 32, 32, 8, 4)       \
+  X(11, 64, 32, 8, 4)       \
+  X(12, 128, 32, 8, 4)
 
 int check_frame_args(int64_t n, int d, int r, int m, int sign_mode) {
   GFST_REQUIRE(n >= 0, GFST_ERR_ARG, "n_frames must be >= 0 (got %lld)", (long long)n);
@@ -65,9 +67,9 @@ extern "C" int gfst_frame_update_qr(const float* U, const float* A, const float*
   GFST_REQUIRE(U != nullptr && Uout != nullptr, GFST_ERR_ARG, "U and Uout must be non-null");
   GFST_REQUIRE(m == 0 || (A != nullptr && B != nullptr), GFST_ERR_ARG, "A and B must be non-null when m > 0");
   switch (pick_shape(d, r)) {
-#define X(idx, D, R, TPF) \
-  case idx:               \
-    return launch_update<D, R, TPF>(U, A, B, beta, Uout, n_frames, d, r, m, eps_sign, sign_mode, stream);
+#define X(idx, D, R, RG, CG) \
+  case idx:                  \
+    return launch_update<D, R, RG, CG>(U, A, B, beta, Uout, n_frames, d, r, m, eps_sign, sign_mode, stream);
     GFST_SHAPE_CASES(X)
 #undef X
     default:
@@ -92,9 +94,9 @@ extern "C" int gfst_frame_stream(float* U, const float* A, const float* B, float
                "streaming needs d*m and r*m to be multiples of 4 (d=%d r=%d m=%d)", d, r, m);
   GFST_REQUIRE(aligned16(A) && aligned16(B), GFST_ERR_ALIGN, "A and B must be 16-byte aligned");
   switch (pick_shape(d, r)) {
-#define X(idx, D, R, TPF)                                                                                   \
+#define X(idx, D, R, RG, CG)                                                                                \
   case idx:                                                                                                 \
-    return launch_stream<D, R, TPF>(U, A, B, beta, n_frames, T, d, r, m, eps_sign, sign_mode, frames_out, \
+    return launch_stream<D, R, RG, CG>(U, A, B, beta, n_frames, T, d, r, m, eps_sign, sign_mode, frames_out, \
                                     out_every, stream);
     GFST_SHAPE_CASES(X)
 #undef X

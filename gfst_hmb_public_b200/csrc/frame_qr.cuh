@@ -1,15 +1,18 @@
 // Register-resident Householder thin QR of one d x r fp32 frame per lane group.
 //
-// Layout: TPF consecutive lanes of a warp (a "frame group", TPF a power of two
-// <= 32) own one frame of capacity DMAX x RMAX.  Group lane t holds rows
-// t, t + TPF, t + 2*TPF, ... (RPT = DMAX / TPF rows), all RMAX columns of each,
-// in registers.  Rows >= d and columns >= r are zero padding: a zero row adds
-// nothing to any reflector and a zero trailing column leaves the leading
-// columns of Q unchanged, so the leading d x r block of the padded result is
-// the QR of the unpadded frame.
+// Layout (2-D cyclic): a frame group is TPF = RG * CG consecutive lanes of one
+// warp.  Group lane t is (rg, cg) = (t % RG, t / RG); it owns rows
+// rg + s*RG (s < RPT = DMAX/RG) of columns cg + c*CG (c < CPT = RMAX/CG), all in
+// registers, stored as float2 row pairs (slots 2i, 2i+1) so the update and the
+// dot products issue packed fma.f32x2.  Cyclic columns keep every column group
+// busy until the last reflector; the dot products of a step only need a
+// reduction over the RG lanes of one column group.  Rows >= d and columns >= r
+// are zero padding: a zero row adds nothing to any reflector and zero trailing
+// columns leave the leading columns of Q unchanged, so the leading d x r block
+// of the padded result is the QR of the unpadded frame.
 //
 // Arithmetic follows LAPACK's unblocked sgeqr2/slarfg + sorg2r (the path that
-// torch.linalg.qr takes for these sizes, gfst.py:26-32 in the reference) and the
+// torch.linalg.qr takes for these sizes; gfst.py:26-32 of the reference) and the
 // reference's own fixed-order device kernel
 // (src/gfst_hmb_mpuc/csrc/mathdx/mathdx_runtime.cu:447-549):
 //   step k:  alpha = A[k,k], xnorm^2 = sum_{i>k} A[i,k]^2
@@ -17,20 +20,19 @@
 //            otherwise       beta = -sign(alpha) * sqrt(alpha^2 + xnorm^2)
 //                            tau  = (beta - alpha) / beta,  v = [1; x / (alpha - beta)]
 //   trailing update A[k:, j] -= tau * v * (v^T A[k:, j]).
-// Every step needs one reduction across the group.  The reduction carries the
-// "Gram row" c_j = sum_{i>k} x_i A[i,j] together with xnorm^2, so
-// v^T A[k:,j] = A[k,j] + c_j / (alpha - beta) is known without a second pass.
-// Reductions are recursive-halving butterflies over the group's lanes (each
-// lane ends with a slice of the totals), followed by a shared-memory gather.
+// The step's reduction carries the "Gram row" c_j = sum_{i>k} x_i A[i,j], so
+// v^T A[k:,j] = A[k,j] + c_j / (alpha - beta) needs no second pass.  Q is then
+// accumulated backward from the identity in place (sorg2r order).
 #pragma once
 
 #include "gfst_common.cuh"
 
 namespace gfst {
 
-// Sum v[0..P) over the TPF lanes of a frame group (group lane index t).
-// On return: if P >= TPF, v[0..P/TPF) holds the totals of values
-// [t*P/TPF, (t+1)*P/TPF); if P < TPF, v[0] holds the total of value t/(TPF/P).
+// Sum v[0..P) over the G lanes of a lane subgroup (subgroup lane index t; the
+// subgroup is G consecutive lanes, G a power of two).  On return: if P >= G,
+// v[0..P/G) holds the totals of values [t*P/G, (t+1)*P/G); if P < G, v[0]
+// holds the total of value t/(G/P).
 template <int S, int O, int P>
 struct ReduceScatter {
   __device__ static __forceinline__ void run(float (&v)[P], int t) {
@@ -52,289 +54,360 @@ struct ReduceScatter {
   }
 };
 
-template <int P, int TPF>
-__device__ __forceinline__ void group_reduce_scatter(float (&v)[P], int t) {
-  ReduceScatter<P, TPF / 2, P>::run(v, t);
+template <int P, int G>
+__device__ __forceinline__ void subgroup_reduce_scatter(float (&v)[P], int t) {
+  ReduceScatter<P, G / 2, P>::run(v, t);
 }
 
-// Write the totals left by group_reduce_scatter to red[0..P).
-template <int P, int TPF>
-__device__ __forceinline__ void group_publish(const float (&v)[P], int t, float* red) {
-  if constexpr (P >= TPF) {
-    constexpr int C = P / TPF;
+// Write the totals left by subgroup_reduce_scatter to red[0..P).
+template <int P, int G>
+__device__ __forceinline__ void subgroup_publish(const float (&v)[P], int t, float* red) {
+  if constexpr (P >= G) {
+    constexpr int C = P / G;
 #pragma unroll
     for (int i = 0; i < C; ++i) red[t * C + i] = v[i];
   } else {
-    constexpr int G = TPF / P;
-    if ((t % G) == 0) red[t / G] = v[0];
+    constexpr int Q = G / P;
+    if ((t % Q) == 0) red[t / Q] = v[0];
   }
 }
 
-template <int DMAX, int RMAX, int TPF>
-struct FrameQR {
-  static_assert(TPF >= 2 && TPF <= 32 && (TPF & (TPF - 1)) == 0, "TPF must be a power of two in [2, 32]");
-  static_assert(DMAX % TPF == 0, "DMAX must be a multiple of TPF");
-  static_assert(RMAX >= 1 && RMAX <= 32 && (RMAX & (RMAX - 1)) == 0, "RMAX must be a power of two <= 32");
-  static_assert(RMAX <= DMAX, "thin QR needs r <= d");
-  static constexpr int RPT = DMAX / TPF;
+template <int G>
+__device__ __forceinline__ float subgroup_allreduce(float x) {
+#pragma unroll
+  for (int o = G / 2; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
 
-  // Per-group shared scratch: reduction totals and pivot row (double-buffered by
-  // step parity) and the tau of every reflector.
-  struct Smem {
-    float red[2][RMAX];
-    float piv[2][RMAX];
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+template <int DMAX, int RMAX, int RG, int CG>
+struct FrameQR {
+  static constexpr int TPF = RG * CG;
+  static constexpr int RPT = DMAX / RG;  // row slots per lane
+  static constexpr int RP = RPT / 2;     // row pairs per lane
+  static constexpr int CPT = RMAX / CG;  // local columns per lane
+  static_assert(TPF >= 2 && TPF <= 32 && (TPF & (TPF - 1)) == 0, "TPF must be a power of two <= 32");
+  static_assert((RG & (RG - 1)) == 0 && (CG & (CG - 1)) == 0, "RG, CG powers of two");
+  static_assert(DMAX % (2 * RG) == 0, "each lane needs an even number of row slots");
+  static_assert(RMAX % CG == 0 && (CPT & (CPT - 1)) == 0, "CPT must be a power of two");
+  static_assert(RMAX <= 32 && RMAX <= DMAX, "thin QR needs r <= d, r <= 32");
+  static constexpr int XS = RPT + 4;     // padded row stride of the broadcast buffer (floats)
+
+  // a[i][c] = rows (slot 2i, slot 2i+1) of local column c
+  using Frame = float2[RP][CPT];
+
+  // Per-group shared scratch (double-buffered by step parity).
+  struct __align__(16) Smem {
+    float xb[2][RG][XS];   // column K of this step (reflector source), by row group
+    float piv[2][CG][CPT]; // pivot row K, by column group
+    float red[2][CG][CPT]; // reduced dot products, by column group
     float tau[RMAX];
   };
 
-  // true when the row of slot s of group lane t is > K (folds at compile time
-  // for every slot that lies entirely above or below K).
-  template <int K>
-  __device__ static __forceinline__ bool below(int s, int t) {
-    if (s * TPF > K) return true;
-    if (s * TPF + TPF - 1 <= K) return false;
-    return t + s * TPF > K;
+  __device__ static __forceinline__ float get(const Frame& a, int s, int c) {
+    return (s & 1) ? a[s >> 1][c].y : a[s >> 1][c].x;
   }
-  template <int K>
-  __device__ static __forceinline__ bool at(int s, int t) {
-    if (K < s * TPF || K >= s * TPF + TPF) return false;
-    return t == K - s * TPF;
-  }
-
-  // Partial sums over this lane's rows (> K) of the values [I0, I0+N) of the
-  // step-K list {c_{K+1}, ..., c_{RMAX-1}, xnorm^2}, reduced across the group and
-  // published to red[I0 ..).  Chunks of <= 16 values keep the live partials small;
-  // the butterfly costs about the same number of shuffles either way.
-  template <int K, int I0, int N>
-  __device__ static __forceinline__ void gram_chunk(const float (&a)[RPT][RMAX], int t, float* red) {
-    constexpr int NC = RMAX - K - 1;
-    constexpr int P = pow2_ceil(N);
-    float v[P];
-#pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = 0.f;
-#pragma unroll
-    for (int s = 0; s < RPT; ++s) {
-      const float x = below<K>(s, t) ? a[s][K] : 0.f;
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        if (I0 + i < NC) {
-          v[i] = fmaf(x, a[s][K + 1 + I0 + i], v[i]);
-        } else {
-          v[i] = fmaf(x, x, v[i]);
-        }
-      }
-    }
-    group_reduce_scatter<P, TPF>(v, t);
-    group_publish<P, TPF>(v, t, red + I0);
-  }
-
-  // Same for the orgqr step: values [I0, I0+N) of {v^T Q[:, K+1], ..., v^T Q[:, RMAX-1]}.
-  template <int K, int I0, int N>
-  __device__ static __forceinline__ void vq_chunk(const float (&a)[RPT][RMAX], int t, float* red) {
-    constexpr int P = pow2_ceil(N);
-    float v[P];
-#pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = 0.f;
-#pragma unroll
-    for (int s = 0; s < RPT; ++s) {
-      const float vi = below<K>(s, t) ? a[s][K] : 0.f;
-#pragma unroll
-      for (int i = 0; i < N; ++i) v[i] = fmaf(vi, a[s][K + 1 + I0 + i], v[i]);
-    }
-    group_reduce_scatter<P, TPF>(v, t);
-    group_publish<P, TPF>(v, t, red + I0);
-  }
-
-  static constexpr int kChunk = 16;
-
-  template <int K>
-  __device__ static __forceinline__ void geqrf_step(float (&a)[RPT][RMAX], int t, Smem& sm, uint32_t& rneg) {
-    constexpr int NC = RMAX - K - 1;  // trailing columns
-    constexpr int NV = NC + 1;        // c_{K+1..RMAX-1}, xnorm^2
-    constexpr int NCH = (NV + kChunk - 1) / kChunk;
-    float* red = sm.red[K & 1];
-    float* piv = sm.piv[K & 1];
-
-    // pivot row K: piv[j] = A[K, K+1+j], piv[NC] = A[K, K]
-    constexpr int SK = K / TPF;
-    if (t == K % TPF) {
-#pragma unroll
-      for (int j = 0; j < NC; ++j) piv[j] = a[SK][K + 1 + j];
-      piv[NC] = a[SK][K];
-    }
-    static_for<0, NCH>([&](auto cc) {
-      constexpr int C = decltype(cc)::value;
-      constexpr int I0 = C * kChunk;
-      constexpr int N = (NV - I0) < kChunk ? (NV - I0) : kChunk;
-      gram_chunk<K, I0, N>(a, t, red);
-    });
-    __syncwarp();
-
-    const float alpha = piv[NC];
-    const float xn2 = red[NC];
-    float beta, tau, scal;
-    if (xn2 == 0.f) {
-      beta = alpha;
-      tau = 0.f;
-      scal = 0.f;
+  __device__ static __forceinline__ void set(Frame& a, int s, int c, float v) {
+    if (s & 1) {
+      a[s >> 1][c].y = v;
     } else {
-      const float sigma = sqrtf(fmaf(alpha, alpha, xn2));
-      beta = alpha >= 0.f ? -sigma : sigma;
-      tau = (beta - alpha) / beta;
-      scal = 1.f / (alpha - beta);
+      a[s >> 1][c].x = v;
     }
-    rneg |= (beta < 0.f ? 1u : 0u) << K;
-    if (t == 0) sm.tau[K] = tau;
+  }
 
+  // Reflectors are processed in groups of CG consecutive steps K = C0*CG + j
+  // (j < CG): within a group the local column index (C0) and the row slot
+  // holding row K (SK) are compile-time constants, so the group's code is a
+  // rolled loop over j.  This keeps the unrolled code CG times smaller than a
+  // fully unrolled factorisation (instruction-cache bound otherwise).
+  static_assert(RG % CG == 0, "a group of CG steps must fall inside one row slot");
+
+  // row of slot s is > K, for K in group C0 (compile-time except slot SK)
+  template <int C0>
+  __device__ static __forceinline__ bool below(int s, int rg, int K) {
+    constexpr int SK = (C0 * CG) / RG;
+    if (s > SK) return true;
+    if (s < SK) return false;
+    return rg + s * RG > K;
+  }
+
+  // Read column K (written by its column group) from the broadcast buffer,
+  // zeroing rows <= K.
+  template <int C0>
+  __device__ static __forceinline__ void read_column(float2 (&x)[RP], const float* xb, int rg, int K) {
 #pragma unroll
-    for (int j = 0; j < NC; ++j) {
-      const float w = fmaf(scal, red[j], piv[j]);  // v^T A[K:, K+1+j]
-      const float tw = tau * w;
-      const float g = tw * scal;
-#pragma unroll
-      for (int s = 0; s < RPT; ++s) {
-        if (below<K>(s, t)) {
-          a[s][K + 1 + j] = fmaf(-g, a[s][K], a[s][K + 1 + j]);
-        } else if (at<K>(s, t)) {
-          a[s][K + 1 + j] -= tw;
-        }
+    for (int i = 0; i < RP; i += 2) {
+      if (i + 1 < RP) {
+        const float4 q = *reinterpret_cast<const float4*>(xb + rg * XS + 2 * i);
+        x[i] = make_float2(q.x, q.y);
+        x[i + 1] = make_float2(q.z, q.w);
+      } else {
+        x[i] = *reinterpret_cast<const float2*>(xb + rg * XS + 2 * i);
       }
     }
 #pragma unroll
-    for (int s = 0; s < RPT; ++s) {
-      if (below<K>(s, t)) {
-        a[s][K] *= scal;  // v_i, i > K
-      } else if (at<K>(s, t)) {
-        a[s][K] = beta;   // R_KK
+    for (int i = 0; i < RP; ++i) {
+      if (!below<C0>(2 * i, rg, K)) x[i].x = 0.f;
+      if (!below<C0>(2 * i + 1, rg, K)) x[i].y = 0.f;
+    }
+  }
+
+  template <int C0>
+  __device__ static __forceinline__ void write_column(const Frame& a, float* xb, int rg) {
+#pragma unroll
+    for (int i = 0; i < RP; i += 2) {
+      if (i + 1 < RP) {
+        *reinterpret_cast<float4*>(xb + rg * XS + 2 * i) =
+            make_float4(a[i][C0].x, a[i][C0].y, a[i + 1][C0].x, a[i + 1][C0].y);
+      } else {
+        *reinterpret_cast<float2*>(xb + rg * XS + 2 * i) = a[i][C0];
+      }
+    }
+  }
+
+  // Dot products of the (masked) column x with local columns c in [C0, CPT) --
+  // c == C0 counts only for column groups right of K's (cg > j) -- reduced over
+  // the RG lanes of the column group and published to red[0 ..).
+  template <int C0>
+  __device__ static __forceinline__ void column_dots(const Frame& a, const float2 (&x)[RP], int rg, bool first_live,
+                                                     float* red) {
+    constexpr int NV = CPT - C0;
+    constexpr int P = pow2_ceil(NV);
+    float v[P];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < RP; ++p) acc = ffma2(x[p], a[p][C0 + i], acc);
+      v[i] = acc.x + acc.y;
+    }
+#pragma unroll
+    for (int i = NV; i < P; ++i) v[i] = 0.f;
+    if (!first_live) v[0] = 0.f;
+    subgroup_reduce_scatter<P, RG>(v, rg);
+    subgroup_publish<P, RG>(v, rg, red);
+  }
+
+  template <int C0>
+  __device__ static __forceinline__ void geqrf_group(Frame& a, int rg, int cg, Smem& sm, uint32_t& rneg) {
+    constexpr int NV = CPT - C0, SK = (C0 * CG) / RG;
+#pragma unroll 1
+    for (int j = 0; j < CG; ++j) {
+      const int K = C0 * CG + j;
+      float* xb = &sm.xb[K & 1][0][0];
+      float* piv = &sm.piv[K & 1][0][0];
+      float* red = &sm.red[K & 1][cg][0];
+      const bool own_pivot = (rg == K - SK * RG);  // this lane holds row K (slot SK)
+      const bool first_live = cg > j;              // local column C0 is right of K
+      if (cg == j) write_column<C0>(a, xb, rg);
+      if (own_pivot) {
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) piv[cg * CPT + c] = get(a, SK, c);
+      }
+      __syncwarp();
+      float2 x[RP];
+      read_column<C0>(x, xb, rg, K);
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < RP; ++p) acc = ffma2(x[p], x[p], acc);
+      const float xn2 = subgroup_allreduce<RG>(acc.x + acc.y);
+      column_dots<C0>(a, x, rg, first_live, red);
+      __syncwarp();
+
+      const float alpha = piv[j * CPT + C0];
+      float beta, tau, scal;
+      if (xn2 == 0.f) {
+        beta = alpha;
+        tau = 0.f;
+        scal = 0.f;
+      } else {
+        const float sigma = sqrtf(fmaf(alpha, alpha, xn2));
+        beta = alpha >= 0.f ? -sigma : sigma;
+        tau = (beta - alpha) / beta;
+        scal = 1.f / (alpha - beta);
+      }
+      rneg |= (beta < 0.f ? 1u : 0u) << K;
+      if (rg == 0 && cg == 0) sm.tau[K] = tau;
+
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = C0 + i;
+        const float w = fmaf(scal, red[i], piv[cg * CPT + c]);  // v^T A[K:, column]
+        float tw = tau * w;
+        if (i == 0 && !first_live) tw = 0.f;  // column K or a finished column
+        const float g = tw * scal;
+        const float2 ng = make_float2(-g, -g);
+#pragma unroll
+        for (int p = 0; p < RP; ++p) a[p][c] = ffma2(ng, x[p], a[p][c]);
+        if (own_pivot) set(a, SK, c, get(a, SK, c) - tw);
+      }
+      if (cg == j) {
+        // column K: v below the diagonal, beta on it
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+          if (below<C0>(2 * p, rg, K)) a[p][C0].x *= scal;
+          if (below<C0>(2 * p + 1, rg, K)) a[p][C0].y *= scal;
+        }
+        if (own_pivot) set(a, SK, C0, beta);
       }
     }
   }
 
   // Backward accumulation of the explicit thin Q (sorg2r order), in place.
-  template <int K>
-  __device__ static __forceinline__ void orgqr_step(float (&a)[RPT][RMAX], int t, Smem& sm) {
-    constexpr int NC = RMAX - K - 1;
-    const float tau = sm.tau[K];
-    if constexpr (NC > 0) {
-      constexpr int NCH = (NC + kChunk - 1) / kChunk;
-      float* red = sm.red[K & 1];
-      static_for<0, NCH>([&](auto cc) {
-        constexpr int C = decltype(cc)::value;
-        constexpr int I0 = C * kChunk;
-        constexpr int N = (NC - I0) < kChunk ? (NC - I0) : kChunk;
-        vq_chunk<K, I0, N>(a, t, red);
-      });
-      __syncwarp();
+  template <int C0>
+  __device__ static __forceinline__ void orgqr_group(Frame& a, int rg, int cg, Smem& sm) {
+    constexpr int NV = CPT - C0, SK = (C0 * CG) / RG;
+#pragma unroll 1
+    for (int j = CG - 1; j >= 0; --j) {
+      const int K = C0 * CG + j;
+      const float tau = sm.tau[K];
+      const bool own_pivot = (rg == K - SK * RG);
+      const bool first_live = cg > j;
+      if (K + 1 < RMAX) {
+        float* xb = &sm.xb[K & 1][0][0];
+        float* red = &sm.red[K & 1][cg][0];
+        if (cg == j) write_column<C0>(a, xb, rg);
+        __syncwarp();
+        float2 v[RP];
+        read_column<C0>(v, xb, rg, K);
+        column_dots<C0>(a, v, rg, first_live, red);
+        __syncwarp();
 #pragma unroll
-      for (int j = 0; j < NC; ++j) {
-        const float tp = tau * red[j];
+        for (int i = 0; i < NV; ++i) {
+          const int c = C0 + i;
+          const bool trailing = !(i == 0 && !first_live);
+          const float tp = trailing ? tau * red[i] : 0.f;
+          const float2 ntp = make_float2(-tp, -tp);
+#pragma unroll
+          for (int p = 0; p < RP; ++p) a[p][c] = ffma2(ntp, v[p], a[p][c]);
+          // row K of a trailing column was zeroed at that column's own step
+          if (own_pivot && trailing) set(a, SK, c, -tp);
+        }
+      }
+      if (cg == j) {
 #pragma unroll
         for (int s = 0; s < RPT; ++s) {
-          if (below<K>(s, t)) {
-            a[s][K + 1 + j] = fmaf(-tp, a[s][K], a[s][K + 1 + j]);
-          } else if (at<K>(s, t)) {
-            a[s][K + 1 + j] = -tp;  // row K of column K+1+j was zeroed at its own step
+          if (below<C0>(s, rg, K)) {
+            set(a, s, C0, get(a, s, C0) * -tau);
+          } else if (s == SK && own_pivot) {
+            set(a, s, C0, 1.f - tau);
+          } else {
+            set(a, s, C0, 0.f);  // rows < K: discard R
           }
         }
       }
     }
-#pragma unroll
-    for (int s = 0; s < RPT; ++s) {
-      if (below<K>(s, t)) {
-        a[s][K] *= -tau;
-      } else if (at<K>(s, t)) {
-        a[s][K] = 1.f - tau;
-      } else {
-        a[s][K] = 0.f;  // rows < K: discard R
-      }
-    }
   }
 
-  // Bitmask of columns whose sign must flip under the reference's
-  // first-significant-entry rule (gfst.py:35-46): first row with |q| > eps_sign,
-  // negative -> flip.  cols_mask selects the real (unpadded) columns.
-  __device__ static __forceinline__ uint32_t first_significant_flips(const float (&a)[RPT][RMAX], int lane,
-                                                                     float eps_sign, uint32_t cols_mask) {
-    const int gbase = (lane / TPF) * TPF;
-    const uint32_t gmask = TPF == 32 ? 0xffffffffu : ((1u << TPF) - 1u);
+  // Columns to negate under the reference's first-significant-entry rule
+  // (gfst.py:35-46): first row (in row order) with |q| > eps_sign, negative ->
+  // flip.  Bit c of the result refers to local column c.
+  __device__ static __forceinline__ uint32_t first_significant_flips(const Frame& a, int lane, int cg,
+                                                                     float eps_sign, uint32_t local_mask) {
+    const int sub = (lane / TPF) * TPF + cg * RG;  // first lane of my column group
+    const uint32_t gmask = RG == 32 ? 0xffffffffu : ((1u << RG) - 1u);
     uint32_t flip = 0u, found = 0u;
 #pragma unroll
     for (int s = 0; s < RPT; ++s) {
 #pragma unroll
-      for (int j = 0; j < RMAX; ++j) {
-        const uint32_t sig = (__ballot_sync(0xffffffffu, fabsf(a[s][j]) > eps_sign) >> gbase) & gmask;
-        const uint32_t neg = (__ballot_sync(0xffffffffu, a[s][j] < 0.f) >> gbase) & gmask;
-        if (!((found >> j) & 1u) && sig != 0u) {
-          found |= 1u << j;
-          flip |= ((neg >> (__ffs(sig) - 1)) & 1u) << j;
+      for (int c = 0; c < CPT; ++c) {
+        const float q = get(a, s, c);
+        const uint32_t sig = (__ballot_sync(0xffffffffu, fabsf(q) > eps_sign) >> sub) & gmask;
+        const uint32_t neg = (__ballot_sync(0xffffffffu, q < 0.f) >> sub) & gmask;
+        if (!((found >> c) & 1u) && sig != 0u) {
+          found |= 1u << c;
+          flip |= ((neg >> (__ffs(sig) - 1)) & 1u) << c;
         }
       }
-      if (!__any_sync(0xffffffffu, (found & cols_mask) != cols_mask)) break;
+      if (!__any_sync(0xffffffffu, (found & local_mask) != local_mask)) break;
     }
     return flip;
   }
 
-  // Full thin QR in place: a <- sign-fixed Q.
-  __device__ static __forceinline__ void qr(float (&a)[RPT][RMAX], int lane, int t, Smem& sm, float eps_sign,
-                                            int sign_mode, uint32_t cols_mask) {
+  // In place: a <- sign-fixed thin Q.  r = number of real columns.
+  __device__ static __forceinline__ void qr(Frame& a, int lane, int t, Smem& sm, float eps_sign, int sign_mode,
+                                            int r) {
+    const int rg = t % RG, cg = t / RG;
     uint32_t rneg = 0u;
-    static_for<0, RMAX>([&](auto kc) { geqrf_step<decltype(kc)::value>(a, t, sm, rneg); });
-    // tau[RMAX-1] is written by one lane in the last step, which has no
-    // reduction (and so no __syncwarp) after it; order it before any reader.
-    __syncwarp();
-    static_for_down<0, RMAX>([&](auto kc) { orgqr_step<decltype(kc)::value>(a, t, sm); });
-    const uint32_t flip = (sign_mode == GFST_SIGN_R_DIAG_POSITIVE)
-                              ? rneg
-                              : first_significant_flips(a, lane, eps_sign, cols_mask);
+    static_for<0, CPT>([&](auto cc) { geqrf_group<decltype(cc)::value>(a, rg, cg, sm, rneg); });
+    __syncwarp();  // tau[] writes before any orgqr read
+    static_for_down<0, CPT>([&](auto cc) { orgqr_group<decltype(cc)::value>(a, rg, cg, sm); });
+    uint32_t flip = 0u;
+    if (sign_mode == GFST_SIGN_R_DIAG_POSITIVE) {
 #pragma unroll
-    for (int s = 0; s < RPT; ++s) {
+      for (int c = 0; c < CPT; ++c) flip |= ((rneg >> (cg + c * CG)) & 1u) << c;
+    } else {
+      uint32_t local_mask = 0u;
 #pragma unroll
-      for (int j = 0; j < RMAX; ++j) {
-        if ((flip >> j) & 1u) a[s][j] = -a[s][j];
+      for (int c = 0; c < CPT; ++c) local_mask |= (cg + c * CG < r ? 1u : 0u) << c;
+      flip = first_significant_flips(a, lane, cg, eps_sign, local_mask);
+    }
+#pragma unroll
+    for (int p = 0; p < RP; ++p) {
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        if ((flip >> c) & 1u) a[p][c] = make_float2(-a[p][c].x, -a[p][c].y);
       }
     }
   }
 
-  // Load a dense [d, r] frame (zero padded to DMAX x RMAX).
-  __device__ static __forceinline__ void load(float (&a)[RPT][RMAX], const float* __restrict__ src, int t, int d,
-                                              int r, bool valid, bool vec4) {
+  // Load a dense row-major [d, r] frame, zero padded.
+  __device__ static __forceinline__ void load(Frame& a, const float* __restrict__ src, int t, int d, int r,
+                                              bool valid) {
+    const int rg = t % RG, cg = t / RG;
 #pragma unroll
     for (int s = 0; s < RPT; ++s) {
-      const int row = t + s * TPF;
-      const bool ok = valid && row < d;
-      if (vec4) {
-        // r == RMAX, RMAX % 4 == 0, src 16-byte aligned
+      const int row = rg + s * RG;
 #pragma unroll
-        for (int c = 0; c < RMAX / 4; ++c) {
-          float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (ok) q = __ldg(reinterpret_cast<const float4*>(src + (size_t)row * RMAX) + c);
-          a[s][4 * c + 0] = q.x;
-          a[s][4 * c + 1] = q.y;
-          a[s][4 * c + 2] = q.z;
-          a[s][4 * c + 3] = q.w;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < RMAX; ++j) a[s][j] = (ok && j < r) ? __ldg(src + (size_t)row * r + j) : 0.f;
+      for (int c = 0; c < CPT; ++c) {
+        const int col = cg + c * CG;
+        set(a, s, c, (valid && row < d && col < r) ? __ldg(src + (size_t)row * r + col) : 0.f);
       }
     }
   }
 
-  __device__ static __forceinline__ void store(const float (&a)[RPT][RMAX], float* __restrict__ dst, int t, int d,
-                                               int r, bool valid, bool vec4) {
+  __device__ static __forceinline__ void store(const Frame& a, float* __restrict__ dst, int t, int d, int r,
+                                               bool valid) {
+    const int rg = t % RG, cg = t / RG;
+    if (!valid) return;
 #pragma unroll
     for (int s = 0; s < RPT; ++s) {
-      const int row = t + s * TPF;
-      if (!(valid && row < d)) continue;
-      if (vec4) {
+      const int row = rg + s * RG;
 #pragma unroll
-        for (int c = 0; c < RMAX / 4; ++c) {
-          reinterpret_cast<float4*>(dst + (size_t)row * RMAX)[c] =
-              make_float4(a[s][4 * c + 0], a[s][4 * c + 1], a[s][4 * c + 2], a[s][4 * c + 3]);
-        }
-      } else {
+      for (int c = 0; c < CPT; ++c) {
+        const int col = cg + c * CG;
+        if (row < d && col < r) dst[(size_t)row * r + col] = get(a, s, c);
+      }
+    }
+  }
+
+  __device__ static __forceinline__ void scale(Frame& a, float beta) {
+    const float2 b2 = make_float2(beta, beta);
 #pragma unroll
-        for (int j = 0; j < RMAX; ++j)
-          if (j < r) dst[(size_t)row * r + j] = a[s][j];
+    for (int p = 0; p < RP; ++p)
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) a[p][c] = __fmul2_rn(a[p][c], b2);
+  }
+
+  // a += A B^T with A [d, m], B [r, m] row-major (global or shared memory).
+  __device__ static __forceinline__ void rank_update(Frame& a, const float* A, const float* B, int t, int d, int r,
+                                                     int m) {
+    const int rg = t % RG, cg = t / RG;
+    for (int mm = 0; mm < m; ++mm) {
+      float2 ax[RP];
+#pragma unroll
+      for (int p = 0; p < RP; ++p) {
+        const int r0 = rg + (2 * p) * RG, r1 = rg + (2 * p + 1) * RG;
+        ax[p] = make_float2(r0 < d ? A[r0 * m + mm] : 0.f, r1 < d ? A[r1 * m + mm] : 0.f);
+      }
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        const int col = cg + c * CG;
+        const float b = col < r ? B[col * m + mm] : 0.f;
+        const float2 b2 = make_float2(b, b);
+#pragma unroll
+        for (int p = 0; p < RP; ++p) a[p][c] = ffma2(ax[p], b2, a[p][c]);
       }
     }
   }

@@ -1,6 +1,6 @@
 // Frame kernels: one-step rank-m update + thin QR, and the T-token streaming
 // pass that keeps every frame in registers across tokens.  Templated on the
-// capacity class (DMAX, RMAX, TPF); the classes are instantiated in
+// capacity class (DMAX, RMAX, RG, CG); the classes are instantiated in
 // frame_qr_r8.cu / frame_qr_r16.cu / frame_qr_r32.cu and dispatched in frame_qr.cu.
 //
 // Reference behaviour (paths relative to pkhairkh/gfst-hmb-public):
@@ -13,25 +13,26 @@
 
 namespace gfst {
 
-
 constexpr int kWarps = 4;  // warps per CTA
 
 // Register budget per capacity class: frames holding >= 128 values per lane get
-// the whole register file share of 3 CTAs per SM; smaller ones pack 4.
-template <int DMAX, int RMAX, int TPF>
+// the register file share of 2 CTAs per SM (no spills; 8 frames per SM);
+// smaller ones pack 4.
+template <int DMAX, int RMAX, int RG, int CG>
 constexpr int min_blocks() {
-  return (DMAX / TPF) * RMAX >= 128 ? 3 : 4;
+  return (DMAX / RG) * (RMAX / CG) >= 128 ? 2 : 4;
 }
 
 // ---------------------------------------------------------------------------
 // one step: Uout = QR(beta * U + A B^T)
 // ---------------------------------------------------------------------------
-template <int DMAX, int RMAX, int TPF, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
+template <int DMAX, int RMAX, int RG, int CG, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>()))
     frame_update_qr_kernel(const float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
                            float beta, float* __restrict__ Uout, int64_t n_frames, int d, int r, int m,
-                           float eps_sign, int sign_mode, bool vec4) {
-  using QR = FrameQR<DMAX, RMAX, TPF>;
+                           float eps_sign, int sign_mode) {
+  using QR = FrameQR<DMAX, RMAX, RG, CG>;
+  constexpr int TPF = QR::TPF;
   constexpr int GPW = 32 / TPF;
   __shared__ typename QR::Smem qsm[WARPS * GPW];
 
@@ -41,37 +42,15 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
   const int g = warp * GPW + lane / TPF;
   const int64_t f = (int64_t)blockIdx.x * (WARPS * GPW) + g;
   const bool valid = f < n_frames;
+  const int64_t fs = valid ? f : 0;
   const size_t frame_elems = (size_t)d * r;
 
-  float a[QR::RPT][RMAX];
-  QR::load(a, U + (valid ? f : 0) * frame_elems, t, d, r, valid, vec4);
-
-  if (beta != 1.f) {
-#pragma unroll
-    for (int s = 0; s < QR::RPT; ++s)
-#pragma unroll
-      for (int j = 0; j < RMAX; ++j) a[s][j] *= beta;
-  }
-  if (m > 0 && valid) {
-    const float* Af = A + f * (size_t)d * m;
-    const float* Bf = B + f * (size_t)r * m;
-    for (int mm = 0; mm < m; ++mm) {
-      float bcol[RMAX];
-#pragma unroll
-      for (int j = 0; j < RMAX; ++j) bcol[j] = j < r ? __ldg(Bf + (size_t)j * m + mm) : 0.f;
-#pragma unroll
-      for (int s = 0; s < QR::RPT; ++s) {
-        const int row = t + s * TPF;
-        const float av = row < d ? __ldg(Af + (size_t)row * m + mm) : 0.f;
-#pragma unroll
-        for (int j = 0; j < RMAX; ++j) a[s][j] = fmaf(av, bcol[j], a[s][j]);
-      }
-    }
-  }
-
-  const uint32_t cols_mask = r >= 32 ? 0xffffffffu : ((1u << r) - 1u);
-  QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, cols_mask);
-  QR::store(a, Uout + (valid ? f : 0) * frame_elems, t, d, r, valid, vec4);
+  typename QR::Frame a;
+  QR::load(a, U + fs * frame_elems, t, d, r, valid);
+  if (beta != 1.f) QR::scale(a, beta);
+  if (m > 0 && valid) QR::rank_update(a, A + fs * (size_t)d * m, B + fs * (size_t)r * m, t, d, r, m);
+  QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
+  QR::store(a, Uout + fs * frame_elems, t, d, r, valid);
 }
 
 // ---------------------------------------------------------------------------
@@ -88,12 +67,13 @@ __device__ __forceinline__ void cp_async_wait_all_but_one() {
   asm volatile("cp.async.wait_group 1;\n" ::: "memory");
 }
 
-template <int DMAX, int RMAX, int TPF, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
+template <int DMAX, int RMAX, int RG, int CG, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>()))
     frame_stream_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B, float beta,
                         int64_t n_frames, int T, int d, int r, int m, float eps_sign, int sign_mode,
-                        float* __restrict__ frames_out, int out_every, bool vec4) {
-  using QR = FrameQR<DMAX, RMAX, TPF>;
+                        float* __restrict__ frames_out, int out_every) {
+  using QR = FrameQR<DMAX, RMAX, RG, CG>;
+  constexpr int TPF = QR::TPF;
   constexpr int GPW = 32 / TPF;
   __shared__ typename QR::Smem qsm[WARPS * GPW];
   extern __shared__ __align__(16) float stage[];  // [WARPS*GPW][2][d*m + r*m]
@@ -124,9 +104,8 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
     cp_async_commit();
   };
 
-  float a[QR::RPT][RMAX];
-  QR::load(a, U + fs * frame_elems, t, d, r, valid, vec4);
-  const uint32_t cols_mask = r >= 32 ? 0xffffffffu : ((1u << r) - 1u);
+  typename QR::Frame a;
+  QR::load(a, U + fs * frame_elems, t, d, r, valid);
 
   issue(0);
   for (int tok = 0; tok < T; ++tok) {
@@ -134,71 +113,49 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, TPF>()))
     cp_async_wait_all_but_one();
     __syncwarp();
     const float* sA = my_stage + (tok & 1) * tok_elems;
-    const float* sB = sA + a_elems;
-    if (beta != 1.f) {
-#pragma unroll
-      for (int s = 0; s < QR::RPT; ++s)
-#pragma unroll
-        for (int j = 0; j < RMAX; ++j) a[s][j] *= beta;
-    }
-    if (valid) {
-      for (int mm = 0; mm < m; ++mm) {
-        float bcol[RMAX];
-#pragma unroll
-        for (int j = 0; j < RMAX; ++j) bcol[j] = j < r ? sB[j * m + mm] : 0.f;
-#pragma unroll
-        for (int s = 0; s < QR::RPT; ++s) {
-          const int row = t + s * TPF;
-          const float av = row < d ? sA[row * m + mm] : 0.f;
-#pragma unroll
-          for (int j = 0; j < RMAX; ++j) a[s][j] = fmaf(av, bcol[j], a[s][j]);
-        }
-      }
-    }
-    QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, cols_mask);
+    if (beta != 1.f) QR::scale(a, beta);
+    if (valid) QR::rank_update(a, sA, sA + a_elems, t, d, r, m);
+    QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
     if (frames_out != nullptr && ((tok + 1) % out_every) == 0) {
       const int64_t snap = (tok + 1) / out_every - 1;
-      QR::store(a, frames_out + (snap * n_frames + fs) * frame_elems, t, d, r, valid, vec4);
+      QR::store(a, frames_out + (snap * n_frames + fs) * frame_elems, t, d, r, valid);
     }
     __syncwarp();  // every lane is done with this stage buffer before it is refilled
   }
-  QR::store(a, U + fs * frame_elems, t, d, r, valid, vec4);
+  QR::store(a, U + fs * frame_elems, t, d, r, valid);
 }
 
 // ---------------------------------------------------------------------------
 // launchers (host)
 // ---------------------------------------------------------------------------
 
-template <int DMAX, int RMAX, int TPF>
+template <int DMAX, int RMAX, int RG, int CG>
 int launch_update(const float* U, const float* A, const float* B, float beta, float* Uout, int64_t n, int d, int r,
                   int m, float eps_sign, int sign_mode, cudaStream_t stream) {
-  constexpr int GPW = 32 / TPF;
+  constexpr int GPW = 32 / (RG * CG);
   const int64_t per_block = kWarps * GPW;
   const int64_t blocks = (n + per_block - 1) / per_block;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
-  const bool vec4 = (r == RMAX) && (RMAX % 4 == 0) && aligned16(U) && aligned16(Uout);
-  frame_update_qr_kernel<DMAX, RMAX, TPF, kWarps><<<(unsigned)blocks, kWarps * 32, 0, stream>>>(
-      U, A, B, beta, Uout, n, d, r, m, eps_sign, sign_mode, vec4);
+  frame_update_qr_kernel<DMAX, RMAX, RG, CG, kWarps><<<(unsigned)blocks, kWarps * 32, 0, stream>>>(
+      U, A, B, beta, Uout, n, d, r, m, eps_sign, sign_mode);
   return check_launch("frame_update_qr_kernel");
 }
 
-template <int DMAX, int RMAX, int TPF>
+template <int DMAX, int RMAX, int RG, int CG>
 int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
                   float eps_sign, int sign_mode, float* frames_out, int out_every, cudaStream_t stream) {
-  constexpr int GPW = 32 / TPF;
+  constexpr int GPW = 32 / (RG * CG);
   const int64_t per_block = kWarps * GPW;
   const int64_t blocks = (n + per_block - 1) / per_block;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
-  const bool vec4 = (r == RMAX) && (RMAX % 4 == 0) && aligned16(U) &&
-                    (frames_out == nullptr || aligned16(frames_out));
   const size_t smem = (size_t)per_block * 2 * (size_t)(d * m + r * m) * sizeof(float);
-  auto kern = frame_stream_kernel<DMAX, RMAX, TPF, kWarps>;
+  auto kern = frame_stream_kernel<DMAX, RMAX, RG, CG, kWarps>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
   kern<<<(unsigned)blocks, kWarps * 32, smem, stream>>>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode,
-                                                         frames_out, out_every, vec4);
+                                                         frames_out, out_every);
   return check_launch("frame_stream_kernel");
 }
 
