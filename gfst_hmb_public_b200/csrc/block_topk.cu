@@ -13,6 +13,20 @@ extern "C" int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_stream
   GFST_REQUIRE(dtype == GFST_F32 || dtype == GFST_BF16, GFST_ERR_DTYPE, "unsupported dtype %d", dtype);
   if (n_streams == 0 || n_queries == 0) return GFST_OK;
   GFST_REQUIRE(Q && top_scores && top_idx && (Ksum || n_blocks == 0), GFST_ERR_ARG, "null buffer");
+  if (dtype == GFST_BF16)
+    return block_topk_tc(Q, Ksum, n_streams, n_queries, n_blocks, n_blocks_stride, d, k, top_scores, top_idx,
+                         stream);
   return block_topk_simt(Q, Ksum, n_streams, n_queries, n_blocks, n_blocks_stride, d, k, dtype, top_scores,
                          top_idx, stream);
+}
+
+extern "C" int gfst_check_device_errors(int clear) {
+  unsigned int v = 0;
+  const int st = gfst::read_device_error(clear, &v);
+  if (st != GFST_OK) return st;
+  if (v != 0) {
+    gfst::set_last_error("a kernel gave up a bounded wait (device error word %u)", v);
+    return (int)v;
+  }
+  return GFST_OK;
 }

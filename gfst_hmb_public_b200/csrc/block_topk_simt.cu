@@ -5,8 +5,8 @@
 // Reference: FaissGpuRetriever.exact_topk / search
 // (src/gfst_hmb_mpuc/retrieval.py:136-172 of pkhairkh/gfst-hmb-public), which
 // scores keys @ q in float32 and takes torch.topk.  This kernel serves fp32
-// memories (exact fp32 products; the tensor-core path would round operands),
-// and is the bf16 path's checker-free twin for shapes tcgen05 does not tile.
+// memories: their products must stay exact fp32, which the bf16 tensor-core
+// path (block_topk_tc.cu) cannot give.
 //
 // One thread per query: the CTA stages its 128 queries transposed in shared
 // memory (conflict-free per-thread reads) and streams the stream's summaries
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
   int ti[KCAP];
 #pragma unroll
   for (int j = 0; j < KCAP; ++j) {
-    ts[j] = __int_as_float(0x7fc00000);  // NaN sentinel: ranks below every score
+    ts[j] = -INFINITY;
     ti[j] = 0x7fffffff;
   }
 
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
     }
 #pragma unroll
     for (int j = 0; j < kTile; ++j) {
-      if (b0 + j < n_blocks) topk_insert<KCAP>(ts, ti, acc[j], b0 + j);
+      if (b0 + j < n_blocks && acc[j] > ts[KCAP - 1]) topk_insert<KCAP>(ts, ti, acc[j], b0 + j);
     }
   }
 
@@ -131,8 +131,8 @@ int dispatch_k(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int N
 int block_topk_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, int dtype,
                     float* ts, int32_t* ti, cudaStream_t stream) {
   GFST_REQUIRE(d % 4 == 0, GFST_ERR_SHAPE, "d=%d must be a multiple of 4", d);
-  if (dtype == GFST_F32) return dispatch_k<float>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
-  return dispatch_k<__nv_bfloat16>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  (void)dtype;
+  return dispatch_k<float>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
 }
 
 }  // namespace gfst

@@ -1,0 +1,393 @@
+// Coarse block retrieval on the 5th-generation tensor cores (bf16 operands,
+// fp32 accumulation in TMEM): scores = Q K_sum^T per stream, fused with a
+// per-query top-k in the total order (score descending, block index ascending).
+//
+// Reference: FaissGpuRetriever.exact_topk / search
+// (src/gfst_hmb_mpuc/retrieval.py:136-172 of pkhairkh/gfst-hmb-public) scores
+// keys @ q and takes torch.topk; this is the same selection batched over all
+// queries of a stream, with the score matrix never leaving the SM.
+//
+// One CTA per (stream, 128-query tile), 6 warps:
+//   warp 4  TMA producer: the query tile once, then 128-summary tiles into a
+//           STAGES-deep ring of 128B-swizzled shared-memory buffers
+//   warp 5  MMA issuer: tcgen05.mma.cta_group::1.kind::f16 (M=128, N=128, K=16)
+//           into one of two TMEM accumulators (2 x 128 fp32 columns), then
+//           tcgen05.commit to free the smem stage and publish the accumulator
+//   warps 0-3  epilogue: thread = query row = TMEM lane; tcgen05.ld the row's
+//           128 scores, release the accumulator, insert into a register top-k
+// Every mbarrier wait is bounded (about a second of clock cycles); a wait that
+// gives up sets a sticky device error word (read with gfst_check_device_errors)
+// and the CTA drains its in-flight copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+
+#include "block_topk.cuh"
+
+namespace gfst {
+
+__device__ unsigned int g_device_error = 0;  // sticky GFST_ERR_TIMEOUT report
+
+namespace {
+
+constexpr int BM = 128;            // query rows per CTA (TMEM lanes)
+constexpr int BN = 128;            // summaries per tile (TMEM columns per accumulator)
+constexpr int KBOX = 64;           // bf16 elements per 128-byte swizzle row
+constexpr int kThreadsTC = 192;
+constexpr long long kWaitCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase with the given parity; false if it did not complete
+// within the cycle budget.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 128B-swizzled, K-major operand: 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4)  // start address
+         | ((uint64_t)1 << 16)                // leading byte offset (unused for swizzled K-major)
+         | ((uint64_t)(1024 >> 4) << 32)      // stride byte offset: next 8-row group
+         | ((uint64_t)1 << 46)                // descriptor version (sm_100)
+         | ((uint64_t)2 << 61);               // 128-byte swizzle
+}
+
+// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M=128, N=BN.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int NKB, int STAGES>
+struct TcLayout {
+  static constexpr int A_BYTES = NKB * BM * 128;
+  static constexpr int B_STAGE_BYTES = NKB * BN * 128;
+  static constexpr int BAR_OFF = A_BYTES + STAGES * B_STAGE_BYTES;
+  // full[S], empty[S], tfull[2], tempty[2], afull, done; then tmem slot, flags
+  static constexpr int N_BARS = 2 * STAGES + 6;
+  static constexpr int SMEM_BYTES = 1024 + BAR_OFF + N_BARS * 8 + 64;
+};
+
+template <int NKB, int STAGES, int KCAP>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    block_topk_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         int n_queries, int n_blocks, int n_blocks_stride, int k, float* __restrict__ top_scores,
+                         int32_t* __restrict__ top_idx) {
+  using LY = TcLayout<NKB, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + LY::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* afull = tempty + 2;
+  uint64_t* done = afull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* n_issued = const_cast<int*>(abort_flag + 1);
+  int* n_consumed = n_issued + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t s = blockIdx.y;
+  const int q0 = blockIdx.x * BM;
+  const int n_tiles = (n_blocks + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(afull, 1);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    *n_issued = 0;
+    *n_consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // query tile (rows of other streams or past the end only feed unused rows)
+      mbar_arrive_expect_tx(afull, LY::A_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < NKB; ++kb)
+        tma_load_2d(sA + kb * BM * 128, &tmQ, afull, kb * KBOX, (int)(s * n_queries + q0));
+      int i = 0;
+      for (; i < n_tiles; ++i) {
+        const int st = i % STAGES;
+        if (!mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        mbar_arrive_expect_tx(&full[st], LY::B_STAGE_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < NKB; ++kb)
+          tma_load_2d(sB + (st * NKB + kb) * BN * 128, &tmK, &full[st], kb * KBOX,
+                      (int)(s * n_blocks_stride + i * BN));
+      }
+      *n_issued = i;
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      int i = 0;
+      if (!mbar_wait(afull, 0)) {
+        *abort_flag = 1;
+      } else {
+        for (; i < n_tiles; ++i) {
+          const int st = i % STAGES, acc = i & 1;
+          if (!mbar_wait(&tempty[acc], ((i >> 1) & 1) ^ 1) || !mbar_wait(&full[st], (i / STAGES) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
+#pragma unroll
+          for (int kk = 0; kk < NKB * 4; ++kk) {
+            const int kb = kk >> 2, koff = (kk & 3) * 32;
+            const uint64_t ad = sw128_desc(smem_u32(sA + kb * BM * 128) + koff);
+            const uint64_t bd = sw128_desc(smem_u32(sB + (st * NKB + kb) * BN * 128) + koff);
+            umma_bf16(d_tmem, ad, bd, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[st]);
+          umma_commit(&tfull[acc]);
+        }
+      }
+      *n_consumed = i;
+      umma_commit(done);  // arrives once every MMA issued above has completed
+    }
+  } else {
+    // epilogue: TMEM lane quadrant = warp, row = warp * 32 + lane
+    float ts[KCAP];
+    int ti[KCAP];
+#pragma unroll
+    for (int j = 0; j < KCAP; ++j) {
+      ts[j] = -INFINITY;
+      ti[j] = 0x7fffffff;
+    }
+    for (int i = 0; i < n_tiles; ++i) {
+      const int acc = i & 1;
+      // one lane waits and the warp follows its verdict, so the .sync.aligned
+      // TMEM loads below always run with the whole warp
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait(&tfull[acc], (i >> 1) & 1) ? 1 : 0;
+        if (!ok) *abort_flag = 1;
+        if (*abort_flag) ok = 0;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * BN);
+      float v[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 16; ++c) tmem_ld16(taddr + c * 16, v + c * 16);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      const int b0 = i * BN;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        if (b0 + c < n_blocks && v[c] > ts[KCAP - 1]) topk_insert<KCAP>(ts, ti, v[c], b0 + c);
+      }
+    }
+    const int q = q0 + warp * 32 + lane;
+    if (q < n_queries) {
+      float* os = top_scores + ((size_t)s * n_queries + q) * k;
+      int32_t* oi = top_idx + ((size_t)s * n_queries + q) * k;
+#pragma unroll
+      for (int j = 0; j < KCAP; ++j) {
+        if (j < k) {
+          const bool filled = ti[j] != 0x7fffffff;
+          os[j] = filled ? ts[j] : -INFINITY;
+          oi[j] = filled ? ti[j] : -1;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 32 * 4) {
+    // drain copies that were issued but never consumed (only after a timeout)
+    for (int i = *n_consumed; i < *n_issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+    if (*abort_flag) mbar_wait(afull, 0);
+  }
+  if (warp == 5) {
+    if (!mbar_wait(done, 0)) *abort_flag = 1;
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_device_error, (unsigned)GFST_ERR_TIMEOUT);
+}
+
+// --- host: tensor maps through the driver entry point ------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 map of a [rows, d] row-major matrix, box 64 x box_rows, 128B swizzle.
+int make_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  GFST_REQUIRE(enc != nullptr, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)KBOX, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  GFST_REQUIRE(r == CUDA_SUCCESS, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GFST_OK;
+}
+
+template <int NKB, int STAGES, int KCAP>
+int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
+              int32_t* ti, cudaStream_t stream) {
+  using LY = TcLayout<NKB, STAGES>;
+  auto kern = block_topk_tc_kernel<NKB, STAGES, KCAP>;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM_BYTES);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  dim3 grid((unsigned)((Nq + BM - 1) / BM), (unsigned)S);
+  kern<<<grid, kThreadsTC, LY::SMEM_BYTES, stream>>>(mq, mk, Nq, NB, NBs, k, ts, ti);
+  return check_launch("block_topk_tc_kernel");
+}
+
+template <int NKB, int STAGES>
+int dispatch_kcap(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
+                  int32_t* ti, cudaStream_t stream) {
+  if (k <= 2) return launch_tc<NKB, STAGES, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (k <= 4) return launch_tc<NKB, STAGES, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (k <= 8) return launch_tc<NKB, STAGES, 8>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (k <= 16) return launch_tc<NKB, STAGES, 16>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  return launch_tc<NKB, STAGES, 32>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+}
+
+}  // namespace
+
+int block_topk_tc(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, float* ts,
+                  int32_t* ti, cudaStream_t stream) {
+  GFST_REQUIRE(d % 8 == 0, GFST_ERR_SHAPE, "bf16 retrieval needs d a multiple of 8 (d=%d)", d);
+  GFST_REQUIRE(aligned16(Q) && aligned16(Ksum), GFST_ERR_ALIGN, "Q and Ksum must be 16-byte aligned");
+  GFST_REQUIRE(S <= 65535, GFST_ERR_SHAPE, "n_streams %lld exceeds 65535", (long long)S);
+  GFST_REQUIRE(S * (int64_t)Nq < (1LL << 31) && S * (int64_t)NBs < (1LL << 31), GFST_ERR_SHAPE,
+               "row count exceeds the TMA coordinate range");
+  CUtensorMap mq, mk;
+  int st = make_map(&mq, Q, (uint64_t)S * Nq, d, BM);
+  if (st != GFST_OK) return st;
+  st = make_map(&mk, Ksum, (uint64_t)S * NBs, d, BN);
+  if (st != GFST_OK) return st;
+  const int nkb = (d + KBOX - 1) / KBOX;
+  if (nkb == 1) return dispatch_kcap<1, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (nkb == 2) return dispatch_kcap<2, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  return dispatch_kcap<4, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+}
+
+int read_device_error(int clear, unsigned int* value) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the device error word: %s", cudaGetErrorString(e));
+  if (clear && v != 0) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "clearing the device error word: %s", cudaGetErrorString(e));
+  }
+  *value = v;
+  return GFST_OK;
+}
+
+}  // namespace gfst

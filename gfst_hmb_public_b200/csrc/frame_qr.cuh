@@ -222,10 +222,12 @@ struct FrameQR {
         tau = 0.f;
         scal = 0.f;
       } else {
+        // correctly rounded reciprocals (one rounding more than a division,
+        // well inside the frame tolerances) keep the per-step chain short
         const float sigma = sqrtf(fmaf(alpha, alpha, xn2));
         beta = alpha >= 0.f ? -sigma : sigma;
-        tau = (beta - alpha) / beta;
-        scal = 1.f / (alpha - beta);
+        tau = (beta - alpha) * __frcp_rn(beta);
+        scal = __frcp_rn(alpha - beta);
       }
       rneg |= (beta < 0.f ? 1u : 0u) << K;
       if (rg == 0 && cg == 0) sm.tau[K] = tau;
@@ -352,10 +354,30 @@ struct FrameQR {
     }
   }
 
-  // Load a dense row-major [d, r] frame, zero padded.
+  // Load a dense row-major [d, r] frame, zero padded.  With one column group
+  // (CG == 1) a lane owns whole rows and full-width frames load as float4
+  // (vec4: the host checked 16-byte alignment of every row).
   __device__ static __forceinline__ void load(Frame& a, const float* __restrict__ src, int t, int d, int r,
-                                              bool valid) {
+                                              bool valid, bool vec4) {
     const int rg = t % RG, cg = t / RG;
+    if constexpr (CG == 1 && RMAX % 4 == 0) {
+      if (vec4 && r == RMAX) {
+#pragma unroll
+        for (int s = 0; s < RPT; ++s) {
+          const int row = rg + s * RG;
+#pragma unroll
+          for (int c4 = 0; c4 < RMAX / 4; ++c4) {
+            float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (valid && row < d) q = __ldg(reinterpret_cast<const float4*>(src + (size_t)row * RMAX) + c4);
+            set(a, s, 4 * c4 + 0, q.x);
+            set(a, s, 4 * c4 + 1, q.y);
+            set(a, s, 4 * c4 + 2, q.z);
+            set(a, s, 4 * c4 + 3, q.w);
+          }
+        }
+        return;
+      }
+    }
 #pragma unroll
     for (int s = 0; s < RPT; ++s) {
       const int row = rg + s * RG;
@@ -368,9 +390,24 @@ struct FrameQR {
   }
 
   __device__ static __forceinline__ void store(const Frame& a, float* __restrict__ dst, int t, int d, int r,
-                                               bool valid) {
+                                               bool valid, bool vec4) {
     const int rg = t % RG, cg = t / RG;
     if (!valid) return;
+    if constexpr (CG == 1 && RMAX % 4 == 0) {
+      if (vec4 && r == RMAX) {
+#pragma unroll
+        for (int s = 0; s < RPT; ++s) {
+          const int row = rg + s * RG;
+          if (row >= d) continue;
+#pragma unroll
+          for (int c4 = 0; c4 < RMAX / 4; ++c4) {
+            reinterpret_cast<float4*>(dst + (size_t)row * RMAX)[c4] =
+                make_float4(get(a, s, 4 * c4), get(a, s, 4 * c4 + 1), get(a, s, 4 * c4 + 2), get(a, s, 4 * c4 + 3));
+          }
+        }
+        return;
+      }
+    }
 #pragma unroll
     for (int s = 0; s < RPT; ++s) {
       const int row = rg + s * RG;

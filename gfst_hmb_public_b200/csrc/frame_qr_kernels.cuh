@@ -30,7 +30,7 @@ template <int DMAX, int RMAX, int RG, int CG, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>()))
     frame_update_qr_kernel(const float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
                            float beta, float* __restrict__ Uout, int64_t n_frames, int d, int r, int m,
-                           float eps_sign, int sign_mode) {
+                           float eps_sign, int sign_mode, bool vec4) {
   using QR = FrameQR<DMAX, RMAX, RG, CG>;
   constexpr int TPF = QR::TPF;
   constexpr int GPW = 32 / TPF;
@@ -46,11 +46,11 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>())
   const size_t frame_elems = (size_t)d * r;
 
   typename QR::Frame a;
-  QR::load(a, U + fs * frame_elems, t, d, r, valid);
+  QR::load(a, U + fs * frame_elems, t, d, r, valid, vec4);
   if (beta != 1.f) QR::scale(a, beta);
   if (m > 0 && valid) QR::rank_update(a, A + fs * (size_t)d * m, B + fs * (size_t)r * m, t, d, r, m);
   QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
-  QR::store(a, Uout + fs * frame_elems, t, d, r, valid);
+  QR::store(a, Uout + fs * frame_elems, t, d, r, valid, vec4);
 }
 
 // ---------------------------------------------------------------------------
@@ -71,7 +71,7 @@ template <int DMAX, int RMAX, int RG, int CG, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>()))
     frame_stream_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B, float beta,
                         int64_t n_frames, int T, int d, int r, int m, float eps_sign, int sign_mode,
-                        float* __restrict__ frames_out, int out_every) {
+                        float* __restrict__ frames_out, int out_every, bool vec4) {
   using QR = FrameQR<DMAX, RMAX, RG, CG>;
   constexpr int TPF = QR::TPF;
   constexpr int GPW = 32 / TPF;
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>())
   };
 
   typename QR::Frame a;
-  QR::load(a, U + fs * frame_elems, t, d, r, valid);
+  QR::load(a, U + fs * frame_elems, t, d, r, valid, vec4);
 
   issue(0);
   for (int tok = 0; tok < T; ++tok) {
@@ -118,11 +118,11 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>())
     QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
     if (frames_out != nullptr && ((tok + 1) % out_every) == 0) {
       const int64_t snap = (tok + 1) / out_every - 1;
-      QR::store(a, frames_out + (snap * n_frames + fs) * frame_elems, t, d, r, valid);
+      QR::store(a, frames_out + (snap * n_frames + fs) * frame_elems, t, d, r, valid, vec4);
     }
     __syncwarp();  // every lane is done with this stage buffer before it is refilled
   }
-  QR::store(a, U + fs * frame_elems, t, d, r, valid);
+  QR::store(a, U + fs * frame_elems, t, d, r, valid, vec4);
 }
 
 // ---------------------------------------------------------------------------
@@ -136,8 +136,9 @@ int launch_update(const float* U, const float* A, const float* B, float beta, fl
   const int64_t per_block = kWarps * GPW;
   const int64_t blocks = (n + per_block - 1) / per_block;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
+  const bool vec4 = (r % 4 == 0) && aligned16(U) && aligned16(Uout);
   frame_update_qr_kernel<DMAX, RMAX, RG, CG, kWarps><<<(unsigned)blocks, kWarps * 32, 0, stream>>>(
-      U, A, B, beta, Uout, n, d, r, m, eps_sign, sign_mode);
+      U, A, B, beta, Uout, n, d, r, m, eps_sign, sign_mode, vec4);
   return check_launch("frame_update_qr_kernel");
 }
 
@@ -148,6 +149,7 @@ int launch_stream(float* U, const float* A, const float* B, float beta, int64_t 
   const int64_t per_block = kWarps * GPW;
   const int64_t blocks = (n + per_block - 1) / per_block;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
+  const bool vec4 = (r % 4 == 0) && aligned16(U) && (frames_out == nullptr || aligned16(frames_out));
   const size_t smem = (size_t)per_block * 2 * (size_t)(d * m + r * m) * sizeof(float);
   auto kern = frame_stream_kernel<DMAX, RMAX, RG, CG, kWarps>;
   if (smem > 48 * 1024) {
@@ -155,7 +157,7 @@ int launch_stream(float* U, const float* A, const float* B, float beta, int64_t 
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
   kern<<<(unsigned)blocks, kWarps * 32, smem, stream>>>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode,
-                                                         frames_out, out_every);
+                                                         frames_out, out_every, vec4);
   return check_launch("frame_stream_kernel");
 }
 

@@ -116,15 +116,24 @@ GFST_API int gfst_block_commit_mean(const void* K, const void* V, void* pool_K, 
  * For every stream s and query q:
  *   score[b] = Q[s,q,:] . Ksum[s,b,:]   for b in [0, n_blocks)   (fp32 accumulate)
  *   top_idx[s,q,0..k) / top_scores[s,q,0..k) = the k best blocks in the total
- *   order (score descending, block index ascending).  Slots past n_blocks are
- *   filled with index -1 and score -inf.
+ *   order (score descending, block index ascending).  Blocks scoring NaN or
+ *   -inf are never selected; unfilled slots hold index -1 and score -inf.
  * Q: [n_streams, n_queries, d]; Ksum: [n_streams, n_blocks_stride, d] of which the
  * first n_blocks rows are scored.  dtype GFST_F32 computes with fp32 FMAs;
  * GFST_BF16 runs the tcgen05 tensor-core path (bf16 operands, fp32 accumulate).
- * Limits: 1 <= k <= 32; d a multiple of 8 (bf16) or 4 (f32), d <= 256.     */
+ * Limits: 1 <= k <= 32; d a multiple of 8 (bf16) or 4 (f32), d <= 256;
+ * bf16: n_streams <= 65535, Q and Ksum 16-byte aligned.                     */
 GFST_API int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_streams, int n_queries,
                     int n_blocks, int n_blocks_stride, int d, int k, int dtype,
                     float* top_scores, int32_t* top_idx, cudaStream_t stream);
+
+/* ---- device-side failure report ---------------------------------------------
+ * Kernels that wait on one another inside a CTA (the tensor-core retrieval
+ * pipeline) bound every wait; a wait that gives up records GFST_ERR_TIMEOUT in
+ * a sticky per-device word and the kernel returns without hanging.  This call
+ * synchronises with the current device's work, returns GFST_OK or the
+ * recorded status, and clears the word when `clear` is non-zero.            */
+GFST_API int gfst_check_device_errors(int clear);
 
 /* ---- exact-token readout ------------------------------------------------------
  * For every stream s and query q, over the tokens of the k blocks top_idx[s,q,:]

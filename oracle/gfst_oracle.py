@@ -185,19 +185,22 @@ def block_scores(Q: np.ndarray, Ksum: np.ndarray) -> np.ndarray:
 
 def block_topk(Q: np.ndarray, Ksum: np.ndarray, k: int):
     """retrieval.py:165-172 (exact_topk) batched over streams and queries, with
-    the deterministic total order (score desc, block index asc).  Returns
-    (top_scores f32 [S,Nq,k], top_idx int32 [S,Nq,k], margin_ok bool [S,Nq]);
-    slots past the block count hold (-inf, -1).  margin_ok is False when the
-    k-th and (k+1)-th scores are within 1e-3 relative, where any order of the
-    boundary is acceptable."""
+    the deterministic total order (score desc, block index asc).  Blocks
+    scoring NaN or -inf are never selected.  Returns (top_scores f32 [S,Nq,k],
+    top_idx int32 [S,Nq,k], margin_ok bool [S,Nq]); unfilled slots hold
+    (-inf, -1).  margin_ok is False when the k-th and (k+1)-th scores are within
+    1e-3 relative, where either order of the boundary is acceptable."""
     scores = block_scores(Q, Ksum)
+    scores = np.where(np.isnan(scores), -np.inf, scores)
     nb = scores.shape[-1]
     order = _order_desc_idx_asc(scores)
     kk = min(k, nb)
     top_idx = np.full(scores.shape[:-1] + (k,), -1, np.int32)
     top_sc = np.full(scores.shape[:-1] + (k,), -np.inf, np.float32)
-    top_idx[..., :kk] = order[..., :kk]
-    top_sc[..., :kk] = np.take_along_axis(scores, order[..., :kk], axis=-1).astype(np.float32)
+    sel_sc = np.take_along_axis(scores, order[..., :kk], axis=-1)
+    live = np.isfinite(sel_sc) | (sel_sc > 0)
+    top_idx[..., :kk] = np.where(live, order[..., :kk], -1)
+    top_sc[..., :kk] = np.where(live, sel_sc, -np.inf).astype(np.float32)
     margin_ok = np.ones(scores.shape[:-1], bool)
     if nb > kk:
         sk = np.take_along_axis(scores, order[..., kk - 1:kk], axis=-1)[..., 0]
