@@ -1,0 +1,517 @@
+"""Benchmark of the GFST-HMB streaming hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (per GPU, weak scaling: every rank runs its own batch shard):
+  stream_full -- B=64 batch x H=32 heads = 2048 streams, d=128 x r=32 fp32
+  frames updated per token by a rank-4 u v^T (u, v ~ N(0, 1/128)) then
+  Householder thin QR; bf16 keys / values / queries N(0,1); blocks of L=64
+  tokens in a 512-slot memory ring (full, i.e. the memory of a 32,768-token
+  pass); top-k=16 blocks then exact-token argmax and value fetch.
+  One step = one block (64 tokens) of every stream: 64 frame updates + QRs,
+  64 queries read out, one block committed.  Inputs of a step are 436 MB,
+  larger than L2, and every step re-reads them.
+The metric is tokens/s over all GPUs, a token being one position of one batch
+element through all 32 heads (B*T per second).  A second sub-result is the
+batched-QR microbenchmark (65,536 frames of 64 x 8) in frames/s.
+
+Rank 0 prints one JSON line.  Timing: W warm-up steps, then K steps between a
+barrier + synchronize on both sides, CUDA events on the launching streams, the
+maximum over ranks.  The roofline and per-kernel shares come from CUDA events
+recorded on the stream each kernel is launched on, inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+METRIC = "GFST step tokens/s (QR+readout) at 1/2/4/8 B200; batched-QR frames/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+# stream_full workload
+B_PER_GPU, HEADS, D, R, M, L, SLOTS, K_SEL = 64, 32, 128, 32, 4, 64, 512, 16
+SEED = 20261201 + 4
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def fp32_peak_tflops(clock_mhz: float) -> float:
+    # 148 SMs x 128 FP32 lanes x 2 flops per FMA
+    return 148 * 128 * 2 * clock_mhz * 1e6 / 1e12
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples taken while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self._thread:
+            self._thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def make_inputs(S, device, seed):
+    from gfst_hmb_public_b200 import workloads as wl
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    std = 1.0 / math.sqrt(D)
+    A = torch.randn((S, L, D, M), generator=g, device=device) * std
+    Bm = torch.randn((S, L, R, M), generator=g, device=device) * std
+    Kt, Vt, Qt = wl.token_tensors(S, L, D, seed=seed + 1, device=device, dtype=torch.bfloat16)
+    return A, Bm, Kt, Vt, Qt
+
+
+def build_step(S, device, seed):
+    from gfst_hmb_public_b200 import gfst, step as stp
+
+    st = stp.StreamingStep(S, d=D, r=R, block_len=L, n_slots=SLOTS, k=K_SEL, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 7)
+    U0 = torch.randn((S, D, R), generator=g, device=device)
+    st.set_frames(gfst.frame_update_qr(U0, sign_mode="r_diag_positive"))
+    # fill the memory ring: the state after a 32,768-token pass
+    for b in range(SLOTS):
+        Kb = torch.randn((S, L, D), generator=g, device=device).to(torch.bfloat16)
+        Vb = torch.randn((S, L, D), generator=g, device=device).to(torch.bfloat16)
+        st.memory.commit(Kb, Vb)
+    torch.cuda.synchronize(device)
+    return st
+
+
+class PhaseEvents:
+    """CUDA events around each kernel of a step, on the stream that launches it."""
+
+    def __init__(self):
+        self.records = []
+
+    def wrap(self, st):
+        from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
+
+        ev = self
+
+        def timed(stream_of, fn, name):
+            def inner(*a, **kw):
+                s = stream_of()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                out = fn(*a, **kw)
+                e1.record(s)
+                ev.records.append((name, e0, e1))
+                return out
+            return inner
+
+        cur = lambda: torch.cuda.current_stream()  # noqa: E731 -- the side stream inside step()
+        self._orig = (gfst.stream_frames, retrieval.block_topk, readout.exact_readout, memory.block_commit_mean)
+        gfst.stream_frames = timed(cur, gfst.stream_frames, "frames")
+        retrieval.block_topk = timed(cur, retrieval.block_topk, "topk")
+        readout.exact_readout = timed(cur, readout.exact_readout, "readout")
+        memory.block_commit_mean = timed(cur, memory.block_commit_mean, "commit")
+
+    def unwrap(self):
+        from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
+
+        gfst.stream_frames, retrieval.block_topk, readout.exact_readout, memory.block_commit_mean = self._orig
+
+    def summary(self) -> dict:
+        out: dict[str, list[float]] = {}
+        for name, e0, e1 in self.records:
+            out.setdefault(name, []).append(e0.elapsed_time(e1))
+        return {k: sum(v) / len(v) for k, v in out.items()}
+
+
+def run_ours(args, rank, world, device) -> dict | None:
+    import torch.distributed as dist
+
+    from gfst_hmb_public_b200 import gfst, workloads as wl
+
+    S = B_PER_GPU * HEADS
+    st = build_step(S, device, SEED + 1000 * rank)
+    A, Bm, Kt, Vt, Qt = make_inputs(S, device, SEED + 1000 * rank + 1)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        st.step(A, Bm, Kt, Vt, Qt)
+    torch.cuda.synchronize(device)
+
+    phases = PhaseEvents()
+    phases.wrap(st)
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    barrier()
+    torch.cuda.synchronize(device)
+    sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        out = st.step(A, Bm, Kt, Vt, Qt)
+    t1.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    clocks = sampler.stop()
+    phases.unwrap()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    phase_ms = phases.summary()
+    launches = 4 * args.steps
+
+    # end to end through the public step with host buffers: pinned host inputs
+    # copied in, the step, the per-token results copied back, every step
+    host_in = [t.cpu().pin_memory() for t in (A, Bm, Kt, Vt, Qt)]
+    dev_in = [torch.empty_like(t) for t in (A, Bm, Kt, Vt, Qt)]
+    h_tok = torch.empty((S, L), dtype=torch.int32).pin_memory()
+    h_score = torch.empty((S, L), dtype=torch.float32).pin_memory()
+    h_val = torch.empty((S, L, D), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(2, min(args.steps, 5))
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        o = st.step(*dev_in)
+        h_tok.copy_(o.best_tok, non_blocking=True)
+        h_score.copy_(o.best_score, non_blocking=True)
+        h_val.copy_(o.value, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(device)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = h_tok.numel() * 4 + h_score.numel() * 4 + h_val.numel() * 2
+    del host_in, dev_in
+
+    # batched-QR microbenchmark (65,536 frames of 64 x 8, one QR each)
+    spec = wl.BATCHED_QR
+    xq = wl.batched_qr_inputs(spec["n"], spec["d"], spec["r"], seed=spec["seed"], device=device)
+    oq = torch.empty_like(xq)
+    for _ in range(5):
+        gfst.frame_update_qr(xq, sign_mode="r_diag_positive", out=oq)
+    torch.cuda.synchronize(device)
+    q0 = torch.cuda.Event(enable_timing=True)
+    q1 = torch.cuda.Event(enable_timing=True)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    qr_ms = []
+    for _ in range(10):
+        flush.zero_()  # evict L2 between launches
+        q0.record()
+        gfst.frame_update_qr(xq, sign_mode="r_diag_positive", out=oq)
+        q1.record()
+        torch.cuda.synchronize(device)
+        qr_ms.append(q0.elapsed_time(q1))
+    qr_ms_med = statistics.median(qr_ms)
+    del flush
+
+    if rank != 0:
+        return None
+
+    peaks, peak_src = load_peaks()
+    hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    tokens_per_step = B_PER_GPU * L
+    value = world * tokens_per_step / (ms / 1e3)
+    e2e_value = world * tokens_per_step / (e2e_ms / 1e3)
+
+    # algorithmic bytes per launch (see DESIGN.md "Roofline"):
+    #   frames  -- unfused per-token contract: read U, A, B and write U
+    #   readout -- unique key blocks selected by the step's 64 queries per stream,
+    #              plus queries, selections and the value rows written back
+    #   topk    -- summaries of every slot + queries (tensor-core GEMM, 2*d flops each pair)
+    #   commit  -- read K, V of the block; write them and the summary
+    sel = out.top_idx
+    uniq = 0
+    for s0 in range(0, S, 256):
+        blk = sel[s0:s0 + 256].reshape(sel[s0:s0 + 256].shape[0], -1)
+        srt = torch.sort(blk, dim=1).values
+        uniq += int((srt[:, 1:] != srt[:, :-1]).sum().item() + srt.shape[0])
+    frames_bytes = S * L * (2 * D * R * 4 + (D * M + R * M) * 4)
+    readout_bytes = uniq * L * D * 2 + S * L * (D * 2 + K_SEL * 4 + D * 2 + 8)
+    commit_bytes = S * L * D * 2 * 2 * 2 + S * D * 2
+    topk_flops = 2.0 * S * L * SLOTS * D
+    shares = {k: v / sum(phase_ms.values()) for k, v in phase_ms.items()}
+    dominant = max(phase_ms, key=phase_ms.get)
+    per_kernel = {
+        "frames": {"bytes": frames_bytes, "ms": phase_ms.get("frames")},
+        "readout": {"bytes": readout_bytes, "ms": phase_ms.get("readout")},
+        "commit": {"bytes": commit_bytes, "ms": phase_ms.get("commit")},
+    }
+    traffic = None
+    tp = REPO / "profiles" / "traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get(dominant)
+        except Exception:
+            traffic = None
+    if dominant == "topk":
+        ach = topk_flops / (phase_ms["topk"] / 1e3) / 1e12
+        peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+        roof = {"kernel": "block_topk_tc", "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": traffic}
+    else:
+        kb = per_kernel[dominant]
+        ach = kb["bytes"] / (kb["ms"] / 1e3) / 1e9
+        roof = {"kernel": {"frames": "frame_stream", "readout": "exact_readout", "commit": "block_commit"}[dominant],
+                "bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(ach / hbm_peak, 4), "traffic": traffic}
+    sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
+    frames_flops = S * L * (4.0 * D * R * R + 2.0 * D * R * M)
+    fr_tflops = frames_flops / (phase_ms["frames"] / 1e3) / 1e12
+    roof["peak_source"] = peak_src
+    roof["frames_fp32"] = {"achieved_tflops": round(fr_tflops, 2),
+                           "peak_tflops_at_clock": round(fp32_peak_tflops(sm_mhz), 1),
+                           "frac": round(fr_tflops / fp32_peak_tflops(sm_mhz), 4)}
+    roof["kernel_ms"] = {k: round(v, 4) for k, v in phase_ms.items()}
+    roof["kernel_share"] = {k: round(v, 3) for k, v in shares.items()}
+    roof["readout_unique_block_frac"] = round(uniq / (S * SLOTS), 3)
+
+    qr_bytes = 2 * xq.numel() * 4
+    qr_gbs = qr_bytes / (qr_ms_med / 1e3) / 1e9
+    batched_qr = {"value": round(spec["n"] / (qr_ms_med / 1e3), 1), "unit": "frames/s", "ms": round(qr_ms_med, 4),
+                  "workload": "65,536 frames 64x8 fp32, column j x 10^(-j/2), 1% near-collinear pairs; L2 flushed",
+                  "roofline": {"bound": "hbm", "achieved": round(qr_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                               "frac": round(qr_gbs / hbm_peak, 4), "peak_source": peak_src}}
+
+    cpu = cpu_baseline_sample(rank, world) if (world == 1 and not args.no_cpu_baseline) else None
+
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 frames / bf16 memory (fp32 accumulate)",
+        "data": "synthetic (seeded; no dataset for this path)",
+        "config": {
+            "workload": f"stream_full: per GPU {B_PER_GPU} batch x {HEADS} heads = {S} streams; frames {D}x{R} fp32, "
+                        f"rank-{M} update + Householder thin QR (R-diag-positive) per token; bf16 memory of "
+                        f"{SLOTS} blocks x {L} tokens (full ring); top-{K_SEL} blocks + exact-token argmax; "
+                        f"step = one {L}-token block",
+            "global_batch": B_PER_GPU * world,
+            "heads": HEADS,
+            "tokens_per_step_per_gpu": tokens_per_step,
+            "streams_per_gpu": S,
+            "parallelism": f"dp{world} (streams sharded by batch, no collectives on the data path)",
+            "l2": "step inputs 436 MB > 126 MB L2, re-read every step",
+        },
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "StreamingStep.step with pinned-host inputs copied in and results copied out every step"},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "batched_qr": batched_qr,
+    }
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle restatement of the reference's CPU
+# path, timed on the host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_step(n_streams: int, seed: int, threads: int) -> tuple[float, int]:
+    """One 64-token block for ``n_streams`` streams through the oracle
+    (torch.linalg.qr per token, exact scoring, top-k, exact readout) against a
+    full 512-block memory.  Returns (seconds, tokens)."""
+    import numpy as np
+
+    from oracle import gfst_oracle as go
+
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    std = 1.0 / math.sqrt(D)
+    U0 = torch.linalg.qr(torch.randn((n_streams, D, R), generator=g))[0].numpy()
+    A = (torch.randn((n_streams, L, D, M), generator=g) * std).numpy()
+    Bm = (torch.randn((n_streams, L, R, M), generator=g) * std).numpy()
+    pool = torch.randn((n_streams, SLOTS, L, D), generator=g).to(torch.bfloat16).float().numpy()
+    summary = go.block_commit_mean(pool, bf16=True)
+    Q = torch.randn((n_streams, L, D), generator=g).to(torch.bfloat16).float().numpy()
+    Kb = torch.randn((n_streams, L, D), generator=g).to(torch.bfloat16).float().numpy()
+    t0 = time.perf_counter()
+    go.stream_frames(U0, A, Bm, 1.0, 1e-8, go.SIGN_R_DIAG_POSITIVE)
+    _, top_i, _ = go.block_topk(Q, summary, K_SEL)
+    go.exact_readout(Q, pool, pool, top_i)
+    go.block_commit_mean(Kb, bf16=True)
+    dt = time.perf_counter() - t0
+    return dt, L * n_streams // HEADS
+
+
+def cpu_baseline_sample(rank: int, world: int) -> dict:
+    threads = os.cpu_count() or 1
+    dt, tokens = cpu_reference_step(HEADS, SEED + 99, threads)
+    return {"value": round(tokens / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one batch element ({HEADS} heads) x {L} tokens of the same workload through the oracle "
+                      f"restatement (torch.linalg.qr per token, exact scores, top-k, readout) in {dt:.2f} s"}
+
+
+def run_reference(args, rank, world) -> dict | None:
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_reference_step(HEADS, SEED + 98, threads)
+    times, tokens = [], 0
+    for i in range(args.steps):
+        dt, tok = cpu_reference_step(HEADS, SEED + 100 + i, threads)
+        times.append(dt)
+        tokens = tok
+    per_step = sum(times) / len(times)
+    value = tokens / per_step
+    return {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_step * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 frames / bf16-valued memory (fp32 compute)",
+        "data": "synthetic (seeded; no dataset for this path)",
+        "impl": "reference",
+        "config": {"workload": "stream_full (same per-stream shapes); each step a bounded sample of one batch "
+                               f"element ({HEADS} heads) x {L} tokens on the host cores",
+                   "global_batch": B_PER_GPU * world, "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{HEADS} streams x {L} tokens per step"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core baseline sample")
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        res = run_ours(args, rank, world, device)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -5,27 +5,21 @@
 
 namespace gfst {
 
-// Insert (s, i) into the sorted list ts/ti (best first, `better` order) that
-// keeps the KCAP best candidates seen so far.  Callers scan candidates in
-// increasing index order and only insert when s > ts[KCAP-1]; a tie therefore
-// never displaces an earlier (lower) index, and NaN or -inf scores are never
-// selected.  The list starts filled with (-inf, INT_MAX) sentinels.
-template <int KCAP>
-__device__ __forceinline__ void topk_insert(float (&ts)[KCAP], int (&ti)[KCAP], float s, int i) {
-  if (!better(s, i, ts[KCAP - 1], ti[KCAP - 1])) return;
-  ts[KCAP - 1] = s;
-  ti[KCAP - 1] = i;
-#pragma unroll
-  for (int j = KCAP - 1; j > 0; --j) {
-    if (better(ts[j], ti[j], ts[j - 1], ti[j - 1])) {
-      const float tf = ts[j];
-      ts[j] = ts[j - 1];
-      ts[j - 1] = tf;
-      const int tt = ti[j];
-      ti[j] = ti[j - 1];
-      ti[j - 1] = tt;
-    }
+// Out-of-line insertion into a sorted (better-first) list of `kcap` entries in
+// local memory; returns the new k-th score.  Callers keep the k-th score in a
+// register and call this only when a candidate beats it -- rare once the list
+// has filled -- so the scan loop stays small (an inlined insertion per
+// candidate multiplies the code size and thrashes the instruction cache).
+__device__ __noinline__ inline float topk_insert_local(float* ts, int* ti, int kcap, float s, int i) {
+  int j = kcap - 1;
+  while (j > 0 && better(s, i, ts[j - 1], ti[j - 1])) {
+    ts[j] = ts[j - 1];
+    ti[j] = ti[j - 1];
+    --j;
   }
+  ts[j] = s;
+  ti[j] = i;
+  return ts[kcap - 1];
 }
 
 int block_topk_tc(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, float* ts,

@@ -11,8 +11,8 @@
 // One thread per query: the CTA stages its 128 queries transposed in shared
 // memory (conflict-free per-thread reads) and streams the stream's summaries
 // through a shared tile (broadcast reads).  Each (query, block) score is a
-// sequential fp32 FMA chain over d; each thread keeps a sorted top-KCAP list in
-// registers and inserts blocks in increasing index order.
+// sequential fp32 FMA chain over d; each thread keeps a sorted top-k list and
+// inserts blocks in increasing index order.
 #include "block_topk.cuh"
 
 namespace gfst {
@@ -25,10 +25,8 @@ template <typename T>
 __device__ __forceinline__ float ld_f32(const T* p);
 template <>
 __device__ __forceinline__ float ld_f32<float>(const float* p) { return __ldg(p); }
-template <>
-__device__ __forceinline__ float ld_f32<__nv_bfloat16>(const __nv_bfloat16* p) { return bf16_to_f32(*p); }
 
-template <typename T, int KCAP>
+template <typename T>
 __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict__ Q, const T* __restrict__ Ksum,
                                                              int n_queries, int n_blocks, int n_blocks_stride,
                                                              int d, int k, float* __restrict__ top_scores,
@@ -47,13 +45,13 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
     qT[(size_t)c * kQ + qq] = (q0 + qq < n_queries) ? ld_f32(Qs + (size_t)(q0 + qq) * d + c) : 0.f;
   }
 
-  float ts[KCAP];
-  int ti[KCAP];
-#pragma unroll
-  for (int j = 0; j < KCAP; ++j) {
+  float ts[32];
+  int ti[32];
+  for (int j = 0; j < k; ++j) {
     ts[j] = -INFINITY;
     ti[j] = 0x7fffffff;
   }
+  float kth = -INFINITY;
 
   for (int b0 = 0; b0 < n_blocks; b0 += kTile) {
     __syncthreads();
@@ -81,7 +79,7 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
     }
 #pragma unroll
     for (int j = 0; j < kTile; ++j) {
-      if (b0 + j < n_blocks && acc[j] > ts[KCAP - 1]) topk_insert<KCAP>(ts, ti, acc[j], b0 + j);
+      if (b0 + j < n_blocks && acc[j] > kth) kth = topk_insert_local(ts, ti, k, acc[j], b0 + j);
     }
   }
 
@@ -89,22 +87,19 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
   if (q < n_queries) {
     float* os = top_scores + ((size_t)s * n_queries + q) * k;
     int32_t* oi = top_idx + ((size_t)s * n_queries + q) * k;
-#pragma unroll
-    for (int j = 0; j < KCAP; ++j) {
-      if (j < k) {
-        const bool filled = ti[j] != 0x7fffffff;
-        os[j] = filled ? ts[j] : -INFINITY;
-        oi[j] = filled ? ti[j] : -1;
-      }
+    for (int j = 0; j < k; ++j) {
+      const bool filled = ti[j] != 0x7fffffff;
+      os[j] = filled ? ts[j] : -INFINITY;
+      oi[j] = filled ? ti[j] : -1;
     }
   }
 }
 
-template <typename T, int KCAP>
+template <typename T>
 int launch_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, float* ts,
                 int32_t* ti, cudaStream_t stream) {
   const size_t smem = ((size_t)d * kQ + (size_t)kTile * d) * sizeof(float);
-  auto kern = block_topk_simt_kernel<T, KCAP>;
+  auto kern = block_topk_simt_kernel<T>;
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -116,23 +111,13 @@ int launch_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int 
   return check_launch("block_topk_simt_kernel");
 }
 
-template <typename T>
-int dispatch_k(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, float* ts,
-               int32_t* ti, cudaStream_t stream) {
-  if (k <= 2) return launch_simt<T, 2>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
-  if (k <= 4) return launch_simt<T, 4>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
-  if (k <= 8) return launch_simt<T, 8>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
-  if (k <= 16) return launch_simt<T, 16>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
-  return launch_simt<T, 32>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
-}
-
 }  // namespace
 
 int block_topk_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, int dtype,
                     float* ts, int32_t* ti, cudaStream_t stream) {
   GFST_REQUIRE(d % 4 == 0, GFST_ERR_SHAPE, "d=%d must be a multiple of 4", d);
   (void)dtype;
-  return dispatch_k<float>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  return launch_simt<float>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
 }
 
 }  // namespace gfst

@@ -9,10 +9,15 @@
 // descending and the first token is the copy target (modeling.py:1151-1169).
 //
 // HBM-bound gather.  One CTA per (stream, query); its warps take the selected
-// blocks round robin and each lane scores whole token rows with 16-byte loads
-// (a sequential fp32 FMA chain over d; bf16 products are exact in fp32).
-// Consecutive CTAs are consecutive queries of one stream, so blocks picked by
-// several queries of a stream are served from L2.
+// blocks round robin.  Where a key row is a power-of-two number of 16-byte
+// chunks that divides a warp (d = 64/128/256 bf16, 32/64/128 fp32), a warp
+// load covers whole rows with consecutive lanes on consecutive chunks (fully
+// coalesced 512-byte loads); each lane keeps its chunk of the query in
+// registers, and the per-row partial dots of 16 row groups are combined with
+// one recursive-halving butterfly.  Other widths use a lane-per-row kernel.
+// bf16 products are exact in fp32; sums are fp32.  Consecutive CTAs are
+// consecutive queries of one stream, so blocks picked by several queries of a
+// stream are served from L2.
 #include "gfst_common.cuh"
 
 namespace gfst {
@@ -142,6 +147,115 @@ __global__ void __launch_bounds__(kThreads) exact_readout_kernel(
   }
 }
 
+// 16-byte chunk . query chunk (fp32 accumulate, packed FMAs)
+__device__ __forceinline__ float chunk_dot(const uint4& v, const float* q, float) {
+  float2 acc = make_float2(0.f, 0.f);
+  acc = ffma2(make_float2(__uint_as_float(v.x), __uint_as_float(v.y)), make_float2(q[0], q[1]), acc);
+  acc = ffma2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), make_float2(q[2], q[3]), acc);
+  return acc.x + acc.y;
+}
+__device__ __forceinline__ float chunk_dot(const uint4& v, const float* q, __nv_bfloat16) {
+  float2 acc = make_float2(0.f, 0.f);
+  acc = ffma2(make_float2(bf16_lo(v.x), bf16_hi(v.x)), make_float2(q[0], q[1]), acc);
+  acc = ffma2(make_float2(bf16_lo(v.y), bf16_hi(v.y)), make_float2(q[2], q[3]), acc);
+  acc = ffma2(make_float2(bf16_lo(v.z), bf16_hi(v.z)), make_float2(q[4], q[5]), acc);
+  acc = ffma2(make_float2(bf16_lo(v.w), bf16_hi(v.w)), make_float2(q[6], q[7]), acc);
+  return acc.x + acc.y;
+}
+
+// LPR lanes per key row (16-byte chunks per row), RPL = 32 / LPR rows per warp load.
+template <typename T, int LPR>
+__global__ void __launch_bounds__(kThreads) exact_readout_rows_kernel(
+    const T* __restrict__ Q, const T* __restrict__ pool_K, const T* __restrict__ pool_V,
+    const int32_t* __restrict__ top_idx, int n_queries, int n_slots, int L, int d, int dv, int k,
+    int32_t* __restrict__ best_tok, float* __restrict__ best_score, T* __restrict__ out_V) {
+  constexpr int N = Elems16<T>::N;
+  constexpr int RPL = 32 / LPR;
+  constexpr int G = 16;  // row groups per batch
+  __shared__ float red_s[kWarps];
+  __shared__ int red_i[kWarps];
+  const int64_t sq = blockIdx.x;  // stream * n_queries + query
+  const int64_t s = sq / n_queries;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = lane % LPR, h = lane / LPR;
+
+  float qc[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) qc[i] = to_f32(Q[sq * d + c * N + i]);
+
+  const int32_t* sel = top_idx + sq * k;
+  float bs = __int_as_float(0x7fc00000);  // NaN sentinel ranks last
+  int bi = 0x7fffffff;
+  for (int j = warp; j < k; j += kWarps) {
+    const int b = __ldg(sel + j);
+    if (b < 0 || b >= n_slots) continue;
+    const uint4* blk = reinterpret_cast<const uint4*>(pool_K + ((size_t)s * n_slots + b) * L * d);
+    for (int r0 = 0; r0 < L; r0 += G * RPL) {
+      uint4 raw[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int p = r0 + g * RPL + h;
+        raw[g] = p < L ? __ldg(blk + (size_t)p * LPR + c) : make_uint4(0, 0, 0, 0);
+      }
+      float v[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) v[g] = chunk_dot(raw[g], qc, T());
+      subgroup_reduce_scatter<G, LPR>(v, c);
+      if constexpr (G >= LPR) {
+        constexpr int C = G / LPR;
+#pragma unroll
+        for (int i = 0; i < C; ++i) {
+          const int p = r0 + (c * C + i) * RPL + h;
+          if (p < L && better(v[i], b * L + p, bs, bi)) {
+            bs = v[i];
+            bi = b * L + p;
+          }
+        }
+      } else {
+        const int p = r0 + (c / (LPR / G)) * RPL + h;
+        if (p < L && better(v[0], b * L + p, bs, bi)) {
+          bs = v[0];
+          bi = b * L + p;
+        }
+      }
+    }
+  }
+  warp_best(bs, bi);
+  if (lane == 0) {
+    red_s[warp] = bs;
+    red_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bs = lane < kWarps ? red_s[lane] : __int_as_float(0x7fc00000);
+    bi = lane < kWarps ? red_i[lane] : 0x7fffffff;
+    warp_best(bs, bi);
+    if (lane == 0) {
+      red_s[0] = bs;
+      red_i[0] = bi;
+    }
+  }
+  __syncthreads();
+  bs = red_s[0];
+  bi = red_i[0];
+  const bool found = bi != 0x7fffffff;
+  if (tid == 0) {
+    best_tok[sq] = found ? bi : -1;
+    best_score[sq] = found ? bs : -INFINITY;
+  }
+  if (out_V != nullptr) {
+    const int vv = dv / N;
+    uint4* dst = reinterpret_cast<uint4*>(out_V + sq * dv);
+    if (found) {
+      const int b = bi / L, p = bi % L;
+      const uint4* src = reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + b) * L + p) * dv);
+      for (int cc = tid; cc < vv; cc += kThreads) dst[cc] = __ldg(src + cc);
+    } else {
+      for (int cc = tid; cc < vv; cc += kThreads) dst[cc] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
 template <typename T>
 int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t* top_idx, int64_t S, int Nq,
            int NS, int L, int d, int dv, int k, int32_t* best_tok, float* best_score, void* out_V,
@@ -151,9 +265,28 @@ int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t*
   GFST_REQUIRE(out_V == nullptr || dv % N == 0, GFST_ERR_ALIGN, "dv=%d must be a multiple of %d", dv, N);
   const int64_t grid = S * (int64_t)Nq;
   GFST_REQUIRE(grid <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many queries");
+  const T* q = static_cast<const T*>(Q);
+  const T* pk = static_cast<const T*>(pool_K);
+  const T* pv = static_cast<const T*>(pool_V);
+  T* ov = static_cast<T*>(out_V);
+  switch (d / N) {
+    case 8:
+      exact_readout_rows_kernel<T, 8><<<(unsigned)grid, kThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, NS, L, d, dv, k,
+                                                                              best_tok, best_score, ov);
+      return check_launch("exact_readout_rows_kernel");
+    case 16:
+      exact_readout_rows_kernel<T, 16><<<(unsigned)grid, kThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, NS, L, d, dv,
+                                                                               k, best_tok, best_score, ov);
+      return check_launch("exact_readout_rows_kernel");
+    case 32:
+      exact_readout_rows_kernel<T, 32><<<(unsigned)grid, kThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, NS, L, d, dv,
+                                                                               k, best_tok, best_score, ov);
+      return check_launch("exact_readout_rows_kernel");
+    default:
+      break;
+  }
   exact_readout_kernel<T><<<(unsigned)grid, kThreads, (size_t)d * sizeof(float), stream>>>(
-      static_cast<const T*>(Q), static_cast<const T*>(pool_K), static_cast<const T*>(pool_V), top_idx, Nq, NS, L,
-      d, dv, k, best_tok, best_score, static_cast<T*>(out_V));
+      q, pk, pv, top_idx, Nq, NS, L, d, dv, k, best_tok, best_score, ov);
   return check_launch("exact_readout_kernel");
 }
 

@@ -29,58 +29,6 @@
 
 namespace gfst {
 
-// Sum v[0..P) over the G lanes of a lane subgroup (subgroup lane index t; the
-// subgroup is G consecutive lanes, G a power of two).  On return: if P >= G,
-// v[0..P/G) holds the totals of values [t*P/G, (t+1)*P/G); if P < G, v[0]
-// holds the total of value t/(G/P).
-template <int S, int O, int P>
-struct ReduceScatter {
-  __device__ static __forceinline__ void run(float (&v)[P], int t) {
-    if constexpr (O >= 1) {
-      if constexpr (S > 1) {
-        const bool upper = (t & O) != 0;
-#pragma unroll
-        for (int i = 0; i < S / 2; ++i) {
-          const float send = upper ? v[i] : v[i + S / 2];
-          const float keep = upper ? v[i + S / 2] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
-        }
-        ReduceScatter<S / 2, O / 2, P>::run(v, t);
-      } else {
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], O);
-        ReduceScatter<1, O / 2, P>::run(v, t);
-      }
-    }
-  }
-};
-
-template <int P, int G>
-__device__ __forceinline__ void subgroup_reduce_scatter(float (&v)[P], int t) {
-  ReduceScatter<P, G / 2, P>::run(v, t);
-}
-
-// Write the totals left by subgroup_reduce_scatter to red[0..P).
-template <int P, int G>
-__device__ __forceinline__ void subgroup_publish(const float (&v)[P], int t, float* red) {
-  if constexpr (P >= G) {
-    constexpr int C = P / G;
-#pragma unroll
-    for (int i = 0; i < C; ++i) red[t * C + i] = v[i];
-  } else {
-    constexpr int Q = G / P;
-    if ((t % Q) == 0) red[t / Q] = v[0];
-  }
-}
-
-template <int G>
-__device__ __forceinline__ float subgroup_allreduce(float x) {
-#pragma unroll
-  for (int o = G / 2; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
-
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-
 template <int DMAX, int RMAX, int RG, int CG>
 struct FrameQR {
   static constexpr int TPF = RG * CG;

@@ -1,0 +1,95 @@
+"""The streaming GFST-HMB step on one GPU: frames, block commit and sparse readout.
+
+One step consumes one block of L tokens for every (batch, head) stream:
+
+* frames   ``U <- QR(U + sum_i u_i v_i^T)`` for each of the L tokens, the frame
+           held in registers across the block (gfst_frame_stream);
+* readout  for each of the L queries: score every committed block summary
+           (tcgen05 GEMM + top-k), then score the tokens of the k selected
+           blocks and return the best token and its value row;
+* commit   the block's keys and values go into the memory ring and its summary
+           key (mean of the keys) into the summary table.
+
+The frame update and the readout are independent within a step, so they run on
+two CUDA streams: the frame kernel is FP32-ALU bound and the readout is HBM
+bound, and the two overlap on the SMs.  The commit follows the readout on the
+memory stream (the step's queries see the memory as it was before the step, as
+in the reference, where the block summary is appended after retrieval;
+modeling.py:3618-3632 of pkhairkh/gfst-hmb-public).
+
+Reference loop being replaced (pkhairkh/gfst-hmb-public): the per-token
+``for token: for batch:`` loop of GfstHmbSublayer (src/gfst_hmb_mpuc/modeling.py:
+3943-3961) calling _update_local_bases (2299-2423), _update_block_memory
+(3401-3571) and the retrieval/readout path (2714-2920, 984-1316).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import gfst, memory, readout, retrieval
+
+
+@dataclass
+class StepOutputs:
+    best_tok: torch.Tensor    # [S, L] int32, token index b * L + p of the best token (-1: none)
+    best_score: torch.Tensor  # [S, L] float32
+    value: torch.Tensor       # [S, L, dv] memory dtype
+    top_idx: torch.Tensor     # [S, L, k] int32 selected block slots
+
+
+class StreamingStep:
+    """Frames + block memory + readout for ``n_streams`` independent streams."""
+
+    def __init__(self, n_streams: int, *, d: int, r: int, block_len: int, n_slots: int, k: int,
+                 dtype: torch.dtype = torch.bfloat16, device="cuda", sign_mode="r_diag_positive",
+                 eps_sign: float = 1e-8):
+        self.n_streams, self.d, self.r, self.block_len, self.n_slots, self.k = n_streams, d, r, block_len, n_slots, k
+        self.sign_mode = sign_mode
+        self.eps_sign = eps_sign
+        self.device = torch.device(device)
+        self.U = torch.zeros((n_streams, d, r), dtype=torch.float32, device=self.device)
+        self.memory = memory.BlockMemory(n_streams, n_slots, block_len, d, d, dtype=dtype, device=self.device)
+        self.frames_stream = torch.cuda.Stream(self.device)
+        self.memory_stream = torch.cuda.Stream(self.device)
+
+    def set_frames(self, U0: torch.Tensor) -> None:
+        self.U.copy_(U0)
+
+    def step(self, A: torch.Tensor, B: torch.Tensor, K: torch.Tensor, V: torch.Tensor, Q: torch.Tensor,
+             *, out: StepOutputs | None = None) -> StepOutputs:
+        """A [S, L, d, m], B [S, L, r, m] fp32 update factors; K, V, Q [S, L, d]
+        in the memory dtype.  Work is enqueued on the caller's current stream's
+        device; the call returns once it is enqueued (outputs are ready when the
+        current stream reaches them)."""
+        cur = torch.cuda.current_stream(self.device)
+        self.frames_stream.wait_stream(cur)
+        self.memory_stream.wait_stream(cur)
+        with torch.cuda.stream(self.frames_stream):
+            gfst.stream_frames(self.U, A, B, eps_sign=self.eps_sign, sign_mode=self.sign_mode)
+        with torch.cuda.stream(self.memory_stream):
+            n_valid = self.memory.n_valid
+            if n_valid > 0:
+                top_s, top_i = retrieval.block_topk(Q, self.memory.summary, self.k, n_blocks=n_valid)
+                best_tok, best_score, value = readout.exact_readout(Q, self.memory.pool_K, self.memory.pool_V, top_i)
+            else:
+                S, L = Q.shape[0], Q.shape[1]
+                top_i = torch.full((S, L, self.k), -1, dtype=torch.int32, device=self.device)
+                best_tok = torch.full((S, L), -1, dtype=torch.int32, device=self.device)
+                best_score = torch.full((S, L), float("-inf"), dtype=torch.float32, device=self.device)
+                value = torch.zeros((S, L, V.shape[-1]), dtype=V.dtype, device=self.device)
+            self.memory.commit(K, V)
+        cur.wait_stream(self.frames_stream)
+        cur.wait_stream(self.memory_stream)
+        # tensors produced on side streams are consumed on the current stream
+        for t in (best_tok, best_score, value, top_i, self.U):
+            t.record_stream(cur)
+        result = StepOutputs(best_tok, best_score, value, top_i)
+        if out is not None:
+            out.best_tok.copy_(best_tok)
+            out.best_score.copy_(best_score)
+            out.value.copy_(value)
+            out.top_idx.copy_(top_i)
+            return out
+        return result
