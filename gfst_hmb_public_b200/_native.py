@@ -50,6 +50,7 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p,
     ],
     "gfst_check_device_errors": [_c_int],
+    "gfst_topk_merge": [_c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p],
     "gfst_exact_readout": [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,

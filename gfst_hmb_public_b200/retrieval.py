@@ -121,3 +121,22 @@ class BlockRetriever:
 
 # the reference's class name, for drop-in imports
 FaissGpuRetriever = BlockRetriever
+
+
+def topk_merge(scores: torch.Tensor, idx: torch.Tensor, k: int):
+    """Top-k of candidate lists (score desc, index asc): scores/idx [..., n_cand]
+    -> ([..., k] f32, [..., k] int32).  Negative indices, NaN and -inf skipped."""
+    nat.require_cuda(scores, idx, what="topk_merge")
+    if scores.shape != idx.shape:
+        raise ValueError("topk_merge: scores and idx shapes differ")
+    lead = tuple(scores.shape[:-1])
+    n_cand = int(scores.shape[-1])
+    s2 = scores.to(torch.float32).contiguous().reshape(-1, n_cand)
+    i2 = idx.to(torch.int32).contiguous().reshape(-1, n_cand)
+    rows = s2.shape[0]
+    out_s = torch.empty((rows, k), dtype=torch.float32, device=scores.device)
+    out_i = torch.empty((rows, k), dtype=torch.int32, device=scores.device)
+    with torch.cuda.device(scores.device):
+        nat.call("gfst_topk_merge", nat.ptr(s2), nat.ptr(i2), rows, n_cand, int(k), nat.ptr(out_s), nat.ptr(out_i),
+                 nat.stream_of(s2))
+    return out_s.reshape(*lead, k), out_i.reshape(*lead, k)

@@ -127,6 +127,16 @@ GFST_API int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_streams,
                     int n_blocks, int n_blocks_stride, int d, int k, int dtype,
                     float* top_scores, int32_t* top_idx, cudaStream_t stream);
 
+/* ---- candidate merge ----------------------------------------------------------
+ * For every row: the k best of the row's n_cand (score, index) candidates in the
+ * total order (score descending, index ascending); candidates with index < 0,
+ * NaN or -inf scores are skipped; unfilled slots hold (-inf, -1).  scores/idx:
+ * [rows, n_cand]; out: [rows, k].  Merges per-GPU candidate lists after an
+ * all-gather when the block memory is sharded by block range (no counterpart
+ * in the reference, which runs on one device).  Limits: 1 <= k <= 32.       */
+GFST_API int gfst_topk_merge(const float* scores, const int32_t* idx, int64_t rows, int n_cand,
+                             int k, float* out_scores, int32_t* out_idx, cudaStream_t stream);
+
 /* ---- device-side failure report ---------------------------------------------
  * Kernels that wait on one another inside a CTA (the tensor-core retrieval
  * pipeline) bound every wait; a wait that gives up records GFST_ERR_TIMEOUT in

@@ -1,0 +1,83 @@
+"""Multi-rank paths with the sm_100a kernels.  Two ranks share cuda:0 through
+gloo (collectives staged on the host, no kernel waits on another rank), so the
+test runs on one GPU; the block-range-sharded readout must equal the
+single-rank readout bit for bit."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gfst_hmb_public_b200 import readout, retrieval, sharding
+
+pytestmark = pytest.mark.gpu
+
+
+def test_topk_merge_kernel(cuda_device):
+    g = torch.Generator().manual_seed(3)
+    s = torch.randn((50, 24), generator=g)
+    i = torch.randperm(1000, generator=g)[:24].repeat(50, 1).to(torch.int32)
+    s[0, :5] = 2.0  # ties: lowest index first
+    i[0, :5] = torch.tensor([9, 3, 7, 1, 5], dtype=torch.int32)
+    i[1, 3] = -1
+    s[2, 4] = float("nan")
+    out_s, out_i = retrieval.topk_merge(s.to(cuda_device), i.to(cuda_device), 4)
+    for r in range(50):
+        cand = sorted((-float(s[r, c]), int(i[r, c])) for c in range(24)
+                      if int(i[r, c]) >= 0 and not np.isnan(float(s[r, c])))[:4]
+        assert out_i[r].tolist() == [c[1] for c in cand]
+    assert out_i[0].tolist() == [1, 3, 5, 7]
+
+
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _data(device):
+    g = torch.Generator().manual_seed(11)
+    S, NB, L, d, Nq, k = 3, 40, 64, 128, 100, 8
+    pool = torch.randn((S, NB, L, d), generator=g).to(torch.bfloat16)
+    vals = torch.randn((S, NB, L, d), generator=g).to(torch.bfloat16)
+    needles = torch.randint(0, NB * L, (S, Nq), generator=g)
+    flat = pool.reshape(S, NB * L, d).float()
+    Q = (flat[torch.arange(S)[:, None], needles] + 0.1 * torch.randn((S, Nq, d), generator=g)).to(torch.bfloat16)
+    summary = pool.float().mean(dim=2).to(torch.bfloat16)
+    return [t.to(device) for t in (pool, vals, Q, summary)] + [k]
+
+
+def _worker(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pool, vals, Q, summary, k = _data(torch.device("cuda:0"))
+        shard = sharding.BlockRange(rank, world, pool.shape[1])
+        sl = slice(shard.lo, shard.hi)
+        res = sharding.sharded_readout(Q, summary[:, sl].contiguous(), pool[:, sl].contiguous(),
+                                       vals[:, sl].contiguous(), k, shard)
+        torch.cuda.synchronize()
+        torch.save([t.cpu() for t in res], f"{out_path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_block_range_sharded_readout_two_ranks(cuda_device, tmp_path):
+    world = 2
+    out = str(tmp_path / "res")
+    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
+    pool, vals, Q, summary, k = _data(cuda_device)
+    ref_s, ref_i = retrieval.block_topk(Q, summary, k)
+    ref_t, ref_bs, ref_v = readout.exact_readout(Q, pool, vals, ref_i)
+    for r in range(world):
+        best_t, best_s, value, top_i, top_s = torch.load(f"{out}.{r}")
+        assert torch.equal(top_i, ref_i.cpu())
+        assert torch.equal(top_s, ref_s.cpu())
+        assert torch.equal(best_t, ref_t.cpu())
+        assert torch.equal(best_s, ref_bs.cpu())
+        assert torch.equal(value, ref_v.cpu())
