@@ -26,7 +26,7 @@ __device__ __forceinline__ float ld_f32(const T* p);
 template <>
 __device__ __forceinline__ float ld_f32<float>(const float* p) { return __ldg(p); }
 
-template <typename T>
+template <typename T, int KCAP>
 __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict__ Q, const T* __restrict__ Ksum,
                                                              int n_queries, int n_blocks, int n_blocks_stride,
                                                              int d, int k, float* __restrict__ top_scores,
@@ -45,13 +45,8 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
     qT[(size_t)c * kQ + qq] = (q0 + qq < n_queries) ? ld_f32(Qs + (size_t)(q0 + qq) * d + c) : 0.f;
   }
 
-  float ts[32];
-  int ti[32];
-  for (int j = 0; j < k; ++j) {
-    ts[j] = -INFINITY;
-    ti[j] = 0x7fffffff;
-  }
-  float kth = -INFINITY;
+  TopK<KCAP> top;
+  top.init();
 
   for (int b0 = 0; b0 < n_blocks; b0 += kTile) {
     __syncthreads();
@@ -77,29 +72,20 @@ __global__ void __launch_bounds__(kQ) block_topk_simt_kernel(const T* __restrict
         acc[j] = fmaf(q_3, kv.w, acc[j]);
       }
     }
-#pragma unroll
-    for (int j = 0; j < kTile; ++j) {
-      if (b0 + j < n_blocks && acc[j] > kth) kth = topk_insert_local(ts, ti, k, acc[j], b0 + j);
-    }
+    top.offer16(acc, b0, n_blocks);
   }
 
   const int q = q0 + tid;
   if (q < n_queries) {
-    float* os = top_scores + ((size_t)s * n_queries + q) * k;
-    int32_t* oi = top_idx + ((size_t)s * n_queries + q) * k;
-    for (int j = 0; j < k; ++j) {
-      const bool filled = ti[j] != 0x7fffffff;
-      os[j] = filled ? ts[j] : -INFINITY;
-      oi[j] = filled ? ti[j] : -1;
-    }
+    top.write(top_scores + ((size_t)s * n_queries + q) * k, top_idx + ((size_t)s * n_queries + q) * k, k);
   }
 }
 
-template <typename T>
+template <typename T, int KCAP>
 int launch_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, float* ts,
                 int32_t* ti, cudaStream_t stream) {
   const size_t smem = ((size_t)d * kQ + (size_t)kTile * d) * sizeof(float);
-  auto kern = block_topk_simt_kernel<T>;
+  auto kern = block_topk_simt_kernel<T, KCAP>;
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -117,7 +103,11 @@ int block_topk_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, 
                     float* ts, int32_t* ti, cudaStream_t stream) {
   GFST_REQUIRE(d % 4 == 0, GFST_ERR_SHAPE, "d=%d must be a multiple of 4", d);
   (void)dtype;
-  return launch_simt<float>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  if (k <= 2) return launch_simt<float, 2>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  if (k <= 4) return launch_simt<float, 4>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  if (k <= 8) return launch_simt<float, 8>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  if (k <= 16) return launch_simt<float, 16>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
+  return launch_simt<float, 32>(Q, Ksum, S, Nq, NB, NBs, d, k, ts, ti, stream);
 }
 
 }  // namespace gfst

@@ -130,7 +130,7 @@ struct TcLayout {
   static constexpr int SMEM_BYTES = 1024 + BAR_OFF + N_BARS * 8 + 64;
 };
 
-template <int NKB, int STAGES>
+template <int NKB, int STAGES, int KCAP>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     block_topk_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          int n_queries, int n_blocks, int n_blocks_stride, int k, float* __restrict__ top_scores,
@@ -237,15 +237,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       umma_commit(done);  // arrives once every MMA issued above has completed
     }
   } else {
-    // epilogue: TMEM lane quadrant = warp, row = warp * 32 + lane.  The top-k
-    // list lives in local memory; the k-th score stays in a register.
-    float ts[32];
-    int ti[32];
-    for (int j = 0; j < k; ++j) {
-      ts[j] = -INFINITY;
-      ti[j] = 0x7fffffff;
-    }
-    float kth = -INFINITY;
+    // epilogue: TMEM lane quadrant = warp, row = warp * 32 + lane
+    TopK<KCAP> top;
+    top.init();
     for (int i = 0; i < n_tiles; ++i) {
       const int acc = i & 1;
       // one lane waits and the warp follows its verdict, so the .sync.aligned
@@ -260,32 +254,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * BN);
-      const int b0 = i * BN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(taddr + c0, v);
-        tmem_wait_ld();
+      float v[BN];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int b = b0 + c0 + c;
-          if (b < n_blocks && v[c] > kth) kth = topk_insert_local(ts, ti, k, v[c], b);
-        }
-      }
+      for (int c0 = 0; c0 < BN; c0 += 16) tmem_ld16(taddr + c0, v + c0);
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-    }
-    const int q = q0 + warp * 32 + lane;
-    if (q < n_queries) {
-      float* os = top_scores + ((size_t)s * n_queries + q) * k;
-      int32_t* oi = top_idx + ((size_t)s * n_queries + q) * k;
-      for (int j = 0; j < k; ++j) {
-        const bool filled = ti[j] != 0x7fffffff;
-        os[j] = filled ? ts[j] : -INFINITY;
-        oi[j] = filled ? ti[j] : -1;
+      if (lane == 0) mbar_arrive(&tempty[acc]);  // accumulator free for tile i + 2
+      const int b0 = i * BN;
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float w[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) w[c] = v[c0 + c];
+        top.offer16(w, b0 + c0, n_blocks);
       }
     }
+    const int q = q0 + warp * 32 + lane;
+    if (q < n_queries)
+      top.write(top_scores + ((size_t)s * n_queries + q) * k, top_idx + ((size_t)s * n_queries + q) * k, k);
   }
 
   __syncthreads();
@@ -336,16 +323,26 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int box_r
   return GFST_OK;
 }
 
-template <int NKB, int STAGES>
+template <int NKB, int STAGES, int KCAP>
 int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
               int32_t* ti, cudaStream_t stream) {
   using LY = TcLayout<NKB, STAGES>;
-  auto kern = block_topk_tc_kernel<NKB, STAGES>;
+  auto kern = block_topk_tc_kernel<NKB, STAGES, KCAP>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM_BYTES);
   GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   dim3 grid((unsigned)((Nq + BM - 1) / BM), (unsigned)S);
   kern<<<grid, kThreadsTC, LY::SMEM_BYTES, stream>>>(mq, mk, Nq, NB, NBs, k, ts, ti);
   return check_launch("block_topk_tc_kernel");
+}
+
+template <int NKB, int STAGES>
+int dispatch_kcap(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
+                  int32_t* ti, cudaStream_t stream) {
+  if (k <= 2) return launch_tc<NKB, STAGES, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (k <= 4) return launch_tc<NKB, STAGES, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (k <= 8) return launch_tc<NKB, STAGES, 8>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (k <= 16) return launch_tc<NKB, STAGES, 16>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  return launch_tc<NKB, STAGES, 32>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
 }
 
 }  // namespace
@@ -363,9 +360,9 @@ int block_topk_tc(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, in
   st = make_map(&mk, Ksum, (uint64_t)S * NBs, d, BN);
   if (st != GFST_OK) return st;
   const int nkb = (d + KBOX - 1) / KBOX;
-  if (nkb == 1) return launch_tc<1, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
-  if (nkb == 2) return launch_tc<2, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
-  return launch_tc<4, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (nkb == 1) return dispatch_kcap<1, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (nkb == 2) return dispatch_kcap<2, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  return dispatch_kcap<4, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
 }
 
 int read_device_error(int clear, unsigned int* value) {

@@ -137,6 +137,39 @@ struct FrameQR {
     subgroup_publish<P, RG>(v, rg, red);
   }
 
+  static_assert(CPT % 4 == 0, "local column rows move as float4");
+
+  // this lane's slot-SK row (row K when the lane owns it) -> dst[0..CPT)
+  template <int SK>
+  __device__ static __forceinline__ void write_row(const Frame& a, float* dst) {
+#pragma unroll
+    for (int c = 0; c < CPT; c += 4)
+      *reinterpret_cast<float4*>(dst + c) = make_float4(get(a, SK, c), get(a, SK, c + 1), get(a, SK, c + 2),
+                                                        get(a, SK, c + 3));
+  }
+  __device__ static __forceinline__ void read_row(float (&v)[CPT], const float* src) {
+#pragma unroll
+    for (int c = 0; c < CPT; c += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(src + c);
+      v[c] = q.x;
+      v[c + 1] = q.y;
+      v[c + 2] = q.z;
+      v[c + 3] = q.w;
+    }
+  }
+
+  // a[:, C0 + i] -= g[i] * x for i < NV (packed, two columns' scalars at a time)
+  template <int C0>
+  __device__ static __forceinline__ void rank1_update(Frame& a, const float2 (&x)[RP], const float (&g)[CPT]) {
+    constexpr int NV = CPT - C0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float2 ng = make_float2(-g[i], -g[i]);
+#pragma unroll
+      for (int p = 0; p < RP; ++p) a[p][C0 + i] = ffma2(ng, x[p], a[p][C0 + i]);
+    }
+  }
+
   template <int C0>
   __device__ static __forceinline__ void geqrf_group(Frame& a, int rg, int cg, Smem& sm, uint32_t& rneg) {
     constexpr int NV = CPT - C0, SK = (C0 * CG) / RG;
@@ -149,10 +182,7 @@ struct FrameQR {
       const bool own_pivot = (rg == K - SK * RG);  // this lane holds row K (slot SK)
       const bool first_live = cg > j;              // local column C0 is right of K
       if (cg == j) write_column<C0>(a, xb, rg);
-      if (own_pivot) {
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) piv[cg * CPT + c] = get(a, SK, c);
-      }
+      if (own_pivot) write_row<SK>(a, piv + cg * CPT);
       __syncwarp();
       float2 x[RP];
       read_column<C0>(x, xb, rg, K);
@@ -164,36 +194,55 @@ struct FrameQR {
       __syncwarp();
 
       const float alpha = piv[j * CPT + C0];
+      float pv[CPT], rv[CPT];
+      read_row(pv, piv + cg * CPT);
+      read_row(rv, red);
       float beta, tau, scal;
       if (xn2 == 0.f) {
         beta = alpha;
         tau = 0.f;
         scal = 0.f;
       } else {
-        // correctly rounded reciprocals (one rounding more than a division,
-        // well inside the frame tolerances) keep the per-step chain short
-        const float sigma = sqrtf(fmaf(alpha, alpha, xn2));
+        // sigma = sqrt(alpha^2 + xnorm^2), beta = -sign(alpha) sigma,
+        // tau = (beta - alpha) / beta = 1 + |alpha| / sigma, scal = 1 / (alpha - beta);
+        // correctly rounded rsqrt / rcp keep the per-step chain short
+        const float ss = fmaf(alpha, alpha, xn2);
+        const float rs = __frsqrt_rn(ss);
+        const float sigma = ss * rs;
         beta = alpha >= 0.f ? -sigma : sigma;
-        tau = (beta - alpha) * __frcp_rn(beta);
+        tau = fmaf(fabsf(alpha), rs, 1.f);
         scal = __frcp_rn(alpha - beta);
       }
       rneg |= (beta < 0.f ? 1u : 0u) << K;
       if (rg == 0 && cg == 0) sm.tau[K] = tau;
 
+      // g_i = tau * (piv_i + scal * c_i) * scal, zero for column K / finished columns
+      float g[CPT];
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int c = C0 + i;
-        const float w = fmaf(scal, red[i], piv[cg * CPT + c]);  // v^T A[K:, column]
-        float tw = tau * w;
-        if (i == 0 && !first_live) tw = 0.f;  // column K or a finished column
-        const float g = tw * scal;
-        const float2 ng = make_float2(-g, -g);
-#pragma unroll
-        for (int p = 0; p < RP; ++p) a[p][c] = ffma2(ng, x[p], a[p][c]);
-        if (own_pivot) set(a, SK, c, get(a, SK, c) - tw);
+      for (int i = 0; i < NV; i += 2) {
+        if (i + 1 < NV) {
+          const float2 w = ffma2(make_float2(scal, scal), make_float2(rv[i], rv[i + 1]),
+                                 make_float2(pv[C0 + i], pv[C0 + i + 1]));
+          const float2 gg = __fmul2_rn(__fmul2_rn(w, make_float2(tau, tau)), make_float2(scal, scal));
+          g[i] = gg.x;
+          g[i + 1] = gg.y;
+        } else {
+          g[i] = tau * fmaf(scal, rv[i], pv[C0 + i]) * scal;
+        }
       }
+      if (!first_live) g[0] = 0.f;
+      // row K takes A[K, j] -= tau * w_j: with x_K = alpha - beta the packed
+      // update g * x_K gives exactly that term (g = tau w scal, scal = 1/(alpha-beta))
+      if (own_pivot) {
+        if (SK & 1) {
+          x[SK >> 1].y = alpha - beta;
+        } else {
+          x[SK >> 1].x = alpha - beta;
+        }
+      }
+      rank1_update<C0>(a, x, g);
       if (cg == j) {
-        // column K: v below the diagonal, beta on it
+        // column K: v = x * scal below the diagonal, beta on it
 #pragma unroll
         for (int p = 0; p < RP; ++p) {
           if (below<C0>(2 * p, rg, K)) a[p][C0].x *= scal;
@@ -223,17 +272,29 @@ struct FrameQR {
         read_column<C0>(v, xb, rg, K);
         column_dots<C0>(a, v, rg, first_live, red);
         __syncwarp();
+        float rv[CPT], g[CPT];
+        read_row(rv, red);
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          const int c = C0 + i;
-          const bool trailing = !(i == 0 && !first_live);
-          const float tp = trailing ? tau * red[i] : 0.f;
-          const float2 ntp = make_float2(-tp, -tp);
-#pragma unroll
-          for (int p = 0; p < RP; ++p) a[p][c] = ffma2(ntp, v[p], a[p][c]);
-          // row K of a trailing column was zeroed at that column's own step
-          if (own_pivot && trailing) set(a, SK, c, -tp);
+        for (int i = 0; i < NV; i += 2) {
+          if (i + 1 < NV) {
+            const float2 tp = __fmul2_rn(make_float2(tau, tau), make_float2(rv[i], rv[i + 1]));
+            g[i] = tp.x;
+            g[i + 1] = tp.y;
+          } else {
+            g[i] = tau * rv[i];
+          }
         }
+        if (!first_live) g[0] = 0.f;
+        // v_K = 1: row K of each trailing column (zeroed at that column's own
+        // step) becomes -tau * (v^T Q[:, column]) through the packed update
+        if (own_pivot) {
+          if (SK & 1) {
+            v[SK >> 1].y = 1.f;
+          } else {
+            v[SK >> 1].x = 1.f;
+          }
+        }
+        rank1_update<C0>(a, v, g);
       }
       if (cg == j) {
 #pragma unroll

@@ -11,15 +11,19 @@ namespace {
 
 constexpr int kThreads = 128;
 
+// Candidates arrive in arbitrary index order, so insertion compares with the
+// full (score, index) order.
+template <int KCAP>
 __global__ void __launch_bounds__(kThreads) topk_merge_kernel(const float* __restrict__ scores,
                                                               const int32_t* __restrict__ idx, int64_t rows,
                                                               int n_cand, int k, float* __restrict__ out_s,
                                                               int32_t* __restrict__ out_i) {
   const int64_t row = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   if (row >= rows) return;
-  float ts[32];
-  int ti[32];
-  for (int j = 0; j < k; ++j) {
+  float ts[KCAP];
+  int ti[KCAP];
+#pragma unroll
+  for (int j = 0; j < KCAP; ++j) {
     ts[j] = -INFINITY;
     ti[j] = 0x7fffffff;
   }
@@ -29,12 +33,28 @@ __global__ void __launch_bounds__(kThreads) topk_merge_kernel(const float* __res
     const float s = sr[c];
     const int i = ir[c];
     if (i < 0 || !(s > -INFINITY)) continue;
-    if (better(s, i, ts[k - 1], ti[k - 1])) topk_insert_local(ts, ti, k, s, i);
+    if (!better(s, i, ts[KCAP - 1], ti[KCAP - 1])) continue;
+    ts[KCAP - 1] = s;
+    ti[KCAP - 1] = i;
+#pragma unroll
+    for (int j = KCAP - 1; j > 0; --j) {
+      if (better(ts[j], ti[j], ts[j - 1], ti[j - 1])) {
+        const float a = ts[j];
+        ts[j] = ts[j - 1];
+        ts[j - 1] = a;
+        const int b = ti[j];
+        ti[j] = ti[j - 1];
+        ti[j - 1] = b;
+      }
+    }
   }
-  for (int j = 0; j < k; ++j) {
-    const bool filled = ti[j] != 0x7fffffff;
-    out_s[row * k + j] = filled ? ts[j] : -INFINITY;
-    out_i[row * k + j] = filled ? ti[j] : -1;
+#pragma unroll
+  for (int j = 0; j < KCAP; ++j) {
+    if (j < k) {
+      const bool filled = ti[j] != 0x7fffffff;
+      out_s[row * k + j] = filled ? ts[j] : -INFINITY;
+      out_i[row * k + j] = filled ? ti[j] : -1;
+    }
   }
 }
 
@@ -50,6 +70,13 @@ extern "C" int gfst_topk_merge(const float* scores, const int32_t* idx, int64_t 
   GFST_REQUIRE(out_scores && out_idx && (n_cand == 0 || (scores && idx)), GFST_ERR_ARG, "null buffer");
   const int64_t blocks = (rows + kThreads - 1) / kThreads;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many rows");
-  topk_merge_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(scores, idx, rows, n_cand, k, out_scores, out_idx);
+  if (k <= 2) {
+    topk_merge_kernel<2><<<(unsigned)blocks, kThreads, 0, stream>>>(scores, idx, rows, n_cand, k, out_scores, out_idx);
+  } else if (k <= 8) {
+    topk_merge_kernel<8><<<(unsigned)blocks, kThreads, 0, stream>>>(scores, idx, rows, n_cand, k, out_scores, out_idx);
+  } else {
+    topk_merge_kernel<32><<<(unsigned)blocks, kThreads, 0, stream>>>(scores, idx, rows, n_cand, k, out_scores,
+                                                                      out_idx);
+  }
   return check_launch("topk_merge_kernel");
 }
