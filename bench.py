@@ -235,31 +235,24 @@ def run_ours(args, rank, world, device) -> dict | None:
     phase_ms = phases.summary()
     launches = 4 * args.steps
 
-    # end to end through the public step with host buffers: pinned host inputs
-    # copied in, the step, the per-token results copied back, every step
+    # end to end with host buffers: every step's inputs start in pinned host
+    # memory and its per-token results end there (HostPipeline overlaps the
+    # copies of step i+1 with the kernels of step i)
+    from gfst_hmb_public_b200.step import HostPipeline
+
+    e2e_steps = max(3, min(args.steps, 6))
     host_in = [t.cpu().pin_memory() for t in (A, Bm, Kt, Vt, Qt)]
-    dev_in = [torch.empty_like(t) for t in (A, Bm, Kt, Vt, Qt)]
-    h_tok = torch.empty((S, L), dtype=torch.int32).pin_memory()
-    h_score = torch.empty((S, L), dtype=torch.float32).pin_memory()
-    h_val = torch.empty((S, L, D), dtype=torch.bfloat16).pin_memory()
-    e2e_steps = max(2, min(args.steps, 5))
-
-    def e2e_step():
-        for d_, h_ in zip(dev_in, host_in):
-            d_.copy_(h_, non_blocking=True)
-        o = st.step(*dev_in)
-        h_tok.copy_(o.best_tok, non_blocking=True)
-        h_score.copy_(o.best_score, non_blocking=True)
-        h_val.copy_(o.value, non_blocking=True)
-
-    e2e_step()
+    host_out = [(torch.empty((S, L), dtype=torch.int32).pin_memory(),
+                 torch.empty((S, L), dtype=torch.float32).pin_memory(),
+                 torch.empty((S, L, D), dtype=torch.bfloat16).pin_memory()) for _ in range(2)]
+    pipe = HostPipeline(st, (A, Bm, Kt, Vt, Qt))
+    pipe.run([host_in] * 2, host_out[:2])  # warm-up
     torch.cuda.synchronize(device)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
+    pipe.run([host_in] * e2e_steps, [host_out[i % 2] for i in range(e2e_steps)])
     e1.record()
     torch.cuda.synchronize(device)
     barrier()
@@ -269,8 +262,8 @@ def run_ours(args, rank, world, device) -> dict | None:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
     h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = h_tok.numel() * 4 + h_score.numel() * 4 + h_val.numel() * 2
-    del host_in, dev_in
+    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+    del host_in, pipe
 
     # batched-QR microbenchmark (65,536 frames of 64 x 8, one QR each)
     spec = wl.BATCHED_QR
@@ -392,7 +385,8 @@ def run_ours(args, rank, world, device) -> dict | None:
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "StreamingStep.step with pinned-host inputs copied in and results copied out every step"},
+                "path": "HostPipeline.run: each step's inputs copied from pinned host memory, its results copied "
+                        "back; copies of step i+1 overlap the kernels of step i"},
         "gpu_launches": launches,
         "clocks": clocks,
         "batched_qr": batched_qr,

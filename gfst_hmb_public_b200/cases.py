@@ -1,0 +1,85 @@
+"""Single-kernel cases for profiling (ncu) and quick timing.
+
+    python -m gfst_hmb_public_b200.cases CASE [--streams S] [--repeat R]
+
+Each case builds seeded inputs on cuda:0, launches its kernel ``repeat`` times
+(the first launch is a warm-up) and prints one line with the CUDA-event time of
+the last launch.  CASE is one of:
+
+  frames      streaming pass of 64 tokens, 128x32 frames, rank-4 updates
+  batched_qr  one update+QR launch over 65,536 frames of 64x8
+  topk        tensor-core score + top-16 of 64 queries over 512 summaries per stream
+  topk_long   tensor-core score + top-8 of 1024 queries over 8192 summaries per stream
+  readout     exact-token readout of 64 queries x 16 blocks of 64 tokens per stream
+  commit      one 64-token block commit per stream
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from . import gfst, memory, readout, retrieval, workloads as wl
+
+
+def _timed(fn, repeat: int) -> float:
+    ms = 0.0
+    for _ in range(repeat):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    return ms
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit"])
+    parser.add_argument("--streams", type=int, default=None)
+    parser.add_argument("--repeat", type=int, default=2)
+    args = parser.parse_args()
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(20261201)
+    bf = torch.bfloat16
+
+    if args.case == "frames":
+        S = args.streams or 2048
+        U = gfst.frame_update_qr(torch.randn((S, 128, 32), generator=g, device=dev), sign_mode="r_diag_positive")
+        A = torch.randn((S, 64, 128, 4), generator=g, device=dev) / math.sqrt(128)
+        B = torch.randn((S, 64, 32, 4), generator=g, device=dev) / math.sqrt(128)
+        ms = _timed(lambda: gfst.stream_frames(U, A, B, sign_mode="r_diag_positive"), args.repeat)
+        units = f"{S * 64 / ms / 1e3:.2f} M frame-tokens/s"
+    elif args.case == "batched_qr":
+        x = wl.batched_qr_inputs(65536, 64, 8, seed=20261202, device=dev)
+        out = torch.empty_like(x)
+        ms = _timed(lambda: gfst.frame_update_qr(x, sign_mode="r_diag_positive", out=out), args.repeat)
+        units = f"{2 * x.numel() * 4 / ms / 1e6:.0f} GB/s"
+    elif args.case in ("topk", "topk_long"):
+        S, Nq, NB, k = (args.streams or 2048, 64, 512, 16) if args.case == "topk" else (args.streams or 64, 1024, 8192, 8)
+        Q = torch.randn((S, Nq, 128), generator=g, device=dev).to(bf)
+        K = torch.randn((S, NB, 128), generator=g, device=dev).to(bf)
+        ms = _timed(lambda: retrieval.block_topk(Q, K, k), args.repeat)
+        units = f"{2.0 * S * Nq * NB * 128 / ms / 1e9:.1f} TFLOP/s"
+    elif args.case == "readout":
+        S = args.streams or 1024
+        pool = torch.randn((S, 512, 64, 128), generator=g, device=dev).to(bf)
+        Q = torch.randn((S, 64, 128), generator=g, device=dev).to(bf)
+        sel = torch.randint(0, 512, (S, 64, 16), generator=g, device=dev, dtype=torch.int32)
+        ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel), args.repeat)
+        units = f"{S * 64 * 16 * 64 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bytes"
+    else:  # commit
+        S = args.streams or 2048
+        mem = memory.BlockMemory(S, 4, 64, 128, dtype=bf, device=dev)
+        Kb = torch.randn((S, 64, 128), generator=g, device=dev).to(bf)
+        ms = _timed(lambda: mem.commit(Kb, Kb), args.repeat)
+        units = f"{S * 64 * 128 * 2 * 4 / ms / 1e6:.0f} GB/s"
+    print(f"{args.case}: {ms:.4f} ms  {units}", flush=True)
+
+
+if __name__ == "__main__":
+    main()

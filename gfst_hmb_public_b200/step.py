@@ -93,3 +93,59 @@ class StreamingStep:
             out.top_idx.copy_(top_i)
             return out
         return result
+
+
+class HostPipeline:
+    """Runs a StreamingStep on inputs held in pinned host memory.
+
+    The inputs of step i+1 are copied to the device on an upload stream while
+    step i computes (two device input buffers), and each step's results are
+    copied back to pinned host buffers on a download stream, so host<->device
+    traffic overlaps the kernels.  This is the end-to-end path a host-side
+    caller uses; every byte of every step crosses the bus.
+    """
+
+    def __init__(self, step: StreamingStep, example_inputs):
+        dev = step.device
+        self.step_obj = step
+        self.buffers = [[torch.empty_like(t, device=dev) for t in example_inputs] for _ in range(2)]
+        self.upload = torch.cuda.Stream(dev)
+        self.download = torch.cuda.Stream(dev)
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.free = [torch.cuda.Event() for _ in range(2)]
+        for e in self.free:
+            e.record(torch.cuda.current_stream(dev))
+
+    def _upload(self, i: int, host_inputs) -> None:
+        b = i % 2
+        self.upload.wait_event(self.free[b])
+        with torch.cuda.stream(self.upload):
+            for d, h in zip(self.buffers[b], host_inputs):
+                d.copy_(h, non_blocking=True)
+        self.ready[b].record(self.upload)
+
+    def run(self, host_inputs_per_step, host_outputs_per_step) -> None:
+        """host_inputs_per_step: sequence of (A, B, K, V, Q) pinned tensors;
+        host_outputs_per_step: sequence of (best_tok, best_score, value) pinned
+        tensors receiving each step's results.  Returns once all work is enqueued."""
+        cur = torch.cuda.current_stream(self.step_obj.device)
+        n = len(host_inputs_per_step)
+        if n == 0:
+            return
+        self._upload(0, host_inputs_per_step[0])
+        for i in range(n):
+            if i + 1 < n:
+                self._upload(i + 1, host_inputs_per_step[i + 1])
+            b = i % 2
+            cur.wait_event(self.ready[b])
+            out = self.step_obj.step(*self.buffers[b])
+            self.free[b].record(cur)
+            done = torch.cuda.Event()
+            done.record(cur)
+            self.download.wait_event(done)
+            with torch.cuda.stream(self.download):
+                for h, d in zip(host_outputs_per_step[i], (out.best_tok, out.best_score, out.value)):
+                    h.copy_(d, non_blocking=True)
+                for t in (out.best_tok, out.best_score, out.value):
+                    t.record_stream(self.download)
+        cur.wait_stream(self.download)
