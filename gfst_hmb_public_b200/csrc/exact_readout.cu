@@ -8,16 +8,14 @@
 // (src/gfst_hmb_mpuc/modeling.py:599-657); the collapsed scores are sorted
 // descending and the first token is the copy target (modeling.py:1151-1169).
 //
-// HBM-bound gather.  One CTA per (stream, query); its warps take the selected
-// blocks round robin.  Where a key row is a power-of-two number of 16-byte
-// chunks that divides a warp (d = 64/128/256 bf16, 32/64/128 fp32), a warp
-// load covers whole rows with consecutive lanes on consecutive chunks (fully
-// coalesced 512-byte loads); each lane keeps its chunk of the query in
-// registers, and the per-row partial dots of 16 row groups are combined with
-// one recursive-halving butterfly.  Other widths use a lane-per-row kernel.
-// bf16 products are exact in fp32; sums are fp32.  Consecutive CTAs are
-// consecutive queries of one stream, so blocks picked by several queries of a
-// stream are served from L2.
+// HBM-bound gather.  Where a key row is a power-of-two number of 16-byte
+// chunks that divides a warp (d = 64/128/256 bf16, 32/64/128 fp32), one CTA
+// serves a chunk of 64 queries of a stream: their (block, query) selections are
+// sorted by block so each selected block is read from HBM about once per chunk,
+// and a warp load covers whole rows (fully coalesced 512-byte loads, the
+// query's chunk in registers, one butterfly per 16 row groups).  Other widths
+// use a lane-per-row kernel (one CTA per query).  bf16 products are exact in
+// fp32; sums are fp32.  NaN scores never win.
 #include "gfst_common.cuh"
 
 namespace gfst {
@@ -163,33 +161,96 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, const float* q, __nv_
   return acc.x + acc.y;
 }
 
-// LPR lanes per key row (16-byte chunks per row), RPL = 32 / LPR rows per warp load.
+// LPR lanes per key row (16-byte chunks per row), RPL = 32 / LPR rows per warp
+// load: consecutive lanes read consecutive 16-byte chunks of whole rows.
+// ---------------------------------------------------------------------------
+// grouped readout: one CTA per (stream, chunk of QC queries).  The chunk's
+// (block, query) selections are sorted by block, and warps take the sorted
+// pairs round robin, so every query that picked a block reads it at about the
+// same time from one SM (L1 / L2 hits): each selected block crosses HBM about
+// once per chunk instead of once per query.  A query's best token is kept in
+// shared memory as a 64-bit key (orderable score, inverted token index) and
+// combined with atomicMax, which is order independent.
+// ---------------------------------------------------------------------------
+constexpr int kGWarps = 8;
+constexpr int kGThreads = kGWarps * 32;
+constexpr int kQC = 64;          // queries per CTA
+constexpr int kMaxPairs = 2048;  // kQC * k, k <= 32
+
+// larger key = better: higher score, then lower token index; NaN never wins
+__device__ __forceinline__ unsigned long long pack_best(float s, int tok) {
+  uint32_t u = __float_as_uint(s);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if (s != s) u = 0u;
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)tok);
+}
+__device__ __forceinline__ float unpack_score(unsigned long long key) {
+  uint32_t u = (uint32_t)(key >> 32);
+  u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+  return __uint_as_float(u);
+}
+
 template <typename T, int LPR>
-__global__ void __launch_bounds__(kThreads) exact_readout_rows_kernel(
+__global__ void __launch_bounds__(kGThreads) exact_readout_grouped_kernel(
     const T* __restrict__ Q, const T* __restrict__ pool_K, const T* __restrict__ pool_V,
-    const int32_t* __restrict__ top_idx, int n_queries, int n_slots, int L, int d, int dv, int k,
+    const int32_t* __restrict__ top_idx, int n_queries, int n_chunks, int n_slots, int L, int d, int dv, int k,
     int32_t* __restrict__ best_tok, float* __restrict__ best_score, T* __restrict__ out_V) {
   constexpr int N = Elems16<T>::N;
   constexpr int RPL = 32 / LPR;
-  constexpr int G = 16;  // row groups per batch
-  __shared__ float red_s[kWarps];
-  __shared__ int red_i[kWarps];
-  const int64_t sq = blockIdx.x;  // stream * n_queries + query
-  const int64_t s = sq / n_queries;
+  constexpr int G = 16;
+  __shared__ uint32_t keys[kMaxPairs];
+  __shared__ unsigned long long best[kQC];
+  const int64_t s = blockIdx.x / n_chunks;
+  const int q0 = (int)(blockIdx.x % n_chunks) * kQC;
+  const int nq = min(kQC, n_queries - q0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = lane % LPR, h = lane / LPR;
 
-  float qc[N];
-#pragma unroll
-  for (int i = 0; i < N; ++i) qc[i] = to_f32(Q[sq * d + c * N + i]);
+  // (block << 11 | local query) keys; invalid selections sort last
+  const int n_pairs = nq * k;
+  int n_pow2 = 1;
+  while (n_pow2 < n_pairs) n_pow2 <<= 1;
+  const int32_t* sel = top_idx + ((size_t)s * n_queries + q0) * k;
+  for (int e = tid; e < n_pow2; e += kGThreads) {
+    uint32_t key = 0xffffffffu;
+    if (e < n_pairs) {
+      const int b = __ldg(sel + e);
+      if (b >= 0 && b < n_slots) key = ((uint32_t)b << 11) | (uint32_t)(e / k);
+    }
+    keys[e] = key;
+  }
+  for (int q = tid; q < kQC; q += kGThreads) best[q] = 0ull;
+  __syncthreads();
+  // bitonic sort of keys[0 .. n_pow2)
+  for (int size = 2; size <= n_pow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int e = tid; e < n_pow2; e += kGThreads) {
+        const int partner = e ^ stride;
+        if (partner > e) {
+          const bool up = (e & size) == 0;
+          const uint32_t a = keys[e], b = keys[partner];
+          if ((a > b) == up) {
+            keys[e] = b;
+            keys[partner] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
 
-  const int32_t* sel = top_idx + sq * k;
-  float bs = __int_as_float(0x7fc00000);  // NaN sentinel ranks last
-  int bi = 0x7fffffff;
-  for (int j = warp; j < k; j += kWarps) {
-    const int b = __ldg(sel + j);
-    if (b < 0 || b >= n_slots) continue;
+  const T* Qs = Q + ((size_t)s * n_queries + q0) * d;
+  for (int pi = warp; pi < n_pairs; pi += kGWarps) {
+    const uint32_t key = keys[pi];
+    if (key == 0xffffffffu) break;  // sorted: the rest are invalid
+    if (pi > 0 && keys[pi - 1] == key) continue;  // the same block listed twice for a query
+    const int b = (int)(key >> 11), ql = (int)(key & 2047u);
+    float qc[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) qc[i] = to_f32(Qs[(size_t)ql * d + c * N + i]);
     const uint4* blk = reinterpret_cast<const uint4*>(pool_K + ((size_t)s * n_slots + b) * L * d);
+    float bs = __int_as_float(0x7fc00000);
+    int bi = 0x7fffffff;
     for (int r0 = 0; r0 < L; r0 += G * RPL) {
       uint4 raw[G];
 #pragma unroll
@@ -219,39 +280,31 @@ __global__ void __launch_bounds__(kThreads) exact_readout_rows_kernel(
         }
       }
     }
-  }
-  warp_best(bs, bi);
-  if (lane == 0) {
-    red_s[warp] = bs;
-    red_i[warp] = bi;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    bs = lane < kWarps ? red_s[lane] : __int_as_float(0x7fc00000);
-    bi = lane < kWarps ? red_i[lane] : 0x7fffffff;
     warp_best(bs, bi);
-    if (lane == 0) {
-      red_s[0] = bs;
-      red_i[0] = bi;
-    }
+    if (lane == 0 && bi != 0x7fffffff) atomicMax(&best[ql], pack_best(bs, bi));
   }
   __syncthreads();
-  bs = red_s[0];
-  bi = red_i[0];
-  const bool found = bi != 0x7fffffff;
-  if (tid == 0) {
-    best_tok[sq] = found ? bi : -1;
-    best_score[sq] = found ? bs : -INFINITY;
-  }
-  if (out_V != nullptr) {
-    const int vv = dv / N;
-    uint4* dst = reinterpret_cast<uint4*>(out_V + sq * dv);
-    if (found) {
-      const int b = bi / L, p = bi % L;
-      const uint4* src = reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + b) * L + p) * dv);
-      for (int cc = tid; cc < vv; cc += kThreads) dst[cc] = __ldg(src + cc);
-    } else {
-      for (int cc = tid; cc < vv; cc += kThreads) dst[cc] = make_uint4(0, 0, 0, 0);
+
+  // outputs: one warp per query
+  for (int ql = warp; ql < nq; ql += kGWarps) {
+    const unsigned long long key = best[ql];
+    const bool found = key != 0ull;
+    const int tok = found ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : -1;
+    const int64_t sq = (int64_t)s * n_queries + q0 + ql;
+    if (lane == 0) {
+      best_tok[sq] = tok;
+      best_score[sq] = found ? unpack_score(key) : -INFINITY;
+    }
+    if (out_V != nullptr) {
+      const int vv = dv / N;
+      uint4* dst = reinterpret_cast<uint4*>(out_V + sq * dv);
+      if (found) {
+        const int bb = tok / L, p = tok % L;
+        const uint4* src = reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + bb) * L + p) * dv);
+        for (int cc = lane; cc < vv; cc += 32) dst[cc] = __ldg(src + cc);
+      } else {
+        for (int cc = lane; cc < vv; cc += 32) dst[cc] = make_uint4(0, 0, 0, 0);
+      }
     }
   }
 }
@@ -269,21 +322,26 @@ int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t*
   const T* pk = static_cast<const T*>(pool_K);
   const T* pv = static_cast<const T*>(pool_V);
   T* ov = static_cast<T*>(out_V);
-  switch (d / N) {
-    case 8:
-      exact_readout_rows_kernel<T, 8><<<(unsigned)grid, kThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, NS, L, d, dv, k,
-                                                                              best_tok, best_score, ov);
-      return check_launch("exact_readout_rows_kernel");
-    case 16:
-      exact_readout_rows_kernel<T, 16><<<(unsigned)grid, kThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, NS, L, d, dv,
-                                                                               k, best_tok, best_score, ov);
-      return check_launch("exact_readout_rows_kernel");
-    case 32:
-      exact_readout_rows_kernel<T, 32><<<(unsigned)grid, kThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, NS, L, d, dv,
-                                                                               k, best_tok, best_score, ov);
-      return check_launch("exact_readout_rows_kernel");
-    default:
-      break;
+  const int64_t n_chunks = (Nq + kQC - 1) / kQC;
+  const bool grouped_ok = (int64_t)NS < (1LL << 21) && S * n_chunks <= 0x7fffffffLL;
+  if (grouped_ok) {
+    const unsigned ggrid = (unsigned)(S * n_chunks);
+    switch (d / N) {
+      case 8:
+        exact_readout_grouped_kernel<T, 8><<<ggrid, kGThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS, L,
+                                                                             d, dv, k, best_tok, best_score, ov);
+        return check_launch("exact_readout_grouped_kernel");
+      case 16:
+        exact_readout_grouped_kernel<T, 16><<<ggrid, kGThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS,
+                                                                              L, d, dv, k, best_tok, best_score, ov);
+        return check_launch("exact_readout_grouped_kernel");
+      case 32:
+        exact_readout_grouped_kernel<T, 32><<<ggrid, kGThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS,
+                                                                              L, d, dv, k, best_tok, best_score, ov);
+        return check_launch("exact_readout_grouped_kernel");
+      default:
+        break;
+    }
   }
   exact_readout_kernel<T><<<(unsigned)grid, kThreads, (size_t)d * sizeof(float), stream>>>(
       q, pk, pv, top_idx, Nq, NS, L, d, dv, k, best_tok, best_score, ov);

@@ -215,7 +215,8 @@ def block_topk(Q: np.ndarray, Ksum: np.ndarray, k: int):
 def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, top_idx: np.ndarray):
     """modeling.py:599-657 (_score_block_tokens: token score = key . query) and
     modeling.py:1151-1169 (best token = first of the scores sorted descending),
-    with token index b*L + p and the total order (score desc, index asc).
+    with token index b*L + p and the total order (score desc, index asc); NaN
+    scores never win and a block listed twice counts once.
     Q [S,Nq,d]; pool_K [S,NB,L,d]; pool_V [S,NB,L,dv]; top_idx [S,Nq,k] int.
     Returns (best_tok int32 [S,Nq], best_score f32 [S,Nq], out_V [S,Nq,dv] or None,
     margin_ok bool [S,Nq] -- False when the runner-up is within 1e-3 relative)."""
@@ -235,7 +236,11 @@ def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, 
             keys = np.concatenate([pool_K[s, b] for b in blocks], axis=0).astype(np.float64)
             toks = np.concatenate([b * L + np.arange(L) for b in blocks])
             sc = keys @ np.asarray(Q[s, q], np.float64)
-            order = np.lexsort((toks, -np.where(np.isnan(sc), -np.inf, sc)))
+            keep = ~np.isnan(sc)  # NaN scores never win
+            if not keep.any():
+                continue
+            keys, toks, sc = keys[keep], toks[keep], sc[keep]
+            order = np.lexsort((toks, -sc))
             w = order[0]
             best_tok[s, q] = toks[w]
             best_score[s, q] = np.float32(sc[w])

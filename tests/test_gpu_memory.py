@@ -169,6 +169,30 @@ def test_exact_readout_matches_oracle(cuda_device, dtype, S, Nq, NS, L, d, dv, k
     assert np.array_equal(_np(out_V)[ok], ref_V[ok])
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_exact_readout_grouped_chunks_and_duplicates(cuda_device, dtype):
+    # 150 queries per stream -> three query chunks (the last partial); some
+    # queries list the same block twice, some list out-of-range slots
+    S, Nq, NS, L, d, k = 3, 150, 40, 64, 128, 6
+    g = torch.Generator().manual_seed(21)
+    pool_K = torch.randn((S, NS, L, d), generator=g).to(dtype)
+    pool_V = torch.randn((S, NS, L, d), generator=g).to(dtype)
+    Q = torch.randn((S, Nq, d), generator=g).to(dtype)
+    sel = torch.randint(0, NS, (S, Nq, k), generator=g, dtype=torch.int32)
+    sel[:, ::7, 1] = sel[:, ::7, 0]
+    sel[:, ::11, 2] = NS + 3
+    sel[1, 5, :] = -1
+    tok, score, val = readout.exact_readout(Q.to(cuda_device), pool_K.to(cuda_device), pool_V.to(cuda_device),
+                                            sel.to(cuda_device))
+    ref_tok, ref_score, ref_V, ok = go.exact_readout(_np(Q), _np(pool_K), _np(pool_V),
+                                                     np.where(sel.numpy() < NS, sel.numpy(), -1))
+    got = tok.cpu().numpy()
+    assert got[1, 5] == -1 and ref_tok[1, 5] == -1
+    assert np.array_equal(got[ok], ref_tok[ok])
+    np.testing.assert_allclose(score.cpu().numpy()[ok], ref_score[ok], rtol=1e-5, atol=1e-5)
+    assert np.array_equal(_np(val)[ok], ref_V[ok])
+
+
 def test_exact_readout_no_valid_block(cuda_device):
     pool = torch.randn((1, 4, 8, 16), device=cuda_device)
     sel = torch.full((1, 2, 3), -1, dtype=torch.int32, device=cuda_device)
