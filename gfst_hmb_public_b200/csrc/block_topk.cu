@@ -21,9 +21,12 @@ extern "C" int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_stream
 }
 
 extern "C" int gfst_check_device_errors(int clear) {
-  unsigned int v = 0;
-  const int st = gfst::read_device_error(clear, &v);
+  unsigned int v = 0, w = 0;
+  int st = gfst::read_device_error(clear, &v);
   if (st != GFST_OK) return st;
+  st = gfst::read_readout_error(clear, &w);
+  if (st != GFST_OK) return st;
+  v = v != 0 ? v : w;
   if (v != 0) {
     gfst::set_last_error("a kernel gave up a bounded wait (device error word %u)", v);
     return (int)v;

@@ -93,6 +93,7 @@ struct TopK {
 int block_topk_tc(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, float* ts,
                   int32_t* ti, cudaStream_t stream);
 int read_device_error(int clear, unsigned int* value);
+int read_readout_error(int clear, unsigned int* value);  // exact_readout.cu
 
 int block_topk_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, int dtype,
                     float* ts, int32_t* ti, cudaStream_t stream);

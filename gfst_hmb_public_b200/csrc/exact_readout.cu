@@ -11,14 +11,32 @@
 // HBM-bound gather.  Where a key row is a power-of-two number of 16-byte
 // chunks that divides a warp (d = 64/128/256 bf16, 32/64/128 fp32), one CTA
 // serves a chunk of 64 queries of a stream: their (block, query) selections are
-// sorted by block so each selected block is read from HBM about once per chunk,
-// and a warp load covers whole rows (fully coalesced 512-byte loads, the
-// query's chunk in registers, one butterfly per 16 row groups).  Other widths
-// use a lane-per-row kernel (one CTA per query).  bf16 products are exact in
-// fp32; sums are fp32.  NaN scores never win.
+// sorted by block, each distinct selected block is streamed from HBM once per
+// chunk into a shared-memory ring by 1-D TMA bulk copies, and the consumer
+// warps score the block's rows from shared memory (the query's chunk in
+// registers, one butterfly per 16 row groups).  Other widths use a lane-per-row
+// kernel (one CTA per query).  bf16 products are exact in fp32; sums are fp32.
+// NaN scores never win.
 #include "gfst_common.cuh"
 
 namespace gfst {
+
+// sticky GFST_ERR_TIMEOUT report of the pipelined readout's bounded waits
+__device__ unsigned int g_readout_error = 0;
+
+int read_readout_error(int clear, unsigned int* value) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_readout_error, sizeof(v));
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the readout error word: %s", cudaGetErrorString(e));
+  if (clear && v != 0) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_readout_error, &zero, sizeof(zero));
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "clearing the readout error word: %s", cudaGetErrorString(e));
+  }
+  *value = v;
+  return GFST_OK;
+}
+
 namespace {
 
 constexpr int kWarps = 4;
@@ -164,18 +182,26 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, const float* q, __nv_
 // LPR lanes per key row (16-byte chunks per row), RPL = 32 / LPR rows per warp
 // load: consecutive lanes read consecutive 16-byte chunks of whole rows.
 // ---------------------------------------------------------------------------
-// grouped readout: one CTA per (stream, chunk of QC queries).  The chunk's
-// (block, query) selections are sorted by block, and warps take the sorted
-// pairs round robin, so every query that picked a block reads it at about the
-// same time from one SM (L1 / L2 hits): each selected block crosses HBM about
-// once per chunk instead of once per query.  A query's best token is kept in
-// shared memory as a 64-bit key (orderable score, inverted token index) and
-// combined with atomicMax, which is order independent.
+// pipelined readout: one CTA per (stream, chunk of kQC queries).
+//  1. the chunk's (block, query) selections are sorted by block (bitonic, smem)
+//     and grouped into runs, one run per distinct block;
+//  2. a producer thread streams each distinct block, once, into a ring of
+//     shared-memory stages with 1-D TMA bulk copies (cp.async.bulk, completion
+//     on an mbarrier with the byte count);
+//  3. consumer warps take the sorted pairs round robin, wait for their block's
+//     stage, score the block's rows against the pair's query from shared
+//     memory and fold the best token into the query's 64-bit key with a shared
+//     atomicMax (order independent); the last pair of a run frees its stage.
+// Each selected block crosses HBM once per query chunk, fully overlapped with
+// the scoring.  All waits are bounded; a wait that gives up raises the sticky
+// device error word and the CTA drains its copies and returns.
 // ---------------------------------------------------------------------------
-constexpr int kGWarps = 8;
-constexpr int kGThreads = kGWarps * 32;
-constexpr int kQC = 64;          // queries per CTA
-constexpr int kMaxPairs = 2048;  // kQC * k, k <= 32
+constexpr int kCWarps = 8;                    // consumer warps
+constexpr int kPThreads = (kCWarps + 1) * 32;  // + one producer warp
+constexpr int kQC = 64;                        // queries per CTA
+constexpr int kMaxPairs = 2048;                // kQC * k, k <= 32
+constexpr int kMaxStages = 8;
+constexpr long long kWaitCycles = 2000000000LL;
 
 // larger key = better: higher score, then lower token index; NaN never wins
 __device__ __forceinline__ unsigned long long pack_best(float s, int tok) {
@@ -190,28 +216,80 @@ __device__ __forceinline__ float unpack_score(unsigned long long key) {
   return __uint_as_float(u);
 }
 
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
 template <typename T, int LPR>
-__global__ void __launch_bounds__(kGThreads) exact_readout_grouped_kernel(
+__global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
     const T* __restrict__ Q, const T* __restrict__ pool_K, const T* __restrict__ pool_V,
     const int32_t* __restrict__ top_idx, int n_queries, int n_chunks, int n_slots, int L, int d, int dv, int k,
-    int32_t* __restrict__ best_tok, float* __restrict__ best_score, T* __restrict__ out_V) {
+    int n_stages, int32_t* __restrict__ best_tok, float* __restrict__ best_score, T* __restrict__ out_V) {
   constexpr int N = Elems16<T>::N;
   constexpr int RPL = 32 / LPR;
   constexpr int G = 16;
+  extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ uint32_t keys[kMaxPairs];
+  __shared__ uint16_t run_of[kMaxPairs];
+  __shared__ uint16_t run_start[kMaxPairs + 1];
   __shared__ unsigned long long best[kQC];
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ int pending[kMaxStages];
+  __shared__ int stage_run[kMaxStages];  // run whose block the stage holds (or is receiving)
+  __shared__ int warp_heads[kCWarps];
+  __shared__ int n_runs_s, n_valid_s, abort_s, issued_s;
+  volatile int* abort_v = &abort_s;
+  volatile int* stage_run_v = stage_run;
+
+  const uint32_t block_bytes = (uint32_t)L * d * sizeof(T);
+  T* stage = reinterpret_cast<T*>(dyn);                                   // [n_stages][L][d]
+  T* qs = reinterpret_cast<T*>(dyn + (size_t)n_stages * block_bytes);     // [kQC][d]
   const int64_t s = blockIdx.x / n_chunks;
   const int q0 = (int)(blockIdx.x % n_chunks) * kQC;
   const int nq = min(kQC, n_queries - q0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = lane % LPR, h = lane / LPR;
 
-  // (block << 11 | local query) keys; invalid selections sort last
+  // ---- selections -> sorted (block << 11 | local query) keys ----
   const int n_pairs = nq * k;
   int n_pow2 = 1;
   while (n_pow2 < n_pairs) n_pow2 <<= 1;
   const int32_t* sel = top_idx + ((size_t)s * n_queries + q0) * k;
-  for (int e = tid; e < n_pow2; e += kGThreads) {
+  for (int e = tid; e < n_pow2; e += kPThreads) {
     uint32_t key = 0xffffffffu;
     if (e < n_pairs) {
       const int b = __ldg(sel + e);
@@ -219,12 +297,27 @@ __global__ void __launch_bounds__(kGThreads) exact_readout_grouped_kernel(
     }
     keys[e] = key;
   }
-  for (int q = tid; q < kQC; q += kGThreads) best[q] = 0ull;
+  for (int q = tid; q < kQC; q += kPThreads) best[q] = 0ull;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(Q + ((size_t)s * n_queries + q0) * d);
+    uint4* dst = reinterpret_cast<uint4*>(qs);
+    for (int e = tid; e < nq * d / N; e += kPThreads) dst[e] = __ldg(src + e);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < n_stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      stage_run[i] = -1;
+    }
+    abort_s = 0;
+    issued_s = 0;
+    n_valid_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
-  // bitonic sort of keys[0 .. n_pow2)
   for (int size = 2; size <= n_pow2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int e = tid; e < n_pow2; e += kGThreads) {
+      for (int e = tid; e < n_pow2; e += kPThreads) {
         const int partner = e ^ stride;
         if (partner > e) {
           const bool up = (e & size) == 0;
@@ -238,55 +331,168 @@ __global__ void __launch_bounds__(kGThreads) exact_readout_grouped_kernel(
       __syncthreads();
     }
   }
-
-  const T* Qs = Q + ((size_t)s * n_queries + q0) * d;
-  for (int pi = warp; pi < n_pairs; pi += kGWarps) {
-    const uint32_t key = keys[pi];
-    if (key == 0xffffffffu) break;  // sorted: the rest are invalid
-    if (pi > 0 && keys[pi - 1] == key) continue;  // the same block listed twice for a query
-    const int b = (int)(key >> 11), ql = (int)(key & 2047u);
-    float qc[N];
+  // runs: one per distinct block.  Consumer thread t scans keys [8t, 8t+8):
+  // it flags run heads, the heads are prefix-summed over the CTA and each key
+  // gets its run index.
+  {
+    constexpr int PER = kMaxPairs / (kCWarps * 32);
+    int cnt = 0, incl = 0;
+    uint32_t heads = 0;
+    const int e0 = tid * PER;
+    if (warp < kCWarps) {
 #pragma unroll
-    for (int i = 0; i < N; ++i) qc[i] = to_f32(Qs[(size_t)ql * d + c * N + i]);
-    const uint4* blk = reinterpret_cast<const uint4*>(pool_K + ((size_t)s * n_slots + b) * L * d);
-    float bs = __int_as_float(0x7fc00000);
-    int bi = 0x7fffffff;
-    for (int r0 = 0; r0 < L; r0 += G * RPL) {
-      uint4 raw[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const int p = r0 + g * RPL + h;
-        raw[g] = p < L ? __ldg(blk + (size_t)p * LPR + c) : make_uint4(0, 0, 0, 0);
-      }
-      float v[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) v[g] = chunk_dot(raw[g], qc, T());
-      subgroup_reduce_scatter<G, LPR>(v, c);
-      if constexpr (G >= LPR) {
-        constexpr int C = G / LPR;
-#pragma unroll
-        for (int i = 0; i < C; ++i) {
-          const int p = r0 + (c * C + i) * RPL + h;
-          if (p < L && better(v[i], b * L + p, bs, bi)) {
-            bs = v[i];
-            bi = b * L + p;
+      for (int i = 0; i < PER; ++i) {
+        const int e = e0 + i;
+        if (e < n_pairs) {
+          const uint32_t key = keys[e];
+          if (key != 0xffffffffu) {
+            if (e == 0 || (keys[e - 1] >> 11) != (key >> 11)) {
+              heads |= 1u << i;
+              ++cnt;
+            }
+            if (e + 1 == n_pairs || keys[e + 1] == 0xffffffffu) n_valid_s = e + 1;
           }
         }
-      } else {
-        const int p = r0 + (c / (LPR / G)) * RPL + h;
-        if (p < L && better(v[0], b * L + p, bs, bi)) {
-          bs = v[0];
-          bi = b * L + p;
+      }
+      incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (lane == 31) warp_heads[warp] = incl;
+    }
+    __syncthreads();
+    if (warp < kCWarps) {
+      int base = 0;
+      for (int w = 0; w < warp; ++w) base += warp_heads[w];
+      int r = base + incl - cnt - 1;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = e0 + i;
+        if (e < n_pairs && keys[e] != 0xffffffffu) {
+          if ((heads >> i) & 1u) {
+            ++r;
+            run_start[r] = (uint16_t)e;
+          }
+          run_of[e] = (uint16_t)r;
         }
       }
+      if (tid == kCWarps * 32 - 1) n_runs_s = base + incl;
     }
-    warp_best(bs, bi);
-    if (lane == 0 && bi != 0x7fffffff) atomicMax(&best[ql], pack_best(bs, bi));
+    __syncthreads();
+    if (tid == 0) run_start[n_runs_s] = (uint16_t)n_valid_s;
+    __syncthreads();
+  }
+  const int n_runs = n_runs_s;
+  const int n_valid = n_valid_s;
+
+  if (warp == kCWarps) {
+    // ---- producer: one bulk copy per distinct block ----
+    if (lane == 0) {
+      int r = 0;
+      for (; r < n_runs; ++r) {
+        const int st = r % n_stages;
+        if (!mbar_wait(&empty[st], ((r / n_stages) & 1) ^ 1)) {
+          *abort_v = 1;
+          break;
+        }
+        if (*abort_v) break;
+        const int b = (int)(keys[run_start[r]] >> 11);
+        pending[st] = run_start[r + 1] - run_start[r];
+        stage_run_v[st] = r;
+        mbar_arrive_expect_tx(&full[st], block_bytes);
+        bulk_load(reinterpret_cast<uint8_t*>(stage) + (size_t)st * block_bytes,
+                  pool_K + ((size_t)s * n_slots + b) * L * d, block_bytes, &full[st]);
+      }
+      issued_s = r;
+    }
+  } else {
+    // ---- consumers ----
+    // A pair of run r waits until its stage is tagged with r (the producer
+    // tags a stage only after the stage's previous run is fully consumed), then
+    // on the stage's full barrier for that phase: a warp that runs ahead of
+    // the ring can never mistake an older phase of the same parity for its own.
+    const int c = lane % LPR, h = lane / LPR;
+    for (int pi = warp; pi < n_valid; pi += kCWarps) {
+      const int r = run_of[pi];
+      const int st = r % n_stages;
+      int ok = 1;
+      if (lane == 0) {
+        if (stage_run_v[st] != r) {
+          const long long t0 = clock64();
+          while (stage_run_v[st] != r) {
+            if (*abort_v || clock64() - t0 > kWaitCycles) {
+              ok = 0;
+              break;
+            }
+          }
+        }
+        if (ok && !mbar_wait(&full[st], (r / n_stages) & 1)) ok = 0;
+        if (!ok) *abort_v = 1;
+        if (*abort_v) ok = 0;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const uint32_t key = keys[pi];
+      const int b = (int)(key >> 11), ql = (int)(key & 2047u);
+      const bool dup = pi > 0 && keys[pi - 1] == key;  // a block listed twice for one query
+      if (!dup) {
+        float qc[N];
+        {
+          const uint4 qv = reinterpret_cast<const uint4*>(qs + (size_t)ql * d)[c];
+          const T* qe = reinterpret_cast<const T*>(&qv);
+#pragma unroll
+          for (int i = 0; i < N; ++i) qc[i] = to_f32(qe[i]);
+        }
+        const uint4* blk = reinterpret_cast<const uint4*>(reinterpret_cast<uint8_t*>(stage) + (size_t)st * block_bytes);
+        float bs = __int_as_float(0x7fc00000);
+        int bi = 0x7fffffff;
+        for (int r0 = 0; r0 < L; r0 += G * RPL) {
+          float v[G];
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const int p = r0 + g * RPL + h;
+            v[g] = p < L ? chunk_dot(blk[(size_t)p * LPR + c], qc, T()) : 0.f;
+          }
+          subgroup_reduce_scatter<G, LPR>(v, c);
+          if constexpr (G >= LPR) {
+            constexpr int C = G / LPR;
+#pragma unroll
+            for (int i = 0; i < C; ++i) {
+              const int p = r0 + (c * C + i) * RPL + h;
+              if (p < L && better(v[i], b * L + p, bs, bi)) {
+                bs = v[i];
+                bi = b * L + p;
+              }
+            }
+          } else {
+            const int p = r0 + (c / (LPR / G)) * RPL + h;
+            if (p < L && better(v[0], b * L + p, bs, bi)) {
+              bs = v[0];
+              bi = b * L + p;
+            }
+          }
+        }
+        warp_best(bs, bi);
+        if (lane == 0 && bi != 0x7fffffff) atomicMax(&best[ql], pack_best(bs, bi));
+      }
+      __syncwarp();
+      if (lane == 0 && atomicSub(&pending[st], 1) == 1) mbar_arrive(&empty[st]);
+    }
   }
   __syncthreads();
+  if (tid == kCWarps * 32) {
+    // after a timeout: wait (bounded) for the copies still in flight
+    if (*abort_v) {
+      const int issued = issued_s;
+      for (int r = max(0, issued - n_stages); r < issued; ++r) mbar_wait(&full[r % n_stages], (r / n_stages) & 1);
+      atomicExch(&g_readout_error, (unsigned)GFST_ERR_TIMEOUT);
+    }
+  }
 
-  // outputs: one warp per query
-  for (int ql = warp; ql < nq; ql += kGWarps) {
+  // ---- outputs: one warp per query ----
+  for (int ql = warp; ql < nq; ql += kCWarps + 1) {
     const unsigned long long key = best[ql];
     const bool found = key != 0ull;
     const int tok = found ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : -1;
@@ -323,22 +529,30 @@ int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t*
   const T* pv = static_cast<const T*>(pool_V);
   T* ov = static_cast<T*>(out_V);
   const int64_t n_chunks = (Nq + kQC - 1) / kQC;
-  const bool grouped_ok = (int64_t)NS < (1LL << 21) && S * n_chunks <= 0x7fffffffLL;
-  if (grouped_ok) {
-    const unsigned ggrid = (unsigned)(S * n_chunks);
+  const size_t block_bytes = (size_t)L * d * sizeof(T);
+  // stages: about 80 KB of ring per CTA (two CTAs per SM), 2 to 8 blocks
+  int n_stages = (int)((80u * 1024u) / block_bytes);
+  n_stages = n_stages < 2 ? 2 : (n_stages > kMaxStages ? kMaxStages : n_stages);
+  const size_t dyn = (size_t)n_stages * block_bytes + (size_t)kQC * d * sizeof(T);
+  const bool pipelined_ok = (int64_t)NS < (1LL << 21) && S * n_chunks <= 0x7fffffffLL && dyn <= 200u * 1024u &&
+                            (L * (int64_t)d * (int64_t)sizeof(T)) % 16 == 0 && aligned16(Q) && k <= 32;
+  if (pipelined_ok) {
+    const unsigned pgrid = (unsigned)(S * n_chunks);
+    cudaError_t e = cudaSuccess;
     switch (d / N) {
-      case 8:
-        exact_readout_grouped_kernel<T, 8><<<ggrid, kGThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS, L,
-                                                                             d, dv, k, best_tok, best_score, ov);
-        return check_launch("exact_readout_grouped_kernel");
-      case 16:
-        exact_readout_grouped_kernel<T, 16><<<ggrid, kGThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS,
-                                                                              L, d, dv, k, best_tok, best_score, ov);
-        return check_launch("exact_readout_grouped_kernel");
-      case 32:
-        exact_readout_grouped_kernel<T, 32><<<ggrid, kGThreads, 0, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS,
-                                                                              L, d, dv, k, best_tok, best_score, ov);
-        return check_launch("exact_readout_grouped_kernel");
+#define GFST_READOUT_CASE(LPRV)                                                                                   \
+  case LPRV: {                                                                                                    \
+    auto kern = exact_readout_pipelined_kernel<T, LPRV>;                                                           \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);                         \
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));           \
+    kern<<<pgrid, kPThreads, dyn, stream>>>(q, pk, pv, top_idx, Nq, (int)n_chunks, NS, L, d, dv, k, n_stages,       \
+                                            best_tok, best_score, ov);                                             \
+    return check_launch("exact_readout_pipelined_kernel");                                                         \
+  }
+      GFST_READOUT_CASE(8)
+      GFST_READOUT_CASE(16)
+      GFST_READOUT_CASE(32)
+#undef GFST_READOUT_CASE
       default:
         break;
     }

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gfst_hmb_public_b200 import memory, readout, retrieval, workloads as wl
+from gfst_hmb_public_b200 import _native, memory, readout, retrieval, workloads as wl
 from oracle import gfst_oracle as go
 
 pytestmark = pytest.mark.gpu
@@ -191,6 +191,32 @@ def test_exact_readout_grouped_chunks_and_duplicates(cuda_device, dtype):
     assert np.array_equal(got[ok], ref_tok[ok])
     np.testing.assert_allclose(score.cpu().numpy()[ok], ref_score[ok], rtol=1e-5, atol=1e-5)
     assert np.array_equal(_np(val)[ok], ref_V[ok])
+
+
+@pytest.mark.parametrize("pattern", ["spread", "shared"])
+def test_exact_readout_stage_ring_wraps(cuda_device, pattern):
+    # 64 queries x k=32 selections per chunk: with 8 KB blocks the staging ring
+    # (8 stages) wraps dozens of times ("spread": ~280 distinct blocks), or
+    # every query of the chunk reads the same 32 blocks ("shared": 64 queries
+    # per staged block)
+    S, Nq, NS, L, d, k = 2, 64, 300, 32, 128, 32
+    g = torch.Generator().manual_seed(5)
+    pool_K = torch.randn((S, NS, L, d), generator=g).to(torch.bfloat16)
+    pool_V = torch.randn((S, NS, L, d), generator=g).to(torch.bfloat16)
+    Q = torch.randn((S, Nq, d), generator=g).to(torch.bfloat16)
+    if pattern == "spread":
+        sel = torch.stack([torch.stack([torch.randperm(NS, generator=g)[:k] for _ in range(Nq)]) for _ in range(S)])
+    else:
+        sel = torch.randperm(NS, generator=g)[:k].expand(S, Nq, k).clone()
+    sel = sel.to(torch.int32)
+    tok, score, val = readout.exact_readout(Q.to(cuda_device), pool_K.to(cuda_device), pool_V.to(cuda_device),
+                                            sel.to(cuda_device))
+    ref_tok, ref_score, ref_V, ok = go.exact_readout(_np(Q), _np(pool_K), _np(pool_V), sel.numpy())
+    assert ok.mean() > 0.9
+    assert np.array_equal(tok.cpu().numpy()[ok], ref_tok[ok])
+    np.testing.assert_allclose(score.cpu().numpy()[ok], ref_score[ok], rtol=1e-5, atol=1e-5)
+    assert np.array_equal(_np(val)[ok], ref_V[ok])
+    assert _native.load().gfst_check_device_errors(1) == 0
 
 
 def test_exact_readout_no_valid_block(cuda_device):
