@@ -18,8 +18,7 @@
 // Every mbarrier wait is bounded (about a second of clock cycles); a wait that
 // gives up sets a sticky device error word (read with gfst_check_device_errors)
 // and the CTA drains its in-flight copies and MMAs, frees TMEM and returns.
-#include <cuda.h>
-
+#include "async_copy.cuh"
 #include "block_topk.cuh"
 
 namespace gfst {
@@ -32,51 +31,6 @@ constexpr int BM = 128;            // query rows per CTA (TMEM lanes)
 constexpr int BN = 128;            // summaries per tile (TMEM columns per accumulator)
 constexpr int KBOX = 64;           // bf16 elements per 128-byte swizzle row
 constexpr int kThreadsTC = 192;
-constexpr long long kWaitCycles = 2000000000LL;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Wait for the phase with the given parity; false if it did not complete
-// within the cycle budget.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -292,37 +246,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // --- host: tensor maps through the driver entry point ------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = []() -> EncodeTiledFn {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-// 2-D bf16 map of a [rows, d] row-major matrix, box 64 x box_rows, 128B swizzle.
-int make_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int box_rows) {
-  EncodeTiledFn enc = encode_fn();
-  GFST_REQUIRE(enc != nullptr, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)d * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)KBOX, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  GFST_REQUIRE(r == CUDA_SUCCESS, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return GFST_OK;
-}
-
 template <int NKB, int STAGES, int KCAP>
 int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
               int32_t* ti, cudaStream_t stream) {
@@ -355,14 +278,44 @@ int block_topk_tc(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, in
   GFST_REQUIRE(S * (int64_t)Nq < (1LL << 31) && S * (int64_t)NBs < (1LL << 31), GFST_ERR_SHAPE,
                "row count exceeds the TMA coordinate range");
   CUtensorMap mq, mk;
-  int st = make_map(&mq, Q, (uint64_t)S * Nq, d, BM);
+  int st = make_bf16_map(&mq, Q, (uint64_t)S * Nq, d, BM);
   if (st != GFST_OK) return st;
-  st = make_map(&mk, Ksum, (uint64_t)S * NBs, d, BN);
+  st = make_bf16_map(&mk, Ksum, (uint64_t)S * NBs, d, BN);
   if (st != GFST_OK) return st;
   const int nkb = (d + KBOX - 1) / KBOX;
   if (nkb == 1) return dispatch_kcap<1, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
   if (nkb == 2) return dispatch_kcap<2, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
   return dispatch_kcap<4, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+int make_bf16_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  GFST_REQUIRE(enc != nullptr, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  GFST_REQUIRE(r == CUDA_SUCCESS, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GFST_OK;
 }
 
 int read_device_error(int clear, unsigned int* value) {

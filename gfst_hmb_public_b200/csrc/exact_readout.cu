@@ -17,7 +17,9 @@
 // registers, one butterfly per 16 row groups).  Other widths use a lane-per-row
 // kernel (one CTA per query).  bf16 products are exact in fp32; sums are fp32.
 // NaN scores never win.
-#include "gfst_common.cuh"
+#include <type_traits>
+
+#include "async_copy.cuh"
 
 namespace gfst {
 
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(kThreads) exact_readout_kernel(
   __syncthreads();
   bs = red_s[0];
   bi = red_i[0];
-  const bool found = bi != 0x7fffffff;
+  const bool found = bi != 0x7fffffff && bs == bs;  // NaN scores never win
   if (tid == 0) {
     best_tok[sq] = found ? bi : -1;
     best_score[sq] = found ? bs : -INFINITY;
@@ -179,29 +181,29 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, const float* q, __nv_
   return acc.x + acc.y;
 }
 
-// LPR lanes per key row (16-byte chunks per row), RPL = 32 / LPR rows per warp
-// load: consecutive lanes read consecutive 16-byte chunks of whole rows.
 // ---------------------------------------------------------------------------
 // pipelined readout: one CTA per (stream, chunk of kQC queries).
 //  1. the chunk's (block, query) selections are sorted by block (bitonic, smem)
 //     and grouped into runs, one run per distinct block;
 //  2. a producer thread streams each distinct block, once, into a ring of
-//     shared-memory stages with 1-D TMA bulk copies (cp.async.bulk, completion
-//     on an mbarrier with the byte count);
-//  3. consumer warps take the sorted pairs round robin, wait for their block's
-//     stage, score the block's rows against the pair's query from shared
-//     memory and fold the best token into the query's 64-bit key with a shared
-//     atomicMax (order independent); the last pair of a run frees its stage.
-// Each selected block crosses HBM once per query chunk, fully overlapped with
-// the scoring.  All waits are bounded; a wait that gives up raises the sticky
-// device error word and the CTA drains its copies and returns.
+//     shared-memory stages (TMA, completion on an mbarrier with the byte count);
+//  3. consumer warps wait for their block's stage, score its token rows against
+//     the queries that selected it, fold each query's best token into a 64-bit
+//     key with a shared atomicMax (order independent) and free the stage.
+// Each selected block crosses HBM once per query chunk, overlapped with the
+// scoring.  All waits are bounded; a wait that gives up raises the sticky
+// readout error word and the CTA drains its copies and returns.
+//
+// Ring protocol: the producer tags a stage with the run it is loading only
+// after the stage's previous run is fully consumed; a consumer of run r waits
+// for the tag r, then for the stage's full barrier in r's phase.  A consumer
+// that runs ahead of the ring therefore never takes an older phase of the same
+// parity for its own.
 // ---------------------------------------------------------------------------
-constexpr int kCWarps = 8;                    // consumer warps
-constexpr int kPThreads = (kCWarps + 1) * 32;  // + one producer warp
-constexpr int kQC = 64;                        // queries per CTA
-constexpr int kMaxPairs = 2048;                // kQC * k, k <= 32
+constexpr int kQC = 64;          // queries per CTA
+constexpr int kMaxPairs = 2048;  // kQC * k, k <= 32
 constexpr int kMaxStages = 8;
-constexpr long long kWaitCycles = 2000000000LL;
+constexpr uint32_t kNoKey = 0xffffffffu;
 
 // larger key = better: higher score, then lower token index; NaN never wins
 __device__ __forceinline__ unsigned long long pack_best(float s, int tok) {
@@ -216,44 +218,165 @@ __device__ __forceinline__ float unpack_score(unsigned long long key) {
   return __uint_as_float(u);
 }
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
+struct RunTable {
+  uint32_t keys[kMaxPairs];           // sorted (block << 11 | local query); kNoKey = no entry
+  uint16_t run_start[kMaxPairs + 1];  // first key of each run; run_start[n_runs] = n_valid
+  int warp_heads[32];
+  int n_runs, n_valid;
+};
+
+// Fill, sort and split the chunk's selections into runs.  Every thread of the
+// CTA (NT) calls; the first NSCAN threads scan kMaxPairs / NSCAN keys each.
+// run_of (optional) receives each key's run index.
+template <int NT, int NSCAN>
+__device__ __forceinline__ void build_runs(RunTable& rt, uint16_t* run_of, const int32_t* __restrict__ sel,
+                                           int n_pairs, int k, int n_slots) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int n_pow2 = 1;
+  while (n_pow2 < n_pairs) n_pow2 <<= 1;
+  for (int e = tid; e < n_pow2; e += NT) {
+    uint32_t key = kNoKey;
+    if (e < n_pairs) {
+      const int b = __ldg(sel + e);
+      if (b >= 0 && b < n_slots) key = ((uint32_t)b << 11) | (uint32_t)(e / k);
+    }
+    rt.keys[e] = key;
   }
-  return true;
+  if (tid == 0) rt.n_valid = 0;
+  __syncthreads();
+  for (int size = 2; size <= n_pow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int e = tid; e < n_pow2; e += NT) {
+        const int partner = e ^ stride;
+        if (partner > e) {
+          const bool up = (e & size) == 0;
+          const uint32_t a = rt.keys[e], b = rt.keys[partner];
+          if ((a > b) == up) {
+            rt.keys[e] = b;
+            rt.keys[partner] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // run heads, prefix-summed over the scanning threads
+  constexpr int PER = kMaxPairs / NSCAN;
+  static_assert(NSCAN % 32 == 0 && NSCAN <= NT && kMaxPairs % NSCAN == 0 && PER <= 32, "scan split");
+  int cnt = 0, incl = 0;
+  uint32_t heads = 0;
+  const int e0 = tid * PER;
+  if (tid < NSCAN) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = e0 + i;
+      if (e < n_pairs) {
+        const uint32_t key = rt.keys[e];
+        if (key != kNoKey) {
+          if (e == 0 || (rt.keys[e - 1] >> 11) != (key >> 11)) {
+            heads |= 1u << i;
+            ++cnt;
+          }
+          if (e + 1 == n_pairs || rt.keys[e + 1] == kNoKey) rt.n_valid = e + 1;
+        }
+      }
+    }
+    incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) rt.warp_heads[warp] = incl;
+  }
+  __syncthreads();
+  if (tid < NSCAN) {
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += rt.warp_heads[w];
+    int r = base + incl - cnt - 1;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = e0 + i;
+      if (e < n_pairs && rt.keys[e] != kNoKey) {
+        if ((heads >> i) & 1u) {
+          ++r;
+          rt.run_start[r] = (uint16_t)e;
+        }
+        if (run_of != nullptr) run_of[e] = (uint16_t)r;
+      }
+    }
+    if (tid == NSCAN - 1) rt.n_runs = base + incl;
+  }
+  __syncthreads();
+  if (tid == 0) rt.run_start[rt.n_runs] = (uint16_t)rt.n_valid;
+  __syncthreads();
 }
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_addr(dst)),
-               "l"(src), "r"(bytes), "r"(smem_addr(bar))
-               : "memory");
+
+// Consumer side of the ring: wait until stage st holds run r.  Lane 0 waits;
+// the verdict is broadcast.  false: give up (timeout or another warp aborted).
+__device__ __forceinline__ bool wait_stage(volatile int* stage_run, uint64_t* full, volatile int* abort_flag,
+                                           int st, int r, int n_stages) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    if (stage_run[st] != r) {
+      const long long t0 = clock64();
+      while (stage_run[st] != r) {
+        if (*abort_flag || clock64() - t0 > kMbarWaitCycles) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    if (ok && !mbar_wait(&full[st], (r / n_stages) & 1)) ok = 0;
+    if (!ok) *abort_flag = 1;
+    if (*abort_flag) ok = 0;
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
+
+// After a give-up: wait (bounded) for the copies still in flight, then report.
+__device__ __forceinline__ void drain_after_abort(uint64_t* full, int issued, int n_stages) {
+  for (int r = max(0, issued - n_stages); r < issued; ++r) mbar_wait(&full[r % n_stages], (r / n_stages) & 1);
+  atomicExch(&g_readout_error, (unsigned)GFST_ERR_TIMEOUT);
+}
+
+// Outputs of the chunk: one warp per query.
+template <typename T>
+__device__ __forceinline__ void write_outputs(const unsigned long long* best, int nq, int nwarps, int64_t sq0, int L,
+                                              int n_slots, int dv, int64_t s, const T* __restrict__ pool_V,
+                                              int32_t* __restrict__ best_tok, float* __restrict__ best_score,
+                                              T* __restrict__ out_V) {
+  constexpr int N = Elems16<T>::N;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int ql = warp; ql < nq; ql += nwarps) {
+    const unsigned long long key = best[ql];
+    const bool found = key != 0ull;
+    const int tok = found ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : -1;
+    const int64_t sq = sq0 + ql;
+    if (lane == 0) {
+      best_tok[sq] = tok;
+      best_score[sq] = found ? unpack_score(key) : -INFINITY;
+    }
+    if (out_V != nullptr) {
+      const int vv = dv / N;
+      uint4* dst = reinterpret_cast<uint4*>(out_V + sq * dv);
+      if (found) {
+        const int bb = tok / L, p = tok % L;
+        const uint4* src = reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + bb) * L + p) * dv);
+        for (int cc = lane; cc < vv; cc += 32) dst[cc] = __ldg(src + cc);
+      } else {
+        for (int cc = lane; cc < vv; cc += 32) dst[cc] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+}
+
+// ---- SIMT consumers (fp32 pools, and bf16 shapes the tensor-core kernel does
+// not take).  1-D bulk copies of whole blocks; consumer warps take the sorted
+// pairs round robin (LPR lanes per key row, RPL = 32 / LPR rows per warp load)
+// and the last pair of a run frees its stage.
+constexpr int kCWarps = 8;
+constexpr int kPThreads = (kCWarps + 1) * 32;
 
 template <typename T, int LPR>
 __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
@@ -264,39 +387,24 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
   constexpr int RPL = 32 / LPR;
   constexpr int G = 16;
   extern __shared__ __align__(128) uint8_t dyn[];
-  __shared__ uint32_t keys[kMaxPairs];
+  __shared__ RunTable rt;
   __shared__ uint16_t run_of[kMaxPairs];
-  __shared__ uint16_t run_start[kMaxPairs + 1];
   __shared__ unsigned long long best[kQC];
   __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
   __shared__ int pending[kMaxStages];
-  __shared__ int stage_run[kMaxStages];  // run whose block the stage holds (or is receiving)
-  __shared__ int warp_heads[kCWarps];
-  __shared__ int n_runs_s, n_valid_s, abort_s, issued_s;
+  __shared__ int stage_run[kMaxStages];
+  __shared__ int abort_s, issued_s;
   volatile int* abort_v = &abort_s;
   volatile int* stage_run_v = stage_run;
 
   const uint32_t block_bytes = (uint32_t)L * d * sizeof(T);
-  T* stage = reinterpret_cast<T*>(dyn);                                   // [n_stages][L][d]
-  T* qs = reinterpret_cast<T*>(dyn + (size_t)n_stages * block_bytes);     // [kQC][d]
+  T* stage = reinterpret_cast<T*>(dyn);                                // [n_stages][L][d]
+  T* qs = reinterpret_cast<T*>(dyn + (size_t)n_stages * block_bytes);  // [kQC][d]
   const int64_t s = blockIdx.x / n_chunks;
   const int q0 = (int)(blockIdx.x % n_chunks) * kQC;
   const int nq = min(kQC, n_queries - q0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  // ---- selections -> sorted (block << 11 | local query) keys ----
-  const int n_pairs = nq * k;
-  int n_pow2 = 1;
-  while (n_pow2 < n_pairs) n_pow2 <<= 1;
-  const int32_t* sel = top_idx + ((size_t)s * n_queries + q0) * k;
-  for (int e = tid; e < n_pow2; e += kPThreads) {
-    uint32_t key = 0xffffffffu;
-    if (e < n_pairs) {
-      const int b = __ldg(sel + e);
-      if (b >= 0 && b < n_slots) key = ((uint32_t)b << 11) | (uint32_t)(e / k);
-    }
-    keys[e] = key;
-  }
   for (int q = tid; q < kQC; q += kPThreads) best[q] = 0ull;
   {
     const uint4* src = reinterpret_cast<const uint4*>(Q + ((size_t)s * n_queries + q0) * d);
@@ -311,84 +419,13 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
     }
     abort_s = 0;
     issued_s = 0;
-    n_valid_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_init_fence();
   }
-  __syncthreads();
-  for (int size = 2; size <= n_pow2; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int e = tid; e < n_pow2; e += kPThreads) {
-        const int partner = e ^ stride;
-        if (partner > e) {
-          const bool up = (e & size) == 0;
-          const uint32_t a = keys[e], b = keys[partner];
-          if ((a > b) == up) {
-            keys[e] = b;
-            keys[partner] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  // runs: one per distinct block.  Consumer thread t scans keys [8t, 8t+8):
-  // it flags run heads, the heads are prefix-summed over the CTA and each key
-  // gets its run index.
-  {
-    constexpr int PER = kMaxPairs / (kCWarps * 32);
-    int cnt = 0, incl = 0;
-    uint32_t heads = 0;
-    const int e0 = tid * PER;
-    if (warp < kCWarps) {
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int e = e0 + i;
-        if (e < n_pairs) {
-          const uint32_t key = keys[e];
-          if (key != 0xffffffffu) {
-            if (e == 0 || (keys[e - 1] >> 11) != (key >> 11)) {
-              heads |= 1u << i;
-              ++cnt;
-            }
-            if (e + 1 == n_pairs || keys[e + 1] == 0xffffffffu) n_valid_s = e + 1;
-          }
-        }
-      }
-      incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      if (lane == 31) warp_heads[warp] = incl;
-    }
-    __syncthreads();
-    if (warp < kCWarps) {
-      int base = 0;
-      for (int w = 0; w < warp; ++w) base += warp_heads[w];
-      int r = base + incl - cnt - 1;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int e = e0 + i;
-        if (e < n_pairs && keys[e] != 0xffffffffu) {
-          if ((heads >> i) & 1u) {
-            ++r;
-            run_start[r] = (uint16_t)e;
-          }
-          run_of[e] = (uint16_t)r;
-        }
-      }
-      if (tid == kCWarps * 32 - 1) n_runs_s = base + incl;
-    }
-    __syncthreads();
-    if (tid == 0) run_start[n_runs_s] = (uint16_t)n_valid_s;
-    __syncthreads();
-  }
-  const int n_runs = n_runs_s;
-  const int n_valid = n_valid_s;
+  build_runs<kPThreads, kCWarps * 32>(rt, run_of, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
+  const int n_runs = rt.n_runs;
+  const int n_valid = rt.n_valid;
 
   if (warp == kCWarps) {
-    // ---- producer: one bulk copy per distinct block ----
     if (lane == 0) {
       int r = 0;
       for (; r < n_runs; ++r) {
@@ -398,8 +435,8 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
           break;
         }
         if (*abort_v) break;
-        const int b = (int)(keys[run_start[r]] >> 11);
-        pending[st] = run_start[r + 1] - run_start[r];
+        const int b = (int)(rt.keys[rt.run_start[r]] >> 11);
+        pending[st] = rt.run_start[r + 1] - rt.run_start[r];
         stage_run_v[st] = r;
         mbar_arrive_expect_tx(&full[st], block_bytes);
         bulk_load(reinterpret_cast<uint8_t*>(stage) + (size_t)st * block_bytes,
@@ -408,35 +445,14 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
       issued_s = r;
     }
   } else {
-    // ---- consumers ----
-    // A pair of run r waits until its stage is tagged with r (the producer
-    // tags a stage only after the stage's previous run is fully consumed), then
-    // on the stage's full barrier for that phase: a warp that runs ahead of
-    // the ring can never mistake an older phase of the same parity for its own.
     const int c = lane % LPR, h = lane / LPR;
     for (int pi = warp; pi < n_valid; pi += kCWarps) {
       const int r = run_of[pi];
       const int st = r % n_stages;
-      int ok = 1;
-      if (lane == 0) {
-        if (stage_run_v[st] != r) {
-          const long long t0 = clock64();
-          while (stage_run_v[st] != r) {
-            if (*abort_v || clock64() - t0 > kWaitCycles) {
-              ok = 0;
-              break;
-            }
-          }
-        }
-        if (ok && !mbar_wait(&full[st], (r / n_stages) & 1)) ok = 0;
-        if (!ok) *abort_v = 1;
-        if (*abort_v) ok = 0;
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const uint32_t key = keys[pi];
+      if (!wait_stage(stage_run_v, full, abort_v, st, r, n_stages)) break;
+      const uint32_t key = rt.keys[pi];
       const int b = (int)(key >> 11), ql = (int)(key & 2047u);
-      const bool dup = pi > 0 && keys[pi - 1] == key;  // a block listed twice for one query
+      const bool dup = pi > 0 && rt.keys[pi - 1] == key;  // a block listed twice for one query
       if (!dup) {
         float qc[N];
         {
@@ -445,7 +461,8 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
 #pragma unroll
           for (int i = 0; i < N; ++i) qc[i] = to_f32(qe[i]);
         }
-        const uint4* blk = reinterpret_cast<const uint4*>(reinterpret_cast<uint8_t*>(stage) + (size_t)st * block_bytes);
+        const uint4* blk =
+            reinterpret_cast<const uint4*>(reinterpret_cast<uint8_t*>(stage) + (size_t)st * block_bytes);
         float bs = __int_as_float(0x7fc00000);
         int bi = 0x7fffffff;
         for (int r0 = 0; r0 < L; r0 += G * RPL) {
@@ -475,44 +492,236 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
           }
         }
         warp_best(bs, bi);
-        if (lane == 0 && bi != 0x7fffffff) atomicMax(&best[ql], pack_best(bs, bi));
+        if (lane == 0 && bi != 0x7fffffff && bs == bs) atomicMax(&best[ql], pack_best(bs, bi));
       }
       __syncwarp();
       if (lane == 0 && atomicSub(&pending[st], 1) == 1) mbar_arrive(&empty[st]);
     }
   }
   __syncthreads();
-  if (tid == kCWarps * 32) {
-    // after a timeout: wait (bounded) for the copies still in flight
-    if (*abort_v) {
-      const int issued = issued_s;
-      for (int r = max(0, issued - n_stages); r < issued; ++r) mbar_wait(&full[r % n_stages], (r / n_stages) & 1);
-      atomicExch(&g_readout_error, (unsigned)GFST_ERR_TIMEOUT);
-    }
-  }
+  if (tid == kCWarps * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
+  write_outputs<T>(best, nq, kCWarps + 1, (int64_t)s * n_queries + q0, L, n_slots, dv, s, pool_V, best_tok,
+                   best_score, out_V);
+}
 
-  // ---- outputs: one warp per query ----
-  for (int ql = warp; ql < nq; ql += kCWarps + 1) {
-    const unsigned long long key = best[ql];
-    const bool found = key != 0ull;
-    const int tok = found ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : -1;
-    const int64_t sq = (int64_t)s * n_queries + q0 + ql;
-    if (lane == 0) {
-      best_tok[sq] = tok;
-      best_score[sq] = found ? unpack_score(key) : -INFINITY;
-    }
-    if (out_V != nullptr) {
-      const int vv = dv / N;
-      uint4* dst = reinterpret_cast<uint4*>(out_V + sq * dv);
-      if (found) {
-        const int bb = tok / L, p = tok % L;
-        const uint4* src = reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + bb) * L + p) * dv);
-        for (int cc = lane; cc < vv; cc += 32) dst[cc] = __ldg(src + cc);
-      } else {
-        for (int cc = lane; cc < vv; cc += 32) dst[cc] = make_uint4(0, 0, 0, 0);
+// ---- tensor-core consumers (bf16 pools, d = 64 * NKB, L % 16 == 0) ----
+// The producer loads a block as NKB TMA boxes of [L rows x 64 columns] with the
+// 128-byte swizzle, so a warp's ldmatrix of 8 rows x 16 bytes hits 8 distinct
+// bank groups.  A consumer warp takes whole runs (warp w: runs w, w + 4, ...)
+// and, for each group of up to 8 queries that selected the block, computes the
+// [L x 8] score tile with mma.sync m16n8k16 (bf16 products are exact in fp32;
+// fp32 accumulation), keeping per lane the best token of its two query columns.
+// Queries sit in shared memory with their 16-byte chunks XOR-swizzled by row
+// (chunk c of query q at (c & ~7) | ((c ^ q) & 7)); unused query columns read a
+// zero row and are ignored.  The scores are N <= 8 columns wide per block: the
+// warp-level MMA keeps them in registers with no accumulator round trip, and the
+// kernel stays bound by HBM, not by the tensor pipe.
+#ifndef GFST_READOUT_RING_KB
+#define GFST_READOUT_RING_KB 64u
+#endif
+constexpr int kMWarps = 4;
+constexpr int kMThreads = (kMWarps + 1) * 32;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Best (score, token) of one query column as seen by one lane.  Tokens are
+// offered in increasing order, so an equal score never replaces the held one;
+// NaN never replaces a number, and a lane that saw only NaN holds nothing.
+struct TokenBest {
+  float s = -INFINITY;
+  int i = 0x7fffffff;
+  __device__ __forceinline__ void offer(float v, int tok) {
+    const bool take = v > s || (i == 0x7fffffff && v == v);
+    s = take ? v : s;
+    i = take ? tok : i;
+  }
+  // combine the 8 lanes that hold the same query columns (lane % 4 equal)
+  __device__ __forceinline__ void reduce_rows() {
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+      if (i2 != 0x7fffffff && (i == 0x7fffffff || better(s2, i2, s, i))) {
+        s = s2;
+        i = i2;
       }
     }
   }
+  __device__ __forceinline__ bool found() const { return i != 0x7fffffff; }
+};
+
+template <int NKB>
+__global__ void __launch_bounds__(kMThreads) exact_readout_mma_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __nv_bfloat16* __restrict__ Q,
+    const __nv_bfloat16* __restrict__ pool_V, const int32_t* __restrict__ top_idx, int n_queries, int n_chunks,
+    int n_slots, int L, int dv, int k, int n_stages, int32_t* __restrict__ best_tok, float* __restrict__ best_score,
+    __nv_bfloat16* __restrict__ out_V) {
+  constexpr int D = NKB * 64;
+  constexpr int QROW = D * 2;   // bytes per key / query row
+  constexpr int KSTEPS = D / 16;
+  extern __shared__ uint8_t dyn_raw[];
+  __shared__ RunTable rt;
+  __shared__ unsigned long long best[kQC];
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ int stage_run[kMaxStages];
+  __shared__ int abort_s, issued_s;
+  volatile int* abort_v = &abort_s;
+  volatile int* stage_run_v = stage_run;
+
+  const uint32_t stage_bytes = (uint32_t)L * QROW;  // NKB boxes of L x 128 bytes
+  const uint32_t raw = smem_u32(dyn_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;     // the 128-byte swizzle repeats every 1024 bytes
+  uint8_t* dyn = dyn_raw + (base - raw);
+  uint8_t* qs = dyn + (size_t)n_stages * stage_bytes;  // [kQC][D], chunk-swizzled
+  uint8_t* zrow = qs + kQC * QROW;                     // one zero row
+  const uint32_t qs_u = base + n_stages * stage_bytes;
+  const uint32_t zrow_u = qs_u + kQC * QROW;
+  const int64_t s = blockIdx.x / n_chunks;
+  const int q0 = (int)(blockIdx.x % n_chunks) * kQC;
+  const int nq = min(kQC, n_queries - q0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  for (int q = tid; q < kQC; q += kMThreads) best[q] = 0ull;
+  {
+    constexpr int CPR = QROW / 16;  // 16-byte chunks per row
+    const uint4* src = reinterpret_cast<const uint4*>(Q + ((size_t)s * n_queries + q0) * D);
+    for (int e = tid; e < nq * CPR; e += kMThreads) {
+      const int q = e / CPR, c = e % CPR;
+      const int pos = (c & ~7) | ((c ^ q) & 7);
+      *reinterpret_cast<uint4*>(qs + q * QROW + pos * 16) = __ldg(src + e);
+    }
+    for (int e = tid; e < CPR; e += kMThreads) reinterpret_cast<uint4*>(zrow)[e] = make_uint4(0, 0, 0, 0);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < n_stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      stage_run[i] = -1;
+    }
+    abort_s = 0;
+    issued_s = 0;
+    mbar_init_fence();
+  }
+  build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
+  const int n_runs = rt.n_runs;
+
+  if (warp == kMWarps) {
+    if (lane == 0) {
+      int r = 0;
+      for (; r < n_runs; ++r) {
+        const int st = r % n_stages;
+        if (!mbar_wait(&empty[st], ((r / n_stages) & 1) ^ 1)) {
+          *abort_v = 1;
+          break;
+        }
+        if (*abort_v) break;
+        const int b = (int)(rt.keys[rt.run_start[r]] >> 11);
+        const int row0 = (int)(((int64_t)s * n_slots + b) * L);
+        stage_run_v[st] = r;
+        mbar_arrive_expect_tx(&full[st], stage_bytes);
+#pragma unroll
+        for (int kb = 0; kb < NKB; ++kb)
+          tma_load_2d(dyn + (size_t)st * stage_bytes + (size_t)kb * L * 128, &tmK, &full[st], kb * 64, row0);
+      }
+      issued_s = r;
+    }
+  } else {
+    // ldmatrix address roles: A (token rows) lane -> row (lane & 7) + 8 * ((lane >> 3) & 1),
+    // 16-byte chunk 2 kk + (lane >> 4); B (queries) lane -> query column lane & 7,
+    // chunk 2 kk + (lane >> 3) (two k-steps per x4 load)
+    const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int a_hi = lane >> 4;
+    const int bcol = lane & 7;
+    const int nt = L / 16;
+    // per k-step offset of this lane's A chunk inside a 16-row tile: box (kk / 4),
+    // 16-byte chunk (2 kk + a_hi) % 8 XOR (row % 8), row % 8 == lane % 8
+    uint32_t aoff[KSTEPS];
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+      aoff[kk] = (uint32_t)((kk >> 2) * L * 128) + (uint32_t)((((2 * kk + a_hi) & 7) ^ (lane & 7)) << 4);
+    for (int r = warp; r < n_runs; r += kMWarps) {
+      const int st = r % n_stages;
+      if (!wait_stage(stage_run_v, full, abort_v, st, r, n_stages)) break;
+      const int p0 = rt.run_start[r], p1 = rt.run_start[r + 1];
+      const int b = (int)(rt.keys[p0] >> 11);
+      const uint32_t abase = base + st * stage_bytes + a_row * 128;
+      for (int g0 = p0; g0 < p1; g0 += 8) {
+        const int pn = g0 + bcol;
+        const int qn = pn < p1 ? (int)(rt.keys[pn] & 2047u) : -1;
+        uint32_t bq[KSTEPS][2];
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; kk += 2) {
+          const int c = 2 * kk + (lane >> 3);
+          const uint32_t addr =
+              qn >= 0 ? qs_u + qn * QROW + (uint32_t)(((c & ~7) | ((c ^ qn) & 7)) << 4) : zrow_u + (uint32_t)(c << 4);
+          ldsm_x4(addr, bq[kk][0], bq[kk][1], bq[kk + 1][0], bq[kk + 1][1]);
+        }
+        TokenBest best0, best1;
+        int t = 0;
+        // four 16-row tiles at a time: independent accumulators hide the MMA latency
+        for (; t + 4 <= nt; t += 4) {
+          float acc[4][4] = {};
+#pragma unroll
+          for (int kk = 0; kk < KSTEPS; ++kk) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint32_t a0, a1, a2, a3;
+              ldsm_x4(abase + (uint32_t)((t + u) * 16 * 128) + aoff[kk], a0, a1, a2, a3);
+              mma_16816(acc[u], a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            // acc[u][0], [1]: token row 16 (t + u) + lane / 4, query columns 2 (lane % 4), +1;
+            // acc[u][2], [3]: the same columns, token row + 8
+            const int tok = b * L + (t + u) * 16 + (lane >> 2);
+            best0.offer(acc[u][0], tok);
+            best1.offer(acc[u][1], tok);
+            best0.offer(acc[u][2], tok + 8);
+            best1.offer(acc[u][3], tok + 8);
+          }
+        }
+        for (; t < nt; ++t) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int kk = 0; kk < KSTEPS; ++kk) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(abase + (uint32_t)(t * 16 * 128) + aoff[kk], a0, a1, a2, a3);
+            mma_16816(acc, a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
+          }
+          const int tok = b * L + t * 16 + (lane >> 2);
+          best0.offer(acc[0], tok);
+          best1.offer(acc[1], tok);
+          best0.offer(acc[2], tok + 8);
+          best1.offer(acc[3], tok + 8);
+        }
+        best0.reduce_rows();
+        best1.reduce_rows();
+        if (lane < 4) {
+          const int n0 = g0 + 2 * lane, n1 = n0 + 1;
+          if (n0 < p1 && best0.found()) atomicMax(&best[rt.keys[n0] & 2047u], pack_best(best0.s, best0.i));
+          if (n1 < p1 && best1.found()) atomicMax(&best[rt.keys[n1] & 2047u], pack_best(best1.s, best1.i));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+  }
+  __syncthreads();
+  if (tid == kMWarps * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
+  write_outputs<__nv_bfloat16>(best, nq, kMWarps + 1, (int64_t)s * n_queries + q0, L, n_slots, dv, s, pool_V,
+                               best_tok, best_score, out_V);
 }
 
 template <typename T>
@@ -529,8 +738,43 @@ int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t*
   const T* pv = static_cast<const T*>(pool_V);
   T* ov = static_cast<T*>(out_V);
   const int64_t n_chunks = (Nq + kQC - 1) / kQC;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    // tensor-core consumers: a ring of GFST_READOUT_RING_KB (4 stages of 16 KB for
+    // 64 x 128 blocks: two CTAs per SM, with room left for a frame-update CTA)
+    const size_t stage_bytes = (size_t)L * d * 2;
+    const bool mma_ok = (d == 64 || d == 128 || d == 256) && L % 16 == 0 && L <= 256 &&
+                        (int64_t)NS < (1LL << 21) && S * (int64_t)NS * L < (1LL << 31) &&
+                        S * n_chunks <= 0x7fffffffLL && aligned16(Q) && k <= 32;
+    int n_stages = (int)((GFST_READOUT_RING_KB * 1024u) / stage_bytes);
+    n_stages = n_stages < 2 ? 2 : (n_stages > kMaxStages ? kMaxStages : n_stages);
+    const size_t dyn = 1024 + (size_t)n_stages * stage_bytes + (size_t)(kQC + 1) * d * 2;
+    if (mma_ok && dyn <= 200u * 1024u) {
+      CUtensorMap tm;
+      const int st = make_bf16_map(&tm, pool_K, (uint64_t)S * NS * L, d, L);
+      if (st != GFST_OK) return st;
+      const unsigned mgrid = (unsigned)(S * n_chunks);
+      cudaError_t e = cudaSuccess;
+      switch (d / 64) {
+#define GFST_READOUT_MMA(NKBV)                                                                                   \
+  case NKBV: {                                                                                                   \
+    auto kern = exact_readout_mma_kernel<NKBV>;                                                                  \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);                       \
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));         \
+    kern<<<mgrid, kMThreads, dyn, stream>>>(tm, q, pv, top_idx, Nq, (int)n_chunks, NS, L, dv, k, n_stages,       \
+                                            best_tok, best_score, ov);                                           \
+    return check_launch("exact_readout_mma_kernel");                                                             \
+  }
+        GFST_READOUT_MMA(1)
+        GFST_READOUT_MMA(2)
+        GFST_READOUT_MMA(4)
+#undef GFST_READOUT_MMA
+        default:
+          break;
+      }
+    }
+  }
   const size_t block_bytes = (size_t)L * d * sizeof(T);
-  // stages: about 80 KB of ring per CTA (two CTAs per SM), 2 to 8 blocks
+  // stages: about 80 KB of ring per CTA, 2 to 8 blocks
   int n_stages = (int)((80u * 1024u) / block_bytes);
   n_stages = n_stages < 2 ? 2 : (n_stages > kMaxStages ? kMaxStages : n_stages);
   const size_t dyn = (size_t)n_stages * block_bytes + (size_t)kQC * d * sizeof(T);

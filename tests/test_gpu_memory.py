@@ -150,7 +150,8 @@ def test_retriever_rejects_cpu_and_wrong_device(cuda_device):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("S,Nq,NS,L,d,dv,k", [(3, 40, 16, 16, 64, 64, 2), (2, 33, 64, 64, 128, 128, 4),
-                                               (2, 9, 9, 128, 128, 64, 8), (1, 5, 4, 5, 16, 24, 3)])
+                                               (2, 9, 9, 128, 128, 64, 8), (1, 5, 4, 5, 16, 24, 3),
+                                               (2, 70, 12, 32, 256, 64, 5), (1, 12, 7, 24, 128, 32, 3)])
 def test_exact_readout_matches_oracle(cuda_device, dtype, S, Nq, NS, L, d, dv, k):
     g = torch.Generator().manual_seed(S * 100 + Nq)
     pool_K = torch.randn((S, NS, L, d), generator=g).to(dtype)
@@ -217,6 +218,45 @@ def test_exact_readout_stage_ring_wraps(cuda_device, pattern):
     np.testing.assert_allclose(score.cpu().numpy()[ok], ref_score[ok], rtol=1e-5, atol=1e-5)
     assert np.array_equal(_np(val)[ok], ref_V[ok])
     assert _native.load().gfst_check_device_errors(1) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_exact_readout_ties_pick_lowest_token(cuda_device, dtype):
+    # the same key at tokens 67 (block 4), 32 (block 2) and 25 (block 1)
+    S, NS, L, d = 1, 6, 16, 64
+    g = torch.Generator().manual_seed(9)
+    pool = (0.1 * torch.randn((S, NS, L, d), generator=g)).to(dtype)
+    v = torch.randn(d, generator=g).to(dtype)
+    for b, p in ((4, 3), (2, 0), (1, 9)):
+        pool[0, b, p] = v
+    Q = v.reshape(1, 1, d).clone()
+    sel = torch.tensor([[[4, 2, 1, 5]]], dtype=torch.int32)
+    tok, score, val = readout.exact_readout(Q.to(cuda_device), pool.to(cuda_device), pool.to(cuda_device),
+                                            sel.to(cuda_device))
+    assert tok.item() == 25
+    assert torch.equal(val.cpu()[0, 0], v)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("d", [64, 24])
+def test_exact_readout_nan_scores_never_win(cuda_device, dtype, d):
+    # block 1: every token scores NaN; block 2: one NaN token.  A query that
+    # selected only NaN tokens has no winner (-1, -inf, zero value row).
+    S, NS, L = 1, 4, 16
+    g = torch.Generator().manual_seed(13)
+    pool = torch.randn((S, NS, L, d), generator=g)
+    pool[0, 1, :, 0] = float("nan")
+    pool[0, 2, 5, 3] = float("nan")
+    pool = pool.to(dtype)
+    Q = torch.randn((S, 3, d), generator=g).to(dtype)
+    sel = torch.tensor([[[1, 1], [1, 2], [2, 3]]], dtype=torch.int32)
+    tok, score, val = readout.exact_readout(Q.to(cuda_device), pool.to(cuda_device), pool.to(cuda_device),
+                                            sel.to(cuda_device))
+    ref_tok, ref_score, ref_V, ok = go.exact_readout(_np(Q), _np(pool), _np(pool), sel.numpy())
+    assert ref_tok[0, 0] == -1 and tok[0, 0].item() == -1
+    assert torch.isinf(score[0, 0]).item() and (val[0, 0] == 0).all().item()
+    assert np.array_equal(tok.cpu().numpy()[ok], ref_tok[ok])
+    assert not np.isnan(score.cpu().numpy()).any()
 
 
 def test_exact_readout_no_valid_block(cuda_device):
