@@ -28,22 +28,6 @@ int pick_shape(int d, int r) {
   return -1;
 }
 
-// (index, DMAX, RMAX, RG, CG): RG row groups x CG column groups of lanes per frame
-#define GFST_SHAPE_CASES(X) \
-  X(0, 8, 8, 4, 2)          \
-  X(1, 32, 8, 8, 1)         \
-  X(2, 64, 8, 8, 1)         \
-  X(3, 128, 8, 16, 1)       \
-  X(4, 256, 8, 32, 1)       \
-  X(5, 16, 16, 8, 2)        \
-  X(6, 32, 16, 8, 2)        \
-  X(7, 64, 16, 8, 4)        \
-  X(8, 128, 16, 8, 4)       \
-  X(9, 256, 16, 16, 2)      \
-  X(10, 32, 32, 8, 4)       \
-  X(11, 64, 32, 8, 4)       \
-  X(12, 128, 32, 8, 4)
-
 int check_frame_args(int64_t n, int d, int r, int m, int sign_mode) {
   GFST_REQUIRE(n >= 0, GFST_ERR_ARG, "n_frames must be >= 0 (got %lld)", (long long)n);
   GFST_REQUIRE(r >= 1 && r <= d, GFST_ERR_SHAPE, "need 1 <= r <= d (d=%d r=%d)", d, r);

@@ -428,6 +428,45 @@ struct FrameQR {
     }
   }
 
+  // Rows of a d-vector owned by this lane, as row pairs (zero beyond d).
+  __device__ static __forceinline__ void load_rows(float2 (&xr)[RP], const float* x, int t, int d) {
+    const int rg = t % RG;
+#pragma unroll
+    for (int p = 0; p < RP; ++p) {
+      const int r0 = rg + (2 * p) * RG, r1 = rg + (2 * p + 1) * RG;
+      xr[p] = make_float2(r0 < d ? x[r0] : 0.f, r1 < d ? x[r1] : 0.f);
+    }
+  }
+
+  // w[c] = a[:, c] . x for this lane's columns (all rows: reduced over the RG
+  // lanes of the column group; every lane of the group gets the same bits).
+  __device__ static __forceinline__ void col_dots(const Frame& a, const float2 (&xr)[RP], float (&w)[CPT]) {
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < RP; ++p) acc = ffma2(a[p][c], xr[p], acc);
+      w[c] = subgroup_allreduce<RG>(acc.x + acc.y);
+    }
+  }
+
+  // proj[p] = a[rows of p, :] . w (all columns: reduced over the CG lanes that
+  // share this lane's rows).
+  __device__ static __forceinline__ void row_dots(const Frame& a, const float (&w)[CPT], float2 (&proj)[RP]) {
+#pragma unroll
+    for (int p = 0; p < RP; ++p) {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) acc = ffma2(a[p][c], make_float2(w[c], w[c]), acc);
+#pragma unroll
+      for (int o = CG / 2; o >= 1; o >>= 1) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o * RG);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o * RG);
+      }
+      proj[p] = acc;
+    }
+  }
+
   __device__ static __forceinline__ void scale(Frame& a, float beta) {
     const float2 b2 = make_float2(beta, beta);
 #pragma unroll

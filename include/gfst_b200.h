@@ -17,6 +17,9 @@
  *   gfst_frame_stream      <- the per-token loop GfstHmbSublayer._update_local_bases
  *                             src/gfst_hmb_mpuc/modeling.py:2299-2423 (largest level), with the
  *                             frame kept on chip across tokens
+ *   gfst_local_tracker_stream <- GfstHmbSublayer._update_local_bases (all flag levels, rule
+ *                             residual_rank_one_v1) + _local_alignment_features, per token
+ *                             src/gfst_hmb_mpuc/modeling.py:2284-2437, gfst.py:91-112
  *   gfst_block_commit_mean <- GfstDecodeState.append_exact_token block commit
  *                             src/gfst_hmb_mpuc/state.py:651-815 and the block summary of
  *                             GfstHmbSublayer._update_block_memory modeling.py:3482-3535
@@ -98,6 +101,28 @@ GFST_API int gfst_frame_stream(float* U, const float* A, const float* B, float b
                       int64_t n_frames, int T, int d, int r, int m,
                       float eps_sign, int sign_mode,
                       float* frames_out, int out_every, cudaStream_t stream);
+
+/* ---- local tracker: all flag levels + alignment features, T tokens --------
+ * Per stream s and token t (x = x[s,t], a d-vector), with the reference rule
+ * residual_rank_one_v1 (gfst.py:91-112) on a basis B and a vector v at rate a:
+ *     w = B^T v,  s = (v - B w) / sqrt(||v||^2 + eps_update^2),
+ *     B <- QR_signfixed((1 - a) B + a v w^T + a s e_last^T)
+ *   U <- rule(U, x, rates[n_levels]);  p = U^T x;
+ *   V_l <- rule(V_l, p, rates[l]) for l < n_levels (thin Q keeps dims[l] columns);
+ *   features[s,t] = (c_0, c_0, c_1, c_1 - c_0, ..., c_L, c_L - c_{L-1}) with
+ *     c_l = ||V_l^T p||^2 / max(||x||^2, eps) (l < L), c_L = ||p||^2 / max(||x||^2, eps).
+ * U: [n_streams, d, r] (in/out, r = the largest flag dim); nested:
+ * [n_streams, n_levels, r, r] (in/out; level l occupies columns [0, dims[l]),
+ * other columns are ignored on input and zero on output); x: [n_streams, T, d]
+ * (16-byte aligned, d % 4 == 0); dims: host array of n_levels strictly
+ * increasing sizes in [1, r); rates: host array of n_levels + 1 forgetting
+ * rates (nested levels, then U); features: [n_streams, T, 2 (n_levels + 1)] or
+ * NULL.  Limits: r <= 32, d as gfst_frame_update_qr, n_levels <= 4.  fp32.   */
+GFST_API int gfst_local_tracker_stream(float* U, float* nested, const float* x, int64_t n_streams,
+                              int T, int d, int r, int n_levels, const int32_t* dims,
+                              const double* rates, double eps, double eps_update,
+                              float eps_sign, int sign_mode, float* features,
+                              cudaStream_t stream);
 
 /* ---- block commit ----------------------------------------------------------
  * For every stream s in [0, n_streams):

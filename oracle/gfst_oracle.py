@@ -114,6 +114,72 @@ def stream_frames(U0: np.ndarray, A: np.ndarray, B: np.ndarray, beta: float = 1.
     return U, (np.stack(snaps) if snaps else None)
 
 
+def _residual_rank_one_candidate_2d(basis: torch.Tensor, value: torch.Tensor, alpha: float,
+                                    eps_update: float) -> torch.Tensor:
+    """gfst.py:91-112 (update_basis_candidate): the unbatched form, with the
+    matrix-vector products of one tracker."""
+    weights = basis.transpose(0, 1) @ value
+    residual = value - basis @ weights
+    norm = torch.linalg.vector_norm(value)
+    scaled = residual / torch.sqrt(norm.square() + float(eps_update) ** 2)
+    novelty = torch.zeros_like(weights)
+    novelty[-1] = 1.0
+    return (1.0 - alpha) * basis + alpha * torch.outer(value, weights) + alpha * torch.outer(scaled, novelty)
+
+
+def _canonical_qr_1(candidate: torch.Tensor, eps_sign: float, sign_mode: int) -> torch.Tensor:
+    """gfst.py:26-32 on a batch of one, as the tracker calls it."""
+    return torch.from_numpy(qr_reference(candidate.unsqueeze(0).numpy(), eps_sign, sign_mode)[0])
+
+
+def local_tracker_stream(U0: np.ndarray, nested0: list, xs: np.ndarray, flag_dims, forgetting_rates,
+                         eps: float = 1e-6, eps_update: float = 1e-6, eps_sign: float = 1e-8,
+                         sign_mode: int = SIGN_FIRST_SIGNIFICANT, out_every: int = 0):
+    """Per-token local tracker of modeling.py:2299-2423 (_update_local_bases)
+    followed by modeling.py:2425-2437 (_local_alignment_features), one tracker
+    per stream, in the reference's own unbatched torch calls.
+
+    U0 [S, d, r] (r = max flag dim); nested0: list of [S, r, dim_l] for the
+    flag levels but the last; xs [S, T, d].  Per token: the largest basis takes
+    the residual_rank_one_v1 candidate at rate forgetting_rates[-1] and its
+    canonical QR; p = U^T x; nested level l takes the same rule on p at
+    forgetting_rates[l]; features = (cumulative, increment) pairs of
+    ||V_l^T p||^2 / max(||x||^2, eps), then ||p||^2 / max(||x||^2, eps).
+    Returns (U, nested list, features [S, T, 2 (L + 1)], snapshots [T//out_every, S, d, r] or None).
+    """
+    xs = np.asarray(xs, np.float32)
+    S, T, _ = xs.shape
+    nl = len(nested0)
+    U_out = np.array(U0, np.float32, copy=True)
+    V_out = [np.array(v, np.float32, copy=True) for v in nested0]
+    feats = np.zeros((S, T, 2 * (nl + 1)), np.float32)
+    snaps = np.zeros((T // out_every if out_every else 0, S) + U_out.shape[1:], np.float32)
+    for s in range(S):
+        U = torch.from_numpy(U_out[s].copy())
+        V = [torch.from_numpy(v[s].copy()) for v in V_out]
+        for t in range(T):
+            x = torch.from_numpy(xs[s, t].copy())
+            U = _canonical_qr_1(_residual_rank_one_candidate_2d(U, x, float(forgetting_rates[-1]), eps_update),
+                                eps_sign, sign_mode)
+            p = U.transpose(0, 1) @ x
+            for lvl in range(nl):
+                cand = _residual_rank_one_candidate_2d(V[lvl], p, float(forgetting_rates[lvl]), eps_update)
+                V[lvl] = _canonical_qr_1(cand, eps_sign, sign_mode)[:, : int(flag_dims[lvl])]
+            p = U.transpose(0, 1) @ x
+            den = torch.clamp(x.square().sum(), min=float(eps))
+            cum = [(Vl.transpose(0, 1) @ p).square().sum() / den for Vl in V]
+            cum.append(p.square().sum() / den)
+            c = torch.stack(cum)
+            prev = torch.cat((torch.zeros_like(c[:1]), c[:-1]))
+            feats[s, t] = torch.stack((c, c - prev), dim=-1).reshape(-1).numpy()
+            if out_every and (t + 1) % out_every == 0:
+                snaps[(t + 1) // out_every - 1, s] = U.numpy()
+        U_out[s] = U.numpy()
+        for lvl in range(nl):
+            V_out[lvl][s] = V[lvl].numpy()
+    return U_out, V_out, feats, (snaps if out_every else None)
+
+
 # frame metrics ---------------------------------------------------------------
 def orthogonality_error(Q: np.ndarray) -> np.ndarray:
     """max |Q^T Q - I| per frame (float64 arithmetic)."""

@@ -169,6 +169,48 @@ def main() -> None:
              blocks=blocks.numpy(), positions=positions.numpy(), unique_ids=uid.numpy(),
              grouped_scores=gsc.numpy(), grouped_blocks=gbl.numpy(), grouped_positions=gpo.numpy(),
              selected_token=int(uid[order[0]]))
+    # 8. the per-token local tracker: GfstHmbSublayer._update_local_bases
+    #    (modeling.py:2299-2423: largest-level update + QR, projection, nested
+    #    flag levels in r-space) and _local_alignment_features (2425-2437),
+    #    called unbound on a minimal host object that carries the config and
+    #    switches every capture hook off
+    modeling = importlib.import_module("gfst_hmb_mpuc.modeling")
+    config = importlib.import_module("gfst_hmb_mpuc.config")
+    state_mod = importlib.import_module("gfst_hmb_mpuc.state")
+    sub = modeling.GfstHmbSublayer
+    for name, d, flag_dims, n_streams, T, seed in (("local_tracker_d64", 64, (8, 16, 32), 4, 48, 21),
+                                                   ("local_tracker_d128", 128, (4, 8, 16), 3, 32, 22)):
+        cfg = config.GfstHmbConfig(reduced_dim=d, flag_dims=flag_dims, key_dim=2 * d)
+        host = types.SimpleNamespace(gfst_config=cfg, layer_idx=0, _active_transition_probe_capture=None,
+                                     _current_transition_token_context=None)
+        host._should_capture_transition_probe = lambda **kw: False
+        host._should_capture_local_qr = lambda **kw: False
+        host._should_record_local_qr_pool = lambda: False
+        host._initialise_local_tracker = types.MethodType(sub._initialise_local_tracker, host)
+        g = torch.Generator().manual_seed(seed)
+        xs = torch.randn((n_streams, T, d), generator=g)
+        r = max(flag_dims)
+        nl = len(flag_dims) - 1
+        feats = np.zeros((n_streams, T, 2 * (nl + 1)), np.float32)
+        snaps = np.zeros((n_streams, T // 8, d, r), np.float32)
+        U_out = np.zeros((n_streams, d, r), np.float32)
+        V_out = np.zeros((n_streams, nl, r, r), np.float32)
+        bases_out = []
+        for s in range(n_streams):
+            st = state_mod._GfstTrackerState()
+            for t in range(T):
+                local = sub._update_local_bases(host, st, xs[s, t])
+                feats[s, t] = sub._local_alignment_features(host, st, xs[s, t]).numpy()
+                if (t + 1) % 8 == 0:
+                    snaps[s, (t + 1) // 8 - 1] = st.largest_basis.numpy()
+            U_out[s] = st.largest_basis.numpy()
+            for lvl, vb in enumerate(st.nested_bases):
+                V_out[s, lvl, :, : vb.shape[1]] = vb.numpy()
+            bases_out.append(np.concatenate([b.numpy() for b in local], axis=1))
+        np.savez(OUT / f"{name}.npz", values=xs.numpy(), flag_dims=np.array(flag_dims),
+                 forgetting_rates=np.array(cfg.forgetting_rates, np.float64), eps=np.float64(cfg.eps),
+                 eps_update=np.float64(cfg.eps_update), eps_sign=np.float64(cfg.eps_sign), features=feats,
+                 frames_every8=snaps, largest_basis=U_out, nested_bases=V_out, local_bases=np.stack(bases_out))
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -54,6 +54,19 @@ def test_host_validation_rejects_without_launching():
     assert lib.gfst_block_topk(None, None, 1, 1, 4, 4, 64, 33, 0, None, None, None) == 2
     assert lib.gfst_block_topk(None, None, 1, 1, 4, 4, 64, 2, 5, None, None, None) == 7
     assert lib.gfst_exact_readout(None, None, None, None, 1, 1, 4, 16, 64, 64, 0, 1, None, None, None, None) == 2
+    # local tracker: d % 4, nested dims not increasing, too many levels
+    import ctypes
+    dims = (ctypes.c_int32 * 2)(8, 16)
+    bad = (ctypes.c_int32 * 2)(16, 8)
+    rates = (ctypes.c_double * 3)(0.05, 0.1, 0.2)
+    assert lib.gfst_local_tracker_stream(None, None, None, 2, 4, 66, 32, 2, dims, rates, 1e-6, 1e-6, 1e-8, 0,
+                                         None, None) == 3
+    assert lib.gfst_local_tracker_stream(None, None, None, 2, 4, 64, 32, 2, bad, rates, 1e-6, 1e-6, 1e-8, 0,
+                                         None, None) == 2
+    assert lib.gfst_local_tracker_stream(None, None, None, 2, 4, 64, 32, 5, dims, rates, 1e-6, 1e-6, 1e-8, 0,
+                                         None, None) == 2
+    assert lib.gfst_local_tracker_stream(None, None, None, 0, 4, 64, 32, 2, dims, rates, 1e-6, 1e-6, 1e-8, 0,
+                                         None, None) == 0
 
 
 def test_python_ops_reject_cpu_tensors():
@@ -68,6 +81,11 @@ def test_python_ops_reject_cpu_tensors():
     with pytest.raises(RuntimeError):
         readout.exact_readout(torch.randn(1, 2, 8), torch.randn(1, 2, 4, 8), None,
                               torch.zeros(1, 2, 2, dtype=torch.int32))
+    from gfst_hmb_public_b200 import tracker
+
+    with pytest.raises(RuntimeError):
+        tracker.local_tracker_stream(torch.eye(8, 4)[None].contiguous(), torch.zeros(1, 1, 4, 4),
+                                     torch.randn(1, 3, 8), flag_dims=(2, 4), forgetting_rates=(0.1, 0.2))
     with pytest.raises(RuntimeError):
         retrieval.BlockRetriever().search(state=object(), layer_idx=0, batch_idx=0, keys_tensor=torch.eye(4),
                                           query_tensor=torch.ones(4), top_k=2)

@@ -100,3 +100,31 @@ def test_readout_collapse_identity_for_unique_positions():
     pool[0, 0, 1, 0] = 2.0  # tie: lower token index (0*3+1) wins
     tok, sc, _, _ = go.exact_readout(Q, pool, None, np.array([[[1, 0]]]))
     assert tok[0, 0] == 1 and sc[0, 0] == 2.0
+
+
+def _tracker_golden(name):
+    z = load(name)
+    xs = z["values"]
+    fd = [int(v) for v in z["flag_dims"]]
+    S, T, d = xs.shape
+    r = fd[-1]
+    U0 = np.broadcast_to(np.eye(d, r, dtype=np.float32), (S, d, r))
+    V0 = [np.broadcast_to(np.eye(r, k, dtype=np.float32), (S, r, k)) for k in fd[:-1]]
+    return z, fd, U0, V0
+
+
+def test_local_tracker_matches_reference_methods():
+    # golden: GfstHmbSublayer._update_local_bases + _local_alignment_features
+    # (modeling.py:2299-2437) called on the reference's own tracker state
+    for name in ("local_tracker_d64.npz", "local_tracker_d128.npz"):
+        z, fd, U0, V0 = _tracker_golden(name)
+        U, V, feats, snaps = go.local_tracker_stream(U0, V0, z["values"], fd, z["forgetting_rates"],
+                                                     float(z["eps"]), float(z["eps_update"]),
+                                                     float(z["eps_sign"]), out_every=8)
+        assert np.array_equal(U, z["largest_basis"])
+        assert np.array_equal(feats, z["features"])
+        assert np.array_equal(np.swapaxes(snaps, 0, 1), z["frames_every8"])
+        for lvl, dim in enumerate(fd[:-1]):
+            assert np.array_equal(V[lvl], z["nested_bases"][:, lvl, :, :dim])
+        bases = np.concatenate([U @ V[lvl] for lvl in range(len(fd) - 1)] + [U], axis=-1)
+        np.testing.assert_allclose(bases, z["local_bases"], atol=1e-6)
