@@ -12,6 +12,7 @@ the last launch.  CASE is one of:
   topk_long   tensor-core score + top-8 of 1024 queries over 8192 summaries per stream
   readout     exact-token readout of 64 queries x 16 blocks of 64 tokens per stream
   commit      one 64-token block commit per stream
+  tracker     64 tokens of the local tracker (d=64, flag dims 8/16/32, nested levels + features)
 """
 from __future__ import annotations
 
@@ -20,7 +21,7 @@ import math
 
 import torch
 
-from . import gfst, memory, readout, retrieval, workloads as wl
+from . import gfst, memory, readout, retrieval, tracker, workloads as wl
 
 
 def _timed(fn, repeat: int) -> float:
@@ -38,7 +39,7 @@ def _timed(fn, repeat: int) -> float:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit"])
+    parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     args = parser.parse_args()
@@ -72,6 +73,12 @@ def main() -> None:
         sel = torch.randint(0, 512, (S, 64, 16), generator=g, device=dev, dtype=torch.int32)
         ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel), args.repeat)
         units = f"{S * 64 * 16 * 64 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bytes"
+    elif args.case == "tracker":
+        S = args.streams or 2048
+        tr = tracker.LocalTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), device=dev)
+        x = torch.randn((S, 64, 64), generator=g, device=dev)
+        ms = _timed(lambda: tr.step(x), args.repeat)
+        units = f"{S * 64 / ms / 1e3:.2f} M tokens/s"
     else:  # commit
         S = args.streams or 2048
         mem = memory.BlockMemory(S, 4, 64, 128, dtype=bf, device=dev)

@@ -325,6 +325,7 @@ __device__ __forceinline__ bool wait_stage(volatile int* stage_run, uint64_t* fu
           ok = 0;
           break;
         }
+        __nanosleep(64);  // leave the issue slots to warps with work
       }
     }
     if (ok && !mbar_wait(&full[st], (r / n_stages) & 1)) ok = 0;
