@@ -152,7 +152,8 @@ int launch_stream(float* U, const float* A, const float* B, float beta, int64_t 
   const bool vec4 = (r % 4 == 0) && aligned16(U) && (frames_out == nullptr || aligned16(frames_out));
   const size_t smem = (size_t)per_block * 2 * (size_t)(d * m + r * m) * sizeof(float);
   auto kern = frame_stream_kernel<DMAX, RMAX, RG, CG, kWarps>;
-  if (smem > 48 * 1024) {
+  {
+    // static scratch + the staged factors can pass 48 KB together: always opt in
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }

@@ -45,12 +45,12 @@ __host__ __device__ constexpr int tracker_stash_floats() {
   return (DMAX / RG) * (RMAX / CG) >= 128 ? DMAX * RMAX : 0;
 }
 
-// shared floats per frame group beyond the static buffers: x stage, nested
-// bases, parked frame
-__host__ __device__ inline int tracker_group_floats(int d, int r, const TrackerParams& prm, int stash) {
+// dynamic shared floats per frame group: QR scratch (`fixed`, a multiple of 4),
+// x stage, nested bases, parked frame
+__host__ __device__ inline int tracker_group_floats(int d, int r, const TrackerParams& prm, int stash, int fixed) {
   const int nl = prm.n_levels;
   const int nested_floats = nl > 0 ? prm.voff[nl - 1] + r * prm.dims[nl - 1] : 0;
-  return 2 * d + ((nested_floats + 3) & ~3) + stash;
+  return fixed + 2 * d + ((nested_floats + 3) & ~3) + stash;
 }
 
 // Column-per-lane Householder thin QR of an m x n matrix, m <= RMAX <= 32,
@@ -159,11 +159,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   constexpr int NG = WARPS * GPW;
   constexpr int RP = QR::RP, CPT = QR::CPT;
   static_assert(TPF >= RMAX, "a frame group needs a lane per nested row and column");
-  __shared__ typename QR::Smem qsm[NG];
-  __shared__ typename SQ::Smem ssm[NG];
   __shared__ float pbuf[NG][RMAX], wbuf[NG][RMAX], sbuf[NG][RMAX];
   __shared__ float featb[NG][kMaxTrackerLevels];
-  extern __shared__ __align__(16) float dyn[];  // per group: x stage [2][d], nested [sum r*dim_l]
+  // per group: QR scratch, small-QR scratch, x stage [2][d], nested [sum r*dim_l], parked frame
+  extern __shared__ __align__(16) float dyn[];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -175,8 +174,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int64_t fs = valid ? f : 0;
   const int NL = prm.n_levels;
   constexpr int STASH = tracker_stash_floats<DMAX, RMAX, RG, CG>();
-  const int group_floats = tracker_group_floats(d, r, prm, STASH);
-  float* xstage = dyn + (size_t)g * group_floats;
+  constexpr int FIXED = (int)((sizeof(typename QR::Smem) + sizeof(typename SQ::Smem)) / sizeof(float));
+  static_assert(sizeof(typename QR::Smem) % 16 == 0 && sizeof(typename SQ::Smem) % 16 == 0, "16-byte parts");
+  const int group_floats = tracker_group_floats(d, r, prm, STASH, FIXED);
+  float* gbase = dyn + (size_t)g * group_floats;
+  typename QR::Smem& qsm_g = *reinterpret_cast<typename QR::Smem*>(gbase);
+  typename SQ::Smem& ssm_g = *reinterpret_cast<typename SQ::Smem*>(gbase + sizeof(typename QR::Smem) / sizeof(float));
+  float* xstage = gbase + FIXED;
   float* vs = xstage + 2 * d;
   float2* park = reinterpret_cast<float2*>(dyn + (size_t)(g + 1) * group_floats - STASH);  // [RP*CPT][TPF]
   const float* Xf = X + fs * (size_t)T * d;
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         a[p][c].y = tracker_candidate(om_u, a_u, a[p][c].y, xr[p].y, w[c], s1, nov);
       }
     }
-    QR::qr(a, lane, t, qsm[g], prm.eps_sign, prm.sign_mode, r);
+    QR::qr(a, lane, t, qsm_g, prm.eps_sign, prm.sign_mode, r);
 
     // ---- p = U^T x (new U) ----
     QR::col_dots(a, xr, w);
@@ -283,7 +287,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         for (int i = 0; i < RMAX; ++i)
           if (i < r) c[i] = tracker_candidate(om, al, c[i], pbuf[g][i], wj, sbuf[g][i], t == n - 1);
       }
-      SQ::qr(c, t, n, ssm[g], prm.eps_sign, prm.sign_mode);
+      SQ::qr(c, t, n, ssm_g, prm.eps_sign, prm.sign_mode);
       float vp = 0.f;
       if (t < n) {
 #pragma unroll
@@ -333,7 +337,11 @@ int launch_tracker(float* U, float* nested, const float* X, int64_t n, int T, in
   const int64_t blocks = (n + NG - 1) / NG;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many streams: %lld", (long long)n);
   const size_t smem =
-      (size_t)NG * tracker_group_floats(d, r, prm, tracker_stash_floats<DMAX, RMAX, RG, CG>()) * sizeof(float);
+      (size_t)NG *
+      tracker_group_floats(d, r, prm, tracker_stash_floats<DMAX, RMAX, RG, CG>(),
+                           (int)((sizeof(typename FrameQR<DMAX, RMAX, RG, CG>::Smem) +
+                                  sizeof(typename SmallQR<RMAX>::Smem)) / sizeof(float))) *
+      sizeof(float);
   GFST_REQUIRE(smem <= 200u * 1024u, GFST_ERR_SHAPE, "tracker state needs %zu bytes of shared memory", smem);
   auto kern = local_tracker_stream_kernel<DMAX, RMAX, RG, CG, kTrackerWarps>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
