@@ -13,6 +13,7 @@ the last launch.  CASE is one of:
   readout     exact-token readout of 64 queries x 16 blocks of 64 tokens per stream
   commit      one 64-token block commit per stream
   tracker     64 tokens of the local tracker (d=64, flag dims 8/16/32, nested levels + features)
+  readout_long  exact-token readout of 1024 queries x 8 blocks of 128 tokens per stream out of 8192 blocks
 """
 from __future__ import annotations
 
@@ -39,7 +40,8 @@ def _timed(fn, repeat: int) -> float:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker"])
+    parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
+                                         "readout_long"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     args = parser.parse_args()
@@ -73,6 +75,13 @@ def main() -> None:
         sel = torch.randint(0, 512, (S, 64, 16), generator=g, device=dev, dtype=torch.int32)
         ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel), args.repeat)
         units = f"{S * 64 * 16 * 64 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bytes"
+    elif args.case == "readout_long":
+        S = args.streams or 16
+        pool = torch.randn((S, 8192, 128, 128), generator=g, device=dev, dtype=bf)
+        Q = torch.randn((S, 1024, 128), generator=g, device=dev).to(bf)
+        sel = torch.randint(0, 8192, (S, 1024, 8), generator=g, device=dev, dtype=torch.int32)
+        ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel), args.repeat)
+        units = f"{S * 1024 * 8 * 128 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bytes"
     elif args.case == "tracker":
         S = args.streams or 2048
         tr = tracker.LocalTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), device=dev)
