@@ -595,10 +595,16 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
+    # stdout carries only the JSON line: everything else that writes to file
+    # descriptor 1 (library banners such as NCCL's version line) goes to stderr
+    json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
+
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=json_out, flush=True)
         return
 
     import datetime
@@ -616,7 +622,7 @@ def main() -> None:
             dist.barrier()
             dist.destroy_process_group()
     if res is not None:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=json_out, flush=True)
 
 
 if __name__ == "__main__":

@@ -81,3 +81,44 @@ def test_block_range_sharded_readout_two_ranks(cuda_device, tmp_path):
         assert torch.equal(best_t, ref_t.cpu())
         assert torch.equal(best_s, ref_bs.cpu())
         assert torch.equal(value, ref_v.cpu())
+
+
+def _nccl_worker(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        pool, vals, Q, summary, k = _data(dev)
+        shard = sharding.BlockRange(rank, world, pool.shape[1])
+        sl = slice(shard.lo, shard.hi)
+        res = sharding.sharded_readout(Q, summary[:, sl].contiguous(), pool[:, sl].contiguous(),
+                                       vals[:, sl].contiguous(), k, shard)
+        torch.cuda.synchronize(dev)
+        torch.save([t.cpu() for t in res], f"{out_path}.{rank}")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_block_range_sharded_readout_nccl_two_gpus(cuda_device, tmp_path):
+    # one rank per GPU over NCCL: all-gather of candidates and winners, all-reduce
+    # of the owner's value row; equal to the single-GPU readout bit for bit
+    world = 2
+    out = str(tmp_path / "nccl")
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
+    pool, vals, Q, summary, k = _data(cuda_device)
+    ref_s, ref_i = retrieval.block_topk(Q, summary, k)
+    ref_t, ref_bs, ref_v = readout.exact_readout(Q, pool, vals, ref_i)
+    for r in range(world):
+        best_t, best_s, value, top_i, top_s = torch.load(f"{out}.{r}")
+        assert torch.equal(top_i, ref_i.cpu())
+        assert torch.equal(top_s, ref_s.cpu())
+        assert torch.equal(best_t, ref_t.cpu())
+        assert torch.equal(best_s, ref_bs.cpu())
+        assert torch.equal(value, ref_v.cpu())
