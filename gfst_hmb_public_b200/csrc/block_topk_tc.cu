@@ -7,14 +7,16 @@
 // keys @ q and takes torch.topk; this is the same selection batched over all
 // queries of a stream, with the score matrix never leaving the SM.
 //
-// One CTA per (stream, 128-query tile), 6 warps:
-//   warp 4  TMA producer: the query tile once, then 128-summary tiles into a
+// One CTA per (stream, 128-query tile), 10 warps:
+//   warp 8  TMA producer: the query tile once, then 128-summary tiles into a
 //           STAGES-deep ring of 128B-swizzled shared-memory buffers
-//   warp 5  MMA issuer: tcgen05.mma.cta_group::1.kind::f16 (M=128, N=128, K=16)
+//   warp 9  MMA issuer: tcgen05.mma.cta_group::1.kind::f16 (M=128, N=128, K=16)
 //           into one of two TMEM accumulators (2 x 128 fp32 columns), then
 //           tcgen05.commit to free the smem stage and publish the accumulator
-//   warps 0-3  epilogue: thread = query row = TMEM lane; tcgen05.ld the row's
-//           128 scores, release the accumulator, insert into a register top-k
+//   warps 0-7  epilogue: warp w reads TMEM lane quadrant w % 4 (thread = query
+//           row) and column half w / 4 of each accumulator with tcgen05.ld,
+//           releases the accumulator and inserts the 64 scores into a register
+//           top-k list; the two halves of a row are merged at the end
 // Every mbarrier wait is bounded (about a second of clock cycles); a wait that
 // gives up sets a sticky device error word (read with gfst_check_device_errors)
 // and the CTA drains its in-flight copies and MMAs, frees TMEM and returns.
@@ -30,7 +32,17 @@ namespace {
 constexpr int BM = 128;            // query rows per CTA (TMEM lanes)
 constexpr int BN = 128;            // summaries per tile (TMEM columns per accumulator)
 constexpr int KBOX = 64;           // bf16 elements per 128-byte swizzle row
-constexpr int kThreadsTC = 192;
+// EPW epilogue warps (4 or 8: the TMEM lane quadrants x 1 or 2 column parts),
+// then one TMA producer warp and one MMA warp
+template <int EPW>
+struct TcWarps {
+  static_assert(EPW == 4 || EPW == 8, "4 or 8 epilogue warps");
+  static constexpr int kEpiWarps = EPW;
+  static constexpr int kProducerWarp = EPW;
+  static constexpr int kMmaWarp = EPW + 1;
+  static constexpr int kThreads = (EPW + 2) * 32;
+  static constexpr int kPartN = BN / (EPW / 4);  // accumulator columns per epilogue warp
+};
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -84,12 +96,15 @@ struct TcLayout {
   static constexpr int SMEM_BYTES = 1024 + BAR_OFF + N_BARS * 8 + 64;
 };
 
-template <int NKB, int STAGES, int KCAP>
-__global__ void __launch_bounds__(kThreadsTC, 1)
+template <int NKB, int STAGES, int KCAP, int EPW>
+__global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 1)
     block_topk_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          int n_queries, int n_blocks, int n_blocks_stride, int k, float* __restrict__ top_scores,
                          int32_t* __restrict__ top_idx) {
   using LY = TcLayout<NKB, STAGES>;
+  using W = TcWarps<EPW>;
+  constexpr int kEpiWarps = W::kEpiWarps, kProducerWarp = W::kProducerWarp, kMmaWarp = W::kMmaWarp;
+  constexpr int kHalfN = W::kPartN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -118,7 +133,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], kEpiWarps);
     }
     mbar_init(afull, 1);
     mbar_init(done, 1);
@@ -127,7 +142,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     *n_consumed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(2 * BN)
                  : "memory");
@@ -138,7 +153,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {
       // query tile (rows of other streams or past the end only feed unused rows)
       mbar_arrive_expect_tx(afull, LY::A_BYTES);
@@ -161,7 +176,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       *n_issued = i;
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       int i = 0;
       if (!mbar_wait(afull, 0)) {
@@ -191,7 +206,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       umma_commit(done);  // arrives once every MMA issued above has completed
     }
   } else {
-    // epilogue: TMEM lane quadrant = warp, row = warp * 32 + lane
+    // epilogue: warp w reads TMEM lane quadrant w % 4 (row = 32 (w % 4) + lane)
+    // and column part w / 4 of every accumulator; with two parts each keeps its
+    // own top-k list and the two are merged per row at the end
+    const int quad = warp & 3, half = warp >> 2;
     TopK<KCAP> top;
     top.init();
     for (int i = 0; i < n_tiles; ++i) {
@@ -207,35 +225,80 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * BN);
-      float v[BN];
+      const uint32_t taddr =
+          tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(half * kHalfN);
+      float v[kHalfN];
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) tmem_ld16(taddr + c0, v + c0);
+      for (int c0 = 0; c0 < kHalfN; c0 += 16) tmem_ld16(taddr + c0, v + c0);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);  // accumulator free for tile i + 2
-      const int b0 = i * BN;
+      const int b0 = i * BN + half * kHalfN;
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = 0; c0 < kHalfN; c0 += 16) {
         float w[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) w[c] = v[c0 + c];
         top.offer16(w, b0 + c0, n_blocks);
       }
     }
-    const int q = q0 + warp * 32 + lane;
-    if (q < n_queries)
-      top.write(top_scores + ((size_t)s * n_queries + q) * k, top_idx + ((size_t)s * n_queries + q) * k, k);
-  }
-
+    if constexpr (EPW == 4) {
+      const int q = q0 + quad * 32 + lane;
+      if (q < n_queries)
+        top.write(top_scores + ((size_t)s * n_queries + q) * k, top_idx + ((size_t)s * n_queries + q) * k, k);
+    } else {
+      // merge the two halves of each row through shared memory (the B ring is
+      // idle once every tile has been consumed; after a timeout nothing is merged)
+      const int row = quad * 32 + lane;
+      const int q = q0 + row;
+      float* ms = reinterpret_cast<float*>(sB);                 // [2][BM][KCAP]
+      int* mi = reinterpret_cast<int*>(sB + 2 * BM * KCAP * 4);  // [2][BM][KCAP]
+      const bool merge = *abort_flag == 0;
+      if (merge) {
+  #pragma unroll
+        for (int j = 0; j < KCAP; ++j) {
+          ms[(half * BM + row) * KCAP + j] = top.s[j];
+          mi[(half * BM + row) * KCAP + j] = top.i[j];
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      if (half == 0 && q < n_queries) {
+        float* os = top_scores + ((size_t)s * n_queries + q) * k;
+        int32_t* oi = top_idx + ((size_t)s * n_queries + q) * k;
+        if (merge) {
+          const float* as = ms + row * KCAP;
+          const int* ai = mi + row * KCAP;
+          const float* bs = ms + (BM + row) * KCAP;
+          const int* bi = mi + (BM + row) * KCAP;
+          int pa = 0, pb = 0;
+          for (int j = 0; j < k; ++j) {
+            const float sa = pa < KCAP ? as[pa] : -INFINITY;
+            const int ia = pa < KCAP ? ai[pa] : 0x7fffffff;
+            const float sb2 = pb < KCAP ? bs[pb] : -INFINITY;
+            const int ib = pb < KCAP ? bi[pb] : 0x7fffffff;
+            const bool take_a = better(sa, ia, sb2, ib);
+            const float sv = take_a ? sa : sb2;
+            const int iv = take_a ? ia : ib;
+            pa += take_a ? 1 : 0;
+            pb += take_a ? 0 : 1;
+            const bool filled = iv != 0x7fffffff;
+            os[j] = filled ? sv : -INFINITY;
+            oi[j] = filled ? iv : -1;
+          }
+        } else {
+          top.write(os, oi, k);
+        }
+      }
+    }
+    }
   __syncthreads();
-  if (threadIdx.x == 32 * 4) {
+  if (threadIdx.x == 32 * kProducerWarp) {
     // drain copies that were issued but never consumed (only after a timeout)
     for (int i = *n_consumed; i < *n_issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
     if (*abort_flag) mbar_wait(afull, 0);
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     if (!mbar_wait(done, 0)) *abort_flag = 1;
     __syncwarp();
     tc_fence_after();
@@ -246,16 +309,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // --- host: tensor maps through the driver entry point ------------------------
-template <int NKB, int STAGES, int KCAP>
-int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
-              int32_t* ti, cudaStream_t stream) {
+template <int NKB, int STAGES, int KCAP, int EPW>
+int launch_tc_epw(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k,
+                  float* ts, int32_t* ti, cudaStream_t stream) {
   using LY = TcLayout<NKB, STAGES>;
-  auto kern = block_topk_tc_kernel<NKB, STAGES, KCAP>;
+  auto kern = block_topk_tc_kernel<NKB, STAGES, KCAP, EPW>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM_BYTES);
   GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   dim3 grid((unsigned)((Nq + BM - 1) / BM), (unsigned)S);
-  kern<<<grid, kThreadsTC, LY::SMEM_BYTES, stream>>>(mq, mk, Nq, NB, NBs, k, ts, ti);
+  kern<<<grid, TcWarps<EPW>::kThreads, LY::SMEM_BYTES, stream>>>(mq, mk, Nq, NB, NBs, k, ts, ti);
   return check_launch("block_topk_tc_kernel");
+}
+
+// Long score rows (many summary tiles per query tile) keep the top-k epilogue
+// busy: split each row's columns over two warps.  Short rows use one.
+template <int NKB, int STAGES, int KCAP>
+int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, int64_t S, int Nq, int NB, int NBs, int k, float* ts,
+              int32_t* ti, cudaStream_t stream) {
+  if (NB > 16 * BN) return launch_tc_epw<NKB, STAGES, KCAP, 8>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  return launch_tc_epw<NKB, STAGES, KCAP, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
 }
 
 template <int NKB, int STAGES>

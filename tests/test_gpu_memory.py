@@ -75,7 +75,8 @@ def test_block_topk_matches_oracle(cuda_device, dtype, S, Nq, NB, d, k):
 
 @pytest.mark.parametrize("S,Nq,NB,d,k", [(2, 300, 1000, 128, 8), (3, 64, 512, 128, 16), (1, 129, 257, 64, 4),
                                           (2, 40, 130, 256, 32), (2, 77, 300, 96, 8), (1, 5, 3, 200, 4),
-                                          (2, 128, 0, 128, 2)])
+                                          (2, 128, 0, 128, 2), (1, 200, 2100, 128, 8), (2, 64, 4096, 64, 32),
+                                          (1, 130, 3000, 256, 16)])
 def test_block_topk_tensor_core_tiles(cuda_device, S, Nq, NB, d, k):
     # bf16 memories run the tcgen05 pipeline: partial query and block tiles,
     # K boxes padded by the tensor map, more than two accumulator rounds
@@ -99,6 +100,19 @@ def test_block_topk_ties_pick_lowest_index(cuda_device, dtype):
     Q[0, 0, 0] = 1.0
     scores, idx = retrieval.block_topk(Q.to(dtype).to(cuda_device), Ksum.to(dtype).to(cuda_device), 4)
     assert idx.cpu().tolist() == [[[5, 130, 200, 0]]]
+
+
+def test_block_topk_ties_across_column_parts(cuda_device):
+    # long rows split each tile's columns over two epilogue warps: equal best
+    # scores in both parts and in far-apart tiles still come out lowest index first
+    Ksum = torch.zeros((1, 2500, 64))
+    Ksum[0, [2300, 1000, 64, 30], 0] = 1.0
+    Ksum[0, 1500, 0] = 0.5
+    Q = torch.zeros((1, 3, 64))
+    Q[0, :, 0] = 1.0
+    scores, idx = retrieval.block_topk(Q.to(torch.bfloat16).to(cuda_device), Ksum.to(torch.bfloat16).to(cuda_device), 6)
+    assert idx.cpu().tolist() == [[[30, 64, 1000, 2300, 1500, 0]] * 3]
+    assert scores.cpu()[0, 0, :5].tolist() == [1.0, 1.0, 1.0, 1.0, 0.5]
 
 
 def test_block_topk_partial_bank(cuda_device):
