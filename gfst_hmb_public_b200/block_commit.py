@@ -1,0 +1,93 @@
+"""Reference-faithful block commit (the eigen summary of a closed block) on the GPU.
+
+Drop-in for the reference's accelerated commit op
+``runtime_backends.gfst_block_commit(projector_sum=, reduced_sum=, token_count=,
+max_flag_dim=, flag_dims=) -> (summary_basis, reduced_mean, top_vector,
+average_projector)`` (call sites src/gfst_hmb_mpuc/modeling.py:3487-3495 and
+src/gfst_hmb_mpuc/diagnostics/block_commit_replay.py:144-154), computing what
+its torch path computes (average projector, ``top_eig_summary``,
+src/gfst_hmb_mpuc/gfst.py:172-430) with the sm_100a kernel
+``gfst_block_commit_eig``.  ``replay_block_commit_bundle`` mirrors the
+replay diagnostic's ``implementation="candidate"`` branch
+(block_commit_replay.py:141-175) on a bundle of the same layout.  There is no
+CPU path: the reference's own ``"native"`` replay is the comparison point.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Sequence
+
+import torch
+
+from . import _native as nat
+
+
+def gfst_block_commit(*, projector_sum: torch.Tensor, reduced_sum: torch.Tensor, token_count: int,
+                      max_flag_dim: int, flag_dims: Sequence[int], eps_sign: float = 1e-8):
+    """projector_sum [d, d] (or [S, d, d]) and reduced_sum [d] (or [S, d]) float32
+    CUDA tensors.  Returns (summary_basis [.., d, max_flag_dim], reduced_mean,
+    top_vector, average_projector), float32 on the same device."""
+    nat.require_cuda(projector_sum, reduced_sum, what="gfst_block_commit")
+    single = projector_sum.ndim == 2
+    ps = projector_sum.unsqueeze(0) if single else projector_sum
+    rs = reduced_sum.unsqueeze(0) if single else reduced_sum
+    if ps.ndim != 3 or ps.shape[1] != ps.shape[2] or rs.shape != ps.shape[:2]:
+        raise ValueError(f"gfst_block_commit: projector_sum {tuple(projector_sum.shape)} and reduced_sum "
+                         f"{tuple(reduced_sum.shape)} do not match")
+    for name, t in (("projector_sum", ps), ("reduced_sum", rs)):
+        if t.dtype != torch.float32:
+            raise RuntimeError(f"gfst_block_commit: {name} must be float32")
+    if rs.device != ps.device:
+        raise RuntimeError("gfst_block_commit: tensors on different devices")
+    S, d = ps.shape[0], ps.shape[1]
+    dims = [int(v) for v in flag_dims]
+    ps, rs = ps.contiguous(), rs.contiguous()
+    basis = torch.empty((S, d, int(max_flag_dim)), device=ps.device, dtype=torch.float32)
+    mean = torch.empty((S, d), device=ps.device, dtype=torch.float32)
+    top = torch.empty((S, d), device=ps.device, dtype=torch.float32)
+    avg = torch.empty((S, d, d), device=ps.device, dtype=torch.float32)
+    dims_arr = (ctypes.c_int32 * max(len(dims), 1))(*dims)
+    with torch.cuda.device(ps.device):
+        nat.call("gfst_block_commit_eig", nat.ptr(ps), nat.ptr(rs), S, d, int(token_count), int(max_flag_dim),
+                 ctypes.cast(dims_arr, ctypes.c_void_p), len(dims), float(eps_sign), nat.ptr(basis), nat.ptr(mean),
+                 nat.ptr(top), nat.ptr(avg), nat.stream_of(ps))
+    if single:
+        return basis[0], mean[0], top[0], avg[0]
+    return basis, mean, top, avg
+
+
+def _prefix_projectors(basis: torch.Tensor, prefix_dims: Sequence[int]) -> dict[int, torch.Tensor]:
+    """block_commit_replay.py:35-41: symmetrised B[:, :k] B[:, :k]^T for each prefix width."""
+    out = {}
+    for k in prefix_dims:
+        if int(k) <= basis.shape[-1]:
+            b = basis[..., : int(k)]
+            p = b @ b.transpose(-1, -2)
+            out[int(k)] = 0.5 * (p + p.transpose(-1, -2))
+    return out
+
+
+def replay_block_commit_bundle(bundle: dict[str, Any], *, implementation: str = "candidate",
+                               device: str | torch.device = "cuda") -> dict[str, Any]:
+    """The replay diagnostic's accelerated branch on this kernel.  Bundle keys as
+    block_commit_bundle_from_capture builds them (projector_sum, reduced_sum,
+    token_count, max_flag_dim, flag_dims, eps_sign, prefix_dims,
+    block_key_proj_weight)."""
+    if implementation != "candidate":
+        raise ValueError(f"only the 'candidate' (GPU) replay lives here, not {implementation!r}")
+    dev = torch.device(device)
+    basis, mean, top, avg = gfst_block_commit(
+        projector_sum=bundle["projector_sum"].to(dev, torch.float32),
+        reduced_sum=bundle["reduced_sum"].to(dev, torch.float32),
+        token_count=int(bundle["token_count"]), max_flag_dim=int(bundle["max_flag_dim"]),
+        flag_dims=tuple(int(v) for v in bundle["flag_dims"]), eps_sign=float(bundle.get("eps_sign", 1e-8)))
+    prefix = _prefix_projectors(basis, tuple(int(v) for v in bundle.get("prefix_dims", ())))
+    weight = bundle.get("block_key_proj_weight")
+    key = None
+    if weight is not None:  # block_commit_replay.py:44-53: W [mean; top_vector]
+        key = torch.nn.functional.linear(torch.cat((mean, top)), weight.to(dev, torch.float32))
+    cpu = lambda t: t.detach().to("cpu", torch.float32).clone()  # noqa: E731
+    return {"implementation": "candidate", "used_accelerated_kernel": True,
+            "average_projector": cpu(avg), "summary_basis": cpu(basis),
+            "prefix_projectors": {k: cpu(v) for k, v in prefix.items()},
+            "reduced_mean": cpu(mean), "top_vector": cpu(top), "block_key": None if key is None else cpu(key)}

@@ -36,6 +36,7 @@ extern "C" const char* gfst_status_string(int status) {
     case GFST_ERR_DEVICE: return "CUDA runtime error";
     case GFST_ERR_TIMEOUT: return "device-side wait timed out";
     case GFST_ERR_DTYPE: return "unsupported dtype";
+    case GFST_ERR_NUMERIC: return "numerical routine did not converge";
     default: return "unknown status";
   }
 }

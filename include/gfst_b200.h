@@ -24,6 +24,10 @@
  *                             src/gfst_hmb_mpuc/state.py:651-815 and the block summary of
  *                             GfstHmbSublayer._update_block_memory modeling.py:3482-3535
  *                             (summary key = mean of the block's token keys)
+ *   gfst_block_commit_eig  <- runtime_backends.gfst_block_commit(projector_sum, reduced_sum,
+ *                             token_count, max_flag_dim, flag_dims) and its torch path
+ *                             top_eig_summary, modeling.py:3482-3507, gfst.py:172-430,
+ *                             diagnostics/block_commit_replay.py:97-181
  *   gfst_block_topk        <- FaissGpuRetriever.search / exact_topk
  *                             src/gfst_hmb_mpuc/retrieval.py:136-172
  *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
@@ -54,7 +58,8 @@ enum gfst_status {
   GFST_ERR_LAUNCH = 4,      /* the CUDA launch itself failed (cudaGetLastError)       */
   GFST_ERR_DEVICE = 5,      /* device is not sm_100 or a CUDA runtime call failed     */
   GFST_ERR_TIMEOUT = 6,     /* a bounded device-side wait gave up                     */
-  GFST_ERR_DTYPE = 7        /* unsupported element type                               */
+  GFST_ERR_DTYPE = 7,       /* unsupported element type                               */
+  GFST_ERR_NUMERIC = 8      /* a device-side numerical routine did not converge      */
 };
 
 /* Sign convention applied to every column of a thin-QR factor Q. */
@@ -136,6 +141,27 @@ GFST_API int gfst_local_tracker_stream(float* U, float* nested, const float* x, 
 GFST_API int gfst_block_commit_mean(const void* K, const void* V, void* pool_K, void* pool_V,
                            void* summary, int64_t n_streams, int n_slots, int slot,
                            int L, int d, int dv, int dtype, cudaStream_t stream);
+
+/* ---- reference-faithful block commit: eigen summary of a closed block ------
+ * For every stream s (fp32 in, fp32 out, float64 eigenproblem):
+ *   average_projector[s] = projector_sum[s] / token_count        (d x d)
+ *   reduced_mean[s]      = reduced_sum[s] / token_count          (d)
+ *   eigenpairs of (average + average^T) / 2 in float64; eigenvalue clusters
+ *   (|a - b| <= 1e-9 + 1e-7 |b|) taken from the top until T = max(max_flag_dim,
+ *   max(flag_dims), 1) columns are filled, each replaced by its canonical basis
+ *   (Gram-Schmidt over the cluster projector's columns in descending-diagonal
+ *   order, signs by the first entry with |x| > eps_sign), cast to fp32, signs
+ *   fixed again;
+ *   summary_basis[s] = columns [0, max_flag_dim)  (d x max_flag_dim), top_vector[s] = column 0.
+ * projector_sum: [n_streams, d, d]; reduced_sum: [n_streams, d]; flag_dims: host
+ * array of n_flags sizes.  Limits: d <= 64, 1 <= max_flag_dim <= d.  An
+ * eigensolver that does not converge, or a cluster basis short of its rank,
+ * records GFST_ERR_NUMERIC for gfst_check_device_errors().                    */
+GFST_API int gfst_block_commit_eig(const float* projector_sum, const float* reduced_sum,
+                          int64_t n_streams, int d, int token_count, int max_flag_dim,
+                          const int32_t* flag_dims, int n_flags, double eps_sign,
+                          float* summary_basis, float* reduced_mean, float* top_vector,
+                          float* average_projector, cudaStream_t stream);
 
 /* ---- coarse block retrieval: score + top-k ---------------------------------
  * For every stream s and query q:

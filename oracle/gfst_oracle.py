@@ -230,6 +230,84 @@ def block_commit_mean(K_block: np.ndarray, bf16: bool) -> np.ndarray:
     return to_bf16_f32(mean) if bf16 else mean
 
 
+EIG_CLUSTER_ATOL = 1e-9   # gfst.py:6
+EIG_CLUSTER_RTOL = 1e-7   # gfst.py:7
+
+
+def _first_significant_signs(q: torch.Tensor, eps_sign: float) -> torch.Tensor:
+    """gfst.py:35-46 on a torch tensor of any float dtype."""
+    mask = q.abs() > float(eps_sign)
+    first = torch.argmax(mask.to(torch.int64), dim=-2)
+    vals = torch.gather(q, -2, first.unsqueeze(-2)).squeeze(-2)
+    sign = torch.where(mask.any(dim=-2) & vals.lt(0), -torch.ones_like(vals), torch.ones_like(vals))
+    return q * sign.unsqueeze(-2)
+
+
+def _cluster_basis(cluster: torch.Tensor, target_rank: int, eps: float, eps_sign: float) -> torch.Tensor:
+    """gfst.py:172-214 (_canonical_basis_from_cluster_space): Gram-Schmidt over the
+    cluster projector's columns taken in descending-diagonal order (ties: lower
+    axis first), then over the cluster's own columns if that falls short; signs
+    by the first significant entry.  float64."""
+    projector = cluster @ cluster.transpose(0, 1)
+    diag = torch.diag(projector)
+    order = sorted(range(projector.shape[0]), key=lambda a: (-float(diag[a].item()), a))
+    cols: list[torch.Tensor] = []
+
+    def append(candidate):
+        v = candidate.clone()
+        for c in cols:
+            v = v - torch.dot(c, v) * c
+        n = torch.linalg.norm(v)
+        if float(n.item()) > eps:
+            cols.append(v / n)
+
+    for a in order:
+        if len(cols) >= target_rank:
+            break
+        append(projector[:, a])
+    for j in range(cluster.shape[1]):
+        if len(cols) >= target_rank:
+            break
+        append(cluster[:, j])
+    if len(cols) < target_rank:
+        raise RuntimeError("cluster basis short of its rank")
+    return _first_significant_signs(torch.stack(cols[:target_rank], dim=1), eps_sign)
+
+
+def block_commit_eig(projector_sum, reduced_sum, token_count: int, max_flag_dim: int, flag_dims,
+                     eps_sign: float = 1e-8):
+    """Reference-faithful block commit for one block: replay_block_commit_bundle
+    native path (diagnostics/block_commit_replay.py:97-139) = average projector,
+    top_eig_summary (gfst.py:389-430: symmetrise in the input dtype, float64
+    eigh, clusters of eigenvalues equal within atol 1e-9 / rtol 1e-7 walked from
+    the top, each replaced by its canonical basis, gfst.py:232-297), reduced mean.
+    projector_sum [d, d] float32, reduced_sum [d] float32.  Returns numpy float32
+    (summary_basis [d, max_flag_dim], reduced_mean [d], top_vector [d],
+    average_projector [d, d])."""
+    ps = torch.as_tensor(np.asarray(projector_sum, np.float32))
+    rs = torch.as_tensor(np.asarray(reduced_sum, np.float32))
+    avg = ps / float(token_count)
+    mean = rs / float(token_count)
+    sym = (0.5 * (avg + avg.transpose(0, 1))).to(torch.float64)
+    vals, vecs = torch.linalg.eigh(sym)
+    target = max(int(max_flag_dim), max((int(b) for b in flag_dims), default=0), 1)
+    rank = max(0, min(target, vecs.shape[0]))
+    parts, remaining, end = [], rank, vals.shape[0] - 1
+    while end >= 0 and remaining > 0:
+        start = end
+        while start > 0 and abs(float(vals[start - 1]) - float(vals[start])) <= \
+                EIG_CLUSTER_ATOL + EIG_CLUSTER_RTOL * abs(float(vals[start])):
+            start -= 1
+        take = min(end - start + 1, remaining)
+        parts.append(_cluster_basis(vecs[:, start:end + 1], take, 1e-9, eps_sign))
+        remaining -= take
+        end = start - 1
+    full = _first_significant_signs(torch.cat(parts, dim=1).to(torch.float32), eps_sign)
+    basis = full[:, : max(0, min(int(max_flag_dim), full.shape[1]))]
+    top = full[:, 0] if full.shape[1] > 0 else torch.zeros(ps.shape[0])
+    return basis.numpy(), mean.numpy(), top.numpy(), avg.numpy()
+
+
 # ---------------------------------------------------------------------------
 # top-k block select
 # ---------------------------------------------------------------------------

@@ -211,6 +211,49 @@ def main() -> None:
                  forgetting_rates=np.array(cfg.forgetting_rates, np.float64), eps=np.float64(cfg.eps),
                  eps_update=np.float64(cfg.eps_update), eps_sign=np.float64(cfg.eps_sign), features=feats,
                  frames_every8=snaps, largest_basis=U_out, nested_bases=V_out, local_bases=np.stack(bases_out))
+    # 9. reference block commits (replay_block_commit_bundle, native path:
+    #    block_commit_replay.py:97-139 -> top_eig_summary, gfst.py:389-430) on
+    #    projector sums of real block-tracker passes (modeling.py:3460-3479:
+    #    rule update, canonical QR, projector_sum += U U^T, reduced_sum += x)
+    #    and on degenerate spectra (repeated eigenvalues -> cluster bases)
+    cases = []
+    for s_idx, (d, fds, T) in enumerate(((64, (8, 16, 32), 64), (64, (8, 16, 32), 64), (64, (4, 8, 16), 48),
+                                         (32, (2, 4, 8), 16), (16, (2, 4), 40))):
+        g = torch.Generator().manual_seed(100 + s_idx)
+        r = max(fds)
+        U = torch.eye(d, r)
+        ps = torch.zeros((d, d))
+        rs = torch.zeros((d,))
+        for _ in range(T):
+            x = torch.randn((d,), generator=g)
+            U = gfst.canonical_qr_batched(gfst.update_basis_candidate(U, x, 0.20, eps_update=1e-6).unsqueeze(0),
+                                          eps_sign=1e-8).squeeze(0)
+            ps = ps + gfst.basis_projector(U[:, :r])
+            rs = rs + x
+        cases.append((ps, rs, T, r, fds))
+    # degenerate: one projector repeated (eigenvalue 1 with multiplicity r, 0 otherwise)
+    g = torch.Generator().manual_seed(200)
+    Uq = gfst.canonical_qr(torch.randn((16, 4), generator=g))
+    cases.append((8.0 * gfst.basis_projector(Uq), torch.randn((16,), generator=g), 8, 4, (2, 4)))
+    # the reference test's capture: diag(0, 0, 1, 1) summed twice
+    cases.append((2.0 * torch.diag(torch.tensor([0.0, 0.0, 1.0, 1.0])), 2.0 * torch.tensor([1.0, -0.5, 0.25, 0.75]),
+                  2, 2, (1, 2)))
+    # two repeated projectors of different weights: clusters {1/3 x2}, {2/3 x2} inside d=12
+    Ua = gfst.canonical_qr(torch.randn((12, 4), generator=g))
+    cases.append((gfst.basis_projector(Ua[:, :2]) + 2.0 * gfst.basis_projector(Ua[:, 2:]),
+                  torch.randn((12,), generator=g), 3, 4, (2, 4)))
+    out = {}
+    for ci, (ps, rs, T, r, fds) in enumerate(cases):
+        bundle = {"projector_sum": ps, "reduced_sum": rs, "token_count": T, "max_flag_dim": r, "flag_dims": fds,
+                  "eps": 1e-6, "eps_sign": 1e-8, "block_key_proj_weight": None, "prefix_dims": fds}
+        rep = bcr.replay_block_commit_bundle(bundle, implementation="native")
+        out[f"c{ci}_projector_sum"] = ps.numpy()
+        out[f"c{ci}_reduced_sum"] = rs.numpy()
+        out[f"c{ci}_meta"] = np.array([T, r] + list(fds))
+        for key in ("average_projector", "summary_basis", "reduced_mean", "top_vector"):
+            out[f"c{ci}_{key}"] = rep[key].numpy()
+    out["n_cases"] = np.array(len(cases))
+    np.savez(OUT / "block_commit_eig_cases.npz", **out)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -1,0 +1,129 @@
+"""Parity of the reference-faithful block commit kernel (float64 Jacobi eigen
+summary, canonical eigenvalue-cluster bases) against the reference's own
+replays (golden vectors of replay_block_commit_bundle, "native") and the CPU
+oracle, through the C ABI.
+
+Bar: the replay diagnostic's clean-commit classification
+(block_commit_replay.py:184-238): average projector, reduced mean, top vector,
+summary basis and every prefix projector within 1e-8.  Where several
+eigenvalues lie within a few 1e-7 of each other (a repeated projector), the
+eigenvectors themselves are determined only to about 1e-9 by any float64
+solver, and the float32 basis may round one or two ulps apart: there the bar
+is 6e-8 on the basis and the replay's projector tolerance, 1e-7, on the prefix
+projectors.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from gfst_hmb_public_b200 import _native, block_commit
+from oracle import gfst_oracle as go
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CLEAN = 1e-8
+
+
+def _prefix(basis, dims):
+    out = {}
+    for k in dims:
+        if k <= basis.shape[1]:
+            p = basis[:, :k] @ basis[:, :k].T
+            out[k] = 0.5 * (p + p.T)
+    return out
+
+
+def _check(got, ref_basis, ref_mean, ref_top, ref_avg, dims, degenerate=False):
+    basis, mean, top, avg = (t.cpu().numpy() for t in got)
+    vec_tol, proj_tol = (6e-8, 1e-7) if degenerate else (CLEAN, CLEAN)
+    assert np.abs(avg - ref_avg).max() <= CLEAN
+    assert np.abs(mean - ref_mean).max() <= CLEAN
+    assert np.abs(top - ref_top).max() <= vec_tol
+    assert np.abs(basis - ref_basis).max() <= vec_tol
+    pg, pr = _prefix(basis.astype(np.float64), dims), _prefix(ref_basis.astype(np.float64), dims)
+    for k in pr:
+        assert np.abs(pg[k] - pr[k]).max() <= proj_tol
+
+
+def test_block_commit_matches_reference_replays(cuda_device):
+    z = np.load(GOLDEN / "block_commit_eig_cases.npz")
+    for c in range(int(z["n_cases"])):
+        meta = [int(v) for v in z[f"c{c}_meta"]]
+        got = block_commit.gfst_block_commit(
+            projector_sum=torch.from_numpy(z[f"c{c}_projector_sum"]).to(cuda_device),
+            reduced_sum=torch.from_numpy(z[f"c{c}_reduced_sum"]).to(cuda_device),
+            token_count=meta[0], max_flag_dim=meta[1], flag_dims=meta[2:])
+        # cases 5 and 7 repeat projectors: eigenvalue groups a few 1e-7 apart
+        _check(got, z[f"c{c}_summary_basis"], z[f"c{c}_reduced_mean"], z[f"c{c}_top_vector"],
+               z[f"c{c}_average_projector"], meta[2:], degenerate=c in (5, 7))
+    assert _native.load().gfst_check_device_errors(1) == 0
+
+
+def test_block_commit_batched_streams_match_oracle(cuda_device):
+    # 48 streams of d=64 block-tracker-like projector sums (rank-32 projectors
+    # of drifting frames), a zero block (one cluster of the whole space) and a
+    # block that repeats one rank-32 projector (eigenvalue 1 with multiplicity 32)
+    g = torch.Generator().manual_seed(3)
+    S, d, r, T = 48, 64, 32, 24
+    ps = torch.zeros((S, d, d))
+    for s in range(S - 2):
+        U = torch.linalg.qr(torch.randn((d, r), generator=g))[0]
+        for _ in range(T):
+            U = torch.linalg.qr(U + 0.2 * torch.randn((d, r), generator=g) / d ** 0.5)[0]
+            ps[s] += U @ U.T
+    Ur = torch.linalg.qr(torch.randn((d, 32), generator=g))[0]
+    ps[S - 1] = float(T) * (Ur @ Ur.T)
+    rs = torch.randn((S, d), generator=g)
+    dims = (8, 16, 32)
+    got = block_commit.gfst_block_commit(projector_sum=ps.to(cuda_device), reduced_sum=rs.to(cuda_device),
+                                         token_count=T, max_flag_dim=32, flag_dims=dims)
+    for s in range(S):
+        ref = go.block_commit_eig(ps[s].numpy(), rs[s].numpy(), T, 32, dims)
+        _check([t[s] for t in got], *ref, dims, degenerate=s == S - 1)
+    assert _native.load().gfst_check_device_errors(1) == 0
+
+
+@pytest.mark.parametrize("d,max_flag,dims", [(7, 3, (1, 3)), (33, 8, (2, 4, 8)), (1, 1, (1,))])
+def test_block_commit_odd_and_tiny_sizes(cuda_device, d, max_flag, dims):
+    g = torch.Generator().manual_seed(d)
+    A = torch.randn((2, d, d), generator=g)
+    ps = A @ A.transpose(1, 2)
+    rs = torch.randn((2, d), generator=g)
+    got = block_commit.gfst_block_commit(projector_sum=ps.to(cuda_device), reduced_sum=rs.to(cuda_device),
+                                         token_count=5, max_flag_dim=max_flag, flag_dims=dims)
+    for s in range(2):
+        ref = go.block_commit_eig(ps[s].numpy(), rs[s].numpy(), 5, max_flag, dims)
+        _check([t[s] for t in got], *ref, dims)
+
+
+def test_replay_bundle_candidate_path(cuda_device):
+    # the capture of the reference's replay test: diag(0, 0, 1, 1) summed twice,
+    # a two-fold top cluster; block key = W [mean; top_vector]
+    projector = torch.diag(torch.tensor([0.0, 0.0, 1.0, 1.0]))
+    reduced = torch.tensor([1.0, -0.5, 0.25, 0.75])
+    weight = torch.zeros((2, 8))
+    weight[0, 0] = 1.0
+    weight[1, 4] = 1.0
+    bundle = {"projector_sum": 2.0 * projector, "reduced_sum": 2.0 * reduced, "token_count": 2, "max_flag_dim": 2,
+              "flag_dims": (1, 2), "eps_sign": 1e-8, "prefix_dims": (1, 2), "block_key_proj_weight": weight}
+    out = block_commit.replay_block_commit_bundle(bundle, device=cuda_device)
+    b, m, t, a = go.block_commit_eig((2.0 * projector).numpy(), (2.0 * reduced).numpy(), 2, 2, (1, 2))
+    assert out["used_accelerated_kernel"]
+    assert np.abs(out["summary_basis"].numpy() - b).max() <= CLEAN
+    assert torch.allclose(out["block_key"], torch.tensor([m[0], t[0]]), atol=CLEAN)
+    assert set(out["prefix_projectors"]) == {1, 2}
+    with pytest.raises(ValueError):
+        block_commit.replay_block_commit_bundle(bundle, implementation="native")
+
+
+def test_block_commit_rejects(cuda_device):
+    with pytest.raises(RuntimeError):  # d > 64
+        block_commit.gfst_block_commit(projector_sum=torch.zeros((65, 65), device=cuda_device),
+                                       reduced_sum=torch.zeros(65, device=cuda_device), token_count=1,
+                                       max_flag_dim=4, flag_dims=(4,))
+    with pytest.raises(RuntimeError):
+        block_commit.gfst_block_commit(projector_sum=torch.zeros((4, 4)), reduced_sum=torch.zeros(4),
+                                       token_count=1, max_flag_dim=2, flag_dims=(2,))

@@ -128,3 +128,21 @@ def test_local_tracker_matches_reference_methods():
             assert np.array_equal(V[lvl], z["nested_bases"][:, lvl, :, :dim])
         bases = np.concatenate([U @ V[lvl] for lvl in range(len(fd) - 1)] + [U], axis=-1)
         np.testing.assert_allclose(bases, z["local_bases"], atol=1e-6)
+
+
+def test_block_commit_eig_matches_reference_replays():
+    # golden: replay_block_commit_bundle(..., "native") of the reference on
+    # projector sums of real block-tracker passes and on degenerate spectra
+    z = load("block_commit_eig_cases.npz")
+    for c in range(int(z["n_cases"])):
+        meta = z[f"c{c}_meta"]
+        b, m, t, a = go.block_commit_eig(z[f"c{c}_projector_sum"], z[f"c{c}_reduced_sum"], int(meta[0]),
+                                         int(meta[1]), [int(v) for v in meta[2:]])
+        assert np.array_equal(b, z[f"c{c}_summary_basis"])
+        assert np.array_equal(m, z[f"c{c}_reduced_mean"])
+        assert np.array_equal(t, z[f"c{c}_top_vector"])
+        assert np.array_equal(a, z[f"c{c}_average_projector"])
+    z = load("block_commit_replay.npz")
+    b, m, t, a = go.block_commit_eig(z["projector_sum"], z["reduced_sum"], int(z["token_count"]), 4,
+                                     [int(v) for v in z["flag_dims"]])
+    assert np.array_equal(b, z["summary_basis"]) and np.array_equal(t, z["top_vector"])
