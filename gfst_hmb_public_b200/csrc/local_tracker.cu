@@ -7,7 +7,8 @@ namespace gfst {
 
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_tracker_dispatch(float* U, float* nested, const float* X, int64_t n, int T, int d, int r,
-                            const TrackerParams& prm, float* features, cudaStream_t stream);
+                            const TrackerParams& prm, float* features, float* proj_sum, float* red_sum,
+                            cudaStream_t stream);
 
 }  // namespace gfst
 
@@ -51,7 +52,45 @@ extern "C" int gfst_local_tracker_stream(float* U, float* nested, const float* x
   switch (pick_shape(d, r)) {
 #define X(idx, D, R, RG, CG) \
   case idx:                  \
-    return launch_tracker_dispatch<D, R, RG, CG>(U, nested, x, n_streams, T, d, r, prm, features, stream);
+    return launch_tracker_dispatch<D, R, RG, CG>(U, nested, x, n_streams, T, d, r, prm, features, nullptr, nullptr, \
+                                                 stream);
+    GFST_SHAPE_CASES(X)
+#undef X
+    default:
+      break;
+  }
+  set_last_error("no kernel for d=%d r=%d", d, r);
+  return GFST_ERR_SHAPE;
+}
+
+extern "C" int gfst_block_tracker_stream(float* U, float* projector_sum, float* reduced_sum, const float* x,
+                                         int64_t n_streams, int T, int d, int r, double rate, double eps_update,
+                                         float eps_sign, int sign_mode, cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(n_streams >= 0 && T >= 0, GFST_ERR_ARG, "negative size");
+  GFST_REQUIRE(r >= 1 && r <= d && r <= 32 && r % 4 == 0, GFST_ERR_SHAPE,
+               "need r in [1, min(d, 32)], r %% 4 == 0 (d=%d r=%d)", d, r);
+  GFST_REQUIRE(d <= 64 && d % 4 == 0, GFST_ERR_SHAPE, "block tracker needs d <= 64, d %% 4 == 0 (d=%d)", d);
+  GFST_REQUIRE(pick_shape(d, r) >= 0, GFST_ERR_SHAPE, "d=%d r=%d outside the supported classes", d, r);
+  GFST_REQUIRE(rate >= 0.0 && rate <= 1.0, GFST_ERR_ARG, "rate outside [0, 1]");
+  GFST_REQUIRE(sign_mode == GFST_SIGN_FIRST_SIGNIFICANT || sign_mode == GFST_SIGN_R_DIAG_POSITIVE, GFST_ERR_ARG,
+               "unknown sign_mode %d", sign_mode);
+  if (n_streams == 0 || T == 0) return GFST_OK;
+  GFST_REQUIRE(U && projector_sum && reduced_sum && x, GFST_ERR_ARG, "null buffer");
+  GFST_REQUIRE(aligned16(x), GFST_ERR_ALIGN, "x must be 16-byte aligned");
+  TrackerParams prm{};
+  prm.n_levels = 0;
+  prm.rate[0] = (float)rate;
+  prm.one_minus[0] = (float)(1.0 - rate);
+  prm.eps = 1e-6f;  // features are not produced
+  prm.eps_update_sq = (float)(eps_update * eps_update);
+  prm.eps_sign = eps_sign;
+  prm.sign_mode = sign_mode;
+  switch (pick_shape(d, r)) {
+#define X(idx, D, R, RG, CG)                                                                                      \
+  case idx:                                                                                                       \
+    return launch_tracker_dispatch<D, R, RG, CG>(U, nullptr, x, n_streams, T, d, r, prm, nullptr, projector_sum, \
+                                                 reduced_sum, stream);
     GFST_SHAPE_CASES(X)
 #undef X
     default:

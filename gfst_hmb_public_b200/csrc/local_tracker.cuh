@@ -46,11 +46,13 @@ __host__ __device__ constexpr int tracker_stash_floats() {
 }
 
 // dynamic shared floats per frame group: QR scratch (`fixed`, a multiple of 4),
-// x stage, nested bases, parked frame
-__host__ __device__ inline int tracker_group_floats(int d, int r, const TrackerParams& prm, int stash, int fixed) {
+// x stage, nested bases, parked frame, and with block accumulation the frame
+// rows [d][r] and the projector sum [d][d]
+__host__ __device__ inline int tracker_group_floats(int d, int r, const TrackerParams& prm, int stash, int fixed,
+                                                    bool accumulate) {
   const int nl = prm.n_levels;
   const int nested_floats = nl > 0 ? prm.voff[nl - 1] + r * prm.dims[nl - 1] : 0;
-  return fixed + 2 * d + ((nested_floats + 3) & ~3) + stash;
+  return fixed + 2 * d + ((nested_floats + 3) & ~3) + stash + (accumulate ? d * r + d * d : 0);
 }
 
 // Column-per-lane Householder thin QR of an m x n matrix, m <= RMAX <= 32,
@@ -151,7 +153,8 @@ template <int DMAX, int RMAX, int RG, int CG, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     local_tracker_stream_kernel(float* __restrict__ U, float* __restrict__ nested, const float* __restrict__ X,
                                 int64_t n_streams, int T, int d, int r, TrackerParams prm,
-                                float* __restrict__ features) {
+                                float* __restrict__ features, float* __restrict__ proj_sum,
+                                float* __restrict__ red_sum) {
   using QR = FrameQR<DMAX, RMAX, RG, CG>;
   using SQ = SmallQR<RMAX>;
   constexpr int TPF = QR::TPF;
@@ -176,13 +179,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   constexpr int STASH = tracker_stash_floats<DMAX, RMAX, RG, CG>();
   constexpr int FIXED = (int)((sizeof(typename QR::Smem) + sizeof(typename SQ::Smem)) / sizeof(float));
   static_assert(sizeof(typename QR::Smem) % 16 == 0 && sizeof(typename SQ::Smem) % 16 == 0, "16-byte parts");
-  const int group_floats = tracker_group_floats(d, r, prm, STASH, FIXED);
+  // block tracker (projector and token sums): frames of at most 64 rows only
+  constexpr bool kCanAcc = DMAX <= 64;
+  const bool acc = kCanAcc && proj_sum != nullptr;
+  const int group_floats = tracker_group_floats(d, r, prm, STASH, FIXED, acc);
   float* gbase = dyn + (size_t)g * group_floats;
   typename QR::Smem& qsm_g = *reinterpret_cast<typename QR::Smem*>(gbase);
   typename SQ::Smem& ssm_g = *reinterpret_cast<typename SQ::Smem*>(gbase + sizeof(typename QR::Smem) / sizeof(float));
   float* xstage = gbase + FIXED;
   float* vs = xstage + 2 * d;
-  float2* park = reinterpret_cast<float2*>(dyn + (size_t)(g + 1) * group_floats - STASH);  // [RP*CPT][TPF]
+  const int acc_floats = acc ? d * r + d * d : 0;
+  float2* park = reinterpret_cast<float2*>(dyn + (size_t)(g + 1) * group_floats - acc_floats - STASH);  // [RP*CPT][TPF]
+  float* ubuf = dyn + (size_t)(g + 1) * group_floats - acc_floats;  // [d][r]
+  float* pacc = ubuf + d * r;                                         // [d][d]
   const float* Xf = X + fs * (size_t)T * d;
 
   auto issue = [&](int tok) {
@@ -199,6 +208,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   typename QR::Frame a;
   QR::load(a, U + fs * (size_t)d * r, t, d, r, valid, false);
+  float2 racc[kCanAcc ? RP : 1];  // running token sum of this lane's rows (block tracker)
+  if constexpr (kCanAcc) {
+   if (acc) {
+    const float* ps = proj_sum + fs * (size_t)d * d;
+    for (int e = t; e < d * d; e += TPF) pacc[e] = valid ? ps[e] : 0.f;
+#pragma unroll
+    for (int p = 0; p < RP; ++p) {
+      const int r0 = rg + (2 * p) * RG, r1 = rg + (2 * p + 1) * RG;
+      racc[p] = make_float2(valid && r0 < d ? red_sum[fs * d + r0] : 0.f, valid && r1 < d ? red_sum[fs * d + r1] : 0.f);
+    }
+   }
+  }
   for (int l = 0; l < NL; ++l) {
     const int n = prm.dims[l];
     const float* src = nested + ((size_t)fs * NL + l) * r * r;
@@ -239,6 +260,60 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
     QR::qr(a, lane, t, qsm_g, prm.eps_sign, prm.sign_mode, r);
+
+    // ---- block tracker: projector_sum += U U^T, reduced_sum += x ----
+    if constexpr (kCanAcc) {
+     if (acc) {
+#pragma unroll
+      for (int p = 0; p < RP; ++p) racc[p] = __fadd2_rn(racc[p], xr[p]);
+#pragma unroll
+      for (int sl = 0; sl < QR::RPT; ++sl) {
+        const int row = rg + sl * RG;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          const int col = cg + c * CG;
+          if (row < d && col < r) ubuf[row * r + col] = QR::get(a, sl, c);
+        }
+      }
+      __syncwarp();
+      // 2 x 2 tiles of the upper triangle (row pairs i2 <= j2), each dot in column order
+      const int h = d / 2, n_tiles = h * (h + 1) / 2;
+      for (int e = t; e < n_tiles; e += TPF) {
+        int i2 = 0, rem = e;
+        while (rem >= h - i2) {
+          rem -= h - i2;
+          ++i2;
+        }
+        const int j2 = i2 + rem;
+        const float4* u0 = reinterpret_cast<const float4*>(ubuf + (2 * i2) * r);
+        const float4* u1 = reinterpret_cast<const float4*>(ubuf + (2 * i2 + 1) * r);
+        const float4* v0 = reinterpret_cast<const float4*>(ubuf + (2 * j2) * r);
+        const float4* v1 = reinterpret_cast<const float4*>(ubuf + (2 * j2 + 1) * r);
+        float d00 = 0.f, d01 = 0.f, d10 = 0.f, d11 = 0.f;
+        for (int c4 = 0; c4 < r / 4; ++c4) {
+          const float4 a0 = u0[c4], a1 = u1[c4], b0 = v0[c4], b1 = v1[c4];
+          d00 = fmaf(a0.x, b0.x, d00); d00 = fmaf(a0.y, b0.y, d00); d00 = fmaf(a0.z, b0.z, d00); d00 = fmaf(a0.w, b0.w, d00);
+          d01 = fmaf(a0.x, b1.x, d01); d01 = fmaf(a0.y, b1.y, d01); d01 = fmaf(a0.z, b1.z, d01); d01 = fmaf(a0.w, b1.w, d01);
+          d10 = fmaf(a1.x, b0.x, d10); d10 = fmaf(a1.y, b0.y, d10); d10 = fmaf(a1.z, b0.z, d10); d10 = fmaf(a1.w, b0.w, d10);
+          d11 = fmaf(a1.x, b1.x, d11); d11 = fmaf(a1.y, b1.y, d11); d11 = fmaf(a1.z, b1.z, d11); d11 = fmaf(a1.w, b1.w, d11);
+        }
+        const int i = 2 * i2, j = 2 * j2;
+        pacc[i * d + j] += d00;
+        pacc[i * d + j + 1] += d01;
+        pacc[(i + 1) * d + j + 1] += d11;
+        if (i2 != j2) {
+          pacc[(i + 1) * d + j] += d10;
+          pacc[j * d + i] += d00;
+          pacc[(j + 1) * d + i] += d01;
+          pacc[j * d + i + 1] += d10;
+          pacc[(j + 1) * d + i + 1] += d11;
+        } else {
+          pacc[(i + 1) * d + j] += d01;  // the tile's transposed corner: same dot, same bits
+        }
+      }
+      __syncwarp();
+     }
+    }
 
     // ---- p = U^T x (new U) ----
     QR::col_dots(a, xr, w);
@@ -322,6 +397,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __syncwarp();  // stage buffer and shared vectors free before the next token
   }
   QR::store(a, U + fs * (size_t)d * r, t, d, r, valid, false);
+  if constexpr (kCanAcc) {
+   if (acc && valid) {
+    float* ps = proj_sum + fs * (size_t)d * d;
+    for (int e = t; e < d * d; e += TPF) ps[e] = pacc[e];
+    if (cg == 0) {
+#pragma unroll
+      for (int p = 0; p < RP; ++p) {
+        const int r0 = rg + (2 * p) * RG, r1 = rg + (2 * p + 1) * RG;
+        if (r0 < d) red_sum[fs * d + r0] = racc[p].x;
+        if (r1 < d) red_sum[fs * d + r1] = racc[p].y;
+      }
+    }
+   }
+  }
   for (int l = 0; l < NL; ++l) {
     const int n = prm.dims[l];
     float* dst = nested + ((size_t)fs * NL + l) * r * r;
@@ -332,7 +421,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_tracker(float* U, float* nested, const float* X, int64_t n, int T, int d, int r, const TrackerParams& prm,
-                   float* features, cudaStream_t stream) {
+                   float* features, float* proj_sum, float* red_sum, cudaStream_t stream) {
   constexpr int NG = kTrackerWarps * (32 / (RG * CG));
   const int64_t blocks = (n + NG - 1) / NG;
   GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many streams: %lld", (long long)n);
@@ -340,13 +429,15 @@ int launch_tracker(float* U, float* nested, const float* X, int64_t n, int T, in
       (size_t)NG *
       tracker_group_floats(d, r, prm, tracker_stash_floats<DMAX, RMAX, RG, CG>(),
                            (int)((sizeof(typename FrameQR<DMAX, RMAX, RG, CG>::Smem) +
-                                  sizeof(typename SmallQR<RMAX>::Smem)) / sizeof(float))) *
+                                  sizeof(typename SmallQR<RMAX>::Smem)) / sizeof(float)),
+                           proj_sum != nullptr) *
       sizeof(float);
   GFST_REQUIRE(smem <= 200u * 1024u, GFST_ERR_SHAPE, "tracker state needs %zu bytes of shared memory", smem);
   auto kern = local_tracker_stream_kernel<DMAX, RMAX, RG, CG, kTrackerWarps>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  kern<<<(unsigned)blocks, kTrackerWarps * 32, smem, stream>>>(U, nested, X, n, T, d, r, prm, features);
+  kern<<<(unsigned)blocks, kTrackerWarps * 32, smem, stream>>>(U, nested, X, n, T, d, r, prm, features, proj_sum,
+                                                                red_sum);
   return check_launch("local_tracker_stream_kernel");
 }
 

@@ -120,3 +120,79 @@ class LocalTracker:
         """U V_l for each nested level, then U (modeling.py:2417-2420)."""
         U = self.largest_basis
         return [torch.matmul(U, V) for V in self.nested_bases] + [U[..., : self.flag_dims[-1]]]
+
+
+def block_tracker_stream(U: torch.Tensor, projector_sum: torch.Tensor, reduced_sum: torch.Tensor, x: torch.Tensor, *,
+                         rate: float, eps_update: float = 1e-6, eps_sign: float = 1e-8,
+                         sign_mode="first_significant") -> None:
+    """Per-token block tracker over x [S, T, d]: U [S, d, r] takes the rule update
+    at ``rate`` and its canonical QR, projector_sum [S, d, d] += U U^T,
+    reduced_sum [S, d] += x; all three updated in place (modeling.py:3460-3479)."""
+    nat.require_cuda(U, projector_sum, reduced_sum, x, what="block_tracker_stream")
+    if U.ndim != 3 or x.ndim != 3:
+        raise ValueError("block_tracker_stream expects U [S,d,r], x [S,T,d]")
+    S, d, r = U.shape
+    T = int(x.shape[1])
+    if tuple(x.shape) != (S, T, d) or tuple(projector_sum.shape) != (S, d, d) or tuple(reduced_sum.shape) != (S, d):
+        raise ValueError("block_tracker_stream: shape mismatch")
+    for name, t in (("U", U), ("projector_sum", projector_sum), ("reduced_sum", reduced_sum), ("x", x)):
+        if t.dtype != torch.float32:
+            raise RuntimeError(f"block_tracker_stream: {name} must be float32")
+        if t.device != U.device:
+            raise RuntimeError("block_tracker_stream: all tensors must be on one device")
+    for t in (U, projector_sum, reduced_sum):
+        if not t.is_contiguous():
+            raise ValueError("block_tracker_stream: state tensors must be contiguous (updated in place)")
+    x = x.contiguous()
+    with torch.cuda.device(U.device):
+        nat.call("gfst_block_tracker_stream", nat.ptr(U), nat.ptr(projector_sum), nat.ptr(reduced_sum), nat.ptr(x), S,
+                 T, d, r, float(rate), float(eps_update), float(eps_sign), _sign_mode(sign_mode), nat.stream_of(U))
+
+
+class BlockTracker:
+    """Batched block compressors: the reference's ``_GfstBlockCompressorState``
+    (state.py:99-107) driven by ``_update_block_memory`` (modeling.py:3401-3571):
+    per token the block basis update and the projector / token sums, and at
+    every ``block_len`` tokens the reference-faithful eigen commit
+    (``block_commit.gfst_block_commit``) followed by the reset of
+    ``_reset_block_tracker`` (modeling.py:2464-2484)."""
+
+    def __init__(self, n_streams: int, *, reduced_dim: int = 64, flag_dims: Sequence[int] = (8, 16, 32),
+                 forgetting_rates: Sequence[float] = (0.05, 0.10, 0.20), block_len: int = 64,
+                 eps_update: float = 1e-6, eps_sign: float = 1e-8, sign_mode="first_significant", device="cuda"):
+        self.n_streams, self.d = int(n_streams), int(reduced_dim)
+        self.flag_dims = tuple(int(v) for v in flag_dims)
+        self.r = self.flag_dims[-1]
+        self.rate = float(forgetting_rates[-1])
+        self.block_len = int(block_len)
+        self.eps_update, self.eps_sign, self.sign_mode = eps_update, eps_sign, sign_mode
+        self.device = torch.device(device)
+        self.reset()
+
+    def reset(self) -> None:
+        S, d, r = self.n_streams, self.d, self.r
+        self.largest_basis = torch.eye(d, r, device=self.device).expand(S, d, r).contiguous()
+        self.projector_sum = torch.zeros((S, d, d), device=self.device)
+        self.reduced_sum = torch.zeros((S, d), device=self.device)
+        self.current_block_tokens = 0
+
+    def step(self, x: torch.Tensor) -> list[tuple[torch.Tensor, ...]]:
+        """Consume tokens x [S, T, reduced_dim]; returns one (summary_basis,
+        reduced_mean, top_vector, average_projector) tuple per block closed."""
+        from . import block_commit
+
+        commits = []
+        t0, T = 0, int(x.shape[1])
+        while t0 < T:
+            n = min(T - t0, self.block_len - self.current_block_tokens)
+            block_tracker_stream(self.largest_basis, self.projector_sum, self.reduced_sum, x[:, t0:t0 + n],
+                                 rate=self.rate, eps_update=self.eps_update, eps_sign=self.eps_sign,
+                                 sign_mode=self.sign_mode)
+            self.current_block_tokens += n
+            t0 += n
+            if self.current_block_tokens == self.block_len:
+                commits.append(block_commit.gfst_block_commit(
+                    projector_sum=self.projector_sum, reduced_sum=self.reduced_sum, token_count=self.block_len,
+                    max_flag_dim=self.r, flag_dims=self.flag_dims, eps_sign=self.eps_sign))
+                self.reset()
+        return commits

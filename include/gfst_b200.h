@@ -24,6 +24,9 @@
  *                             src/gfst_hmb_mpuc/state.py:651-815 and the block summary of
  *                             GfstHmbSublayer._update_block_memory modeling.py:3482-3535
  *                             (summary key = mean of the block's token keys)
+ *   gfst_block_tracker_stream <- the per-token block tracker of GfstHmbSublayer._update_block_memory
+ *                             modeling.py:3460-3479 (rule update + QR, projector_sum += U U^T,
+ *                             reduced_sum += x)
  *   gfst_block_commit_eig  <- runtime_backends.gfst_block_commit(projector_sum, reduced_sum,
  *                             token_count, max_flag_dim, flag_dims) and its torch path
  *                             top_eig_summary, modeling.py:3482-3507, gfst.py:172-430,
@@ -127,6 +130,19 @@ GFST_API int gfst_local_tracker_stream(float* U, float* nested, const float* x, 
                               int T, int d, int r, int n_levels, const int32_t* dims,
                               const double* rates, double eps, double eps_update,
                               float eps_sign, int sign_mode, float* features,
+                              cudaStream_t stream);
+
+/* ---- block tracker: per-token accumulation of a block's commit inputs -----
+ * Per stream s and token t (x = x[s,t]): U <- QR_signfixed((1 - rate) U +
+ * rate x w^T + rate s e_last^T) with the rule of gfst_local_tracker_stream;
+ * projector_sum[s] += U U^T (d x d); reduced_sum[s] += x.  Inputs are updated
+ * in place, so a block can be fed in several calls; a new block starts from
+ * U = eye(d, r) and zero sums.  Replaces the per-token part of
+ * GfstHmbSublayer._update_block_memory (modeling.py:3460-3479) of the reference.
+ * Limits: d <= 64, d % 4 == 0, r % 4 == 0, r <= 32; x 16-byte aligned.      */
+GFST_API int gfst_block_tracker_stream(float* U, float* projector_sum, float* reduced_sum,
+                              const float* x, int64_t n_streams, int T, int d, int r,
+                              double rate, double eps_update, float eps_sign, int sign_mode,
                               cudaStream_t stream);
 
 /* ---- block commit ----------------------------------------------------------

@@ -180,6 +180,32 @@ def local_tracker_stream(U0: np.ndarray, nested0: list, xs: np.ndarray, flag_dim
     return U_out, V_out, feats, (snaps if out_every else None)
 
 
+def block_tracker_stream(U0: np.ndarray, projector_sum0: np.ndarray, reduced_sum0: np.ndarray, xs: np.ndarray,
+                         rate: float, eps_update: float = 1e-6, eps_sign: float = 1e-8,
+                         sign_mode: int = SIGN_FIRST_SIGNIFICANT):
+    """Per-token part of the block tracker, modeling.py:3460-3479: the rule
+    update at ``rate`` (forgetting_rates[-1]) and canonical QR of the block
+    basis, projector_sum += basis_projector(U) (gfst.py:143-144), reduced_sum +=
+    x; one tracker per stream in the reference's unbatched torch calls.
+    U0 [S, d, r], projector_sum0 [S, d, d], reduced_sum0 [S, d], xs [S, T, d]."""
+    xs = np.asarray(xs, np.float32)
+    S, T, _ = xs.shape
+    U_out = np.array(U0, np.float32, copy=True)
+    P_out = np.array(projector_sum0, np.float32, copy=True)
+    R_out = np.array(reduced_sum0, np.float32, copy=True)
+    for s in range(S):
+        U = torch.from_numpy(U_out[s].copy())
+        P = torch.from_numpy(P_out[s].copy())
+        R = torch.from_numpy(R_out[s].copy())
+        for t in range(T):
+            x = torch.from_numpy(xs[s, t].copy())
+            U = _canonical_qr_1(_residual_rank_one_candidate_2d(U, x, float(rate), eps_update), eps_sign, sign_mode)
+            P = P + U @ U.transpose(0, 1)
+            R = R + x
+        U_out[s], P_out[s], R_out[s] = U.numpy(), P.numpy(), R.numpy()
+    return U_out, P_out, R_out
+
+
 # frame metrics ---------------------------------------------------------------
 def orthogonality_error(Q: np.ndarray) -> np.ndarray:
     """max |Q^T Q - I| per frame (float64 arithmetic)."""

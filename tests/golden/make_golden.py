@@ -242,6 +242,31 @@ def main() -> None:
     Ua = gfst.canonical_qr(torch.randn((12, 4), generator=g))
     cases.append((gfst.basis_projector(Ua[:, :2]) + 2.0 * gfst.basis_projector(Ua[:, 2:]),
                   torch.randn((12,), generator=g), 3, 4, (2, 4)))
+    # a full block of the block tracker with its tokens kept: x, then the
+    # commit of its sums (modeling.py:3460-3507)
+    g = torch.Generator().manual_seed(300)
+    d, fds, T = 64, (8, 16, 32), 64
+    xs = torch.randn((3, T, d), generator=g)
+    trk = {"values": xs.numpy(), "flag_dims": np.array(fds)}
+    Us, Ps, Rs, bases, tops = [], [], [], [], []
+    for s in range(3):
+        U = torch.eye(d, 32)
+        ps = torch.zeros((d, d))
+        rs = torch.zeros((d,))
+        for t in range(T):
+            U = gfst.canonical_qr_batched(gfst.update_basis_candidate(U, xs[s, t], 0.20, eps_update=1e-6)
+                                          .unsqueeze(0), eps_sign=1e-8).squeeze(0)
+            ps = ps + gfst.basis_projector(U[:, :32])
+            rs = rs + xs[s, t]
+        rep = bcr.replay_block_commit_bundle(
+            {"projector_sum": ps, "reduced_sum": rs, "token_count": T, "max_flag_dim": 32, "flag_dims": fds,
+             "eps": 1e-6, "eps_sign": 1e-8, "block_key_proj_weight": None, "prefix_dims": fds},
+            implementation="native")
+        Us.append(U.numpy()); Ps.append(ps.numpy()); Rs.append(rs.numpy())
+        bases.append(rep["summary_basis"].numpy()); tops.append(rep["top_vector"].numpy())
+    np.savez(OUT / "block_tracker_pass.npz", **trk, largest_basis=np.stack(Us), projector_sum=np.stack(Ps),
+             reduced_sum=np.stack(Rs), summary_basis=np.stack(bases), top_vector=np.stack(tops))
+
     out = {}
     for ci, (ps, rs, T, r, fds) in enumerate(cases):
         bundle = {"projector_sum": ps, "reduced_sum": rs, "token_count": T, "max_flag_dim": r, "flag_dims": fds,

@@ -107,3 +107,68 @@ def test_tracker_rejects(cuda_device):
         tracker.LocalTracker(1, reduced_dim=30, flag_dims=(4, 8), forgetting_rates=(0.1, 0.2),
                              device=cuda_device).step(
             torch.randn(1, 2, 30, device=cuda_device))
+
+
+def test_block_tracker_matches_reference_pass(cuda_device):
+    # golden: one 64-token block of the reference's block tracker per stream
+    # (update + canonical QR + projector / token sums) and its native commit
+    z = np.load(GOLDEN / "block_tracker_pass.npz")
+    xs = torch.from_numpy(z["values"])
+    S, T, d = xs.shape
+    bt = tracker.BlockTracker(S, reduced_dim=d, flag_dims=tuple(int(v) for v in z["flag_dims"]), block_len=T,
+                              device=cuda_device)
+    bt.step(xs[:, :20].to(cuda_device))  # the block in three calls
+    bt.step(xs[:, 20:21].to(cuda_device))
+    np.testing.assert_allclose(_np(bt.largest_basis), go.block_tracker_stream(
+        np.broadcast_to(np.eye(d, 32, dtype=np.float32), (S, d, 32)), np.zeros((S, d, d), np.float32),
+        np.zeros((S, d), np.float32), z["values"][:, :21], 0.2)[0], atol=2e-4)
+    U_mid = bt.largest_basis.clone()
+    P_mid, R_mid = bt.projector_sum.clone(), bt.reduced_sum.clone()
+    commits = bt.step(xs[:, 21:].to(cuda_device))
+    assert len(commits) == 1 and bt.current_block_tokens == 0
+    # the sums at the end of the block, recomputed without the reset
+    U2, P2, R2 = U_mid.clone(), P_mid.clone(), R_mid.clone()
+    tracker.block_tracker_stream(U2, P2, R2, xs[:, 21:].to(cuda_device), rate=0.2)
+    np.testing.assert_allclose(_np(U2), z["largest_basis"], atol=2e-4)
+    np.testing.assert_allclose(_np(P2), z["projector_sum"], atol=1e-4)
+    assert np.array_equal(_np(R2), z["reduced_sum"])  # token sums in token order: bit-exact
+    basis, mean, top, avg = (_np(t) for t in commits[0])
+    assert np.array_equal(mean, z["reduced_sum"] / np.float32(T))
+    for s in range(S):  # the commit of slightly different fp32 sums: same subspaces
+        for k in (8, 16, 32):
+            pg = basis[s][:, :k] @ basis[s][:, :k].T
+            pr = z["summary_basis"][s][:, :k] @ z["summary_basis"][s][:, :k].T
+            assert np.abs(pg - pr).max() < 1e-3
+    # after the reset the tracker starts a fresh block
+    assert torch.equal(bt.largest_basis[0], torch.eye(d, 32, device=cuda_device))
+    assert bt.projector_sum.abs().max().item() == 0.0
+
+
+def test_block_tracker_chunking_is_bitwise(cuda_device):
+    g = torch.Generator().manual_seed(4)
+    S, d, r, T = 5, 32, 8, 24
+    xs = torch.randn((S, T, d), generator=g).to(cuda_device)
+    states = []
+    for cuts in ((T,), (5, 11, 8), (1,) * T):
+        U = torch.eye(d, r, device=cuda_device).expand(S, d, r).contiguous()
+        P = torch.zeros((S, d, d), device=cuda_device)
+        R = torch.zeros((S, d), device=cuda_device)
+        t0 = 0
+        for c in cuts:
+            tracker.block_tracker_stream(U, P, R, xs[:, t0:t0 + c], rate=0.15)
+            t0 += c
+        states.append((U, P, R))
+    for U, P, R in states[1:]:
+        assert torch.equal(U, states[0][0]) and torch.equal(P, states[0][1]) and torch.equal(R, states[0][2])
+    ref = go.block_tracker_stream(np.broadcast_to(np.eye(d, r, dtype=np.float32), (S, d, r)),
+                                  np.zeros((S, d, d), np.float32), np.zeros((S, d), np.float32), _np(xs), 0.15)
+    np.testing.assert_allclose(_np(states[0][0]), ref[0], atol=2e-4)
+    np.testing.assert_allclose(_np(states[0][1]), ref[1], atol=1e-4)
+    assert np.array_equal(_np(states[0][2]), ref[2])
+    P = _np(states[0][1])
+    assert np.array_equal(P, np.swapaxes(P, 1, 2))  # exactly symmetric
+
+
+def test_block_tracker_rejects(cuda_device):
+    with pytest.raises(RuntimeError):  # d > 64
+        tracker.BlockTracker(1, reduced_dim=128, device=cuda_device).step(torch.randn(1, 2, 128, device=cuda_device))
