@@ -14,6 +14,8 @@ the last launch.  CASE is one of:
   commit      one 64-token block commit per stream
   tracker     64 tokens of the local tracker (d=64, flag dims 8/16/32, nested levels + features)
   readout_long  exact-token readout of 1024 queries x 8 blocks of 128 tokens per stream out of 8192 blocks
+  commit_eig  reference-faithful block commit (float64 eigen summary) of 64 x 64 projector sums
+  block_tracker  one 64-token block of the block tracker (d=64, r=32: update + QR + projector sums)
 """
 from __future__ import annotations
 
@@ -22,7 +24,7 @@ import math
 
 import torch
 
-from . import gfst, memory, readout, retrieval, tracker, workloads as wl
+from . import block_commit, gfst, memory, readout, retrieval, tracker, workloads as wl
 
 
 def _timed(fn, repeat: int) -> float:
@@ -41,7 +43,7 @@ def _timed(fn, repeat: int) -> float:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
-                                         "readout_long"])
+                                         "readout_long", "commit_eig", "block_tracker"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     args = parser.parse_args()
@@ -82,6 +84,21 @@ def main() -> None:
         sel = torch.randint(0, 8192, (S, 1024, 8), generator=g, device=dev, dtype=torch.int32)
         ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel), args.repeat)
         units = f"{S * 1024 * 8 * 128 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bytes"
+    elif args.case == "commit_eig":
+        S = args.streams or 2048
+        Uq = torch.linalg.qr(torch.randn((S, 64, 32), generator=g, device=dev))[0]
+        ps = 64.0 * (Uq @ Uq.transpose(1, 2)) + 0.01 * torch.randn((S, 64, 64), generator=g, device=dev)
+        rs = torch.randn((S, 64), generator=g, device=dev)
+        ms = _timed(lambda: block_commit.gfst_block_commit(projector_sum=ps, reduced_sum=rs, token_count=64,
+                                                          max_flag_dim=32, flag_dims=(8, 16, 32)), args.repeat)
+        units = f"{S / ms / 1e3:.2f} M blocks/s"
+    elif args.case == "block_tracker":
+        S = args.streams or 2048
+        bt = tracker.BlockTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), block_len=1 << 30, device=dev)
+        x = torch.randn((S, 64, 64), generator=g, device=dev)
+        ms = _timed(lambda: tracker.block_tracker_stream(bt.largest_basis, bt.projector_sum, bt.reduced_sum, x,
+                                                         rate=0.2), args.repeat)
+        units = f"{S * 64 / ms / 1e3:.2f} M tokens/s"
     elif args.case == "tracker":
         S = args.streams or 2048
         tr = tracker.LocalTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), device=dev)
