@@ -91,3 +91,42 @@ def replay_block_commit_bundle(bundle: dict[str, Any], *, implementation: str = 
             "average_projector": cpu(avg), "summary_basis": cpu(basis),
             "prefix_projectors": {k: cpu(v) for k, v in prefix.items()},
             "reduced_mean": cpu(mean), "top_vector": cpu(top), "block_key": None if key is None else cpu(key)}
+
+
+def global_features(projector_bank: torch.Tensor, sel_idx: torch.Tensor, sel_scores: torch.Tensor, x: torch.Tensor,
+                    *, temperature: float = 1.0, flag_dims: Sequence[int] = (8, 16, 32), max_flag_dim: int | None = None,
+                    eps: float = 1e-6, eps_sign: float = 1e-8, return_sketch: bool = False,
+                    return_basis: bool = False):
+    """Global sketch features of every (stream, query): the torch branch of
+    GfstHmbSublayer._resolve_single_global_request (modeling.py:2996-3108) --
+    softmax-weighted sum of the selected blocks' summary projectors, its
+    canonical top eigen basis, alignment components over the flag dims -- on
+    the kernel ``gfst_global_features``.  projector_bank [S, NB, d, d];
+    sel_idx int32 / sel_scores float32 [S, Nq, K] (entries outside [0, NB) are
+    ignored); x [S, Nq, d].  Returns features [S, Nq, 2 * len(flag_dims)] (and the
+    sketch [S, Nq, d, d] / basis [S, Nq, d, max_flag_dim] when asked)."""
+    nat.require_cuda(projector_bank, sel_idx, sel_scores, x, what="global_features")
+    S, NB, d, _ = projector_bank.shape
+    Nq, K = int(sel_idx.shape[1]), int(sel_idx.shape[2])
+    if tuple(sel_scores.shape) != (S, Nq, K) or tuple(x.shape) != (S, Nq, d) or tuple(sel_idx.shape) != (S, Nq, K):
+        raise ValueError("global_features: shape mismatch")
+    if sel_idx.dtype != torch.int32 or projector_bank.dtype != torch.float32 or x.dtype != torch.float32 \
+            or sel_scores.dtype != torch.float32:
+        raise RuntimeError("global_features: float32 bank / scores / x and int32 indices expected")
+    dims = [int(v) for v in flag_dims]
+    mfd = int(max_flag_dim if max_flag_dim is not None else max(dims))
+    bank, idx, sc, xx = (t.contiguous() for t in (projector_bank, sel_idx, sel_scores, x))
+    feats = torch.empty((S, Nq, 2 * len(dims)), device=x.device, dtype=torch.float32)
+    sketch = torch.empty((S, Nq, d, d), device=x.device, dtype=torch.float32) if return_sketch else None
+    basis = torch.empty((S, Nq, d, mfd), device=x.device, dtype=torch.float32) if return_basis else None
+    dims_arr = (ctypes.c_int32 * len(dims))(*dims)
+    with torch.cuda.device(x.device):
+        nat.call("gfst_global_features", nat.ptr(bank), nat.ptr(idx), nat.ptr(sc), nat.ptr(xx), S, Nq, NB, d, K,
+                 float(temperature), mfd, ctypes.cast(dims_arr, ctypes.c_void_p), len(dims), float(eps),
+                 float(eps_sign), nat.ptr(feats), nat.ptr(sketch), nat.ptr(basis), nat.stream_of(x))
+    out = [feats]
+    if return_sketch:
+        out.append(sketch)
+    if return_basis:
+        out.append(basis)
+    return out[0] if len(out) == 1 else tuple(out)

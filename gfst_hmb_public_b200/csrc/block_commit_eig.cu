@@ -83,6 +83,11 @@ __device__ __forceinline__ void round_pair(int n, int r, int k, int& p, int& q) 
   q = a < b ? b : a;
 }
 
+struct GlobalDims {
+  int n;
+  int v[8];
+};
+
 // first-significant-entry sign of one column (gfst.py:35-46): +1 or -1
 template <typename T>
 __device__ __forceinline__ T first_significant_sign(const T* col, int stride, int d, T eps_sign) {
@@ -93,33 +98,14 @@ __device__ __forceinline__ T first_significant_sign(const T* col, int stride, in
   return T(1);
 }
 
-__global__ void __launch_bounds__(kEigThreads) block_commit_eig_kernel(
-    const float* __restrict__ projector_sum, const float* __restrict__ reduced_sum, int d, float count, int rank,
-    int target, double eps_sign, float* __restrict__ summary_basis, float* __restrict__ reduced_mean,
-    float* __restrict__ top_vector, float* __restrict__ average_projector) {
-  extern __shared__ __align__(16) unsigned char dyn_raw[];
-  EigSmem& sm = *reinterpret_cast<EigSmem*>(dyn_raw);
-  const int64_t s = blockIdx.x;
+// The canonical top basis of the symmetric float64 matrix in sm.a (order d,
+// padded to even n): eigenpairs by Jacobi, clusters from the top, canonical
+// cluster bases (float64, in sm.fb), then the float32 basis with its signs
+// fixed again, written to fb32 [d][target] (which may alias sm.a once the
+// eigenpairs are known).  Every thread of the CTA calls; failures set sm.fail.
+__device__ void canonical_top_basis(EigSmem& sm, int d, int target, double eps_sign) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = d + (d & 1);  // even order for the tournament; a padded index is isolated
-  const float* ps = projector_sum + s * (int64_t)d * d;
-
-  // ---- average projector (float32), symmetrised in float32, widened ----
-  float* avg = reinterpret_cast<float*>(&sm.v[0][0]);  // scratch until V is set up
-  for (int e = tid; e < d * d; e += kEigThreads) {
-    const float x = __fdiv_rn(ps[e], count);
-    avg[e] = x;
-    average_projector[s * (int64_t)d * d + e] = x;
-  }
-  for (int i = tid; i < d; i += kEigThreads)
-    reduced_mean[s * d + i] = __fdiv_rn(reduced_sum[s * d + i], count);
-  if (tid == 0) sm.fail = 0;
-  __syncthreads();
-  for (int e = tid; e < n * n; e += kEigThreads) {
-    const int i = e / n, j = e % n;
-    sm.a[i][j] = (i < d && j < d) ? (double)(0.5f * __fadd_rn(avg[i * d + j], avg[j * d + i])) : 0.0;
-  }
-  __syncthreads();
+  const int n = d + (d & 1);
   for (int e = tid; e < n * n; e += kEigThreads) {
     const int i = e / n, j = e % n;
     sm.v[i][j] = i == j ? 1.0 : 0.0;
@@ -298,7 +284,7 @@ __global__ void __launch_bounds__(kEigThreads) block_commit_eig_kernel(
   }
   __syncthreads();
 
-  // ---- float32 basis, signs again (float32), outputs ----
+  // ---- float32 basis, signs again (float32) ----
   float* fb32 = reinterpret_cast<float*>(&sm.a[0][0]);  // [d][target], the matrix is no longer needed
   for (int e = tid; e < d * target; e += kEigThreads) {
     const int i = e / target, j = e % target;
@@ -310,11 +296,138 @@ __global__ void __launch_bounds__(kEigThreads) block_commit_eig_kernel(
     for (int i = 0; i < d; ++i) fb32[i * target + j] *= sg;
   }
   __syncthreads();
+}
+
+__global__ void __launch_bounds__(kEigThreads) block_commit_eig_kernel(
+    const float* __restrict__ projector_sum, const float* __restrict__ reduced_sum, int d, float count, int rank,
+    int target, double eps_sign, float* __restrict__ summary_basis, float* __restrict__ reduced_mean,
+    float* __restrict__ top_vector, float* __restrict__ average_projector) {
+  extern __shared__ __align__(16) unsigned char dyn_raw[];
+  EigSmem& sm = *reinterpret_cast<EigSmem*>(dyn_raw);
+  const int64_t s = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int n = d + (d & 1);  // even order for the tournament; a padded index is isolated
+  const float* ps = projector_sum + s * (int64_t)d * d;
+
+  // ---- average projector (float32), symmetrised in float32, widened ----
+  float* avg = reinterpret_cast<float*>(&sm.v[0][0]);  // scratch until V is set up
+  for (int e = tid; e < d * d; e += kEigThreads) {
+    const float x = __fdiv_rn(ps[e], count);
+    avg[e] = x;
+    average_projector[s * (int64_t)d * d + e] = x;
+  }
+  for (int i = tid; i < d; i += kEigThreads)
+    reduced_mean[s * d + i] = __fdiv_rn(reduced_sum[s * d + i], count);
+  if (tid == 0) sm.fail = 0;
+  __syncthreads();
+  for (int e = tid; e < n * n; e += kEigThreads) {
+    const int i = e / n, j = e % n;
+    sm.a[i][j] = (i < d && j < d) ? (double)(0.5f * __fadd_rn(avg[i * d + j], avg[j * d + i])) : 0.0;
+  }
+  __syncthreads();
+  canonical_top_basis(sm, d, target, eps_sign);
+  const float* fb32 = reinterpret_cast<const float*>(&sm.a[0][0]);
   for (int e = tid; e < d * rank; e += kEigThreads) {
     const int i = e / rank, j = e % rank;
     summary_basis[s * (int64_t)d * rank + e] = fb32[i * target + j];
   }
   for (int i = tid; i < d; i += kEigThreads) top_vector[s * d + i] = fb32[i * target];
+  if (tid == 0 && sm.fail) atomicExch(&g_commit_error, (unsigned)GFST_ERR_NUMERIC);
+}
+
+
+// ---------------------------------------------------------------------------
+// global sketch features (one CTA per (stream, query))
+// ---------------------------------------------------------------------------
+// weights = softmax(scores * temperature) over the valid selections; sketch =
+// sum_k w_k P[idx_k] (float32, k in order); the canonical top basis B of the
+// sketch as above; for each flag dim m: P_m = B[:, :m] B[:, :m]^T and
+// c_m = x^T P_m x / (x . x + eps); features = (c_m, c_m - c_{m-1}) pairs.
+__global__ void __launch_bounds__(kEigThreads) global_features_kernel(
+    const float* __restrict__ bank, const int32_t* __restrict__ sel_idx, const float* __restrict__ sel_scores,
+    const float* __restrict__ X, int n_queries, int n_blocks, int d, int k, float temperature, int rank, int target,
+    GlobalDims dims, float eps, double eps_sign, float* __restrict__ features, float* __restrict__ sketch_out,
+    float* __restrict__ basis_out) {
+  extern __shared__ __align__(16) unsigned char dyn_raw[];
+  EigSmem& sm = *reinterpret_cast<EigSmem*>(dyn_raw);
+  __shared__ float w[32];
+  __shared__ int bidx[32];
+  __shared__ float xs[kEigMaxD], ys[kEigMaxD];
+  __shared__ int n_sel;
+  const int64_t sq = blockIdx.x;  // (stream, query)
+  const int64_t s = sq / n_queries;
+  const int tid = threadIdx.x;
+  const int n = d + (d & 1);
+  // softmax over the valid selections (float32, max-subtracted)
+  if (tid == 0) {
+    int m = 0;
+    float mx = -INFINITY;
+    for (int j = 0; j < k; ++j) {
+      const int b = sel_idx[sq * k + j];
+      if (b >= 0 && b < n_blocks) {
+        const float z = sel_scores[sq * k + j] * temperature;
+        bidx[m] = b;
+        w[m] = z;
+        mx = fmaxf(mx, z);
+        ++m;
+      }
+    }
+    float sum = 0.f;
+    for (int j = 0; j < m; ++j) {
+      w[j] = expf(w[j] - mx);
+      sum += w[j];
+    }
+    for (int j = 0; j < m; ++j) w[j] = w[j] / sum;
+    n_sel = m;
+    sm.fail = 0;
+  }
+  for (int i = tid; i < d; i += kEigThreads) xs[i] = X[sq * d + i];
+  __syncthreads();
+  const int m = n_sel;
+  float* sketch = reinterpret_cast<float*>(&sm.v[0][0]);  // scratch until V is set up
+  for (int e = tid; e < d * d; e += kEigThreads) {
+    float acc = 0.f;
+    for (int j = 0; j < m; ++j) acc = __fadd_rn(acc, __fmul_rn(w[j], bank[((int64_t)s * n_blocks + bidx[j]) * d * d + e]));
+    sketch[e] = acc;
+    if (sketch_out != nullptr) sketch_out[sq * d * d + e] = acc;
+  }
+  __syncthreads();
+  for (int e = tid; e < n * n; e += kEigThreads) {
+    const int i = e / n, j = e % n;
+    sm.a[i][j] = (i < d && j < d) ? (double)(0.5f * __fadd_rn(sketch[i * d + j], sketch[j * d + i])) : 0.0;
+  }
+  __syncthreads();
+  canonical_top_basis(sm, d, target, eps_sign);
+  const float* fb32 = reinterpret_cast<const float*>(&sm.a[0][0]);
+  if (basis_out != nullptr)
+    for (int e = tid; e < d * rank; e += kEigThreads) basis_out[sq * d * rank + e] = fb32[(e / rank) * target + e % rank];
+  // x^T P_m x for every flag dim m (P_m formed entry by entry, column order)
+  float prev = 0.f;
+  float xx = 0.f;
+  for (int i = 0; i < d; ++i) xx = fmaf(xs[i], xs[i], xx);  // same order on every thread
+  const float denom = __fadd_rn(xx, eps);
+  for (int f = 0; f < dims.n; ++f) {
+    const int mdim = dims.v[f];
+    for (int i = tid; i < d; i += kEigThreads) {
+      float y = 0.f;
+      for (int j = 0; j < d; ++j) {
+        float pij = 0.f;
+        for (int c = 0; c < mdim; ++c) pij = fmaf(fb32[i * target + c], fb32[j * target + c], pij);
+        y = fmaf(pij, xs[j], y);
+      }
+      ys[i] = y;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float num = 0.f;
+      for (int i = 0; i < d; ++i) num = fmaf(xs[i], ys[i], num);
+      const float cum = m > 0 ? __fdiv_rn(num, denom) : 0.f;
+      features[sq * 2 * dims.n + 2 * f] = cum;
+      features[sq * 2 * dims.n + 2 * f + 1] = __fsub_rn(cum, prev);
+      prev = cum;
+    }
+    __syncthreads();
+  }
   if (tid == 0 && sm.fail) atomicExch(&g_commit_error, (unsigned)GFST_ERR_NUMERIC);
 }
 
@@ -349,4 +462,37 @@ extern "C" int gfst_block_commit_eig(const float* projector_sum, const float* re
       projector_sum, reduced_sum, d, (float)token_count, max_flag_dim, target, eps_sign, summary_basis, reduced_mean,
       top_vector, average_projector);
   return check_launch("block_commit_eig_kernel");
+}
+
+extern "C" int gfst_global_features(const float* projector_bank, const int32_t* sel_idx, const float* sel_scores,
+                                    const float* x, int64_t n_streams, int n_queries, int n_blocks, int d, int k,
+                                    float temperature, int max_flag_dim, const int32_t* flag_dims, int n_flags,
+                                    float eps, double eps_sign, float* features, float* sketch_out,
+                                    float* basis_out, cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(n_streams >= 0 && n_queries >= 0 && n_blocks >= 0, GFST_ERR_ARG, "negative size");
+  GFST_REQUIRE(d >= 1 && d <= kEigMaxD, GFST_ERR_SHAPE, "d=%d outside [1, %d]", d, kEigMaxD);
+  GFST_REQUIRE(k >= 1 && k <= 32, GFST_ERR_SHAPE, "k=%d outside [1, 32]", k);
+  GFST_REQUIRE(max_flag_dim >= 1 && max_flag_dim <= d, GFST_ERR_SHAPE, "max_flag_dim=%d outside [1, d]",
+               max_flag_dim);
+  GFST_REQUIRE(n_flags >= 1 && n_flags <= 8 && flag_dims != nullptr, GFST_ERR_SHAPE, "need 1..8 flag dims");
+  GlobalDims dims{};
+  dims.n = n_flags;
+  int target = max_flag_dim;
+  for (int i = 0; i < n_flags; ++i) {
+    GFST_REQUIRE(flag_dims[i] >= 1 && flag_dims[i] <= d, GFST_ERR_SHAPE, "flag dim %d outside [1, d]", flag_dims[i]);
+    dims.v[i] = flag_dims[i];
+    target = flag_dims[i] > target ? flag_dims[i] : target;
+  }
+  if (n_streams == 0 || n_queries == 0) return GFST_OK;
+  GFST_REQUIRE(sel_idx && sel_scores && x && features && (projector_bank || n_blocks == 0), GFST_ERR_ARG,
+               "null buffer");
+  GFST_REQUIRE(n_streams * (int64_t)n_queries <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many requests");
+  const size_t smem = sizeof(EigSmem);
+  cudaError_t e = cudaFuncSetAttribute(global_features_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  global_features_kernel<<<(unsigned)(n_streams * n_queries), kEigThreads, smem, stream>>>(
+      projector_bank, sel_idx, sel_scores, x, n_queries, n_blocks, d, k, temperature, max_flag_dim, target, dims,
+      eps, eps_sign, features, sketch_out, basis_out);
+  return check_launch("global_features_kernel");
 }

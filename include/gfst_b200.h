@@ -31,6 +31,9 @@
  *                             token_count, max_flag_dim, flag_dims) and its torch path
  *                             top_eig_summary, modeling.py:3482-3507, gfst.py:172-430,
  *                             diagnostics/block_commit_replay.py:97-181
+ *   gfst_global_features   <- GfstHmbSublayer._resolve_single_global_request (torch branch)
+ *                             modeling.py:2996-3108: global sketch, top_eig_summary,
+ *                             alignment_components (gfst.py:389-430, 580-588)
  *   gfst_block_topk        <- FaissGpuRetriever.search / exact_topk
  *                             src/gfst_hmb_mpuc/retrieval.py:136-172
  *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
@@ -178,6 +181,24 @@ GFST_API int gfst_block_commit_eig(const float* projector_sum, const float* redu
                           const int32_t* flag_dims, int n_flags, double eps_sign,
                           float* summary_basis, float* reduced_mean, float* top_vector,
                           float* average_projector, cudaStream_t stream);
+
+/* ---- global sketch features per query --------------------------------------
+ * For every stream s and query q, over the selections j with 0 <= sel_idx[s,q,j]
+ * < n_blocks: w = softmax(sel_scores[s,q,j] * temperature); sketch = sum_j w_j
+ * projector_bank[s, sel_idx[s,q,j]] (d x d); B = the canonical top basis of the
+ * sketch (as gfst_block_commit_eig, T = max(max_flag_dim, max(flag_dims)));
+ * for each flag dim m: c_m = x^T B_m B_m^T x / (x . x + eps);
+ * features[s,q] = (c_0, c_0, c_1, c_1 - c_0, ...) (2 n_flags floats; zeros when
+ * no selection is valid).  Optional outputs: sketch_out [S, Nq, d, d],
+ * basis_out [S, Nq, d, max_flag_dim].  projector_bank: [n_streams, n_blocks, d, d];
+ * sel_idx, sel_scores: [n_streams, n_queries, k]; x: [n_streams, n_queries, d].
+ * Limits: d <= 64, k <= 32, 1 <= n_flags <= 8.                              */
+GFST_API int gfst_global_features(const float* projector_bank, const int32_t* sel_idx,
+                          const float* sel_scores, const float* x, int64_t n_streams,
+                          int n_queries, int n_blocks, int d, int k, float temperature,
+                          int max_flag_dim, const int32_t* flag_dims, int n_flags, float eps,
+                          double eps_sign, float* features, float* sketch_out, float* basis_out,
+                          cudaStream_t stream);
 
 /* ---- coarse block retrieval: score + top-k ---------------------------------
  * For every stream s and query q:

@@ -300,6 +300,66 @@ def _cluster_basis(cluster: torch.Tensor, target_rank: int, eps: float, eps_sign
     return _first_significant_signs(torch.stack(cols[:target_rank], dim=1), eps_sign)
 
 
+def _canonical_top_basis(sketch: torch.Tensor, target: int, eps_sign: float) -> torch.Tensor:
+    """gfst.py:389-430 (top_eig_summary's full_basis): symmetrise in float32,
+    float64 eigh, clusters walked from the top, each replaced by its canonical
+    basis (gfst.py:232-297), float32 with signs fixed again."""
+    sym = (0.5 * (sketch + sketch.transpose(0, 1))).to(torch.float64)
+    vals, vecs = torch.linalg.eigh(sym)
+    rank = max(0, min(int(target), vecs.shape[0]))
+    parts, remaining, end = [], rank, vals.shape[0] - 1
+    while end >= 0 and remaining > 0:
+        start = end
+        while start > 0 and abs(float(vals[start - 1]) - float(vals[start])) <= \
+                EIG_CLUSTER_ATOL + EIG_CLUSTER_RTOL * abs(float(vals[start])):
+            start -= 1
+        take = min(end - start + 1, remaining)
+        parts.append(_cluster_basis(vecs[:, start:end + 1], take, 1e-9, eps_sign))
+        remaining -= take
+        end = start - 1
+    return _first_significant_signs(torch.cat(parts, dim=1).to(torch.float32), eps_sign)
+
+
+def global_features(bank, sel_idx, sel_scores, x, temperature: float, flag_dims, max_flag_dim: int,
+                    eps: float = 1e-6, eps_sign: float = 1e-8):
+    """Global sketch features per (stream, query), the torch branch of
+    _resolve_single_global_request (modeling.py:2996-3108): w = softmax(scores *
+    temperature) over the valid selections, sketch = sum_k w_k P[idx_k],
+    top_eig_summary's canonical basis B, prefix projectors 0.5 (B_m B_m^T +
+    (B_m B_m^T)^T), alignment_components (gfst.py:580-588).  bank [S, NB, d, d],
+    sel_idx / sel_scores [S, Nq, K], x [S, Nq, d].  Returns (features [S, Nq, 2F],
+    basis [S, Nq, d, max_flag_dim])."""
+    bank = torch.as_tensor(np.asarray(bank, np.float32))
+    sel_idx = np.asarray(sel_idx)
+    scores = torch.as_tensor(np.asarray(sel_scores, np.float32))
+    x = torch.as_tensor(np.asarray(x, np.float32))
+    S, Nq, _ = sel_idx.shape
+    d = bank.shape[-1]
+    target = max(int(max_flag_dim), max(int(m) for m in flag_dims), 1)
+    feats = np.zeros((S, Nq, 2 * len(flag_dims)), np.float32)
+    bases = np.zeros((S, Nq, d, int(max_flag_dim)), np.float32)
+    for s in range(S):
+        for q in range(Nq):
+            valid = [j for j in range(sel_idx.shape[2]) if 0 <= int(sel_idx[s, q, j]) < bank.shape[1]]
+            if not valid:
+                continue
+            w = torch.softmax(scores[s, q, valid] * float(temperature), dim=0)
+            sketch = torch.einsum("k,kij->ij", w, bank[s, [int(sel_idx[s, q, j]) for j in valid]])
+            full = _canonical_top_basis(sketch, target, eps_sign)
+            v = x[s, q]
+            denom = torch.dot(v, v) + eps
+            cum = []
+            for m in flag_dims:
+                p = full[:, : int(m)] @ full[:, : int(m)].transpose(0, 1)
+                p = 0.5 * (p + p.transpose(0, 1))
+                cum.append(torch.dot(v, p @ v) / denom)
+            c = torch.stack(cum)
+            prev = torch.cat((torch.zeros_like(c[:1]), c[:-1]))
+            feats[s, q] = torch.stack((c, c - prev), dim=-1).reshape(-1).numpy()
+            bases[s, q] = full[:, : int(max_flag_dim)].numpy()
+    return feats, bases
+
+
 def block_commit_eig(projector_sum, reduced_sum, token_count: int, max_flag_dim: int, flag_dims,
                      eps_sign: float = 1e-8):
     """Reference-faithful block commit for one block: replay_block_commit_bundle
@@ -314,21 +374,8 @@ def block_commit_eig(projector_sum, reduced_sum, token_count: int, max_flag_dim:
     rs = torch.as_tensor(np.asarray(reduced_sum, np.float32))
     avg = ps / float(token_count)
     mean = rs / float(token_count)
-    sym = (0.5 * (avg + avg.transpose(0, 1))).to(torch.float64)
-    vals, vecs = torch.linalg.eigh(sym)
     target = max(int(max_flag_dim), max((int(b) for b in flag_dims), default=0), 1)
-    rank = max(0, min(target, vecs.shape[0]))
-    parts, remaining, end = [], rank, vals.shape[0] - 1
-    while end >= 0 and remaining > 0:
-        start = end
-        while start > 0 and abs(float(vals[start - 1]) - float(vals[start])) <= \
-                EIG_CLUSTER_ATOL + EIG_CLUSTER_RTOL * abs(float(vals[start])):
-            start -= 1
-        take = min(end - start + 1, remaining)
-        parts.append(_cluster_basis(vecs[:, start:end + 1], take, 1e-9, eps_sign))
-        remaining -= take
-        end = start - 1
-    full = _first_significant_signs(torch.cat(parts, dim=1).to(torch.float32), eps_sign)
+    full = _canonical_top_basis(avg, target, eps_sign)
     basis = full[:, : max(0, min(int(max_flag_dim), full.shape[1]))]
     top = full[:, 0] if full.shape[1] > 0 else torch.zeros(ps.shape[0])
     return basis.numpy(), mean.numpy(), top.numpy(), avg.numpy()

@@ -267,6 +267,31 @@ def main() -> None:
     np.savez(OUT / "block_tracker_pass.npz", **trk, largest_basis=np.stack(Us), projector_sum=np.stack(Ps),
              reduced_sum=np.stack(Rs), summary_basis=np.stack(bases), top_vector=np.stack(tops))
 
+    # 10. global sketch features, the non-accelerated branch of
+    #     _resolve_single_global_request (modeling.py:2996-3108): softmax of the
+    #     final scores, einsum of the selected summary projectors, top_eig_summary,
+    #     alignment_components over the flag dims (gfst.py:389-430, 580-588)
+    g = torch.Generator().manual_seed(400)
+    S, NB, d, K, NQ, fds = 2, 40, 64, 8, 6, (8, 16, 32)
+    bank = torch.stack([torch.stack([gfst.basis_projector(torch.linalg.qr(torch.randn((d, 32), generator=g))[0])
+                                     for _ in range(NB)]) for _ in range(S)])
+    sel = torch.stack([torch.stack([torch.randperm(NB, generator=g)[:K] for _ in range(NQ)]) for _ in range(S)])
+    scores = 2.0 * torch.randn((S, NQ, K), generator=g)
+    xg = torch.randn((S, NQ, d), generator=g)
+    feats = torch.zeros((S, NQ, 2 * len(fds)))
+    bases = torch.zeros((S, NQ, d, 32))
+    for s_i in range(S):
+        for q in range(NQ):
+            w = torch.softmax(scores[s_i, q] * float(1.0), dim=0)
+            sketch = torch.einsum("k,kij->ij", w, bank[s_i, sel[s_i, q]])
+            summ = gfst.top_eig_summary(sketch, rank=32, rank_boundaries=fds)
+            pp = {int(k): v for k, v in dict(summ["prefix_projectors"]).items()}
+            feats[s_i, q] = gfst.alignment_components(
+                xg[s_i, q], [pp.get(int(m), gfst.basis_projector(summ["basis"][:, :m])) for m in fds], 1e-6)
+            bases[s_i, q] = summ["basis"]
+    np.savez(OUT / "global_features.npz", bank=bank.numpy(), sel=sel.numpy().astype(np.int32), scores=scores.numpy(),
+             x=xg.numpy(), flag_dims=np.array(fds), features=feats.numpy(), basis=bases.numpy())
+
     out = {}
     for ci, (ps, rs, T, r, fds) in enumerate(cases):
         bundle = {"projector_sum": ps, "reduced_sum": rs, "token_count": T, "max_flag_dim": r, "flag_dims": fds,

@@ -127,3 +127,38 @@ def test_block_commit_rejects(cuda_device):
     with pytest.raises(RuntimeError):
         block_commit.gfst_block_commit(projector_sum=torch.zeros((4, 4)), reduced_sum=torch.zeros(4),
                                        token_count=1, max_flag_dim=2, flag_dims=(2,))
+
+
+def test_global_features_match_reference_branch(cuda_device):
+    z = np.load(GOLDEN / "global_features.npz")
+    dims = [int(v) for v in z["flag_dims"]]
+    feats, sketch, basis = block_commit.global_features(
+        torch.from_numpy(z["bank"]).to(cuda_device), torch.from_numpy(z["sel"]).to(cuda_device),
+        torch.from_numpy(z["scores"]).to(cuda_device), torch.from_numpy(z["x"]).to(cuda_device),
+        temperature=1.0, flag_dims=dims, return_sketch=True, return_basis=True)
+    # softmax and the weighted sum round differently from torch's CPU kernels
+    # (float32, ~1e-7); the eigen basis follows to ~1e-6 and the features to ~1e-6
+    np.testing.assert_allclose(feats.cpu().numpy(), z["features"], atol=1e-5)
+    for s in range(basis.shape[0]):
+        for q in range(basis.shape[1]):
+            for m in dims:
+                bg = basis[s, q, :, :m].cpu().numpy()
+                br = z["basis"][s, q, :, :m]
+                assert np.abs(bg @ bg.T - br @ br.T).max() < 1e-4
+    assert _native.load().gfst_check_device_errors(1) == 0
+
+
+def test_global_features_invalid_selections(cuda_device):
+    # selections outside the bank are ignored; a query with none gets zeros
+    g = torch.Generator().manual_seed(8)
+    S, NB, d, K = 1, 6, 16, 4
+    Q = torch.linalg.qr(torch.randn((S, NB, d, 4), generator=g))[0]
+    bank = Q @ Q.transpose(-1, -2)
+    sel = torch.tensor([[[0, 3, -1, 9], [-1, -1, -1, -1], [5, 5, 2, 1]]], dtype=torch.int32)
+    scores = torch.randn((S, 3, K), generator=g)
+    x = torch.randn((S, 3, d), generator=g)
+    feats = block_commit.global_features(bank.to(cuda_device), sel.to(cuda_device), scores.to(cuda_device),
+                                         x.to(cuda_device), flag_dims=(2, 4))
+    ref, _ = go.global_features(bank.numpy(), sel.numpy(), scores.numpy(), x.numpy(), 1.0, (2, 4), 4)
+    np.testing.assert_allclose(feats.cpu().numpy(), ref, atol=1e-5)
+    assert (feats[0, 1] == 0).all()

@@ -146,3 +146,12 @@ def test_block_commit_eig_matches_reference_replays():
     b, m, t, a = go.block_commit_eig(z["projector_sum"], z["reduced_sum"], int(z["token_count"]), 4,
                                      [int(v) for v in z["flag_dims"]])
     assert np.array_equal(b, z["summary_basis"]) and np.array_equal(t, z["top_vector"])
+
+
+def test_global_features_match_reference_branch():
+    # golden: softmax + einsum + top_eig_summary + alignment_components, the
+    # torch branch of _resolve_single_global_request (modeling.py:2996-3108)
+    z = load("global_features.npz")
+    f, b = go.global_features(z["bank"], z["sel"], z["scores"], z["x"], 1.0, [int(v) for v in z["flag_dims"]], 32)
+    assert np.array_equal(f, z["features"])
+    assert np.array_equal(b, z["basis"])
