@@ -41,3 +41,31 @@ def exact_readout(Q: torch.Tensor, pool_K: torch.Tensor, pool_V: torch.Tensor | 
                  n_slots, L, d, dv, k, nat.dtype_code(Q.dtype, "exact_readout"), nat.ptr(best_tok),
                  nat.ptr(best_score), nat.ptr(out_V), nat.stream_of(Q))
     return best_tok, best_score, out_V
+
+
+def exact_readout_collapse(Q: torch.Tensor, pool_K: torch.Tensor, token_ids: torch.Tensor, top_idx: torch.Tensor):
+    """The readout with the reference's log-sum-exp collapse of duplicate token
+    ids (perf.py:164-229 collapse_logsumexp_scores_and_occurrence, then the
+    select of modeling.py:1151-1169): Q [S, Nq, d]; pool_K [S, n_slots, L, d];
+    token_ids [S, n_slots, L] int32 (the id stored at each position, < 0 =
+    padding); top_idx [S, Nq, k].  Returns (best_id, best_score, best_block,
+    best_pos), each [S, Nq]: the winning token id, its group score and the
+    (block, position) of its best occurrence."""
+    nat.require_cuda(Q, pool_K, token_ids, top_idx, what="exact_readout_collapse")
+    S, Nq, d = Q.shape
+    _, n_slots, L, dk = pool_K.shape
+    if dk != d or tuple(token_ids.shape) != (S, n_slots, L) or tuple(top_idx.shape[:2]) != (S, Nq):
+        raise ValueError("exact_readout_collapse: shape mismatch")
+    if Q.dtype != pool_K.dtype:
+        raise RuntimeError("exact_readout_collapse: Q and pool_K must share a dtype")
+    k = top_idx.shape[2]
+    Q, pool_K = Q.contiguous(), pool_K.contiguous()
+    ids = token_ids.to(torch.int32).contiguous()
+    sel = top_idx.to(torch.int32).contiguous()
+    out = [torch.empty((S, Nq), dtype=dt, device=Q.device)
+           for dt in (torch.int32, torch.float32, torch.int32, torch.int32)]
+    with torch.cuda.device(Q.device):
+        nat.call("gfst_exact_readout_collapse", nat.ptr(Q), nat.ptr(pool_K), nat.ptr(ids), nat.ptr(sel), S, Nq,
+                 n_slots, L, d, k, nat.dtype_code(Q.dtype, "exact_readout_collapse"), *(nat.ptr(t) for t in out),
+                 nat.stream_of(Q))
+    return tuple(out)

@@ -34,6 +34,9 @@
  *   gfst_global_features   <- GfstHmbSublayer._resolve_single_global_request (torch branch)
  *                             modeling.py:2996-3108: global sketch, top_eig_summary,
  *                             alignment_components (gfst.py:389-430, 580-588)
+ *   gfst_exact_readout_collapse <- the readout with perf.collapse_logsumexp_scores_and_occurrence
+ *                             (src/gfst_hmb_mpuc/perf.py:164-229) and the select of
+ *                             modeling.py:1151-1169 (duplicate token ids collapsed)
  *   gfst_block_topk        <- FaissGpuRetriever.search / exact_topk
  *                             src/gfst_hmb_mpuc/retrieval.py:136-172
  *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
@@ -181,6 +184,23 @@ GFST_API int gfst_block_commit_eig(const float* projector_sum, const float* redu
                           const int32_t* flag_dims, int n_flags, double eps_sign,
                           float* summary_basis, float* reduced_mean, float* top_vector,
                           float* average_projector, cudaStream_t stream);
+
+/* ---- exact readout with the token-id log-sum-exp collapse ------------------
+ * Candidates of query (s, q): the tokens of its selected blocks in selection
+ * order (a block listed twice counts once; entries < 0 or >= n_slots skipped),
+ * score = key . query (fp32 accumulate).  Grouped by token_ids[s, block, pos]
+ * (ids < 0 and NaN scores take no part): group score = m + log(max(sum
+ * exp(score - m), 1e-8)) with m the group max; the occurrence is the first
+ * candidate (selection order, then position) scoring m.  Output the best group
+ * (score descending, token id ascending): best_id, best_score, best_block,
+ * best_pos [n_streams, n_queries] (-1 / -inf when nothing qualifies).
+ * Q: [n_streams, n_queries, d]; pool_K: [n_streams, n_slots, L, d];
+ * token_ids: [n_streams, n_slots, L] int32; top_idx: [n_streams, n_queries, k].
+ * Limits: k * L <= 2048, d <= 256; dtype GFST_F32 or GFST_BF16.              */
+GFST_API int gfst_exact_readout_collapse(const void* Q, const void* pool_K, const int32_t* token_ids,
+                          const int32_t* top_idx, int64_t n_streams, int n_queries, int n_slots,
+                          int L, int d, int k, int dtype, int32_t* best_id, float* best_score,
+                          int32_t* best_block, int32_t* best_pos, cudaStream_t stream);
 
 /* ---- global sketch features per query --------------------------------------
  * For every stream s and query q, over the selections j with 0 <= sel_idx[s,q,j]

@@ -381,6 +381,67 @@ def block_commit_eig(projector_sum, reduced_sum, token_count: int, max_flag_dim:
     return basis.numpy(), mean.numpy(), top.numpy(), avg.numpy()
 
 
+def collapse_logsumexp(scores, token_ids, blocks, positions):
+    """perf.py:164-229 (collapse_logsumexp_scores_and_occurrence, native
+    branch), restated: unique token ids ascending; per group m = max, score =
+    m + log(max(sum exp(s - m), 1e-8)) with the sum in element order; the
+    occurrence is the first element scoring m.  float32."""
+    s = torch.as_tensor(np.asarray(scores, np.float32))
+    ids = torch.as_tensor(np.asarray(token_ids, np.int64))
+    uid, inv = torch.unique(ids, sorted=True, return_inverse=True)
+    g = int(uid.numel())
+    mx = s.new_full((g,), float("-inf"))
+    mx.scatter_reduce_(0, inv, s, reduce="amax", include_self=True)
+    stable = torch.exp(s - mx.index_select(0, inv))
+    sumexp = s.new_zeros((g,))
+    sumexp.scatter_add_(0, inv, stable)
+    gs = mx + sumexp.clamp_min(1e-8).log()
+    flat = torch.arange(s.numel())
+    cand = torch.where(s.eq(mx.index_select(0, inv)), flat, torch.full_like(flat, s.numel()))
+    first = torch.full((g,), s.numel(), dtype=torch.long)
+    first.scatter_reduce_(0, inv, cand, reduce="amin", include_self=True)
+    b = torch.as_tensor(np.asarray(blocks, np.int64)).index_select(0, first)
+    p = torch.as_tensor(np.asarray(positions, np.int64)).index_select(0, first)
+    return uid.numpy(), gs.numpy(), b.numpy(), p.numpy()
+
+
+def exact_readout_collapse(Q, pool_K, token_ids, top_idx):
+    """Readout with the token-id collapse: candidates = tokens of the selected
+    blocks in selection order (modeling.py:599-657; a block listed twice counts
+    once; ids < 0 and NaN scores left out), float32 scores key . q,
+    collapse_logsumexp, then the best group (score descending, id ascending;
+    modeling.py:1151-1169).  Returns (best_id, best_score, best_block, best_pos)."""
+    Q = np.asarray(Q, np.float32)
+    K = np.asarray(pool_K, np.float32)
+    ids = np.asarray(token_ids)
+    S, Nq, _ = Q.shape
+    L = K.shape[2]
+    out = (np.full((S, Nq), -1, np.int32), np.full((S, Nq), -np.inf, np.float32), np.full((S, Nq), -1, np.int32),
+           np.full((S, Nq), -1, np.int32))
+    for s in range(S):
+        for q in range(Nq):
+            seen, blocks = set(), []
+            for b in top_idx[s, q]:
+                b = int(b)
+                if 0 <= b < K.shape[1] and b not in seen:
+                    seen.add(b)
+                    blocks.append(b)
+            if not blocks:
+                continue
+            keys = torch.as_tensor(np.concatenate([K[s, b] for b in blocks]))
+            sc = (keys @ torch.as_tensor(Q[s, q])).numpy()
+            tid = np.concatenate([ids[s, b] for b in blocks])
+            blk = np.repeat(np.array(blocks), L)
+            pos = np.tile(np.arange(L), len(blocks))
+            keep = (tid >= 0) & ~np.isnan(sc)
+            if not keep.any():
+                continue
+            uid, gs, gb, gp = collapse_logsumexp(sc[keep], tid[keep], blk[keep], pos[keep])
+            w = int(np.lexsort((uid, -gs))[0])
+            out[0][s, q], out[1][s, q], out[2][s, q], out[3][s, q] = uid[w], gs[w], gb[w], gp[w]
+    return out
+
+
 # ---------------------------------------------------------------------------
 # top-k block select
 # ---------------------------------------------------------------------------

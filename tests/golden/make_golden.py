@@ -292,6 +292,32 @@ def main() -> None:
     np.savez(OUT / "global_features.npz", bank=bank.numpy(), sel=sel.numpy().astype(np.int32), scores=scores.numpy(),
              x=xg.numpy(), flag_dims=np.array(fds), features=feats.numpy(), basis=bases.numpy())
 
+    # 11. readout with the token-id collapse end to end: float32 token scores of
+    #     the selected blocks (modeling.py:599-657, k . q), the reference's
+    #     collapse_logsumexp_scores_and_occurrence (perf.py:164-229), best group
+    g = torch.Generator().manual_seed(500)
+    S, NS, L, d, Nq, K = 2, 20, 16, 32, 10, 4
+    poolc = torch.randn((S, NS, L, d), generator=g)
+    ids = torch.randint(0, 50, (S, NS, L), generator=g, dtype=torch.int32)
+    Qc = torch.randn((S, Nq, d), generator=g)
+    selc = torch.stack([torch.stack([torch.randperm(NS, generator=g)[:K] for _ in range(Nq)]) for _ in range(S)])
+    res = np.zeros((4, S, Nq), np.float64)
+    for s_i in range(S):
+        for q in range(Nq):
+            blocks = [int(b) for b in selc[s_i, q]]
+            keys = torch.cat([poolc[s_i, b] for b in blocks])
+            scs = keys @ Qc[s_i, q]
+            tid = torch.cat([ids[s_i, b] for b in blocks])
+            blk = torch.tensor(blocks).repeat_interleave(L)
+            pos = torch.arange(L).repeat(len(blocks))
+            uid, gsc, gbl, gpo = perf.collapse_logsumexp_scores_and_occurrence(scs, tid, blk, pos)
+            w = int(np.lexsort((uid.numpy(), -gsc.numpy()))[0])
+            res[:, s_i, q] = [int(uid[w]), float(gsc[w]), int(gbl[w]), int(gpo[w])]
+    np.savez(OUT / "readout_collapse_e2e.npz", pool_K=poolc.numpy(), token_ids=ids.numpy(), Q=Qc.numpy(),
+             top_idx=selc.numpy().astype(np.int32), best_id=res[0].astype(np.int32),
+             best_score=res[1].astype(np.float32), best_block=res[2].astype(np.int32),
+             best_pos=res[3].astype(np.int32))
+
     out = {}
     for ci, (ps, rs, T, r, fds) in enumerate(cases):
         bundle = {"projector_sum": ps, "reduced_sum": rs, "token_count": T, "max_flag_dim": r, "flag_dims": fds,

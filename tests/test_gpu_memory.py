@@ -6,6 +6,8 @@ selected block indices and exact-token argmax bit-exact wherever the oracle's
 margin to the runner-up exceeds 1e-3 relative; readout values exact copies;
 scores within 1e-5 relative (fp32 accumulation order only).
 """
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -296,3 +298,72 @@ def test_needle_queries_recover_the_needle(cuda_device):
     assert np.array_equal(got_i[ok], ref_i[ok])
     ref_tok, _, _, ok2 = go.exact_readout(_np(Q), _np(pool_K), None, got_i)
     assert np.array_equal(tok.cpu().numpy()[ok2], ref_tok[ok2])
+
+
+def _collapse_margin_ok(Q, pool_K, ids, sel, tol=1e-4):
+    """Queries whose best two token-id groups differ by more than tol (relative)."""
+    S, Nq = sel.shape[:2]
+    ok = np.ones((S, Nq), bool)
+    L = pool_K.shape[2]
+    for s in range(S):
+        for q in range(Nq):
+            blocks = []
+            for b in sel[s, q]:
+                if 0 <= int(b) < pool_K.shape[1] and int(b) not in blocks:
+                    blocks.append(int(b))
+            if not blocks:
+                continue
+            keys = np.concatenate([pool_K[s, b] for b in blocks]).astype(np.float64)
+            sc = keys @ Q[s, q].astype(np.float64)
+            tid = np.concatenate([ids[s, b] for b in blocks])
+            keep = (tid >= 0) & ~np.isnan(sc)
+            groups = {}
+            for t, v in zip(tid[keep], sc[keep]):
+                groups.setdefault(int(t), []).append(v)
+            g = sorted((np.log(np.sum(np.exp(np.array(v) - max(v)))) + max(v) for v in groups.values()), reverse=True)
+            if len(g) > 1:
+                ok[s, q] = abs(g[0] - g[1]) > tol * max(abs(g[0]), 1.0)
+    return ok
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_readout_collapse_matches_reference(cuda_device, dtype):
+    z = np.load(Path(__file__).resolve().parent / "golden" / "readout_collapse_e2e.npz")
+    Q = torch.from_numpy(z["Q"]).to(dtype)
+    pool = torch.from_numpy(z["pool_K"]).to(dtype)
+    got = readout.exact_readout_collapse(Q.to(cuda_device), pool.to(cuda_device),
+                                         torch.from_numpy(z["token_ids"]).to(cuda_device),
+                                         torch.from_numpy(z["top_idx"]).to(cuda_device))
+    if dtype == torch.float32:
+        ref = [z[k] for k in ("best_id", "best_score", "best_block", "best_pos")]
+    else:  # the reference on the bf16-rounded inputs
+        ref = go.exact_readout_collapse(_np(Q), _np(pool), z["token_ids"], z["top_idx"])
+    ok = _collapse_margin_ok(_np(Q), _np(pool), z["token_ids"], z["top_idx"])
+    assert ok.mean() > 0.8
+    for g_t, r_t in zip((got[0], got[2], got[3]), (ref[0], ref[2], ref[3])):
+        assert np.array_equal(g_t.cpu().numpy()[ok], r_t[ok])
+    np.testing.assert_allclose(got[1].cpu().numpy(), ref[1], rtol=1e-5, atol=1e-5)
+
+
+def test_readout_collapse_edge_cases(cuda_device):
+    # duplicate ids within and across blocks, padding ids, a NaN key, a block
+    # listed twice, an out-of-range selection, and a query with nothing valid
+    g = torch.Generator().manual_seed(6)
+    S, NS, L, d, Nq, k = 2, 12, 8, 16, 5, 4
+    pool = torch.randn((S, NS, L, d), generator=g)
+    ids = torch.randint(0, 6, (S, NS, L), generator=g, dtype=torch.int32)
+    ids[0, 3, :4] = -1
+    pool[1, 2, 5, 0] = float("nan")
+    Q = torch.randn((S, Nq, d), generator=g)
+    sel = torch.randint(0, NS, (S, Nq, k), generator=g, dtype=torch.int32)
+    sel[0, 1, 2] = sel[0, 1, 0]
+    sel[1, 3, 1] = NS + 4
+    sel[0, 4, :] = -1
+    got = readout.exact_readout_collapse(Q.to(cuda_device), pool.to(cuda_device), ids.to(cuda_device),
+                                         sel.to(cuda_device))
+    ref = go.exact_readout_collapse(Q.numpy(), pool.numpy(), ids.numpy(), sel.numpy())
+    ok = _collapse_margin_ok(Q.numpy(), pool.numpy(), ids.numpy(), sel.numpy())
+    for g_t, r_t in zip((got[0], got[2], got[3]), (ref[0], ref[2], ref[3])):
+        assert np.array_equal(g_t.cpu().numpy()[ok], r_t[ok])
+    assert got[0][0, 4].item() == -1 and got[2][0, 4].item() == -1
+    assert torch.isinf(got[1][0, 4]).item()

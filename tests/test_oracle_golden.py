@@ -155,3 +155,14 @@ def test_global_features_match_reference_branch():
     f, b = go.global_features(z["bank"], z["sel"], z["scores"], z["x"], 1.0, [int(v) for v in z["flag_dims"]], 32)
     assert np.array_equal(f, z["features"])
     assert np.array_equal(b, z["basis"])
+
+
+def test_readout_collapse_matches_reference():
+    z = load("readout_collapse.npz")
+    uid, gs, gb, gp = go.collapse_logsumexp(z["scores"], z["token_ids"], z["blocks"], z["positions"])
+    assert np.array_equal(uid, z["unique_ids"]) and np.array_equal(gs, z["grouped_scores"])
+    assert np.array_equal(gb, z["grouped_blocks"]) and np.array_equal(gp, z["grouped_positions"])
+    z = load("readout_collapse_e2e.npz")
+    out = go.exact_readout_collapse(z["Q"], z["pool_K"], z["token_ids"], z["top_idx"])
+    for got, key in zip(out, ("best_id", "best_score", "best_block", "best_pos")):
+        assert np.array_equal(got, z[key])
