@@ -41,6 +41,10 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_void_p, _c_float, _c_int64, _c_int, _c_int, _c_int, _c_int,
         _c_float, _c_int, _c_void_p, _c_int, _c_void_p,
     ],
+    "gfst_frame_stream_ex": [
+        _c_void_p, _c_void_p, _c_void_p, _c_float, _c_int64, _c_int, _c_int, _c_int, _c_int,
+        _c_float, _c_int, _c_void_p, _c_int, _c_int, _c_void_p,
+    ],
     "gfst_block_commit_mean": [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_void_p,

@@ -63,12 +63,14 @@ extern "C" int gfst_frame_update_qr(const float* U, const float* A, const float*
   return GFST_ERR_SHAPE;
 }
 
-extern "C" int gfst_frame_stream(float* U, const float* A, const float* B, float beta, int64_t n_frames, int T,
-                                 int d, int r, int m, float eps_sign, int sign_mode, float* frames_out,
-                                 int out_every, cudaStream_t stream) {
+extern "C" int gfst_frame_stream_ex(float* U, const float* A, const float* B, float beta, int64_t n_frames, int T,
+                                    int d, int r, int m, float eps_sign, int sign_mode, float* frames_out,
+                                    int out_every, int qr_method, cudaStream_t stream) {
   using namespace gfst;
   int st = check_frame_args(n_frames, d, r, m, sign_mode);
   if (st != GFST_OK) return st;
+  GFST_REQUIRE(qr_method == GFST_QR_AUTO || qr_method == GFST_QR_HOUSEHOLDER || qr_method == GFST_QR_CHOLESKY2,
+               GFST_ERR_ARG, "unknown qr_method %d", qr_method);
   GFST_REQUIRE(T >= 0, GFST_ERR_ARG, "T must be >= 0 (got %d)", T);
   GFST_REQUIRE(m >= 1, GFST_ERR_SHAPE, "streaming needs an update rank m >= 1");
   if (n_frames == 0 || T == 0) return GFST_OK;
@@ -81,7 +83,7 @@ extern "C" int gfst_frame_stream(float* U, const float* A, const float* B, float
 #define X(idx, D, R, RG, CG)                                                                                \
   case idx:                                                                                                 \
     return launch_stream<D, R, RG, CG>(U, A, B, beta, n_frames, T, d, r, m, eps_sign, sign_mode, frames_out, \
-                                    out_every, stream);
+                                    out_every, qr_method, stream);
     GFST_SHAPE_CASES(X)
 #undef X
     default:
@@ -89,4 +91,11 @@ extern "C" int gfst_frame_stream(float* U, const float* A, const float* B, float
   }
   set_last_error("no kernel for d=%d r=%d", d, r);
   return GFST_ERR_SHAPE;
+}
+
+extern "C" int gfst_frame_stream(float* U, const float* A, const float* B, float beta, int64_t n_frames, int T,
+                                 int d, int r, int m, float eps_sign, int sign_mode, float* frames_out,
+                                 int out_every, cudaStream_t stream) {
+  return gfst_frame_stream_ex(U, A, B, beta, n_frames, T, d, r, m, eps_sign, sign_mode, frames_out, out_every,
+                              GFST_QR_AUTO, stream);
 }

@@ -8,6 +8,7 @@
 //   src/gfst_hmb_mpuc/gfst.py:115-140    update_basis_candidate_batched (beta*U + A B^T form)
 //   src/gfst_hmb_mpuc/modeling.py:2299-2423  per-token largest-level tracker update
 #pragma once
+#include "frame_chol.cuh"
 #include "frame_qr.cuh"
 #include "frame_qr_launch.h"
 
@@ -126,6 +127,64 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>())
 }
 
 // ---------------------------------------------------------------------------
+// streaming with CholeskyQR2 (frame_chol.cuh): one frame per warp in block
+// rows, the Gram copy and R in shared memory next to the staged factors.
+// ---------------------------------------------------------------------------
+template <int DMAX, int RMAX, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 2)
+    frame_stream_chol_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
+                             float beta, int64_t n_frames, int T, int d, int r, int m, float eps_sign, int sign_mode,
+                             float* __restrict__ frames_out, int out_every, bool vec4) {
+  using CQ = FrameChol<DMAX, RMAX>;
+  extern __shared__ __align__(16) unsigned char chol_smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  typename CQ::Smem& sm = reinterpret_cast<typename CQ::Smem*>(chol_smem)[warp];
+  const int a_elems = d * m, b_elems = r * m;
+  const int tok_elems = a_elems + b_elems;  // multiple of 4 (host-checked)
+  float* my_stage = reinterpret_cast<float*>(chol_smem + WARPS * sizeof(typename CQ::Smem)) +
+                    (size_t)warp * 2 * tok_elems;
+
+  const int64_t f = (int64_t)blockIdx.x * WARPS + warp;
+  const bool valid = f < n_frames;
+  const int64_t fs = valid ? f : 0;
+  const size_t frame_elems = (size_t)d * r;
+  const float* Af = A + fs * (size_t)T * a_elems;
+  const float* Bf = B + fs * (size_t)T * b_elems;
+
+  auto issue = [&](int tok) {
+    if (valid && tok < T) {
+      float* dst = my_stage + (tok & 1) * tok_elems;
+      const float* srcA = Af + (size_t)tok * a_elems;
+      const float* srcB = Bf + (size_t)tok * b_elems;
+      for (int c = lane; c < a_elems / 4; c += 32) cp_async16(dst + 4 * c, srcA + 4 * c);
+      for (int c = lane; c < b_elems / 4; c += 32) cp_async16(dst + a_elems + 4 * c, srcB + 4 * c);
+    }
+    cp_async_commit();
+  };
+
+  typename CQ::Frame fr;
+  CQ::load(fr, U + fs * frame_elems, lane, d, r, valid, vec4);
+
+  issue(0);
+  for (int tok = 0; tok < T; ++tok) {
+    issue(tok + 1);
+    cp_async_wait_all_but_one();
+    __syncwarp();
+    const float* sA = my_stage + (tok & 1) * tok_elems;
+    if (beta != 1.f) CQ::scale(fr, beta);
+    if (valid) CQ::rank_update(fr, sA, sA + a_elems, lane, d, r, m);
+    CQ::qr(fr, sm, lane, eps_sign, sign_mode, r);
+    if (frames_out != nullptr && ((tok + 1) % out_every) == 0) {
+      const int64_t snap = (tok + 1) / out_every - 1;
+      CQ::store(fr, frames_out + (snap * n_frames + fs) * frame_elems, lane, d, r, valid, vec4);
+    }
+    __syncwarp();  // every lane is done with this stage buffer before it is refilled
+  }
+  CQ::store(fr, U + fs * frame_elems, lane, d, r, valid, vec4);
+}
+
+// ---------------------------------------------------------------------------
 // launchers (host)
 // ---------------------------------------------------------------------------
 
@@ -142,9 +201,37 @@ int launch_update(const float* U, const float* A, const float* B, float beta, fl
   return check_launch("frame_update_qr_kernel");
 }
 
+template <int DMAX, int RMAX>
+int launch_stream_chol(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
+                       float eps_sign, int sign_mode, float* frames_out, int out_every, cudaStream_t stream) {
+  using CQ = FrameChol<DMAX, RMAX>;
+  const int64_t blocks = (n + kWarps - 1) / kWarps;
+  GFST_REQUIRE(blocks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
+  const bool vec4 = (r % 4 == 0) && aligned16(U) && (frames_out == nullptr || aligned16(frames_out));
+  const size_t smem = kWarps * (sizeof(typename CQ::Smem) + 2 * (size_t)(d * m + r * m) * sizeof(float));
+  auto kern = frame_stream_chol_kernel<DMAX, RMAX, kWarps>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  kern<<<(unsigned)blocks, kWarps * 32, smem, stream>>>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode,
+                                                         frames_out, out_every, vec4);
+  return check_launch("frame_stream_chol_kernel");
+}
+
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
-                  float eps_sign, int sign_mode, float* frames_out, int out_every, cudaStream_t stream) {
+                  float eps_sign, int sign_mode, float* frames_out, int out_every, int qr_method,
+                  cudaStream_t stream) {
+  constexpr bool kChol = (DMAX == 64 || DMAX == 128) && (RMAX == 16 || RMAX == 32) && RG == 8 && CG == 4;
+  if constexpr (kChol) {
+    if (qr_method != GFST_QR_HOUSEHOLDER)
+      return launch_stream_chol<DMAX, RMAX>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode, frames_out,
+                                            out_every, stream);
+  } else {
+    GFST_REQUIRE(qr_method != GFST_QR_CHOLESKY2, GFST_ERR_SHAPE,
+                 "CholeskyQR2 streaming covers d in (32, 128] with 8 < r <= 32 (d=%d r=%d)", d, r);
+  }
   constexpr int GPW = 32 / (RG * CG);
   const int64_t per_block = kWarps * GPW;
   const int64_t blocks = (n + per_block - 1) / per_block;

@@ -13,9 +13,12 @@ template <int DMAX, int RMAX, int RG, int CG>
 int launch_update(const float* U, const float* A, const float* B, float beta, float* Uout, int64_t n, int d, int r,
                   int m, float eps_sign, int sign_mode, cudaStream_t stream);
 
+// qr_method: GFST_QR_AUTO (CholeskyQR2 where the class has it, else
+// Householder), GFST_QR_HOUSEHOLDER or GFST_QR_CHOLESKY2.
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
-                  float eps_sign, int sign_mode, float* frames_out, int out_every, cudaStream_t stream);
+                  float eps_sign, int sign_mode, float* frames_out, int out_every, int qr_method,
+                  cudaStream_t stream);
 
 // Capacity class index for (d, r): the first class with dmax >= d and the
 // column capacity of r; -1 if none (frame_qr.cu).

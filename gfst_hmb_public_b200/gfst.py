@@ -123,6 +123,9 @@ def gfst_local_qr(candidate_matrices: torch.Tensor, eps_sign: float) -> torch.Te
     return canonical_qr_batched(candidate_matrices, eps_sign=float(eps_sign))
 
 
+_QR_METHODS = {"auto": 0, "householder": 1, "cholesky2": 2}
+
+
 def stream_frames(
     U: torch.Tensor,
     A: torch.Tensor,
@@ -132,12 +135,16 @@ def stream_frames(
     eps_sign: float = 1e-8,
     sign_mode="first_significant",
     out_every: int = 0,
+    qr_method: str = "auto",
 ) -> torch.Tensor | None:
     """Run T tokens of ``U <- QR(beta*U + A_t B_t^T)`` with every frame held on chip.
 
     U: [F, d, r] float32, updated in place.  A: [F, T, d, m]; B: [F, T, r, m].
     With ``out_every > 0`` the frames after tokens out_every-1, 2*out_every-1, ...
     are returned as [T // out_every, F, d, r]; otherwise returns None.
+    ``qr_method``: "auto" (CholeskyQR2 for 32 < d <= 128 and 8 < r <= 32,
+    Householder otherwise), "householder" or "cholesky2" (a frame whose Gram
+    pivots fail the conditioning test falls back to Householder for that token).
     """
     nat.require_cuda(U, A, B, what="stream_frames")
     if U.ndim != 3 or A.ndim != 4 or B.ndim != 4:
@@ -158,9 +165,9 @@ def stream_frames(
         snaps = torch.empty((T // out_every, F, d, r), device=U.device, dtype=torch.float32)
     with torch.cuda.device(U.device):
         nat.call(
-            "gfst_frame_stream",
+            "gfst_frame_stream_ex",
             nat.ptr(U), nat.ptr(A), nat.ptr(B), float(beta), F, T, d, r, m, float(eps_sign),
-            _sign_mode(sign_mode), nat.ptr(snaps), int(out_every), nat.stream_of(U),
+            _sign_mode(sign_mode), nat.ptr(snaps), int(out_every), _QR_METHODS[qr_method], nat.stream_of(U),
         )
     return snaps
 

@@ -81,6 +81,19 @@ enum gfst_sign_mode {
   GFST_SIGN_R_DIAG_POSITIVE = 1
 };
 
+/* QR algorithm of the streaming frame pass (gfst_frame_stream_ex). */
+enum gfst_qr_method {
+  /* CholeskyQR2 for 32 < d <= 128 with 8 < r <= 32, Householder otherwise. */
+  GFST_QR_AUTO = 0,
+  /* LAPACK-order Householder (geqrf/orgqr) for every token. */
+  GFST_QR_HOUSEHOLDER = 1,
+  /* Two Cholesky QR passes per token (G = C^T C = R^T R, C <- C R^{-1});
+   * a frame whose pivot R_jj^2 falls below 1e-2 * G_jj (or is not finite)
+   * takes the Householder path for that token.  Same Q as Householder with
+   * R_jj > 0 to fp32 rounding; shapes outside the AUTO range are rejected. */
+  GFST_QR_CHOLESKY2 = 2
+};
+
 /* Element types of key / value / query / summary buffers. */
 enum gfst_dtype { GFST_F32 = 0, GFST_BF16 = 1 };
 
@@ -115,6 +128,14 @@ GFST_API int gfst_frame_stream(float* U, const float* A, const float* B, float b
                       int64_t n_frames, int T, int d, int r, int m,
                       float eps_sign, int sign_mode,
                       float* frames_out, int out_every, cudaStream_t stream);
+
+/* gfst_frame_stream with the QR algorithm chosen explicitly (gfst_qr_method);
+ * gfst_frame_stream is this call with GFST_QR_AUTO.  No reference
+ * counterpart: the reference factorises every token with torch.linalg.qr. */
+GFST_API int gfst_frame_stream_ex(float* U, const float* A, const float* B, float beta,
+                         int64_t n_frames, int T, int d, int r, int m,
+                         float eps_sign, int sign_mode,
+                         float* frames_out, int out_every, int qr_method, cudaStream_t stream);
 
 /* ---- local tracker: all flag levels + alignment features, T tokens --------
  * Per stream s and token t (x = x[s,t], a d-vector), with the reference rule
