@@ -27,11 +27,14 @@
 // chunks are XOR-swizzled per column (conflict-free tile and fragment loads).
 #pragma once
 
+#include <type_traits>
+
 #include "frame_qr.cuh"
 
 namespace gfst {
 
 constexpr float kPivotTol = 1e-2f;
+constexpr float kFirstOrderTol = 3e-4f;  // |E| bound for the first-order second pass
 
 template <int DMAX, int RMAX>
 struct FrameChol {
@@ -91,66 +94,26 @@ struct FrameChol {
     }
   }
 
-  // G = C^T C in FP32 from the column-major copy; lane (bi, bj) =
-  // (lane & 7, lane >> 3) owns rows [TI*bi, +TI) x columns [TJ*bj, +TJ) of G.
-  // Every entry sums the same products in the same order as its mirror, so G
-  // is exactly symmetric.
-  __device__ static __forceinline__ void gram_fp32(Smem& sm, int lane) {
-    const int bi = lane & 7, bj = lane >> 3;
-    float2 acc[TI][TJ];
-#pragma unroll
-    for (int i = 0; i < TI; ++i)
-#pragma unroll
-      for (int j = 0; j < TJ; ++j) acc[i][j] = make_float2(0.f, 0.f);
-    int offa[TI], swa[TI], offb[TJ], swb[TJ];
-#pragma unroll
-    for (int i = 0; i < TI; ++i) {
-      offa[i] = (TI * bi + i) * DMAX;
-      swa[i] = sw(TI * bi + i);
-    }
-#pragma unroll
-    for (int j = 0; j < TJ; ++j) {
-      offb[j] = (TJ * bj + j) * DMAX;
-      swb[j] = sw(TJ * bj + j);
-    }
-#pragma unroll 1
-    for (int ch = 0; ch < NCH; ++ch) {
-      float4 av[TI], bv[TJ];
-#pragma unroll
-      for (int i = 0; i < TI; ++i) av[i] = *reinterpret_cast<const float4*>(sm.mt + offa[i] + 4 * (ch ^ swa[i]));
-#pragma unroll
-      for (int j = 0; j < TJ; ++j) bv[j] = *reinterpret_cast<const float4*>(sm.mt + offb[j] + 4 * (ch ^ swb[j]));
-#pragma unroll
-      for (int i = 0; i < TI; ++i) {
-#pragma unroll
-        for (int j = 0; j < TJ; ++j) {
-          acc[i][j] = ffma2(make_float2(av[i].x, av[i].y), make_float2(bv[j].x, bv[j].y), acc[i][j]);
-          acc[i][j] = ffma2(make_float2(av[i].z, av[i].w), make_float2(bv[j].z, bv[j].w), acc[i][j]);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < TI; ++i) {
-#pragma unroll
-      for (int j = 0; j < TJ; j += 4) {
-        *reinterpret_cast<float4*>(sm.g + (TI * bi + i) * GS + TJ * bj + j) =
-            make_float4(acc[i][j].x + acc[i][j].y, acc[i][j + 1].x + acc[i][j + 1].y,
-                        acc[i][j + 2].x + acc[i][j + 2].y, acc[i][j + 3].x + acc[i][j + 3].y);
-      }
-    }
-  }
-
-  // G = C^T C on the tensor cores in TF32 (inputs rounded to 11 significant
-  // bits, FP32 accumulation): good to about 1e-3 relative, which is all the
-  // first pass needs -- its R only has to leave C R^{-1} well conditioned; the
-  // second pass, in FP32, sets the result.  mma.sync m16n8k8: A = C^T rows
-  // (frame columns) 16*mt + g, +8; B = frame columns 8*nt + g; K = frame rows.
-  // Tiles (mt, nt) on or above the diagonal blocks; the two off-diagonal ones
-  // are mirrored on store.
+  // G = C^T C on the tensor cores (mma.sync m16n8k8, TF32 operands): each
+  // value x is split as hi + lo (hi = x rounded to TF32, lo = the rest rounded
+  // to TF32, |x - hi - lo| <= 2^-22 |x|) and every product is taken as
+  // lo*hi + hi*lo + hi*hi.  Each k-step (8 frame rows) sums its products in a
+  // fresh accumulator, added to the running sums in FP32, so the tensor
+  // cores' internal rounding applies to one step's partial sum only: G comes
+  // out to a few 1e-7 relative, like an FP32 dot product.
+  // A = C^T rows (frame columns) 16*mt + g and 16*mt + 8 + g, B = frame columns
+  // 8*nt + g, K = frame rows.  Tiles (mt, nt) on or above the diagonal blocks
+  // are computed and stored transposed (gT[n][m] = G[m][n]): row j of the
+  // area then holds G[i][j] for every i <= j, which is all the Cholesky of
+  // column j and the first-order correction read.
   __device__ static __forceinline__ uint32_t to_tf32(float x) {
     uint32_t y;
     asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(y) : "f"(x));
     return y;
+  }
+  __device__ static __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+    hi = to_tf32(x);
+    lo = to_tf32(x - __uint_as_float(hi));
   }
   __device__ static __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                   uint32_t b0, uint32_t b1) {
@@ -160,9 +123,10 @@ struct FrameChol {
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
-  __device__ static __forceinline__ void gram_tc(Smem& sm, int lane) {
-    constexpr int NQ = RMAX / 8;                  // frame-column groups of 8 (n tiles)
-    constexpr int NT = RMAX == 32 ? 6 : 2;        // tiles computed
+  __device__ static __forceinline__ void gram(Smem& sm, int lane) {
+    constexpr int NQ = RMAX / 8;            // frame-column groups of 8
+    constexpr int NT = RMAX == 32 ? 6 : 2;  // tiles computed
+    constexpr int MQ[6] = {0, 0, 0, 0, 2, 2}, NQI[6] = {0, 1, 2, 3, 2, 3};
     const int g = lane >> 2, t = lane & 3;
     int off[NQ], swz[NQ];
 #pragma unroll
@@ -175,35 +139,31 @@ struct FrameChol {
     for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll 2
     for (int ks = 0; ks < NCH / 2; ++ks) {
-      uint32_t x0[NQ], x1[NQ];  // frame column 8q+g at rows 8ks+t and 8ks+4+t
+      uint32_t h0[NQ], l0[NQ], h1[NQ], l1[NQ];  // frame column 8q+g at rows 8ks+t and 8ks+4+t
 #pragma unroll
       for (int q = 0; q < NQ; ++q) {
-        x0[q] = to_tf32(sm.mt[off[q] + 4 * ((2 * ks) ^ swz[q])]);
-        x1[q] = to_tf32(sm.mt[off[q] + 4 * ((2 * ks + 1) ^ swz[q])]);
+        split_tf32(sm.mt[off[q] + 4 * ((2 * ks) ^ swz[q])], h0[q], l0[q]);
+        split_tf32(sm.mt[off[q] + 4 * ((2 * ks + 1) ^ swz[q])], h1[q], l1[q]);
       }
-      // m-tile 0 = columns q 0, 1; m-tile 1 = columns q 2, 3
-      mma_tf32(acc[0], x0[0], x0[1], x1[0], x1[1], x0[0], x1[0]);
-      mma_tf32(acc[1], x0[0], x0[1], x1[0], x1[1], x0[1], x1[1]);
-      if constexpr (RMAX == 32) {
-        mma_tf32(acc[2], x0[0], x0[1], x1[0], x1[1], x0[2], x1[2]);
-        mma_tf32(acc[3], x0[0], x0[1], x1[0], x1[1], x0[3], x1[3]);
-        mma_tf32(acc[4], x0[2], x0[3], x1[2], x1[3], x0[2], x1[2]);
-        mma_tf32(acc[5], x0[2], x0[3], x1[2], x1[3], x0[3], x1[3]);
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        const int a = MQ[i], b = NQI[i];
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_tf32(c, l0[a], l0[a + 1], l1[a], l1[a + 1], h0[b], h1[b]);
+        mma_tf32(c, h0[a], h0[a + 1], h1[a], h1[a + 1], l0[b], l1[b]);
+        mma_tf32(c, h0[a], h0[a + 1], h1[a], h1[a + 1], h0[b], h1[b]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] += c[e];
       }
     }
-    // D fragment: (g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1) of the 16 x 8 tile
-    constexpr int MT[6] = {0, 0, 0, 0, 1, 1}, NTI[6] = {0, 1, 2, 3, 2, 3};
+    // D fragment: (g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1) of each 16 x 8 tile
 #pragma unroll
     for (int i = 0; i < NT; ++i) {
-      const int r0 = 16 * MT[i] + g, c0 = 8 * NTI[i] + 2 * t;
-      *reinterpret_cast<float2*>(sm.g + r0 * GS + c0) = make_float2(acc[i][0], acc[i][1]);
-      *reinterpret_cast<float2*>(sm.g + (r0 + 8) * GS + c0) = make_float2(acc[i][2], acc[i][3]);
-      if (NTI[i] >= 2 && MT[i] == 0) {  // mirror of the off-diagonal block
-        sm.g[c0 * GS + r0] = acc[i][0];
-        sm.g[(c0 + 1) * GS + r0] = acc[i][1];
-        sm.g[c0 * GS + r0 + 8] = acc[i][2];
-        sm.g[(c0 + 1) * GS + r0 + 8] = acc[i][3];
-      }
+      const int m0 = 8 * MQ[i] + g, n0 = 8 * NQI[i] + 2 * t;
+      sm.g[n0 * GS + m0] = acc[i][0];
+      sm.g[(n0 + 1) * GS + m0] = acc[i][1];
+      sm.g[n0 * GS + m0 + 8] = acc[i][2];
+      sm.g[(n0 + 1) * GS + m0 + 8] = acc[i][3];
     }
   }
 
@@ -288,23 +248,52 @@ struct FrameChol {
     });
   }
 
-  // One Cholesky QR pass in place; false (input kept in mt) if a pivot failed.
-  __device__ static __forceinline__ bool pass(Frame& f, Smem& sm, int lane, int r, bool first) {
-    __syncwarp();  // the previous pass's reads of mt and the Gram area are done
-    write_mt(f, sm, lane);
-    __syncwarp();
-    if (first) {
-      gram_tc(sm, lane);
-    } else {
-      gram_fp32(sm, lane);
+  // Largest |E_ij| (i <= j, over this lane's column j < r) of E = G - I,
+  // reduced over the warp (float bits order like the values; NaN is larger).
+  __device__ static __forceinline__ float gram_defect(const Smem& sm, int lane, int r) {
+    float e = 0.f;
+    if (lane < RMAX && lane < r) {
+#pragma unroll
+      for (int q = 0; q < RMAX; q += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(sm.g + lane * GS + q);
+        const float w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = q + u;
+          const float x = fabsf(i == lane ? w[u] - 1.f : w[u]);
+          if (i <= lane) e = (x > e || x != x) ? x : e;
+        }
+      }
     }
-    __syncwarp();
-    const bool ok = __all_sync(0xffffffffu, cholesky(sm, lane, r));
-    __syncwarp();
-    if (!ok) return false;
-    read_mt(f, sm, lane);
-    solve(f, sm);
-    return true;
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(e)));
+  }
+
+  // Second pass on a nearly orthonormal f (G = f^T f = I + E, |E| small):
+  // chol(I + E) = I + F + O(E^2) with F = triu(E) - diag(E)/2, so
+  // f <- f (I - F): column j becomes f_j (1 - E_jj/2) - sum_{i<j} f_i E_ij.
+  // Columns run from the last down (each reads only columns left of it), and
+  // the columns are independent of one another.
+  __device__ static __forceinline__ void correct(Frame& f, const Smem& sm) {
+    static_for_down<0, RMAX>([&](auto jc) {
+      constexpr int j = decltype(jc)::value;
+      float e[((j + 4) / 4) * 4];
+#pragma unroll
+      for (int q = 0; q <= j; q += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(sm.g + j * GS + q);
+        e[q] = v.x;
+        e[q + 1] = v.y;
+        e[q + 2] = v.z;
+        e[q + 3] = v.w;
+      }
+      const float fac = fmaf(-0.5f, e[j] - 1.f, 1.f);
+#pragma unroll
+      for (int p = 0; p < RPP; ++p) {
+        float2 s = __fmul2_rn(f[p][j], make_float2(fac, fac));
+#pragma unroll
+        for (int i = 0; i < j; ++i) s = ffma2(f[p][i], make_float2(-e[i], -e[i]), s);
+        f[p][j] = s;
+      }
+    });
   }
 
   // Householder QR (sign rule included) of the matrix held in mt -> f.
@@ -358,14 +347,30 @@ struct FrameChol {
         if ((flip >> c) & 1u) f[p][c] = make_float2(-f[p][c].x, -f[p][c].y);
   }
 
-  // In place: f <- sign-fixed thin Q.
+  // In place: f <- sign-fixed thin Q.  Pass 1: Gram, Cholesky, solve.  Pass 2
+  // on the nearly orthonormal result: Gram, then the first-order correction
+  // when |E| <= kFirstOrderTol (its error is O(|E|^2)), else a full Cholesky
+  // pass.  A failed pivot test sends the pass's input through Householder.
   __device__ static __forceinline__ void qr(Frame& f, Smem& sm, int lane, float eps_sign, int sign_mode, int r) {
-    bool ok = true;
 #pragma unroll 1
-    for (int ps = 0; ps < 2 && ok; ++ps) ok = pass(f, sm, lane, r, ps == 0);  // one copy of the pass code
-    if (!ok) {
-      householder(f, sm, lane, eps_sign, sign_mode, r);
-      return;
+    for (int ps = 0; ps < 2; ++ps) {  // one copy of the pass code
+      __syncwarp();  // the previous reads of mt and the Gram area are done
+      write_mt(f, sm, lane);
+      __syncwarp();
+      gram(sm, lane);
+      __syncwarp();
+      if (ps == 1 && gram_defect(sm, lane, r) <= kFirstOrderTol) {
+        correct(f, sm);
+        break;
+      }
+      const bool ok = __all_sync(0xffffffffu, cholesky(sm, lane, r));
+      __syncwarp();
+      if (!ok) {
+        householder(f, sm, lane, eps_sign, sign_mode, r);
+        return;
+      }
+      read_mt(f, sm, lane);
+      solve(f, sm);
     }
     // R = R2 R1 has a positive diagonal: the R-diagonal rule needs no flips
     if (sign_mode == GFST_SIGN_FIRST_SIGNIFICANT) first_significant(f, eps_sign);
@@ -434,9 +439,48 @@ struct FrameChol {
       for (int c = 0; c < RMAX; ++c) f[p][c] = __fmul2_rn(f[p][c], b2);
   }
 
-  // f += A B^T, A [d, m] and B [r, m] row-major (shared memory).
+  // f += A B^T, A [d, m] and B [r, m] row-major (shared memory).  m = 2, 4, 8:
+  // one vector load per row of A and of B per group of <= 4 update columns.
+  template <int MV>
+  __device__ static __forceinline__ void rank_update_vec(Frame& f, const float* A, const float* B, int lane, int d,
+                                                         int r, int m, int m0) {
+    using V = typename std::conditional<MV == 4, float4, float2>::type;
+    float av[RPL][MV];
+#pragma unroll
+    for (int q = 0; q < RPL; ++q) {
+      const int row = RPL * lane + q;
+      V v{};
+      if (row < d) v = *reinterpret_cast<const V*>(A + row * m + m0);
+      const float* pv = reinterpret_cast<const float*>(&v);
+#pragma unroll
+      for (int u = 0; u < MV; ++u) av[q][u] = pv[u];
+    }
+#pragma unroll
+    for (int c = 0; c < RMAX; ++c) {
+      V v{};
+      if (c < r) v = *reinterpret_cast<const V*>(B + c * m + m0);
+      const float* pb = reinterpret_cast<const float*>(&v);
+#pragma unroll
+      for (int p = 0; p < RPP; ++p) {
+        float2 acc = f[p][c];
+#pragma unroll
+        for (int u = 0; u < MV; ++u)
+          acc = ffma2(make_float2(av[2 * p][u], av[2 * p + 1][u]), make_float2(pb[u], pb[u]), acc);
+        f[p][c] = acc;
+      }
+    }
+  }
+
   __device__ static __forceinline__ void rank_update(Frame& f, const float* A, const float* B, int lane, int d, int r,
                                                      int m) {
+    if (m % 4 == 0) {  // rows of A and B are 16-byte aligned in the stage
+      for (int m0 = 0; m0 < m; m0 += 4) rank_update_vec<4>(f, A, B, lane, d, r, m, m0);
+      return;
+    }
+    if (m == 2) {
+      rank_update_vec<2>(f, A, B, lane, d, r, m, 0);
+      return;
+    }
     for (int mm = 0; mm < m; ++mm) {
       float2 a2[RPP];
 #pragma unroll
