@@ -4,8 +4,10 @@
 
 Workload (per GPU, weak scaling: every rank runs its own batch shard):
   stream_full -- B=64 batch x H=32 heads = 2048 streams, d=128 x r=32 fp32
-  frames updated per token by a rank-4 u v^T (u, v ~ N(0, 1/128)) then
-  Householder thin QR; bf16 keys / values / queries N(0,1); blocks of L=64
+  frames updated per token by a rank-4 u v^T (u, v ~ N(0, 1/128)) then a thin
+  QR (CholeskyQR2 on the tensor cores and FP32 units, Householder fallback;
+  the same Q as Householder to fp32 rounding); bf16 keys / values / queries
+  N(0,1); blocks of L=64
   tokens in a 512-slot memory ring (full, i.e. the memory of a 32,768-token
   pass); top-k=16 blocks then exact-token argmax and value fetch.
   One step = one block (64 tokens) of every stream: 64 frame updates + QRs,
@@ -447,6 +449,8 @@ def run_ours(args, rank, world, device) -> dict | None:
                 "bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(ach / hbm_peak, 4), "traffic": traffic}
     sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
+    # frame work unit: the Householder flop count of a d x r thin QR plus the
+    # rank-m update (4 d r^2 + 2 d r m per token), whatever algorithm runs
     frames_flops = S * L * (4.0 * D * R * R + 2.0 * D * R * M)
     fr_tflops = frames_flops / (phase_ms["frames"] / 1e3) / 1e12
     roof["peak_source"] = peak_src
@@ -481,7 +485,7 @@ def run_ours(args, rank, world, device) -> dict | None:
         "data": "synthetic (seeded; no dataset for this path)",
         "config": {
             "workload": f"stream_full: per GPU {B_PER_GPU} batch x {HEADS} heads = {S} streams; frames {D}x{R} fp32, "
-                        f"rank-{M} update + Householder thin QR (R-diag-positive) per token; bf16 memory of "
+                        f"rank-{M} update + thin QR (R-diag-positive; CholeskyQR2, Householder fallback) per token; bf16 memory of "
                         f"{SLOTS} blocks x {L} tokens (full ring); top-{K_SEL} blocks + exact-token argmax; "
                         f"step = one {L}-token block",
             "global_batch": B_PER_GPU * world,

@@ -46,6 +46,8 @@ def main() -> None:
                                          "readout_long", "commit_eig", "block_tracker"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
+    parser.add_argument("--qr-method", default="auto", choices=["auto", "householder", "cholesky2"],
+                        help="QR of the frames case")
     args = parser.parse_args()
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
@@ -57,7 +59,8 @@ def main() -> None:
         U = gfst.frame_update_qr(torch.randn((S, 128, 32), generator=g, device=dev), sign_mode="r_diag_positive")
         A = torch.randn((S, 64, 128, 4), generator=g, device=dev) / math.sqrt(128)
         B = torch.randn((S, 64, 32, 4), generator=g, device=dev) / math.sqrt(128)
-        ms = _timed(lambda: gfst.stream_frames(U, A, B, sign_mode="r_diag_positive"), args.repeat)
+        ms = _timed(lambda: gfst.stream_frames(U, A, B, sign_mode="r_diag_positive", qr_method=args.qr_method),
+                    args.repeat)
         units = f"{S * 64 / ms / 1e3:.2f} M frame-tokens/s"
     elif args.case == "batched_qr":
         x = wl.batched_qr_inputs(65536, 64, 8, seed=20261202, device=dev)
