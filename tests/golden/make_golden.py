@@ -330,8 +330,114 @@ def main() -> None:
             out[f"c{ci}_{key}"] = rep[key].numpy()
     out["n_cases"] = np.array(len(cases))
     np.savez(OUT / "block_commit_eig_cases.npz", **out)
+    make_centroid_fixture(modeling, state_mod)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
+
+
+def make_centroid_fixture(modeling, state_mod) -> None:
+    """12. The centroid path: tokens written with cell ids / weights / keys /
+    values through GfstDecodeState.append_exact_token (cuda_packed backend,
+    state.py:315-551), blocks read back with load_exact_block, and
+    ExactRecallReadout._build_centroid_candidates (modeling.py:659-982) on
+    several queries and block selections (a partial block, a block without
+    cells, selections that take the BH-FDR set and ones that fall back to
+    the minimum count)."""
+    torch.manual_seed(77)
+    g = torch.Generator().manual_seed(77)
+    hidden, key_dim, H, dk, dv, C, L, NB, W, vocab = 24, 16, 4, 8, 6, 8, 12, 6, 2, 40
+    rd = modeling.ExactRecallReadout(hidden_size=hidden, key_dim=key_dim, centroid_heads=H, centroid_key_dim=dk,
+                                     centroid_value_dim=dv, cells_per_block=C, centroid_top_cells_per_head=5,
+                                     centroid_min_selected_cells_per_head=2)
+    emb = torch.nn.Embedding(vocab, hidden)
+    with torch.no_grad():  # query heads 0, 2 read query[0:8], heads 1, 3 read query[8:16]
+        sel = torch.zeros((H * dk, key_dim))
+        for h in range(H):
+            for j in range(dk):
+                sel[h * dk + j, (h * dk + j) % key_dim] = 1.0
+        rd.centroid_query_proj.weight.copy_(sel)
+    state = state_mod.GfstDecodeState(num_layers=1, batch_size=1, state_pack_backend="cuda_packed")
+    tok = torch.randint(0, vocab, (NB, L), generator=g)
+    cids = torch.randint(0, C + 2, (NB, L, W), generator=g)            # out-of-range ids are clamped
+    cw = torch.rand((NB, L, W), generator=g)
+    cw = cw / cw.sum(-1, keepdim=True)
+    cw[:, ::5, 1] = 0.0                                                 # single-cell tokens
+    cw[3] = 0.0                                                         # block 3 writes no cell
+    ckey = torch.randn((NB, L, dk), generator=g)
+    cval = torch.randn((NB, L, dv), generator=g) * 2.0
+    # blocks 0 and 4: single-cell tokens whose keys follow a per-cell direction,
+    # so a query head along one direction singles out that cell
+    cell_dirs = torch.randn((C, dk), generator=g)
+    for b in (0, 4):
+        cw[b, :, 0], cw[b, :, 1] = 1.0, 0.0
+        first = cids[b, :, 0].clamp(0, C - 1)
+        ckey[b] = 2.5 * cell_dirs[first] + 0.2 * torch.randn((L, dk), generator=g)
+    for b in range(NB):
+        for t in range(L):
+            state.append_exact_token(batch_idx=0, absolute_position=b * L + t, token_id=int(tok[b, t]), block_len=L,
+                                     cells_per_block=C, centroid_key_dim=dk, centroid_value_dim=dv,
+                                     cell_ids=cids[b, t], cell_weights=cw[b, t], cell_key=ckey[b, t],
+                                     cell_value=cval[b, t])
+    recs = [state.load_exact_block(batch_idx=0, block_id=b, block_len=L, cache_capacity=NB) for b in range(NB)]
+    store = {
+        "token_ids": np.stack([r.token_id_tensor.numpy() for r in recs]).astype(np.int32),
+        "token_cell_ids": np.stack([r.token_cell_id_tensor.numpy() for r in recs]).astype(np.uint8),
+        "token_cell_weights_q": np.stack([r.token_cell_weight_q_tensor.numpy() for r in recs]).astype(np.uint8),
+        "cell_keys": np.stack([r.cell_keys.numpy() for r in recs]),
+        "cell_values_q": np.stack([r.cell_values_q.numpy() for r in recs]),
+        "cell_counts": np.stack([r.cell_counts.numpy() for r in recs]),
+    }
+    with torch.no_grad():
+        feats_all = emb(tok.reshape(-1))
+        token_keys = rd.within_block_proj(feats_all).reshape(NB, L, key_dim)
+        token_feats = rd.centroid_token_proj(feats_all).reshape(NB, L, H, dv)
+    # (query, [(block, prefix, score)]) cases
+    cases = [([0, 1, 2], [L, L, L], [0.9, 0.4, -0.2]),
+             ([4, 3, 5, 0], [L, L, 7, L], [1.5, 1.0, 0.2, -0.3]),
+             ([5], [L], [0.0]),
+             ([2, 4], [5, L], [0.3, 0.1]),
+             ([1, 0, 5, 2, 4], [L, L, L, L, L], [0.2, 0.2, 0.1, 0.0, -0.1])]
+    queries = torch.randn((len(cases), key_dim), generator=g) * 2.0
+    # aligned queries: heads 0 / 2 point at one cell's mean key, heads 1 / 3 at
+    # another's, so their robust z-scores pass the BH-FDR test
+    present = [sorted(set(int(c) for c in cids[b, :, 0].clamp(0, C - 1))) for b in range(NB)]
+    aligned = [(([0, 1, 2, 4, 5], [L] * 5, [0.5, 0.1, 0.3, 0.0, -0.2]), present[0][0], present[4][1], 1.5),
+               (([5, 4, 2, 1], [L, L, L, 9], [0.2, 0.2, 0.2, 0.2]), present[4][2], present[4][2], 3.0),
+               (([2, 0, 3], [L, L, L], [0.0, 0.4, 0.8]), present[0][1], present[0][2], 0.8),
+               (([4, 0], [L, 6], [0.0, 0.0]), present[4][0], present[0][-1], 1.0)]
+    extra = []
+    for case, c0, c1, amp in aligned:
+        cases.append(case)
+        extra.append(torch.cat([amp * cell_dirs[c0], amp * cell_dirs[c1]]))
+    queries = torch.cat([queries, torch.stack(extra)])
+    out = {k: v for k, v in store.items()}
+    out.update(cell_ids_in=cids.numpy().astype(np.int32), cell_weights_in=cw.numpy(), cell_keys_in=ckey.numpy(),
+               cell_values_in=cval.numpy(), token_keys=token_keys.numpy(), token_features=token_feats.numpy(),
+               queries=queries.numpy(), dims=np.array([H, dk, dv, C, L, NB, W]), n_cases=np.array(len(cases)))
+    for ci, (blocks, prefixes, bscores) in enumerate(cases):
+        q = queries[ci]
+        entries = [(recs[b], p, s) for b, p, s in zip(blocks, prefixes, bscores)]
+        with torch.no_grad():
+            res = rd._build_centroid_candidates(query=q, embedding_layer=emb, block_entries=entries)
+            qh = rd.centroid_query_proj(q).reshape(H, dk).float()
+            base = [rd._score_block_tokens(query=q, embedding_layer=emb, record=recs[b], prefix_length=p,
+                                           block_score=s)[0] for b, p, s in zip(blocks, prefixes, bscores)]
+        out[f"q{ci}_blocks"] = np.array(blocks, np.int32)
+        out[f"q{ci}_prefixes"] = np.array(prefixes, np.int32)
+        out[f"q{ci}_block_scores"] = np.array(bscores, np.float32)
+        out[f"q{ci}_query_heads"] = qh.numpy()
+        out[f"q{ci}_base_scores"] = np.concatenate([b.numpy() for b in base])
+        out[f"q{ci}_none"] = np.array(res is None)
+        if res is not None:
+            scores, tids, blks, poss, diag = res
+            out[f"q{ci}_scores"] = torch.cat(scores).numpy()
+            out[f"q{ci}_token_ids"] = torch.cat(tids).numpy().astype(np.int32)
+            out[f"q{ci}_positions"] = torch.cat(poss).numpy().astype(np.int32)
+            for key in ("selected_block_slots", "selected_cell_ids", "selected_alphas", "selection_entropy",
+                        "selection_margin", "selected_cells_per_head"):
+                out[f"q{ci}_{key}"] = diag[key].numpy()
+            out[f"q{ci}_confidence"] = np.float32(diag["confidence"])
+    np.savez(OUT / "centroid_path.npz", **out)
 
 
 if __name__ == "__main__":

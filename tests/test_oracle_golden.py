@@ -6,6 +6,7 @@ import numpy as np
 import torch
 
 from oracle import build as oracle_build
+from oracle import centroid_oracle as co
 from oracle import gfst_oracle as go
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -166,3 +167,51 @@ def test_readout_collapse_matches_reference():
     out = go.exact_readout_collapse(z["Q"], z["pool_K"], z["token_ids"], z["top_idx"])
     for got, key in zip(out, ("best_id", "best_score", "best_block", "best_pos")):
         assert np.array_equal(got, z[key])
+
+
+def centroid_case_blocks(z, ci):
+    """Block entries of golden centroid case ci, in the layout centroid_candidates takes."""
+    ents, off = [], 0
+    base = z[f"q{ci}_base_scores"]
+    for b, p, s in zip(z[f"q{ci}_blocks"], z[f"q{ci}_prefixes"], z[f"q{ci}_block_scores"]):
+        ents.append(dict(token_ids=z["token_ids"][b][:p], cell_ids=z["token_cell_ids"][b][:p],
+                         weights_q=z["token_cell_weights_q"][b][:p], cell_keys=z["cell_keys"][b],
+                         cell_values_q=z["cell_values_q"][b], cell_counts=z["cell_counts"][b],
+                         base_scores=base[off:off + p], features=z["token_features"][b][:p], block_score=float(s)))
+        off += int(p)
+    return ents
+
+
+def test_centroid_cell_write_matches_reference():
+    # golden: GfstDecodeState.append_exact_token (cuda_packed, state.py:315-470)
+    # + _finalise_block_cells (state.py:501-551), one block at a time; the
+    # x255 weight rounding of tests/test_state.py:85-99 ([0.75, 0.25] -> [191, 64])
+    z = load("centroid_path.npz")
+    C = int(z["dims"][3])
+    for b in range(int(z["dims"][5])):
+        ids, wq, keys, vals, cnt = co.cell_commit(z["cell_ids_in"][b], z["cell_weights_in"][b], z["cell_keys_in"][b],
+                                                  z["cell_values_in"][b], C)
+        assert np.array_equal(ids, z["token_cell_ids"][b])
+        assert np.array_equal(wq, z["token_cell_weights_q"][b])
+        assert np.array_equal(keys.view(np.uint16), z["cell_keys"][b].view(np.uint16))
+        assert np.array_equal(vals, z["cell_values_q"][b])
+        assert np.array_equal(cnt, z["cell_counts"][b])
+    _, wq, _, _, _ = co.cell_commit([[2, 5]], [[0.75, 0.25]], [[0.1, 0.2, 0.3]], [[0.4, 0.5]], 8)
+    assert wq.tolist() == [[191, 64]]
+
+
+def test_centroid_candidates_match_reference():
+    # golden: ExactRecallReadout._build_centroid_candidates (modeling.py:659-982)
+    # on 9 query / selection cases (BH-FDR sets of 3-5 cells, minimum-count
+    # fallbacks, confidence 0 to 1, a partial block, a block without cells)
+    z = load("centroid_path.npz")
+    for ci in range(int(z["n_cases"])):
+        res = co.centroid_candidates(z[f"q{ci}_query_heads"], centroid_case_blocks(z, ci), top_cells_per_head=5,
+                                     min_selected=2, cells_per_block=int(z["dims"][3]))
+        assert res is not None
+        scores, diag = res
+        assert np.array_equal(np.concatenate([s for s in scores if s is not None]), z[f"q{ci}_scores"])
+        for key in ("selected_block_slots", "selected_cell_ids", "selected_alphas", "selection_entropy",
+                    "selection_margin", "selected_cells_per_head"):
+            assert np.array_equal(diag[key], z[f"q{ci}_{key}"]), key
+        assert np.float32(diag["confidence"]) == z[f"q{ci}_confidence"]
