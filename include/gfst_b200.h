@@ -241,6 +241,83 @@ GFST_API int gfst_global_features(const float* projector_bank, const int32_t* se
                           double eps_sign, float* features, float* sketch_out, float* basis_out,
                           cudaStream_t stream);
 
+/* ---- centroid path: cell write at block commit ---------------------------
+ * GfstDecodeState._append_exact_token_cuda_packed (state.py:315-470) for the L
+ * tokens of a block and _finalise_block_cells (state.py:501-551), for each of
+ * n_blocks blocks.  Inputs [n_blocks, L, W] cell_ids (int32, clamped to
+ * [0, C-1]) and cell_weights (float32); [n_blocks, L, dk] cell_keys and
+ * [n_blocks, L, dv] cell_values (float32).  Outputs: token_cell_ids and
+ * token_cell_weights_q [n_blocks, L, W] u8 (round(w * 255) clamped to
+ * [0, 255], NaN -> 0); block_cell_keys [n_blocks, C, dk] fp16 (mean key of the
+ * cell's tokens weighted by q/255, 0 for an empty cell), block_cell_values_q
+ * [n_blocks, C, dv] int8 (round(mean value * 32) clamped to [-127, 127]),
+ * block_cell_counts [n_blocks, C] int16 (round(weight sum * 32) clamped to
+ * [0, 32767]).  Sums run in token then membership order in IEEE fp32, as the
+ * reference's index_add_ does on the CPU.  Limits: L * W <= 1024, C <= 256. */
+GFST_API int gfst_centroid_cell_commit(const int32_t* cell_ids, const float* cell_weights,
+                              const float* cell_keys, const float* cell_values,
+                              int64_t n_blocks, int L, int W, int C, int dk, int dv,
+                              uint8_t* token_cell_ids, uint8_t* token_cell_weights_q,
+                              void* block_cell_keys, int8_t* block_cell_values_q,
+                              int16_t* block_cell_counts, cudaStream_t stream);
+
+/* Parameters of the centroid readout: the ExactRecallReadout attributes of the
+ * same names (modeling.py:371-448, config defaults in brackets). */
+typedef struct gfst_centroid_params {
+  float block_score_lambda;  /* centroid_block_score_lambda [0.10]             */
+  int background_subtract;   /* centroid_background_subtract [1]               */
+  float count_penalty;       /* centroid_count_penalty [0.5]                   */
+  float self_field_weight;   /* centroid_self_field_weight [0.15]              */
+  int top_cells_per_head;    /* centroid_top_cells_per_head [8], <= 16         */
+  float fdr_q;               /* centroid_fdr_q [0.10]                          */
+  int min_selected;          /* centroid_min_selected_cells_per_head [2]       */
+  float temperature;         /* centroid_selection_temperature [1.0], > 0      */
+  float entropy_low;         /* centroid_gain_entropy_low [0.35]               */
+  float entropy_high;        /* centroid_gain_entropy_high [0.75]              */
+  float gamma_m;             /* centroid_gamma_m [1.0]                         */
+  float gamma_r;             /* centroid_gamma_r [1.0]                         */
+} gfst_centroid_params;
+
+/* ---- centroid path: significance-gated readout ---------------------------
+ * ExactRecallReadout._build_centroid_candidates (modeling.py:659-982) for every
+ * (stream, query), then the log-sum-exp collapse by token id and the best
+ * group (perf.py:164-229, modeling.py:1151-1169).  Per query: the valid
+ * selections (0 <= sel_idx < n_slots, prefix > 0) in order are the block
+ * entries; their cells with count > 0 are scored per centroid head
+ * (query_heads . key / sqrt(dk) + lambda * block score), robust-z-scored,
+ * selected by BH-FDR (minimum-count fallback), weighted by softmax; every
+ * token of an entry (positions < prefix) gets
+ *   base + gamma_m * conf * token_mass + gamma_r * conf * recall
+ * with base = token_keys . Q.  With no candidate cell or no selection the
+ * centroid terms are off (base only, confidence -1), as the reference falls
+ * back to _score_block_tokens.
+ * Q [S, Nq, dq]; query_heads [S, Nq, H, dk] (centroid_query_proj(query));
+ * sel_idx int32 / sel_scores float32 / prefix_len int32 (or NULL: full blocks)
+ * [S, Nq, K]; token_keys [S, n_slots, L, dq] (within_block_proj of the stored
+ * tokens); token_features [S, n_slots, L, H, dv] (centroid_token_proj of the
+ * stored tokens); token_ids [S, n_slots, L]; token_cell_ids /
+ * token_cell_weights_q [S, n_slots, L, W] u8 and cell_keys (fp16) /
+ * cell_values_q / cell_counts [S, n_slots, C, ...] as gfst_centroid_cell_commit
+ * writes them.  Outputs: best_id / best_score / best_block (slot) / best_pos
+ * [S, Nq] (-1 / -inf when nothing is valid); optional (NULL to skip):
+ * cand_scores [S, Nq, K, L] (final token scores, -inf where no token),
+ * sel_block (entry index) / sel_cell / sel_alpha [S, Nq, H, top_cells_per_head],
+ * head_stats [S, Nq, H, 3] (entropy, margin, selected count), confidence
+ * [S, Nq].  Limits: K <= 32, C <= 32, K * C <= 512, K * L <= 2048, H <= 8,
+ * dk <= 64, dv <= 32, dq <= 256, W <= 8.  fp32 throughout.                 */
+GFST_API int gfst_centroid_readout(const float* Q, const float* query_heads, const int32_t* sel_idx,
+                          const float* sel_scores, const int32_t* prefix_len,
+                          const float* token_keys, const float* token_features,
+                          const int32_t* token_ids, const uint8_t* token_cell_ids,
+                          const uint8_t* token_cell_weights_q, const void* cell_keys,
+                          const int8_t* cell_values_q, const int16_t* cell_counts,
+                          int64_t n_streams, int n_queries, int n_slots, int L, int dq, int H,
+                          int dk, int dv, int C, int W, int K, const gfst_centroid_params* params,
+                          float* cand_scores, int32_t* best_id, float* best_score,
+                          int32_t* best_block, int32_t* best_pos, int32_t* sel_block,
+                          int32_t* sel_cell, float* sel_alpha, float* head_stats,
+                          float* confidence, cudaStream_t stream);
+
 /* ---- coarse block retrieval: score + top-k ---------------------------------
  * For every stream s and query q:
  *   score[b] = Q[s,q,:] . Ksum[s,b,:]   for b in [0, n_blocks)   (fp32 accumulate)

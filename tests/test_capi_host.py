@@ -67,6 +67,32 @@ def test_host_validation_rejects_without_launching():
                                          None, None) == 2
     assert lib.gfst_local_tracker_stream(None, None, None, 0, 4, 64, 32, 2, dims, rates, 1e-6, 1e-6, 1e-8, 0,
                                          None, None) == 0
+    # streaming QR method: unknown code; CholeskyQR2 outside its classes (host
+    # buffers stand in for device pointers: the call returns before any launch)
+    buf = (ctypes.c_float * 4096)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.gfst_frame_stream_ex(None, None, None, 1.0, 4, 8, 64, 8, 4, 1e-8, 0, None, 0, 7, None) == 1
+    assert lib.gfst_frame_stream_ex(p, p, p, 1.0, 4, 8, 64, 8, 4, 1e-8, 0, None, 0, 2, None) == 2
+    assert b"CholeskyQR2" in lib.gfst_last_error()
+    # centroid cell write: L * W too large, too many cells, null buffers, empty
+    assert lib.gfst_centroid_cell_commit(None, None, None, None, 4, 512, 4, 16, 32, 16, None, None, None, None,
+                                         None, None) == 2
+    assert lib.gfst_centroid_cell_commit(None, None, None, None, 4, 64, 2, 300, 32, 16, None, None, None, None,
+                                         None, None) == 2
+    assert lib.gfst_centroid_cell_commit(None, None, None, None, 4, 64, 2, 16, 32, 16, None, None, None, None,
+                                         None, None) == 1
+    assert lib.gfst_centroid_cell_commit(None, None, None, None, 0, 64, 2, 16, 32, 16, None, None, None, None,
+                                         None, None) == 0
+    # centroid readout: no params, K > 32, non-positive temperature, too many heads
+    from gfst_hmb_public_b200.centroid import CentroidParams
+    prm = CentroidParams().to_c()
+    pp = ctypes.cast(ctypes.pointer(prm), ctypes.c_void_p)
+    args = lambda K, H, params: (None,) * 13 + (1, 1, 4, 16, 32, H, 8, 4, 8, 2, K, params) + (None,) * 11  # noqa
+    assert lib.gfst_centroid_readout(*args(4, 2, None)) == 1
+    assert lib.gfst_centroid_readout(*args(33, 2, pp)) == 2
+    assert lib.gfst_centroid_readout(*args(4, 9, pp)) == 2
+    bad_t = CentroidParams(temperature=0.0).to_c()
+    assert lib.gfst_centroid_readout(*args(4, 2, ctypes.cast(ctypes.pointer(bad_t), ctypes.c_void_p))) == 1
 
 
 def test_python_ops_reject_cpu_tensors():
