@@ -24,7 +24,7 @@ import math
 
 import torch
 
-from . import block_commit, gfst, memory, readout, retrieval, tracker, workloads as wl
+from . import block_commit, centroid, gfst, memory, readout, retrieval, tracker, workloads as wl
 
 
 def _timed(fn, repeat: int) -> float:
@@ -43,7 +43,8 @@ def _timed(fn, repeat: int) -> float:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
-                                         "readout_long", "commit_eig", "block_tracker"])
+                                         "readout_long", "commit_eig", "block_tracker", "centroid_commit",
+                                         "centroid_readout"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     parser.add_argument("--qr-method", default="auto", choices=["auto", "householder", "cholesky2"],
@@ -102,6 +103,33 @@ def main() -> None:
         ms = _timed(lambda: tracker.block_tracker_stream(bt.largest_basis, bt.projector_sum, bt.reduced_sum, x,
                                                          rate=0.2), args.repeat)
         units = f"{S * 64 / ms / 1e3:.2f} M tokens/s"
+    elif args.case in ("centroid_commit", "centroid_readout"):
+        # streaming shapes: 64-token blocks, 16 cells, 2 memberships, key 32 /
+        # value 16 per head, 4 heads, 128-dim token keys, top-16 blocks
+        S, NB, L, W, C, dk, dv, H, dq, K, Nq = args.streams or 256, 512, 64, 2, 16, 32, 16, 4, 128, 16, 64
+        ids = torch.randint(0, C, (S, NB, L, W), generator=g, device=dev, dtype=torch.int32)
+        w = torch.rand((S, NB, L, W), generator=g, device=dev)
+        w = w / w.sum(-1, keepdim=True)
+        ck = torch.randn((S, NB, L, dk), generator=g, device=dev)
+        cv = torch.randn((S, NB, L, dv), generator=g, device=dev)
+        if args.case == "centroid_commit":
+            ms = _timed(lambda: centroid.centroid_cell_commit(ids, w, ck, cv, C), args.repeat)
+            units = f"{S * NB / ms / 1e3:.2f} M blocks/s"
+        else:
+            tid, twq, keys, vals, cnt = centroid.centroid_cell_commit(ids, w, ck, cv, C)
+            del ck, cv, w, ids
+            store = dict(token_keys=torch.randn((S, NB, L, dq), generator=g, device=dev),
+                         token_features=torch.randn((S, NB, L, H, dv), generator=g, device=dev),
+                         token_ids=torch.randint(0, 32000, (S, NB, L), generator=g, device=dev, dtype=torch.int32),
+                         token_cell_ids=tid, token_cell_weights_q=twq, cell_keys=keys, cell_values_q=vals,
+                         cell_counts=cnt)
+            Q = torch.randn((S, Nq, dq), generator=g, device=dev)
+            qh = torch.randn((S, Nq, H, dk), generator=g, device=dev)
+            sel = torch.randint(0, NB, (S, Nq, K), generator=g, device=dev, dtype=torch.int32)
+            sc = torch.randn((S, Nq, K), generator=g, device=dev)
+            ms = _timed(lambda: centroid.centroid_readout(Q, qh, sel, sc, **store), args.repeat)
+            per_q = K * L * (dq + H * dv) * 4
+            units = f"{S * Nq / ms / 1e3:.2f} M queries/s, {S * Nq * per_q / ms / 1e6:.0f} GB/s of token rows"
     elif args.case == "tracker":
         S = args.streams or 2048
         tr = tracker.LocalTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), device=dev)

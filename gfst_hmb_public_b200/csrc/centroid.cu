@@ -107,6 +107,9 @@ constexpr int kMaxDv = 32;
 constexpr int kMaxWidth = 16;
 constexpr int kMaxCand = 2048;    // K * L candidate tokens
 constexpr int kMaxDq = 256;
+constexpr int kPairsPerLane = kMaxHeads * kMaxWidth / 32;
+static_assert(kMaxCand + (kRThreads / 32) * kMaxHeads * kMaxDv <= kMaxHeads * kMaxCells,
+              "token-phase buffers fit the z-score area");
 constexpr float kSqrt2 = 1.41421356237309515f;  // (float) math.sqrt(2.0)
 
 __device__ __forceinline__ uint32_t orderable(float x) {  // ascending float order as u32
@@ -137,22 +140,31 @@ __device__ void block_sort(unsigned long long* key, int n_pow2) {
 struct ReadoutSmem {
   float q[kMaxDq];
   float qh[kMaxHeads * kMaxDk];
+  int s_sel[kMaxEntries], s_prefix[kMaxEntries];
+  float s_score[kMaxEntries];
+  int s_count[kMaxCells];
   int e_slot[kMaxEntries], e_k[kMaxEntries], e_prefix[kMaxEntries], e_nvalid[kMaxEntries], e_base[kMaxEntries];
   float e_score[kMaxEntries], e_selfmean[kMaxEntries];
   int c_entry[kMaxCells], c_cell[kMaxCells];
   float c_count[kMaxCells];  // count_q / 32
   float c_self[kMaxCells];   // log1p(count_q) - block mean
-  float z[kMaxHeads][kMaxCells];
+  union {
+    float z[kMaxHeads][kMaxCells];  // selection phase
+    struct {                        // token phase
+      float cand[kMaxCand];
+      float feat[kRThreads / 32][kMaxHeads * kMaxDv];
+    };
+  };
   unsigned long long key[kMaxCand];
   int sel[kMaxHeads][kMaxWidth];  // selected cell (index into the compacted list)
   float sel_alpha[kMaxHeads][kMaxWidth], sel_logalpha[kMaxHeads][kMaxWidth];
-  float sel_val[kMaxHeads][kMaxWidth][kMaxDv];
+  float sel_val[kMaxHeads][kMaxWidth][kMaxDv + 1];  // +1: lanes read different rows
+  int pair_h[kMaxHeads * kMaxWidth], pair_j[kMaxHeads * kMaxWidth];
   int sel_count[kMaxHeads];
   float h_entropy[kMaxHeads], h_margin[kMaxHeads], h_signif[kMaxHeads];
   float mass[kMaxEntries * 32];
-  float cand[kMaxCand];
   float red[kRThreads / 32];
-  int n_entries, n_cells, upto;
+  int n_entries, n_cells, upto, n_pairs;
   float conf;
 };
 
@@ -175,20 +187,33 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
 
   for (int i = tid; i < dq; i += kRThreads) sm.q[i] = Q[sq * dq + i];
   for (int i = tid; i < H * dk; i += kRThreads) sm.qh[i] = query_heads[sq * H * dk + i];
-  if (tid == 0) {  // valid entries in selection order (modeling.py:1091-1108)
+  // selections and their cell counts, staged by all threads (global loads in
+  // parallel), then the entry list in selection order (modeling.py:1091-1108)
+  for (int k = tid; k < K; k += kRThreads) {
+    const int b = sel_idx[sq * K + k];
+    int p = prefix_len ? prefix_len[sq * K + k] : L;
+    p = p > L ? L : p;
+    sm.s_sel[k] = (b < 0 || b >= NB || p <= 0) ? -1 : b;
+    sm.s_prefix[k] = p;
+    sm.s_score[k] = sel_scores[sq * K + k];
+  }
+  __syncthreads();
+  for (int i = tid; i < K * C; i += kRThreads) {
+    const int b = sm.s_sel[i / C];
+    sm.s_count[i] = b >= 0 ? cell_counts[((s * NB) + b) * C + i % C] : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
     int ne = 0, nc = 0;
     for (int k = 0; k < K; ++k) {
-      const int b = sel_idx[sq * K + k];
-      int p = prefix_len ? prefix_len[sq * K + k] : L;
-      p = p > L ? L : p;
-      if (b < 0 || b >= NB || p <= 0) continue;
-      sm.e_slot[ne] = b;
+      if (sm.s_sel[k] < 0) continue;
+      sm.e_slot[ne] = sm.s_sel[k];
       sm.e_k[ne] = k;
-      sm.e_prefix[ne] = p;
-      sm.e_score[ne] = sel_scores[sq * K + k];
+      sm.e_prefix[ne] = sm.s_prefix[k];
+      sm.e_score[ne] = sm.s_score[k];
       sm.e_base[ne] = nc;
       int nv = 0;
-      for (int c = 0; c < C; ++c) nv += cell_counts[((s * NB) + b) * C + c] > 0 ? 1 : 0;
+      for (int c = 0; c < C; ++c) nv += sm.s_count[k * C + c] > 0 ? 1 : 0;
       sm.e_nvalid[ne] = nv;
       nc += nv;
       ++ne;
@@ -201,7 +226,7 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
   for (int i = tid; i < kMaxEntries * 32; i += kRThreads) sm.mass[i] = 0.f;
   // compacted cells (modeling.py:690-727) and the per-block self field
   for (int e = tid; e < ne; e += kRThreads) {
-    const int16_t* cc = cell_counts + ((s * NB) + sm.e_slot[e]) * C;
+    const int* cc = sm.s_count + sm.e_k[e] * C;
     int o = sm.e_base[e];
     float lsum = 0.f;
     for (int c = 0; c < C; ++c) {
@@ -217,14 +242,24 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
   }
   __syncthreads();
   for (int i = tid; i < N; i += kRThreads) sm.c_self[i] = sm.c_self[i] - sm.e_selfmean[sm.c_entry[i]];
-  // raw scores (modeling.py:739-745)
-  for (int i = tid; i < H * N; i += kRThreads) {
-    const int h = i / N, n = i % N;
+  // raw scores (modeling.py:739-745): one thread per cell, every head, the
+  // cell's key read once
+  for (int n = tid; n < N; n += kRThreads) {
     const int e = sm.c_entry[n];
     const __half* key = cell_keys + (((s * NB) + sm.e_slot[e]) * C + sm.c_cell[n]) * dk;
-    float acc = 0.f;
-    for (int j = 0; j < dk; ++j) acc = fmaf(sm.qh[h * dk + j], __half2float(key[j]), acc);
-    sm.z[h][n] = __fadd_rn(__fdiv_rn(acc, sqrt_dk), __fmul_rn(prm.block_score_lambda, sm.e_score[e]));
+    float acc[kMaxHeads];
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) acc[h] = 0.f;
+    for (int j = 0; j < dk; ++j) {
+      const float kj = __half2float(key[j]);
+#pragma unroll
+      for (int h = 0; h < kMaxHeads; ++h)
+        if (h < H) acc[h] = fmaf(sm.qh[h * dk + j], kj, acc[h]);
+    }
+    const float bias = __fmul_rn(prm.block_score_lambda, sm.e_score[e]);
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h)
+      if (h < H) sm.z[h][n] = __fadd_rn(__fdiv_rn(acc[h], sqrt_dk), bias);
   }
   __syncthreads();
   bool centroid_on = N > 0 && width > 0;
@@ -337,6 +372,15 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
           ++used;
         }
       }
+      int np = 0;
+      for (int h = 0; h < H; ++h) {
+        for (int j = 0; j < sm.sel_count[h]; ++j) {
+          sm.pair_h[np] = h;
+          sm.pair_j[np] = j;
+          ++np;
+        }
+      }
+      sm.n_pairs = np;
       float conf = -1.f;
       if (used > 0) {
         const float me = __fdiv_rn(se, (float)used), ms = __fdiv_rn(ss, (float)used);
@@ -356,51 +400,79 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
   const int n_cand = ne * L;
   int c_pow2 = 1;
   while (c_pow2 < n_cand) c_pow2 <<= 1;
-  for (int ci = tid; ci < c_pow2; ci += kRThreads) {
+  // one warp per candidate token: coalesced key / feature rows, lanes split the
+  // base dot product and the (head, selected cell) recall terms
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int ci = n_cand + tid; ci < c_pow2; ci += kRThreads) sm.key[ci] = ~0ull;
+  for (int ci = warp; ci < n_cand; ci += kRThreads / 32) {
+    const int e = ci / L, p = ci % L;
+    float score = -INFINITY;
     unsigned long long kv = ~0ull;
-    if (ci < n_cand) {
-      const int e = ci / L, p = ci % L;
-      float score = -INFINITY;
-      if (p < sm.e_prefix[e]) {
-        const int64_t tok = ((s * NB) + sm.e_slot[e]) * L + p;
-        float base = 0.f;
-        const float* kr = tok_keys + tok * dq;
-        for (int j = 0; j < dq; ++j) base = fmaf(kr[j], sm.q[j], base);
-        score = base;
-        if (centroid_on) {
-          float tm = 0.f;
-          for (int w = 0; w < W; ++w) {
-            int c = tok_cell[tok * W + w];
-            c = c > C - 1 ? C - 1 : c;
-            tm = __fadd_rn(tm, __fmul_rn(sm.mass[e * 32 + c], __fdiv_rn((float)tok_wq[tok * W + w], 255.f)));
+    if (p < sm.e_prefix[e]) {
+      const int64_t tok = ((s * NB) + sm.e_slot[e]) * L + p;
+      // issue every load of the token first: its key row and feature row
+      const float* kr = tok_keys + tok * dq;
+      const float* fr = tok_feats + tok * H * dv;
+      float kx[kMaxDq / 32], fx[kMaxHeads * kMaxDv / 32];
+#pragma unroll
+      for (int t = 0; t < kMaxDq / 32; ++t) kx[t] = lane + 32 * t < dq ? kr[lane + 32 * t] : 0.f;
+#pragma unroll
+      for (int t = 0; t < kMaxHeads * kMaxDv / 32; ++t)
+        fx[t] = (centroid_on && lane + 32 * t < H * dv) ? fr[lane + 32 * t] : 0.f;
+      const int tid_tok = tok_ids[tok];
+      float part = 0.f;
+#pragma unroll
+      for (int t = 0; t < kMaxDq / 32; ++t)
+        if (lane + 32 * t < dq) part = fmaf(kx[t], sm.q[lane + 32 * t], part);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      const float base = part;
+      score = base;
+      if (centroid_on) {
+        float* fb = sm.feat[warp];
+#pragma unroll
+        for (int t = 0; t < kMaxHeads * kMaxDv / 32; ++t)
+          if (lane + 32 * t < H * dv) fb[lane + 32 * t] = fx[t];
+        __syncwarp();
+        float seed[kPairsPerLane];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < kPairsPerLane; ++t) {
+          const int pi = lane + 32 * t;
+          seed[t] = -INFINITY;
+          if (pi < sm.n_pairs) {
+            const int h = sm.pair_h[pi], j = sm.pair_j[pi];
+            float d = 0.f;
+            for (int u = 0; u < dv; ++u) d = fmaf(fb[h * dv + u], sm.sel_val[h][j][u], d);
+            seed[t] = __fadd_rn(__fdiv_rn(d, sqrt_dv), sm.sel_logalpha[h][j]);
+            mx = fmaxf(mx, seed[t]);
           }
-          const float* fr = tok_feats + tok * H * dv;
-          float mx = -INFINITY;
-          for (int h = 0; h < H; ++h) {
-            for (int j = 0; j < sm.sel_count[h]; ++j) {
-              float d = 0.f;
-              for (int u = 0; u < dv; ++u) d = fmaf(fr[h * dv + u], sm.sel_val[h][j][u], d);
-              mx = fmaxf(mx, __fadd_rn(__fdiv_rn(d, sqrt_dv), sm.sel_logalpha[h][j]));
-            }
-          }
-          float se = 0.f;
-          for (int h = 0; h < H; ++h) {
-            for (int j = 0; j < sm.sel_count[h]; ++j) {
-              float d = 0.f;
-              for (int u = 0; u < dv; ++u) d = fmaf(fr[h * dv + u], sm.sel_val[h][j][u], d);
-              se += expf(__fsub_rn(__fadd_rn(__fdiv_rn(d, sqrt_dv), sm.sel_logalpha[h][j]), mx));
-            }
-          }
-          const float recall = __fadd_rn(mx, logf(se));
-          score = __fadd_rn(__fadd_rn(base, __fmul_rn(gm, tm)), __fmul_rn(gr, recall));
         }
-        const int id = tok_ids[tok];
-        if (id >= 0 && score == score) kv = ((unsigned long long)(uint32_t)id << 32) | (uint32_t)ci;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float se = 0.f;
+#pragma unroll
+        for (int t = 0; t < kPairsPerLane; ++t)
+          if (lane + 32 * t < sm.n_pairs) se += expf(__fsub_rn(seed[t], mx));
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+        const float recall = __fadd_rn(mx, logf(se));
+        float tm = 0.f;
+        for (int w = 0; w < W; ++w) {
+          int c = tok_cell[tok * W + w];
+          c = c > C - 1 ? C - 1 : c;
+          tm = __fadd_rn(tm, __fmul_rn(sm.mass[e * 32 + c], __fdiv_rn((float)tok_wq[tok * W + w], 255.f)));
+        }
+        score = __fadd_rn(__fadd_rn(base, __fmul_rn(gm, tm)), __fmul_rn(gr, recall));
+        __syncwarp();  // every lane is done with fb before the next token's rows
       }
+      if (tid_tok >= 0 && score == score) kv = ((unsigned long long)(uint32_t)tid_tok << 32) | (uint32_t)ci;
+    }
+    if (lane == 0) {
       sm.cand[ci] = score;
+      sm.key[ci] = kv;
       if (cand_out) cand_out[(sq * K + sm.e_k[e]) * L + p] = score;
     }
-    sm.key[ci] = kv;
   }
   if (cand_out) {  // selections that are not valid entries
     for (int i = tid; i < K * L; i += kRThreads) {
