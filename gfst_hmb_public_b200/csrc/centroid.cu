@@ -108,6 +108,7 @@ constexpr int kMaxWidth = 16;
 constexpr int kMaxCand = 2048;    // K * L candidate tokens
 constexpr int kMaxDq = 256;
 constexpr int kPairsPerLane = kMaxHeads * kMaxWidth / 32;
+constexpr int kRegDv = 16;  // value dims held in registers on the register recall path
 static_assert(kMaxCand + (kRThreads / 32) * kMaxHeads * kMaxDv <= kMaxHeads * kMaxCells,
               "token-phase buffers fit the z-score area");
 constexpr float kSqrt2 = 1.41421356237309515f;  // (float) math.sqrt(2.0)
@@ -137,7 +138,7 @@ __device__ void block_sort(unsigned long long* key, int n_pow2) {
   }
 }
 
-struct ReadoutSmem {
+struct __align__(16) ReadoutSmem {
   float q[kMaxDq];
   float qh[kMaxHeads * kMaxDk];
   int s_sel[kMaxEntries], s_prefix[kMaxEntries];
@@ -163,12 +164,13 @@ struct ReadoutSmem {
   int sel_count[kMaxHeads];
   float h_entropy[kMaxHeads], h_margin[kMaxHeads], h_signif[kMaxHeads];
   float mass[kMaxEntries * 32];
+  float wlut[256];  // q / 255
   float red[kRThreads / 32];
   int n_entries, n_cells, upto, n_pairs;
   float conf;
 };
 
-__global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
+__global__ void __launch_bounds__(kRThreads, 3) centroid_readout_kernel(
     const float* __restrict__ Q, const float* __restrict__ query_heads, const int32_t* __restrict__ sel_idx,
     const float* __restrict__ sel_scores, const int32_t* __restrict__ prefix_len, const float* __restrict__ tok_keys,
     const float* __restrict__ tok_feats, const int32_t* __restrict__ tok_ids, const uint8_t* __restrict__ tok_cell,
@@ -404,38 +406,61 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
   // base dot product and the (head, selected cell) recall terms
   const int lane = tid & 31, warp = tid >> 5;
   for (int ci = n_cand + tid; ci < c_pow2; ci += kRThreads) sm.key[ci] = ~0ull;
-  for (int ci = warp; ci < n_cand; ci += kRThreads / 32) {
-    const int e = ci / L, p = ci % L;
-    float score = -INFINITY;
-    unsigned long long kv = ~0ull;
-    if (p < sm.e_prefix[e]) {
-      const int64_t tok = ((s * NB) + sm.e_slot[e]) * L + p;
-      // issue every load of the token first: its key row and feature row
-      const float* kr = tok_keys + tok * dq;
-      const float* fr = tok_feats + tok * H * dv;
-      float kx[kMaxDq / 32], fx[kMaxHeads * kMaxDv / 32];
+  for (int i = tid; i < 256; i += kRThreads) sm.wlut[i] = __fdiv_rn((float)i, 255.f);
+  float qreg[kMaxDq / 32];
 #pragma unroll
-      for (int t = 0; t < kMaxDq / 32; ++t) kx[t] = lane + 32 * t < dq ? kr[lane + 32 * t] : 0.f;
+  for (int t = 0; t < kMaxDq / 32; ++t) qreg[t] = lane + 32 * t < dq ? sm.q[lane + 32 * t] : 0.f;
+  // register path of the recall terms: one (head, selected cell) pair per lane,
+  // its value row and log-weight in registers
+  const bool reg_pairs = centroid_on && sm.n_pairs <= 32 && dv <= kRegDv && (dv & 3) == 0;
+  float sv[kRegDv];
+  float my_logalpha = -INFINITY;
+  int my_h = 0;
+  if (reg_pairs) {
+    const bool mine = lane < sm.n_pairs;
+    const int h = mine ? sm.pair_h[lane] : 0, j = mine ? sm.pair_j[lane] : 0;
 #pragma unroll
-      for (int t = 0; t < kMaxHeads * kMaxDv / 32; ++t)
-        fx[t] = (centroid_on && lane + 32 * t < H * dv) ? fr[lane + 32 * t] : 0.f;
-      const int tid_tok = tok_ids[tok];
-      float part = 0.f;
+    for (int u = 0; u < kRegDv; ++u) sv[u] = (mine && u < dv) ? sm.sel_val[h][j][u] : 0.f;
+    my_logalpha = mine ? sm.sel_logalpha[h][j] : -INFINITY;
+    my_h = h;
+  }
+  __syncthreads();  // weight table
+  // Score of one candidate token from its rows (this lane's part of the key
+  // row kx[t] = key[lane + 32 t], of the feature row fx[t]) and its membership
+  // (lanes w < W hold cell id and weight w).
+  auto finish_token = [&](int ci, int e, int64_t tok, const float* kx, int nkx, const float* fx, int nfx, int tid_tok,
+                          int mcell, int mwq) {
+    float part = 0.f;
+    for (int t = 0; t < nkx; ++t) part = fmaf(kx[t], qreg[t], part);
 #pragma unroll
-      for (int t = 0; t < kMaxDq / 32; ++t)
-        if (lane + 32 * t < dq) part = fmaf(kx[t], sm.q[lane + 32 * t], part);
+    for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    const float base = part;
+    float score = base;
+    if (centroid_on) {
+      float* fb = sm.feat[warp];
+      for (int t = 0; t < nfx; ++t)
+        if (lane + 32 * t < H * dv) fb[lane + 32 * t] = fx[t];
+      __syncwarp();
+      float seed[kPairsPerLane];
+      float mx = -INFINITY;
+      if (reg_pairs) {
+        const float4* f4 = reinterpret_cast<const float4*>(fb + my_h * dv);
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      const float base = part;
-      score = base;
-      if (centroid_on) {
-        float* fb = sm.feat[warp];
+        for (int u = 0; u < kRegDv; u += 4) {
+          if (u < dv) {
+            const float4 f = f4[u / 4];
+            d0 = fmaf(f.x, sv[u], d0);
+            d1 = fmaf(f.y, sv[u + 1], d1);
+            d2 = fmaf(f.z, sv[u + 2], d2);
+            d3 = fmaf(f.w, sv[u + 3], d3);
+          }
+        }
+        seed[0] = lane < sm.n_pairs ? __fadd_rn(__fdiv_rn((d0 + d1) + (d2 + d3), sqrt_dv), my_logalpha) : -INFINITY;
+        mx = seed[0];
 #pragma unroll
-        for (int t = 0; t < kMaxHeads * kMaxDv / 32; ++t)
-          if (lane + 32 * t < H * dv) fb[lane + 32 * t] = fx[t];
-        __syncwarp();
-        float seed[kPairsPerLane];
-        float mx = -INFINITY;
+        for (int t = 1; t < kPairsPerLane; ++t) seed[t] = -INFINITY;
+      } else {
 #pragma unroll
         for (int t = 0; t < kPairsPerLane; ++t) {
           const int pi = lane + 32 * t;
@@ -448,31 +473,58 @@ __global__ void __launch_bounds__(kRThreads) centroid_readout_kernel(
             mx = fmaxf(mx, seed[t]);
           }
         }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float se = 0.f;
-#pragma unroll
-        for (int t = 0; t < kPairsPerLane; ++t)
-          if (lane + 32 * t < sm.n_pairs) se += expf(__fsub_rn(seed[t], mx));
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
-        const float recall = __fadd_rn(mx, logf(se));
-        float tm = 0.f;
-        for (int w = 0; w < W; ++w) {
-          int c = tok_cell[tok * W + w];
-          c = c > C - 1 ? C - 1 : c;
-          tm = __fadd_rn(tm, __fmul_rn(sm.mass[e * 32 + c], __fdiv_rn((float)tok_wq[tok * W + w], 255.f)));
-        }
-        score = __fadd_rn(__fadd_rn(base, __fmul_rn(gm, tm)), __fmul_rn(gr, recall));
-        __syncwarp();  // every lane is done with fb before the next token's rows
       }
-      if (tid_tok >= 0 && score == score) kv = ((unsigned long long)(uint32_t)tid_tok << 32) | (uint32_t)ci;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float se = 0.f;
+#pragma unroll
+      for (int t = 0; t < kPairsPerLane; ++t)
+        if (seed[t] != -INFINITY) se += expf(__fsub_rn(seed[t], mx));
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+      const float recall = __fadd_rn(mx, logf(se));
+      float tm = 0.f;
+      for (int w = 0; w < W; ++w) {  // modeling.py:929-938, memberships in order
+        int c = __shfl_sync(0xffffffffu, mcell, w);
+        const int q8 = __shfl_sync(0xffffffffu, mwq, w);
+        c = c > C - 1 ? C - 1 : c;
+        tm = __fadd_rn(tm, __fmul_rn(sm.mass[e * 32 + c], sm.wlut[q8]));
+      }
+      score = __fadd_rn(__fadd_rn(base, __fmul_rn(gm, tm)), __fmul_rn(gr, recall));
+      __syncwarp();  // every lane is done with fb before the next token's rows
     }
+    unsigned long long kv = ~0ull;
+    if (tid_tok >= 0 && score == score) kv = ((unsigned long long)(uint32_t)tid_tok << 32) | (uint32_t)ci;
     if (lane == 0) {
       sm.cand[ci] = score;
       sm.key[ci] = kv;
-      if (cand_out) cand_out[(sq * K + sm.e_k[e]) * L + p] = score;
+      if (cand_out) cand_out[(sq * K + sm.e_k[e]) * L + ci % L] = score;
     }
+  };
+  auto dead_token = [&](int ci, int e) {
+    if (lane == 0) {
+      sm.cand[ci] = -INFINITY;
+      sm.key[ci] = ~0ull;
+      if (cand_out) cand_out[(sq * K + sm.e_k[e]) * L + ci % L] = -INFINITY;
+    }
+  };
+  for (int ci = warp; ci < n_cand; ci += kRThreads / 32) {
+    const int e = ci / L, p = ci % L;
+    if (p >= sm.e_prefix[e]) {
+      dead_token(ci, e);
+      continue;
+    }
+    const int64_t tok = ((s * NB) + sm.e_slot[e]) * L + p;
+    const float* kr = tok_keys + tok * dq;
+    const float* fr = tok_feats + tok * H * dv;
+    float kx[kMaxDq / 32], fx[kMaxHeads * kMaxDv / 32];
+#pragma unroll
+    for (int t = 0; t < kMaxDq / 32; ++t) kx[t] = lane + 32 * t < dq ? kr[lane + 32 * t] : 0.f;
+#pragma unroll
+    for (int t = 0; t < kMaxHeads * kMaxDv / 32; ++t)
+      fx[t] = (centroid_on && lane + 32 * t < H * dv) ? fr[lane + 32 * t] : 0.f;
+    finish_token(ci, e, tok, kx, kMaxDq / 32, fx, kMaxHeads * kMaxDv / 32, tok_ids[tok],
+                 lane < W ? tok_cell[tok * W + lane] : 0, lane < W ? tok_wq[tok * W + lane] : 0);
   }
   if (cand_out) {  // selections that are not valid entries
     for (int i = tid; i < K * L; i += kRThreads) {
