@@ -159,7 +159,7 @@ struct __align__(16) ReadoutSmem {
   unsigned long long key[kMaxCand];
   int sel[kMaxHeads][kMaxWidth];  // selected cell (index into the compacted list)
   float sel_alpha[kMaxHeads][kMaxWidth], sel_logalpha[kMaxHeads][kMaxWidth];
-  float sel_val[kMaxHeads][kMaxWidth][kMaxDv + 1];  // +1: lanes read different rows
+  alignas(16) float sel_val[kMaxHeads][kMaxWidth][kMaxDv + 4];  // 16-byte rows, spread over banks
   int pair_h[kMaxHeads * kMaxWidth], pair_j[kMaxHeads * kMaxWidth];
   int sel_count[kMaxHeads];
   float h_entropy[kMaxHeads], h_margin[kMaxHeads], h_signif[kMaxHeads];
@@ -508,7 +508,100 @@ __global__ void __launch_bounds__(kRThreads, 3) centroid_readout_kernel(
       if (cand_out) cand_out[(sq * K + sm.e_k[e]) * L + ci % L] = -INFINITY;
     }
   };
-  for (int ci = warp; ci < n_cand; ci += kRThreads / 32) {
+  // Pair path for 4 heads of 16 value dims (the reference's defaults): two
+  // threads per candidate token, each with half the key row and two heads'
+  // feature rows in registers, the recall log-sum-exp kept online (running
+  // max and scaled sum) and merged across the pair by one shuffle.
+  const bool pair_path = H == 4 && dv == 16 && (dq & 7) == 0 && dq <= kMaxDq &&
+                         ((reinterpret_cast<uintptr_t>(tok_keys) | reinterpret_cast<uintptr_t>(tok_feats)) & 15) == 0;
+  if (pair_path) {
+    const int half = tid & 1;
+    const int dqh = dq / 2;
+    for (int cb = 0; cb < n_cand; cb += kRThreads / 2) {
+      const int ci = cb + (tid >> 1);
+      const bool inb = ci < n_cand;
+      const int e = inb ? ci / L : 0, p = inb ? ci % L : 0;
+      const bool live = inb && p < sm.e_prefix[e];
+      const int64_t tok = live ? ((s * NB) + sm.e_slot[e]) * L + p : 0;
+      float score = -INFINITY;
+      if (live) {
+        const float4* kr = reinterpret_cast<const float4*>(tok_keys + tok * dq + half * dqh);
+        const float4* q4 = reinterpret_cast<const float4*>(sm.q + half * dqh);
+        float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+        for (int j = 0; j < dqh / 4; ++j) {
+          const float4 k = kr[j], qq = q4[j];
+          b0 = fmaf(k.x, qq.x, b0);
+          b1 = fmaf(k.y, qq.y, b1);
+          b2 = fmaf(k.z, qq.z, b2);
+          b3 = fmaf(k.w, qq.w, b3);
+        }
+        score = (b0 + b1) + (b2 + b3);
+      }
+      score += __shfl_xor_sync(0xffffffffu, score, 1);  // base (both halves)
+      float m = -INFINITY, ssum = 0.f;
+      if (live && centroid_on) {
+        const float4* fr = reinterpret_cast<const float4*>(tok_feats + tok * 64 + half * 32);
+        float f[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 v = fr[u];
+          f[4 * u] = v.x;
+          f[4 * u + 1] = v.y;
+          f[4 * u + 2] = v.z;
+          f[4 * u + 3] = v.w;
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int h = 2 * half + hh;
+          for (int j = 0; j < sm.sel_count[h]; ++j) {
+            const float4* sv4 = reinterpret_cast<const float4*>(sm.sel_val[h][j]);
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float4 v = sv4[u];
+              d0 = fmaf(f[16 * hh + 4 * u], v.x, d0);
+              d1 = fmaf(f[16 * hh + 4 * u + 1], v.y, d1);
+              d2 = fmaf(f[16 * hh + 4 * u + 2], v.z, d2);
+              d3 = fmaf(f[16 * hh + 4 * u + 3], v.w, d3);
+            }
+            const float x = __fadd_rn(__fdiv_rn((d0 + d1) + (d2 + d3), sqrt_dv), sm.sel_logalpha[h][j]);
+            if (x > m) {
+              ssum = fmaf(ssum, expf(m - x), 1.f);
+              m = x;
+            } else {
+              ssum += expf(x - m);
+            }
+          }
+        }
+      }
+      // every thread takes part in the pair exchange (the two threads of a
+      // token agree on live)
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, 1), s2 = __shfl_xor_sync(0xffffffffu, ssum, 1);
+      if (live && centroid_on) {
+        const float mm = fmaxf(m, m2);
+        const float se = (m == -INFINITY ? 0.f : ssum * expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - mm));
+        const float recall = __fadd_rn(mm, logf(se));
+        float tm = 0.f;
+        for (int w = 0; w < W; ++w) {  // modeling.py:929-938, memberships in order
+          int c = tok_cell[tok * W + w];
+          c = c > C - 1 ? C - 1 : c;
+          tm = __fadd_rn(tm, __fmul_rn(sm.mass[e * 32 + c], sm.wlut[tok_wq[tok * W + w]]));
+        }
+        score = __fadd_rn(__fadd_rn(score, __fmul_rn(gm, tm)), __fmul_rn(gr, recall));
+      }
+      if (inb && half == 0) {
+        unsigned long long kv = ~0ull;
+        if (live) {
+          const int id = tok_ids[tok];
+          if (id >= 0 && score == score) kv = ((unsigned long long)(uint32_t)id << 32) | (uint32_t)ci;
+        }
+        sm.cand[ci] = live ? score : -INFINITY;
+        sm.key[ci] = kv;
+        if (cand_out) cand_out[(sq * K + sm.e_k[e]) * L + p] = live ? score : -INFINITY;
+      }
+    }
+  }
+  for (int ci = pair_path ? n_cand : warp; ci < n_cand; ci += kRThreads / 32) {
     const int e = ci / L, p = ci % L;
     if (p >= sm.e_prefix[e]) {
       dead_token(ci, e);

@@ -148,9 +148,12 @@ def _oracle_query(store, s, qv, qh, sel, scores, prefix, prm, C):
     return ents, res
 
 
-def test_centroid_readout_random_against_oracle(cuda_device):
-    g = np.random.default_rng(11)
-    S, Nq, NB, L, W, C, dq, H, dk, dv, K = 2, 12, 20, 16, 2, 8, 24, 4, 8, 6, 6
+@pytest.mark.parametrize("dq,H,dv", [(24, 4, 6), (32, 4, 16), (128, 2, 16)])
+def test_centroid_readout_random_against_oracle(cuda_device, dq, H, dv):
+    # (32, 4, 16): the two-threads-per-token path for the reference's default
+    # 4 heads x 16 value dims; the others the warp-per-token path
+    g = np.random.default_rng(11 + dq + H)
+    S, Nq, NB, L, W, C, dk, K = 2, 12, 20, 16, 2, 8, 8, 6
     dev = cuda_device
     store, dirs = _random_store(g, S, NB, L, W, C, dq, H, dk, dv, 60, dev)
     Q = g.standard_normal((S, Nq, dq)).astype(np.float32)
