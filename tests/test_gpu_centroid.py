@@ -144,14 +144,25 @@ def _oracle_query(store, s, qv, qh, sel, scores, prefix, prm, C):
                          base_scores=(np_["token_keys"][b][:p].astype(np.float64) @ qv).astype(np.float32),
                          features=np_["token_features"][b][:p], block_score=float(sc), block=b))
     res = co.centroid_candidates(qh, ents, top_cells_per_head=prm.top_cells_per_head, min_selected=prm.min_selected,
-                                 cells_per_block=C, fdr_q=prm.fdr_q)
+                                 cells_per_block=C, fdr_q=prm.fdr_q, block_score_lambda=prm.block_score_lambda,
+                                 background_subtract=prm.background_subtract, count_penalty=prm.count_penalty,
+                                 self_field_weight=prm.self_field_weight, temperature=prm.temperature,
+                                 entropy_low=prm.entropy_low, entropy_high=prm.entropy_high, gamma_m=prm.gamma_m,
+                                 gamma_r=prm.gamma_r)
     return ents, res
 
 
-@pytest.mark.parametrize("dq,H,dv", [(24, 4, 6), (32, 4, 16), (128, 2, 16)])
-def test_centroid_readout_random_against_oracle(cuda_device, dq, H, dv):
+ALT_PARAMS = centroid.CentroidParams(top_cells_per_head=6, min_selected=3, fdr_q=0.3, background_subtract=False,
+                                     count_penalty=0.3, self_field_weight=0.0, temperature=0.7, block_score_lambda=0.5,
+                                     entropy_low=0.2, entropy_high=0.9, gamma_m=0.5, gamma_r=2.0)
+
+
+@pytest.mark.parametrize("dq,H,dv,alt", [(24, 4, 6, False), (32, 4, 16, False), (128, 2, 16, False),
+                                         (32, 4, 16, True)])
+def test_centroid_readout_random_against_oracle(cuda_device, dq, H, dv, alt):
     # (32, 4, 16): the two-threads-per-token path for the reference's default
-    # 4 heads x 16 value dims; the others the warp-per-token path
+    # 4 heads x 16 value dims; the others the warp-per-token path; alt: no
+    # background subtraction and other weights / gains
     g = np.random.default_rng(11 + dq + H)
     S, Nq, NB, L, W, C, dk, K = 2, 12, 20, 16, 2, 8, 8, 6
     dev = cuda_device
@@ -164,7 +175,7 @@ def test_centroid_readout_random_against_oracle(cuda_device, dq, H, dv):
     scores = g.standard_normal((S, Nq, K)).astype(np.float32)
     prefix = np.full((S, Nq, K), L, np.int32)
     prefix[1, 5, 0] = 9
-    prm = centroid.CentroidParams(top_cells_per_head=6, min_selected=2, fdr_q=0.2)
+    prm = ALT_PARAMS if alt else centroid.CentroidParams(top_cells_per_head=6, min_selected=2, fdr_q=0.2)
     out = centroid.centroid_readout(torch.from_numpy(Q).to(dev), torch.from_numpy(qh).to(dev),
                                     torch.from_numpy(sel).to(dev), torch.from_numpy(scores).to(dev),
                                     prefix_len=torch.from_numpy(prefix).to(dev), params=prm,
