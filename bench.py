@@ -407,7 +407,7 @@ def run_ours(args, rank, world, device) -> dict | None:
     value = world * tokens_per_step / (ms / 1e3)
     e2e_value = world * tokens_per_step / (e2e_ms / 1e3)
 
-    # algorithmic bytes per launch (see DESIGN.md "Roofline"):
+    # algorithmic bytes per launch:
     #   frames  -- unfused per-token contract: read U, A, B and write U
     #   readout -- unique key blocks selected by the step's 64 queries per stream,
     #              plus queries, selections and the value rows written back
