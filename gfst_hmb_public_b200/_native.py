@@ -89,6 +89,14 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
     ],
+    "gfst_segmented_max": [_c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p],
+    "gfst_segmented_logsumexp_occurrence": [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p, _c_void_p,
+        _c_void_p,
+    ],
+    "gfst_exact_block_score": [
+        _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+    ],
 }
 _RESTYPES = {
     "gfst_status_string": ctypes.c_char_p,

@@ -16,6 +16,10 @@ the last launch.  CASE is one of:
   readout_long  exact-token readout of 1024 queries x 8 blocks of 128 tokens per stream out of 8192 blocks
   commit_eig  reference-faithful block commit (float64 eigen summary) of 64 x 64 projector sums
   block_tracker  one 64-token block of the block tracker (d=64, r=32: update + QR + projector sums)
+  centroid_commit  centroid cell commit of 64-token blocks
+  centroid_readout  centroid readout of 64 queries x 8 blocks per stream
+  segmented   log-sum-exp collapse of one candidate list (--streams = elements, default 2048)
+  block_score block token scores through a 128 x 128 bf16 projection (--streams = tokens, default 65536)
 """
 from __future__ import annotations
 
@@ -44,7 +48,7 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
                                          "readout_long", "commit_eig", "block_tracker", "centroid_commit",
-                                         "centroid_readout"])
+                                         "centroid_readout", "segmented", "block_score"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     parser.add_argument("--qr-method", default="auto", choices=["auto", "householder", "cholesky2"],
@@ -130,6 +134,22 @@ def main() -> None:
             ms = _timed(lambda: centroid.centroid_readout(Q, qh, sel, sc, **store), args.repeat)
             per_q = K * L * (dq + H * dv) * 4
             units = f"{S * Nq / ms / 1e3:.2f} M queries/s, {S * Nq * per_q / ms / 1e6:.0f} GB/s of token rows"
+    elif args.case == "segmented":
+        n = args.streams or 2048
+        scores = torch.randn((n,), generator=g, device=dev)
+        inverse = torch.randint(0, max(1, n // 2), (n,), generator=g, device=dev)
+        groups = int(inverse.max()) + 1
+        blk = torch.randint(0, 512, (n,), generator=g, device=dev)
+        ms = _timed(lambda: readout.segmented_logsumexp_occurrence(scores, inverse, blk, blk, group_count=groups),
+                    args.repeat)
+        units = f"{n / ms / 1e3:.2f} M elements/s ({groups} groups)"
+    elif args.case == "block_score":
+        m = args.streams or 65536
+        q = torch.randn((128,), generator=g, device=dev).to(bf)
+        F = torch.randn((m, 128), generator=g, device=dev).to(bf)
+        Wp = torch.randn((128, 128), generator=g, device=dev).to(bf)
+        ms = _timed(lambda: readout.exact_block_score(q, F, Wp), args.repeat)
+        units = f"{2.0 * m * 128 * 128 / ms / 1e9:.2f} TFLOP/s, {m * 128 * 2 / ms / 1e6:.0f} GB/s of features"
     elif args.case == "tracker":
         S = args.streams or 2048
         tr = tracker.LocalTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), device=dev)

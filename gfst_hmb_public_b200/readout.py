@@ -4,7 +4,11 @@ Reference (pkhairkh/gfst-hmb-public): ExactRecallReadout._score_block_tokens
 (src/gfst_hmb_mpuc/modeling.py:599-657) scores every token of each retrieved
 block against the query, and the best-scoring token is the copy target
 (modeling.py:1151-1169).  Token ids here are positions (block * L + p), so the
-reference's log-sum-exp collapse by token id is the identity.
+reference's log-sum-exp collapse by token id is the identity; the collapse by
+stored token ids runs fused (exact_readout_collapse) or as the reference's
+standalone segmented reductions (segmented_max_by_group,
+segmented_logsumexp_occurrence).  exact_block_score scores a block's tokens
+through the within-block projection.
 """
 from __future__ import annotations
 
@@ -69,3 +73,105 @@ def exact_readout_collapse(Q: torch.Tensor, pool_K: torch.Tensor, token_ids: tor
                  n_slots, L, d, k, nat.dtype_code(Q.dtype, "exact_readout_collapse"), *(nat.ptr(t) for t in out),
                  nat.stream_of(Q))
     return tuple(out)
+
+
+SEGMENTED_MAX_ELEMENTS = 16384
+
+
+def _rank1(what: str, *tensors: torch.Tensor) -> int:
+    if any(t.ndim != 1 for t in tensors):
+        raise ValueError(f"{what}: inputs must be rank-1 tensors")
+    n = int(tensors[0].numel())
+    if any(int(t.numel()) != n for t in tensors):
+        raise ValueError(f"{what}: inputs must have matching element counts")
+    return n
+
+
+def segmented_max_by_group(scores: torch.Tensor, inverse: torch.Tensor, group_count: int) -> torch.Tensor:
+    """Per-group max of ``scores`` (runtime backend ``segmented_max_by_group``,
+    src/gfst_hmb_mpuc/csrc/sm120_stub.cu:16-40, 150-172): ``inverse[i]`` in
+    ``[0, group_count)`` names element i's group.  NaN scores are ignored (fmaxf);
+    an empty group gets -inf.  Returns float32 [group_count]."""
+    nat.require_cuda(scores, inverse, what="segmented_max_by_group")
+    n = _rank1("segmented_max_by_group", scores, inverse)
+    scores = scores.float().contiguous()
+    inverse = inverse.to(torch.int64).contiguous()
+    out = torch.empty((int(group_count),), dtype=torch.float32, device=scores.device)
+    with torch.cuda.device(scores.device):
+        nat.call("gfst_segmented_max", nat.ptr(scores), nat.ptr(inverse), n, int(group_count), nat.ptr(out),
+                 nat.stream_of(scores))
+    return out
+
+
+def segmented_logsumexp_occurrence(scores: torch.Tensor, inverse: torch.Tensor, occurrence_blocks: torch.Tensor,
+                                   occurrence_positions: torch.Tensor, *, group_count: int):
+    """Per-group log-sum-exp and best occurrence (runtime backend
+    ``segmented_logsumexp_occurrence``, src/gfst_hmb_mpuc/csrc/sm120_stub.cu:42-111,
+    174-208).  With m the group max: score m + log(max(sum exp(s - m), 1e-8)) and
+    the (block, position) of the group's lowest-index element scoring m when m is
+    finite; m + log(1e-8) and (-1, -1) otherwise.  Returns (grouped_scores f32,
+    grouped_blocks int64, grouped_positions int64), each [group_count]."""
+    nat.require_cuda(scores, inverse, occurrence_blocks, occurrence_positions, what="segmented_logsumexp_occurrence")
+    n = _rank1("segmented_logsumexp_occurrence", scores, inverse, occurrence_blocks, occurrence_positions)
+    scores = scores.float().contiguous()
+    inverse, blocks, positions = (t.to(torch.int64).contiguous()
+                                  for t in (inverse, occurrence_blocks, occurrence_positions))
+    g = int(group_count)
+    out = (torch.empty((g,), dtype=torch.float32, device=scores.device),
+           torch.empty((g,), dtype=torch.int64, device=scores.device),
+           torch.empty((g,), dtype=torch.int64, device=scores.device))
+    with torch.cuda.device(scores.device):
+        nat.call("gfst_segmented_logsumexp_occurrence", nat.ptr(scores), nat.ptr(inverse), nat.ptr(blocks),
+                 nat.ptr(positions), n, g, *(nat.ptr(t) for t in out), nat.stream_of(scores))
+    return out
+
+
+def collapse_max_scores_by_group(scores: torch.Tensor, group_ids: torch.Tensor):
+    """perf.collapse_max_scores_by_group (src/gfst_hmb_mpuc/perf.py:136-161) on the
+    segmented kernel: returns (unique_ids int64 sorted, grouped max f32)."""
+    n = _rank1("collapse_max_scores_by_group", scores, group_ids)
+    if n == 0:
+        return group_ids.new_empty((0,), dtype=torch.long), scores.new_empty((0,), dtype=torch.float32)
+    unique_ids, inverse = torch.unique(group_ids.to(torch.long), sorted=True, return_inverse=True)
+    return unique_ids, segmented_max_by_group(scores, inverse, int(unique_ids.numel()))
+
+
+def collapse_logsumexp_scores_and_occurrence(scores: torch.Tensor, group_ids: torch.Tensor,
+                                             occurrence_blocks: torch.Tensor, occurrence_positions: torch.Tensor):
+    """perf.collapse_logsumexp_scores_and_occurrence (src/gfst_hmb_mpuc/perf.py:164-229)
+    on the segmented kernel: returns (unique_ids, grouped_scores, grouped_blocks,
+    grouped_positions)."""
+    n = _rank1("collapse_logsumexp_scores_and_occurrence", scores, group_ids, occurrence_blocks,
+               occurrence_positions)
+    if n == 0:
+        empty_long = group_ids.new_empty((0,), dtype=torch.long)
+        return empty_long, scores.new_empty((0,), dtype=torch.float32), empty_long, empty_long
+    unique_ids, inverse = torch.unique(group_ids.to(torch.long), sorted=True, return_inverse=True)
+    grouped = segmented_logsumexp_occurrence(scores, inverse, occurrence_blocks, occurrence_positions,
+                                             group_count=int(unique_ids.numel()))
+    return (unique_ids, *grouped)
+
+
+def exact_block_score(query: torch.Tensor, token_features: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """Scores of a block's tokens through the within-block projection (runtime
+    backend ``exact_block_score``; projection exact_block_project_forward,
+    src/gfst_hmb_mpuc/csrc/sm120_cutlass_exact_block_score.cu:42-129, dotted with
+    the query as modeling.py:640-651 does): query [n]; token_features [m, k];
+    weight [n, k] (the bias-free Linear weight).  Returns float32 [m] =
+    (token_features @ weight.T) @ query, with bf16 roundings of the keys and the
+    score for bfloat16 inputs."""
+    nat.require_cuda(query, token_features, weight, what="exact_block_score")
+    if query.ndim != 1 or token_features.ndim != 2 or weight.ndim != 2:
+        raise ValueError("exact_block_score expects query [n], token_features [m, k], weight [n, k]")
+    m, k = token_features.shape
+    n, kw = weight.shape
+    if kw != k or query.shape[0] != n:
+        raise ValueError("exact_block_score: dimension mismatch")
+    if not (query.dtype == token_features.dtype == weight.dtype):
+        raise RuntimeError("exact_block_score: query, token_features and weight must share a dtype")
+    query, token_features, weight = query.contiguous(), token_features.contiguous(), weight.contiguous()
+    scores = torch.empty((m,), dtype=torch.float32, device=query.device)
+    with torch.cuda.device(query.device):
+        nat.call("gfst_exact_block_score", nat.ptr(query), nat.ptr(token_features), nat.ptr(weight), m, n, k,
+                 nat.dtype_code(query.dtype, "exact_block_score"), nat.ptr(scores), nat.stream_of(query))
+    return scores

@@ -41,6 +41,17 @@
  *                             src/gfst_hmb_mpuc/retrieval.py:136-172
  *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
  *                             src/gfst_hmb_mpuc/modeling.py:599-657, 1151-1169
+ *   gfst_segmented_max     <- runtime_backends segmented_max_by_group(scores, inverse, group_count)
+ *                             src/gfst_hmb_mpuc/csrc/sm120_stub.cu:16-40, 150-172, called by
+ *                             perf.collapse_max_scores_by_group perf.py:136-161
+ *   gfst_segmented_logsumexp_occurrence <- runtime_backends segmented_logsumexp_occurrence(
+ *                             scores, inverse, occurrence_blocks, occurrence_positions, group_count)
+ *                             src/gfst_hmb_mpuc/csrc/sm120_stub.cu:42-111, 174-208, called by
+ *                             perf.collapse_logsumexp_scores_and_occurrence perf.py:164-229
+ *   gfst_exact_block_score <- runtime_backends exact_block_score(query, token_features, W), the
+ *                             projection exact_block_project_forward
+ *                             src/gfst_hmb_mpuc/csrc/sm120_cutlass_exact_block_score.cu:42-129
+ *                             and its dot with the query, modeling.py:640-651
  */
 #ifndef GFST_B200_H_
 #define GFST_B200_H_
@@ -368,6 +379,34 @@ GFST_API int gfst_exact_readout(const void* Q, const void* pool_K, const void* p
                        int n_slots, int L, int d, int dv, int k, int dtype,
                        int32_t* best_tok, float* best_score, void* out_V,
                        cudaStream_t stream);
+
+/* ---- segmented reductions over group ids -------------------------------------
+ * inverse[i] in [0, group_count) names element i's group (elements outside
+ * that range take no part).  gfst_segmented_max: grouped[g] = max of the
+ * group's scores (fmaxf: NaN scores are ignored; -inf for an empty group).
+ * gfst_segmented_logsumexp_occurrence: with m the group max, grouped_scores[g]
+ * = m + logf(fmaxf(sum exp(s - m), 1e-8)) when m is finite, m + logf(1e-8)
+ * otherwise; grouped_blocks[g] / grouped_positions[g] = occurrence_blocks /
+ * occurrence_positions of the group's lowest-index element scoring m (-1 when
+ * m is not finite or the group is empty).  Each group's sum runs in element
+ * order.  All arrays are 1-D; outputs have group_count entries.
+ * Limits: n <= 16384, group_count <= 16384 (one CTA; the reference calls them
+ * on one query's candidate list).                                            */
+GFST_API int gfst_segmented_max(const float* scores, const int64_t* inverse, int64_t n,
+                       int64_t group_count, float* grouped, cudaStream_t stream);
+GFST_API int gfst_segmented_logsumexp_occurrence(const float* scores, const int64_t* inverse,
+                       const int64_t* occurrence_blocks, const int64_t* occurrence_positions,
+                       int64_t n, int64_t group_count, float* grouped_scores,
+                       int64_t* grouped_blocks, int64_t* grouped_positions, cudaStream_t stream);
+
+/* ---- block token scores through the within-block projection ------------------
+ * scores[t] = sum_j key[t, j] * query[j], key[t, j] = sum_c token_features[t, c] *
+ * weight[j, c] (fp32 accumulate).  GFST_BF16: key rounded to bf16 and the score
+ * rounded to bf16 before widening, as proj(F) @ q in bf16 is; GFST_F32: no
+ * rounding.  query: [n]; token_features: [m, k]; weight: [n, k] (the Linear
+ * weight, no bias); scores: [m] fp32.  m == 0 is a no-op.                    */
+GFST_API int gfst_exact_block_score(const void* query, const void* token_features, const void* weight,
+                       int64_t m, int n, int k, int dtype, float* scores, cudaStream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -405,6 +405,50 @@ def collapse_logsumexp(scores, token_ids, blocks, positions):
     return uid.numpy(), gs.numpy(), b.numpy(), p.numpy()
 
 
+def segmented_max(scores, inverse, group_count):
+    """sm120_stub.cu:16-40 (segmented_max_kernel), restated: per group the max
+    of its scores with fmaxf semantics (NaN ignored), -inf for an empty group;
+    elements whose group lies outside [0, group_count) take no part.  float32."""
+    s = np.asarray(scores, np.float32)
+    inv = np.asarray(inverse, np.int64)
+    out = np.full(int(group_count), -np.inf, np.float32)
+    for i in range(s.size):
+        g = int(inv[i])
+        if 0 <= g < group_count and not np.isnan(s[i]):
+            out[g] = max(out[g], s[i])
+    return out
+
+
+def segmented_logsumexp_occurrence(scores, inverse, blocks, positions, group_count):
+    """sm120_stub.cu:42-111 (segmented_logsumexp_occurrence_kernel), restated:
+    m = the group max (segmented_max); when m is finite, sum = sum exp(s - m)
+    over the group in element order and the occurrence is the lowest index with
+    s == m; otherwise sum = 0 and no occurrence (-1, -1).  score = m +
+    log(max(sum, 1e-8)), where a NaN sum counts as below 1e-8 (fmaxf).
+    float32 arithmetic throughout."""
+    s = np.asarray(scores, np.float32)
+    inv = np.asarray(inverse, np.int64)
+    bl = np.asarray(blocks, np.int64)
+    po = np.asarray(positions, np.int64)
+    m = segmented_max(s, inv, group_count)
+    gs = np.empty(int(group_count), np.float32)
+    gb = np.full(int(group_count), -1, np.int64)
+    gp = np.full(int(group_count), -1, np.int64)
+    with np.errstate(invalid="ignore", over="ignore"):
+        for g in range(int(group_count)):
+            total, best = np.float32(0.0), -1
+            if np.isfinite(m[g]):
+                for i in np.nonzero(inv == g)[0]:
+                    total = np.float32(total + np.exp(np.float32(s[i] - m[g]), dtype=np.float32))
+                    if best < 0 and s[i] == m[g]:
+                        best = int(i)
+            clamped = np.float32(1e-8) if not total >= np.float32(1e-8) else total
+            gs[g] = np.float32(m[g] + np.log(clamped, dtype=np.float32))
+            if best >= 0:
+                gb[g], gp[g] = bl[best], po[best]
+    return gs, gb, gp
+
+
 def exact_readout_collapse(Q, pool_K, token_ids, top_idx):
     """Readout with the token-id collapse: candidates = tokens of the selected
     blocks in selection order (modeling.py:599-657; a block listed twice counts

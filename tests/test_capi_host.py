@@ -95,6 +95,25 @@ def test_host_validation_rejects_without_launching():
     assert lib.gfst_centroid_readout(*args(4, 2, ctypes.cast(ctypes.pointer(bad_t), ctypes.c_void_p))) == 1
 
 
+def test_segmented_and_block_score_host_rejects():
+    import ctypes
+
+    lib = nat.load()
+    fake = ctypes.c_void_p(256)  # never dereferenced: every call below returns before any launch
+    assert lib.gfst_segmented_max(None, None, 16385, 4, fake, None) == 2
+    assert lib.gfst_segmented_max(None, None, 8, 16385, fake, None) == 2
+    assert lib.gfst_segmented_max(None, None, -1, 4, fake, None) == 1
+    assert lib.gfst_segmented_max(None, None, 8, 0, None, None) == 0
+    assert lib.gfst_segmented_max(fake, fake, 8, 4, None, None) == 1
+    assert lib.gfst_segmented_logsumexp_occurrence(fake, fake, fake, fake, 8, 4, fake, None, fake, None) == 1
+    assert lib.gfst_segmented_logsumexp_occurrence(fake, fake, None, fake, 8, 4, fake, fake, fake, None) == 1
+    assert lib.gfst_segmented_logsumexp_occurrence(None, None, None, None, 20000, 4, fake, fake, fake, None) == 2
+    assert lib.gfst_exact_block_score(None, None, None, -1, 8, 8, 1, None, None) == 1
+    assert lib.gfst_exact_block_score(None, None, None, 0, 8, 8, 1, None, None) == 0
+    assert lib.gfst_exact_block_score(None, None, None, 4, 8, 8, 1, None, None) == 1
+    assert lib.gfst_exact_block_score(fake, fake, fake, 4, 8, 8, 5, fake, None) == 7
+
+
 def test_python_ops_reject_cpu_tensors():
     import torch
 
@@ -107,6 +126,12 @@ def test_python_ops_reject_cpu_tensors():
     with pytest.raises(RuntimeError):
         readout.exact_readout(torch.randn(1, 2, 8), torch.randn(1, 2, 4, 8), None,
                               torch.zeros(1, 2, 2, dtype=torch.int32))
+    with pytest.raises(RuntimeError):
+        readout.segmented_logsumexp_occurrence(torch.randn(4), torch.zeros(4, dtype=torch.long),
+                                               torch.zeros(4, dtype=torch.long), torch.zeros(4, dtype=torch.long),
+                                               group_count=1)
+    with pytest.raises(RuntimeError):
+        readout.exact_block_score(torch.randn(8), torch.randn(3, 8), torch.randn(8, 8))
     from gfst_hmb_public_b200 import tracker
 
     with pytest.raises(RuntimeError):

@@ -169,6 +169,26 @@ def test_readout_collapse_matches_reference():
         assert np.array_equal(got, z[key])
 
 
+def test_segmented_oracle_matches_reference():
+    """The restatement of the CUDA segmented kernels agrees with the reference's
+    native collapse on its golden list, and with the max collapse."""
+    z = load("readout_collapse.npz")
+    uid, inv = np.unique(z["token_ids"], return_inverse=True)
+    assert np.array_equal(uid, z["unique_ids"])
+    gs, gb, gp = go.segmented_logsumexp_occurrence(z["scores"], inv, z["blocks"], z["positions"], uid.size)
+    assert np.array_equal(gs, z["grouped_scores"])
+    assert np.array_equal(gb, z["grouped_blocks"]) and np.array_equal(gp, z["grouped_positions"])
+    mx = go.segmented_max(z["scores"], inv, uid.size)
+    want = np.full(uid.size, -np.inf, np.float32)
+    np.maximum.at(want, inv, z["scores"])
+    assert np.array_equal(mx, want)
+    # non-finite maxima take the stub's branch: no occurrence, score m + log(1e-8)
+    gs, gb, gp = go.segmented_logsumexp_occurrence(np.array([-np.inf, np.inf, 1.0, np.nan], np.float32),
+                                                   np.array([0, 1, 1, 2]), np.arange(4), np.arange(4) + 10, 4)
+    assert gs[0] == -np.inf and gs[1] == np.inf and gs[2] == -np.inf and gs[3] == -np.inf
+    assert list(gb) == [-1, -1, -1, -1] and list(gp) == [-1, -1, -1, -1]
+
+
 def centroid_case_blocks(z, ci):
     """Block entries of golden centroid case ci, in the layout centroid_candidates takes."""
     ents, off = [], 0
