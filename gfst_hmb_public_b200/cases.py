@@ -1,6 +1,6 @@
 """Single-kernel cases for profiling (ncu) and quick timing.
 
-    python -m gfst_hmb_public_b200.cases CASE [--streams S] [--repeat R]
+    python -m gfst_hmb_public_b200.cases CASE [--streams S] [--repeat R] [--batch B]
 
 Each case builds seeded inputs on cuda:0, launches its kernel ``repeat`` times
 (the first launch is a warm-up) and prints one line with the CUDA-event time of
@@ -31,16 +31,20 @@ import torch
 from . import block_commit, centroid, gfst, memory, readout, retrieval, tracker, workloads as wl
 
 
-def _timed(fn, repeat: int) -> float:
+def _timed(fn, repeat: int, batch: int = 1) -> float:
+    """CUDA-event time of the last of ``repeat`` rounds; a round is ``batch``
+    back-to-back calls and the time is per call (batch > 1 hides the Python
+    call overhead of microsecond kernels)."""
     ms = 0.0
     for _ in range(repeat):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        fn()
+        for _ in range(batch):
+            fn()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
+        ms = e0.elapsed_time(e1) / batch
     return ms
 
 
@@ -51,6 +55,7 @@ def main() -> None:
                                          "centroid_readout", "segmented", "block_score"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
+    parser.add_argument("--batch", type=int, default=1, help="calls per timed round (segmented, block_score)")
     parser.add_argument("--qr-method", default="auto", choices=["auto", "householder", "cholesky2"],
                         help="QR of the frames case")
     args = parser.parse_args()
@@ -141,14 +146,14 @@ def main() -> None:
         groups = int(inverse.max()) + 1
         blk = torch.randint(0, 512, (n,), generator=g, device=dev)
         ms = _timed(lambda: readout.segmented_logsumexp_occurrence(scores, inverse, blk, blk, group_count=groups),
-                    args.repeat)
+                    args.repeat, args.batch)
         units = f"{n / ms / 1e3:.2f} M elements/s ({groups} groups)"
     elif args.case == "block_score":
         m = args.streams or 65536
         q = torch.randn((128,), generator=g, device=dev).to(bf)
         F = torch.randn((m, 128), generator=g, device=dev).to(bf)
         Wp = torch.randn((128, 128), generator=g, device=dev).to(bf)
-        ms = _timed(lambda: readout.exact_block_score(q, F, Wp), args.repeat)
+        ms = _timed(lambda: readout.exact_block_score(q, F, Wp), args.repeat, args.batch)
         units = f"{2.0 * m * 128 * 128 / ms / 1e9:.2f} TFLOP/s, {m * 128 * 2 / ms / 1e6:.0f} GB/s of features"
     elif args.case == "tracker":
         S = args.streams or 2048

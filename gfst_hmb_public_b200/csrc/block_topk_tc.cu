@@ -20,8 +20,8 @@
 // Every mbarrier wait is bounded (about a second of clock cycles); a wait that
 // gives up sets a sticky device error word (read with gfst_check_device_errors)
 // and the CTA drains its in-flight copies and MMAs, frees TMEM and returns.
-#include "async_copy.cuh"
 #include "block_topk.cuh"
+#include "umma.cuh"
 
 namespace gfst {
 
@@ -44,47 +44,8 @@ struct TcWarps {
   static constexpr int kPartN = BN / (EPW / 4);  // accumulator columns per epilogue warp
 };
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 128B-swizzled, K-major operand: 8-row core groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4)  // start address
-         | ((uint64_t)1 << 16)                // leading byte offset (unused for swizzled K-major)
-         | ((uint64_t)(1024 >> 4) << 32)      // stride byte offset: next 8-row group
-         | ((uint64_t)1 << 46)                // descriptor version (sm_100)
-         | ((uint64_t)2 << 61);               // 128-byte swizzle
-}
-
-// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M=128, N=BN.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// kind::f16 instruction descriptor of the score tile.
+constexpr uint32_t kIdesc = idesc_bf16(BM, BN);
 
 template <int NKB, int STAGES>
 struct TcLayout {
@@ -143,10 +104,7 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * BN)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc(tmem_slot, 2 * BN);
   }
   tc_fence_before();
   __syncthreads();
@@ -196,7 +154,7 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 1)
             const int kb = kk >> 2, koff = (kk & 3) * 32;
             const uint64_t ad = sw128_desc(smem_u32(sA + kb * BM * 128) + koff);
             const uint64_t bd = sw128_desc(smem_u32(sB + (st * NKB + kb) * BN * 128) + koff);
-            umma_bf16(d_tmem, ad, bd, kk > 0 ? 1u : 0u);
+            umma_bf16(d_tmem, ad, bd, kIdesc, kk > 0 ? 1u : 0u);
           }
           umma_commit(&empty[st]);
           umma_commit(&tfull[acc]);
@@ -302,7 +260,7 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 1)
     if (!mbar_wait(done, 0)) *abort_flag = 1;
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+    tmem_dealloc(tmem, 2 * BN);
   }
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_device_error, (unsigned)GFST_ERR_TIMEOUT);

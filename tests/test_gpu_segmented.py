@@ -116,7 +116,13 @@ def _block_score_ref(q, F, W):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("m,n,k", [(64, 128, 128), (128, 128, 128), (17, 40, 72), (1, 8, 8), (300, 264, 100)])
+@pytest.mark.parametrize("m,n,k", [
+    # tensor-core kernel (bf16, k % 64 == 0, n % 16 == 0): one block, a few tiles, many tiles per CTA,
+    # n not a multiple of 32, the largest W that fits, a single token
+    (64, 128, 128), (128, 128, 128), (300, 256, 64), (1000, 48, 192), (70001, 128, 128), (129, 16, 256),
+    (517, 256, 192), (1, 128, 128),
+    # SIMT kernel (other shapes; W too large for shared memory next to two tiles)
+    (17, 40, 72), (1, 8, 8), (300, 264, 100), (33, 256, 256)])
 def test_exact_block_score(cuda_device, dtype, m, n, k):
     g = torch.Generator().manual_seed(m * 1000 + n + k)
     q = torch.randn(n, generator=g).to(dtype)
