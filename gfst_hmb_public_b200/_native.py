@@ -22,6 +22,7 @@ SIGN_FIRST_SIGNIFICANT = 0
 SIGN_R_DIAG_POSITIVE = 1
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+DTYPE_F64 = 2
 
 _c_void_p = ctypes.c_void_p
 _c_int = ctypes.c_int
@@ -94,6 +95,8 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p, _c_void_p,
         _c_void_p,
     ],
+    "gfst_exact_block_materialize": [_c_void_p, _c_int64, _c_int, _c_int64, _c_int64, _c_void_p, _c_void_p],
+    "gfst_heev": [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "gfst_exact_block_score": [
         _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
     ],

@@ -130,3 +130,55 @@ def global_features(projector_bank: torch.Tensor, sel_idx: torch.Tensor, sel_sco
     if return_basis:
         out.append(basis)
     return out[0] if len(out) == 1 else tuple(out)
+
+
+def gfst_global_sketch(*, summary_projectors: torch.Tensor, final_indices: torch.Tensor, final_scores: torch.Tensor,
+                       reduced_token: torch.Tensor, retrieval_temperature: float, flag_dims: Sequence[int],
+                       max_flag_dim: int, eps: float):
+    """runtime_backends.gfst_global_sketch with the keywords of its call site
+    (modeling.py:3021-3030): one request -- summary_projectors [NB, d, d],
+    final_indices [K] (into summary_projectors), final_scores [K], reduced_token
+    [d] -- on the kernel ``gfst_global_features``.  Returns (features
+    [2 * len(flag_dims)], global_sketch [d, d], eig_basis [d, max_flag_dim])."""
+    nat.require_cuda(summary_projectors, final_indices, final_scores, reduced_token, what="gfst_global_sketch")
+    if summary_projectors.ndim != 3 or final_indices.ndim != 1 or final_scores.shape != final_indices.shape \
+            or reduced_token.ndim != 1:
+        raise ValueError("gfst_global_sketch expects projectors [NB, d, d], indices [K], scores [K], token [d]")
+    bank = summary_projectors.float()[None]
+    idx = final_indices.to(torch.int32)[None, None]
+    sc = final_scores.float()[None, None]
+    x = reduced_token.float()[None, None]
+    feats, sketch, basis = global_features(bank, idx, sc, x, temperature=float(retrieval_temperature),
+                                           flag_dims=flag_dims, max_flag_dim=int(max_flag_dim), eps=float(eps),
+                                           return_sketch=True, return_basis=True)
+    return feats[0, 0], sketch[0, 0], basis[0, 0]
+
+
+def gfst_heev(matrices: torch.Tensor, *, check: bool = True):
+    """runtime_backends.gfst_heev (native gfst_heev_sm120_forward,
+    src/gfst_hmb_mpuc/csrc/mathdx/mathdx_runtime.cu:620-650, 750-780; called at
+    modeling.py:3181): batched symmetric eigendecomposition of [d, d] or
+    [B, d, d] float32 / float64 matrices (lower triangle read, d <= 64),
+    computed in float64.  Returns (eigenvalues [..., d] ascending, eigenvectors
+    [..., d, d] with column j for eigenvalue j) in the input dtype.  With
+    ``check`` a matrix whose iteration did not converge raises RuntimeError, as
+    the reference's info check does (this waits for the stream)."""
+    nat.require_cuda(matrices, what="gfst_heev")
+    if matrices.ndim not in (2, 3) or matrices.shape[-1] != matrices.shape[-2]:
+        raise ValueError("gfst_heev expects [d, d] or [B, d, d] matrices")
+    if matrices.dtype not in (torch.float32, torch.float64):
+        raise RuntimeError(f"gfst_heev: unsupported dtype {matrices.dtype} (float32 or float64)")
+    single = matrices.ndim == 2
+    a = (matrices[None] if single else matrices).contiguous()
+    B, d = int(a.shape[0]), int(a.shape[-1])
+    vals = torch.empty((B, d), dtype=a.dtype, device=a.device)
+    vecs = torch.empty((B, d, d), dtype=a.dtype, device=a.device)
+    info = torch.empty((B,), dtype=torch.int32, device=a.device)
+    code = nat.DTYPE_F32 if a.dtype == torch.float32 else nat.DTYPE_F64
+    with torch.cuda.device(a.device):
+        nat.call("gfst_heev", nat.ptr(a), B, d, code, nat.ptr(vals), nat.ptr(vecs), nat.ptr(info),
+                 nat.stream_of(a))
+    if check and B > 0 and bool((info != 0).any()):
+        raise RuntimeError("gfst_heev: the Jacobi iteration did not converge for "
+                           f"{int((info != 0).sum())} of {B} matrices")
+    return (vals[0], vecs[0]) if single else (vals, vecs)

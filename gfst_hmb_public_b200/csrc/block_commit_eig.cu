@@ -98,12 +98,12 @@ __device__ __forceinline__ T first_significant_sign(const T* col, int stride, in
   return T(1);
 }
 
-// The canonical top basis of the symmetric float64 matrix in sm.a (order d,
-// padded to even n): eigenpairs by Jacobi, clusters from the top, canonical
-// cluster bases (float64, in sm.fb), then the float32 basis with its signs
-// fixed again, written to fb32 [d][target] (which may alias sm.a once the
-// eigenpairs are known).  Every thread of the CTA calls; failures set sm.fail.
-__device__ void canonical_top_basis(EigSmem& sm, int d, int target, double eps_sign) {
+// Eigenpairs of the symmetric float64 matrix in sm.a (order d, padded to an
+// even n with an isolated zero index): cyclic Jacobi in tournament order, V in
+// sm.v (column j for the eigenvalue left in sm.a[j][j]), and sm.order = the
+// indices < d by ascending eigenvalue (ties by index).  Every thread of the
+// CTA calls; 40 sweeps without convergence set sm.fail.
+__device__ void jacobi_eigen(EigSmem& sm, int d) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = d + (d & 1);
   for (int e = tid; e < n * n; e += kEigThreads) {
@@ -189,6 +189,16 @@ __device__ void canonical_top_basis(EigSmem& sm, int d, int target, double eps_s
     sm.order[pos] = i;
   }
   __syncthreads();
+}
+
+// The canonical top basis of the symmetric float64 matrix in sm.a (order d,
+// padded to even n): eigenpairs by Jacobi, clusters from the top, canonical
+// cluster bases (float64, in sm.fb), then the float32 basis with its signs
+// fixed again, written to fb32 [d][target] (which may alias sm.a once the
+// eigenpairs are known).  Every thread of the CTA calls; failures set sm.fail.
+__device__ void canonical_top_basis(EigSmem& sm, int d, int target, double eps_sign) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  jacobi_eigen(sm, d);
 
   // ---- clusters from the top (gfst.py:248-297) ----
   if (tid == 0) {
@@ -431,6 +441,50 @@ __global__ void __launch_bounds__(kEigThreads) global_features_kernel(
   if (tid == 0 && sm.fail) atomicExch(&g_commit_error, (unsigned)GFST_ERR_NUMERIC);
 }
 
+// ---------------------------------------------------------------------------
+// batched symmetric eigendecomposition (one CTA per matrix)
+// ---------------------------------------------------------------------------
+// The lower triangle of each d x d matrix (LAPACK's uplo = 'L'), widened to
+// float64; eigenvalues ascending; column j of the eigenvector matrix belongs
+// to eigenvalue j, its sign fixed so that its largest-magnitude entry (the
+// lowest index among equal magnitudes) is positive.
+template <typename T>
+__global__ void __launch_bounds__(kEigThreads) heev_kernel(const T* __restrict__ A, int d, T* __restrict__ eigvals,
+                                                           T* __restrict__ eigvecs, int32_t* __restrict__ info) {
+  extern __shared__ __align__(16) unsigned char dyn_raw[];
+  EigSmem& sm = *reinterpret_cast<EigSmem*>(dyn_raw);
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int n = d + (d & 1);
+  const T* a = A + b * (int64_t)d * d;
+  if (tid == 0) sm.fail = 0;
+  for (int e = tid; e < n * n; e += kEigThreads) {
+    const int i = e / n, j = e % n;
+    sm.a[i][j] = (i < d && j < d) ? (double)(i >= j ? a[i * d + j] : a[j * d + i]) : 0.0;
+  }
+  __syncthreads();
+  jacobi_eigen(sm, d);
+  for (int j = tid; j < d; j += kEigThreads) {
+    const int src = sm.order[j];
+    eigvals[b * d + j] = (T)sm.a[src][src];
+    int imax = 0;
+    double vmax = -1.0;
+    for (int i = 0; i < d; ++i) {
+      const double x = fabs(sm.v[i][src]);
+      if (x > vmax) {
+        vmax = x;
+        imax = i;
+      }
+    }
+    const double sg = sm.v[imax][src] < 0.0 ? -1.0 : 1.0;
+    for (int i = 0; i < d; ++i) eigvecs[b * (int64_t)d * d + i * d + j] = (T)(sg * sm.v[i][src]);
+  }
+  if (tid == 0) {
+    if (info != nullptr) info[b] = sm.fail ? 1 : 0;
+    if (sm.fail) atomicExch(&g_commit_error, (unsigned)GFST_ERR_NUMERIC);
+  }
+}
+
 }  // namespace
 }  // namespace gfst
 
@@ -495,4 +549,30 @@ extern "C" int gfst_global_features(const float* projector_bank, const int32_t* 
       projector_bank, sel_idx, sel_scores, x, n_queries, n_blocks, d, k, temperature, max_flag_dim, target, dims,
       eps, eps_sign, features, sketch_out, basis_out);
   return check_launch("global_features_kernel");
+}
+
+extern "C" int gfst_heev(const void* matrices, int64_t batch, int d, int dtype, void* eigenvalues,
+                         void* eigenvectors, int32_t* info, cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(batch >= 0, GFST_ERR_ARG, "negative batch");
+  GFST_REQUIRE(d >= 1 && d <= kEigMaxD, GFST_ERR_SHAPE, "d=%d outside [1, %d]", d, kEigMaxD);
+  GFST_REQUIRE(dtype == GFST_F32 || dtype == GFST_F64, GFST_ERR_DTYPE, "unsupported dtype %d (f32 or f64)", dtype);
+  if (batch == 0) return GFST_OK;
+  GFST_REQUIRE(matrices && eigenvalues && eigenvectors, GFST_ERR_ARG, "null buffer");
+  GFST_REQUIRE(batch <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many matrices");
+  const size_t smem = sizeof(EigSmem);
+  if (dtype == GFST_F32) {
+    cudaError_t e = cudaFuncSetAttribute(heev_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    heev_kernel<float><<<(unsigned)batch, kEigThreads, smem, stream>>>(
+        static_cast<const float*>(matrices), d, static_cast<float*>(eigenvalues), static_cast<float*>(eigenvectors),
+        info);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(heev_kernel<double>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    heev_kernel<double><<<(unsigned)batch, kEigThreads, smem, stream>>>(
+        static_cast<const double*>(matrices), d, static_cast<double*>(eigenvalues),
+        static_cast<double*>(eigenvectors), info);
+  }
+  return check_launch("heev_kernel");
 }

@@ -97,3 +97,22 @@ class BlockMemory:
         for b in range(max(0, self.blocks_committed - self.n_slots), self.blocks_committed):
             idx[b % self.n_slots] = b
         return idx
+
+
+def exact_block_materialize(packed: torch.Tensor, start: int, end: int) -> torch.Tensor:
+    """runtime_backends.exact_block_materialize (native
+    exact_block_materialize_forward, src/gfst_hmb_mpuc/csrc/sm120_stub.cu:225-245;
+    called at state.py:568): a new tensor holding packed[start:end] of a 1-D
+    contiguous CUDA tensor, copied by the sm_100a copy kernel.  Raises
+    RuntimeError for a range outside the tensor, as the reference's checks do."""
+    nat.require_cuda(packed, what="exact_block_materialize")
+    if packed.ndim != 1:
+        raise RuntimeError("exact_block_materialize: packed must be rank 1")
+    if not packed.is_contiguous():
+        raise RuntimeError("exact_block_materialize: packed must be contiguous")
+    start, end = int(start), int(end)
+    out = torch.empty((max(end - start, 0),), dtype=packed.dtype, device=packed.device)
+    with torch.cuda.device(packed.device):
+        nat.call("gfst_exact_block_materialize", nat.ptr(packed), int(packed.numel()), int(packed.element_size()),
+                 start, end, nat.ptr(out), nat.stream_of(packed))
+    return out

@@ -48,6 +48,12 @@
  *                             scores, inverse, occurrence_blocks, occurrence_positions, group_count)
  *                             src/gfst_hmb_mpuc/csrc/sm120_stub.cu:42-111, 174-208, called by
  *                             perf.collapse_logsumexp_scores_and_occurrence perf.py:164-229
+ *   gfst_exact_block_materialize <- runtime_backends exact_block_materialize(packed, start, end)
+ *                             src/gfst_hmb_mpuc/csrc/sm120_stub.cu:225-245, called at
+ *                             state.py:568 (_materialize_exact_block)
+ *   gfst_heev              <- runtime_backends gfst_heev(matrices) / native gfst_heev_sm120_forward
+ *                             src/gfst_hmb_mpuc/csrc/mathdx/mathdx_runtime.cu:113-170, 620-650, 750-780
+ *                             (batched symmetric eigendecomposition, called at modeling.py:3181)
  *   gfst_exact_block_score <- runtime_backends exact_block_score(query, token_features, W), the
  *                             projection exact_block_project_forward
  *                             src/gfst_hmb_mpuc/csrc/sm120_cutlass_exact_block_score.cu:42-129
@@ -106,7 +112,7 @@ enum gfst_qr_method {
 };
 
 /* Element types of key / value / query / summary buffers. */
-enum gfst_dtype { GFST_F32 = 0, GFST_BF16 = 1 };
+enum gfst_dtype { GFST_F32 = 0, GFST_BF16 = 1, GFST_F64 = 2 };
 
 /* Human-readable text of a status code (static storage). */
 GFST_API const char* gfst_status_string(int status);
@@ -407,6 +413,24 @@ GFST_API int gfst_segmented_logsumexp_occurrence(const float* scores, const int6
  * weight, no bias); scores: [m] fp32.  m == 0 is a no-op.                    */
 GFST_API int gfst_exact_block_score(const void* query, const void* token_features, const void* weight,
                        int64_t m, int n, int k, int dtype, float* scores, cudaStream_t stream);
+
+/* ---- batched symmetric eigendecomposition -----------------------------------
+ * For each of `batch` d x d matrices (row-major, the lower triangle is read):
+ * eigenvalues ascending [batch, d]; eigenvectors [batch, d, d] with column j
+ * the unit eigenvector of eigenvalue j, signed so that its largest-magnitude
+ * entry (lowest index on ties) is positive.  Computed in float64 (cyclic
+ * Jacobi); dtype GFST_F32 or GFST_F64 for inputs and outputs.  info (may be
+ * NULL): [batch] int32, 0 = converged, 1 = not converged in 40 sweeps (also
+ * recorded as GFST_ERR_NUMERIC for gfst_check_device_errors).  1 <= d <= 64. */
+GFST_API int gfst_heev(const void* matrices, int64_t batch, int d, int dtype, void* eigenvalues,
+                       void* eigenvectors, int32_t* info, cudaStream_t stream);
+
+/* ---- slice of a packed store ------------------------------------------------
+ * out[0 : end - start] = packed[start : end], elements of elem_size bytes
+ * (packed holds n_elements).  0 <= start <= end <= n_elements; an empty range
+ * is a no-op.                                                                 */
+GFST_API int gfst_exact_block_materialize(const void* packed, int64_t n_elements, int elem_size, int64_t start,
+                       int64_t end, void* out, cudaStream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -112,6 +112,14 @@ def test_segmented_and_block_score_host_rejects():
     assert lib.gfst_exact_block_score(None, None, None, 0, 8, 8, 1, None, None) == 0
     assert lib.gfst_exact_block_score(None, None, None, 4, 8, 8, 1, None, None) == 1
     assert lib.gfst_exact_block_score(fake, fake, fake, 4, 8, 8, 5, fake, None) == 7
+    assert lib.gfst_heev(fake, 4, 65, 2, fake, fake, None, None) == 2
+    assert lib.gfst_heev(fake, 4, 8, 1, fake, fake, None, None) == 7
+    assert lib.gfst_heev(None, 0, 8, 2, None, None, None, None) == 0
+    assert lib.gfst_heev(None, 2, 8, 2, None, None, None, None) == 1
+    assert lib.gfst_exact_block_materialize(fake, 10, 4, -1, 2, fake, None) == 1
+    assert lib.gfst_exact_block_materialize(fake, 10, 4, 5, 4, fake, None) == 1
+    assert lib.gfst_exact_block_materialize(fake, 10, 4, 5, 11, fake, None) == 1
+    assert lib.gfst_exact_block_materialize(None, 10, 4, 3, 3, None, None) == 0
 
 
 def test_python_ops_reject_cpu_tensors():

@@ -162,3 +162,79 @@ def test_global_features_invalid_selections(cuda_device):
     ref, _ = go.global_features(bank.numpy(), sel.numpy(), scores.numpy(), x.numpy(), 1.0, (2, 4), 4)
     np.testing.assert_allclose(feats.cpu().numpy(), ref, atol=1e-5)
     assert (feats[0, 1] == 0).all()
+
+
+def test_global_sketch_single_request_matches_batched(cuda_device):
+    """gfst_global_sketch (the reference's keyword form, one request) is the
+    batched kernel at S = Nq = 1, and its sketch is the softmax-weighted sum."""
+    z = np.load(GOLDEN / "global_features.npz")
+    dims = [int(v) for v in z["flag_dims"]]
+    bank = torch.from_numpy(z["bank"][0]).to(cuda_device)
+    idx = torch.from_numpy(z["sel"][0, 0]).long().to(cuda_device)
+    sc = torch.from_numpy(z["scores"][0, 0]).to(cuda_device)
+    x = torch.from_numpy(z["x"][0, 0]).to(cuda_device)
+    feats, sketch, basis = block_commit.gfst_global_sketch(
+        summary_projectors=bank, final_indices=idx, final_scores=sc, reduced_token=x, retrieval_temperature=1.0,
+        flag_dims=dims, max_flag_dim=max(dims), eps=1e-6)
+    bf, bs, bb = block_commit.global_features(bank[None], idx.int()[None, None], sc[None, None], x[None, None],
+                                              flag_dims=dims, max_flag_dim=max(dims), eps=1e-6, return_sketch=True,
+                                              return_basis=True)
+    assert torch.equal(feats, bf[0, 0]) and torch.equal(sketch, bs[0, 0]) and torch.equal(basis, bb[0, 0])
+    w = torch.softmax(sc.double(), 0)
+    ref = torch.einsum("k,kij->ij", w, bank.double()[idx])
+    assert (sketch.double() - ref).abs().max() < 1e-6
+    np.testing.assert_allclose(feats.cpu().numpy(), z["features"][0, 0], atol=1e-5)
+
+
+def _eigh_check(a, vals, vecs, tol):
+    """eigenvalues against torch.linalg.eigh (float64, lower triangle), eigen
+    vectors through reconstruction, orthonormality and the sign rule."""
+    a64 = a.double().cpu()
+    w_ref = torch.linalg.eigh(a64, UPLO="L")[0]
+    sym = torch.tril(a64) + torch.tril(a64, -1).transpose(-1, -2)
+    v, w = vecs.double().cpu(), vals.double().cpu()
+    scale = sym.abs().amax(dim=(-1, -2), keepdim=True).clamp_min(1e-300)
+    assert ((w - w_ref).abs() / scale[..., 0]).max() < tol
+    assert torch.all(w[..., 1:] >= w[..., :-1])
+    rec = v @ torch.diag_embed(w) @ v.transpose(-1, -2)
+    assert ((rec - sym).abs() / scale).max() < 10 * tol
+    eye = torch.eye(a.shape[-1], dtype=torch.float64)
+    assert (v.transpose(-1, -2) @ v - eye).abs().max() < 10 * tol
+    # largest-magnitude entry of every column is positive
+    idx = v.abs().argmax(dim=-2, keepdim=True)
+    assert torch.all(torch.gather(v, -2, idx) > 0)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-12), (torch.float32, 2e-6)])
+@pytest.mark.parametrize("B,d", [(37, 64), (5, 33), (3, 1), (64, 16), (8, 4)])
+def test_heev_matches_torch_eigh(cuda_device, dtype, tol, B, d):
+    g = torch.Generator().manual_seed(B * 100 + d)
+    x = torch.randn((B, d, d), generator=g, dtype=torch.float64)
+    a = (x + x.transpose(-1, -2)).to(dtype)
+    vals, vecs = block_commit.gfst_heev(a.to(cuda_device))
+    assert vals.dtype == dtype and vecs.shape == (B, d, d)
+    _eigh_check(a, vals, vecs, tol)
+
+
+def test_heev_repeated_eigenvalues_and_lower_triangle(cuda_device):
+    g = torch.Generator().manual_seed(3)
+    d = 32
+    # projector sums: eigenvalues 0 and 1 repeated, the summary-cache case
+    q = torch.linalg.qr(torch.randn((4, d, 8), generator=g, dtype=torch.float64))[0]
+    p = q @ q.transpose(-1, -2)
+    vals, vecs = block_commit.gfst_heev(p.to(cuda_device))
+    _eigh_check(p, vals, vecs, 1e-12)
+    top = vecs[:, :, -8:].cpu()
+    assert (top @ top.transpose(-1, -2) - p).abs().max() < 1e-10
+    # only the lower triangle is read
+    a = torch.randn((d, d), generator=g, dtype=torch.float64)
+    vals1, vecs1 = block_commit.gfst_heev(a.to(cuda_device))
+    vals2, vecs2 = block_commit.gfst_heev(torch.tril(a).to(cuda_device))
+    assert torch.equal(vals1, vals2) and torch.equal(vecs1, vecs2)
+    _eigh_check(a[None], vals1[None], vecs1[None], 1e-12)
+    # empty batch, rejects
+    e = block_commit.gfst_heev(torch.empty((0, 4, 4), dtype=torch.float64, device=cuda_device))
+    assert e[0].shape == (0, 4)
+    with pytest.raises(RuntimeError):
+        block_commit.gfst_heev(torch.zeros((2, 65, 65), dtype=torch.float64, device=cuda_device))
+    assert _native.load().gfst_check_device_errors(1) == 0

@@ -367,3 +367,18 @@ def test_readout_collapse_edge_cases(cuda_device):
         assert np.array_equal(g_t.cpu().numpy()[ok], r_t[ok])
     assert got[0][0, 4].item() == -1 and got[2][0, 4].item() == -1
     assert torch.isinf(got[1][0, 4]).item()
+
+
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64, torch.uint8, torch.bfloat16])
+def test_exact_block_materialize_slices(cuda_device, dtype):
+    g = torch.Generator().manual_seed(11)
+    packed = torch.randint(0, 120, (1000,), generator=g).to(dtype)
+    dev = packed.to(cuda_device)
+    for start, end in [(0, 1000), (0, 0), (7, 7), (3, 250), (128, 512), (999, 1000), (1, 998)]:
+        got = memory.exact_block_materialize(dev, start, end)
+        assert got.dtype == dtype and torch.equal(got.cpu(), packed[start:end])
+    for start, end in [(-1, 3), (5, 4), (0, 1001)]:
+        with pytest.raises(RuntimeError):
+            memory.exact_block_materialize(dev, start, end)
+    with pytest.raises(RuntimeError):
+        memory.exact_block_materialize(dev.view(10, 100), 0, 5)
