@@ -20,6 +20,7 @@ the last launch.  CASE is one of:
   centroid_readout  centroid readout of 64 queries x 8 blocks per stream
   segmented   log-sum-exp collapse of one candidate list (--streams = elements, default 2048)
   block_score block token scores through a 128 x 128 bf16 projection (--streams = tokens, default 65536)
+  heev        batched symmetric eigendecomposition of 64 x 64 float64 matrices (--streams = matrices, default 2048)
 """
 from __future__ import annotations
 
@@ -52,7 +53,7 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
                                          "readout_long", "commit_eig", "block_tracker", "centroid_commit",
-                                         "centroid_readout", "segmented", "block_score"])
+                                         "centroid_readout", "segmented", "block_score", "heev"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     parser.add_argument("--batch", type=int, default=1, help="calls per timed round (segmented, block_score)")
@@ -155,6 +156,12 @@ def main() -> None:
         Wp = torch.randn((128, 128), generator=g, device=dev).to(bf)
         ms = _timed(lambda: readout.exact_block_score(q, F, Wp), args.repeat, args.batch)
         units = f"{2.0 * m * 128 * 128 / ms / 1e9:.2f} TFLOP/s, {m * 128 * 2 / ms / 1e6:.0f} GB/s of features"
+    elif args.case == "heev":
+        nb = args.streams or 2048
+        x = torch.randn((nb, 64, 64), generator=g, device=dev, dtype=torch.float64)
+        a = x + x.transpose(-1, -2)
+        ms = _timed(lambda: block_commit.gfst_heev(a, check=False), args.repeat, args.batch)
+        units = f"{nb / ms / 1e3:.2f} M matrices/s"
     elif args.case == "tracker":
         S = args.streams or 2048
         tr = tracker.LocalTracker(S, reduced_dim=64, flag_dims=(8, 16, 32), device=dev)
