@@ -58,7 +58,7 @@ struct TcLayout {
 };
 
 template <int NKB, int STAGES, int KCAP, int EPW>
-__global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 1)
+__global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 2)
     block_topk_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          int n_queries, int n_blocks, int n_blocks_stride, int k, float* __restrict__ top_scores,
                          int32_t* __restrict__ top_idx) {
@@ -185,21 +185,21 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(half * kHalfN);
-      float v[kHalfN];
-#pragma unroll
-      for (int c0 = 0; c0 < kHalfN; c0 += 16) tmem_ld16(taddr + c0, v + c0);
-      tmem_wait_ld();
+      const int b0 = i * BN + half * kHalfN;
+      // 32 columns per TMEM load round keep the register footprint small
+      // enough for two CTAs per SM; the accumulator is released after the last
+#pragma unroll 1
+      for (int c0 = 0; c0 < kHalfN; c0 += 32) {
+        float v[16], w[16];
+        tmem_ld16(taddr + c0, v);
+        tmem_ld16(taddr + c0 + 16, w);
+        tmem_wait_ld();
+        top.offer16(v, b0 + c0, n_blocks);
+        top.offer16(w, b0 + c0 + 16, n_blocks);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);  // accumulator free for tile i + 2
-      const int b0 = i * BN + half * kHalfN;
-#pragma unroll
-      for (int c0 = 0; c0 < kHalfN; c0 += 16) {
-        float w[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) w[c] = v[c0 + c];
-        top.offer16(w, b0 + c0, n_blocks);
-      }
     }
     if constexpr (EPW == 4) {
       const int q = q0 + quad * 32 + lane;
@@ -314,7 +314,7 @@ int block_topk_tc(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, in
   if (st != GFST_OK) return st;
   const int nkb = (d + KBOX - 1) / KBOX;
   if (nkb == 1) return dispatch_kcap<1, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
-  if (nkb == 2) return dispatch_kcap<2, 4>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
+  if (nkb == 2) return dispatch_kcap<2, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
   return dispatch_kcap<4, 2>(mq, mk, S, Nq, NB, NBs, k, ts, ti, stream);
 }
 
