@@ -139,9 +139,15 @@ __device__ void jacobi_eigen(EigSmem& sm, int d) {
         const double apq = sm.a[p][q];
         double c = 1.0, sn = 0.0;
         if (apq * apq > skip) {
-          const double theta = (sm.a[q][q] - sm.a[p][p]) / (2.0 * apq);
-          const double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
-          c = 1.0 / sqrt(t * t + 1.0);
+          // t = the smaller root of t^2 + 2 theta t - 1 = 0, theta = delta / (2 a_pq),
+          // written as 2 a_pq sgn(delta) / (|delta| + sqrt(delta^2 + 4 a_pq^2)):
+          // one square root, one division and one reciprocal square root on the
+          // round's critical path
+          const double delta = sm.a[q][q] - sm.a[p][p];
+          const double two_a = 2.0 * apq;
+          const double rr = sqrt(fma(delta, delta, two_a * two_a));
+          const double t = (delta >= 0.0 ? two_a : -two_a) / (fabs(delta) + rr);
+          c = rsqrt(fma(t, t, 1.0));
           sn = t * c;
           sm.rotated = 1;
         }
@@ -151,25 +157,29 @@ __device__ void jacobi_eigen(EigSmem& sm, int d) {
         sm.rq[tid] = q;
       }
       __syncthreads();
-      for (int e = tid; e < (n / 2) * n; e += kEigThreads) {  // rows: A <- J^T A
-        const int k = e / n, j = e % n;
+      // a warp per rotation, its lanes along the row / column (no index
+      // division; the rotation's parameters are read once per warp)
+      for (int k = warp; k < n / 2; k += kEigWarps) {  // rows: A <- J^T A
         const int p = sm.rp[k], q = sm.rq[k];
         const double c = sm.rc[k], sn = sm.rs[k];
-        const double x = sm.a[p][j], y = sm.a[q][j];
-        sm.a[p][j] = c * x - sn * y;
-        sm.a[q][j] = sn * x + c * y;
+        for (int j = lane; j < n; j += 32) {
+          const double x = sm.a[p][j], y = sm.a[q][j];
+          sm.a[p][j] = c * x - sn * y;
+          sm.a[q][j] = sn * x + c * y;
+        }
       }
       __syncthreads();
-      for (int e = tid; e < (n / 2) * n; e += kEigThreads) {  // columns: A <- A J, V <- V J
-        const int k = e / n, i = e % n;
+      for (int k = warp; k < n / 2; k += kEigWarps) {  // columns: A <- A J, V <- V J
         const int p = sm.rp[k], q = sm.rq[k];
         const double c = sm.rc[k], sn = sm.rs[k];
-        const double x = sm.a[i][p], y = sm.a[i][q];
-        sm.a[i][p] = c * x - sn * y;
-        sm.a[i][q] = sn * x + c * y;
-        const double u = sm.v[i][p], w = sm.v[i][q];
-        sm.v[i][p] = c * u - sn * w;
-        sm.v[i][q] = sn * u + c * w;
+        for (int i = lane; i < n; i += 32) {
+          const double x = sm.a[i][p], y = sm.a[i][q];
+          sm.a[i][p] = c * x - sn * y;
+          sm.a[i][q] = sn * x + c * y;
+          const double u = sm.v[i][p], w = sm.v[i][q];
+          sm.v[i][p] = c * u - sn * w;
+          sm.v[i][q] = sn * u + c * w;
+        }
       }
       __syncthreads();
     }
