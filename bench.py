@@ -67,19 +67,70 @@ def fp32_peak_tflops(clock_mhz: float) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples taken while the timed region runs."""
+    """SM clock and throttle-reason samples taken while the timed region runs.
+
+    Reads NVML every 10 ms from a thread (nvidia_ml_py), so even a timed
+    region of a few tens of milliseconds gets several samples; nvidia-smi's
+    output reaches a pipe only in blocks, which left short regions with none.
+    Falls back to nvidia-smi when NVML cannot be opened.  Read-only: no clock
+    or power setting is touched."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
         self.lines: list[str] = []
         self._thread = None
+        self._stop = threading.Event()
+        self._nvml = None
+        self._handle = None
+        self.samples: list[tuple[float, float, int]] = []
+
+    def _open_nvml(self) -> bool:
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = None
+            try:
+                props = torch.cuda.get_device_properties(self.gpu_index)
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+            self._nvml, self._handle = pynvml, handle
+            self._sample()  # the device answers; this pre-region sample is dropped
+            self.samples.clear()
+            return True
+        except Exception:
+            self._nvml = None
+            return False
+
+    def _sample(self):
+        nv, h = self._nvml, self._handle
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        self.samples.append((float(sm), float(mx), int(get(h))))
+
+    def _poll(self):
+        while not self._stop.wait(0.01):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def start(self):
+        if self._open_nvml():
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -95,6 +146,21 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self) -> dict | None:
+        if self._nvml is not None:
+            self._stop.set()
+            if self._thread:
+                self._thread.join(timeout=2)
+            if not self.samples:  # a region shorter than one period: sample once now
+                try:
+                    self._sample()
+                except Exception:
+                    pass
+            if not self.samples:
+                return None
+            reasons = sorted(n for n, bit in self.REASON_BITS.items() if any(r & bit for _, _, r in self.samples))
+            return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                    "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -121,7 +187,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
