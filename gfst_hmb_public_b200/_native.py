@@ -95,6 +95,7 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p, _c_void_p,
         _c_void_p,
     ],
+    "gfst_debug_bounded_wait": [_c_int64, _c_void_p],
     "gfst_exact_block_materialize": [_c_void_p, _c_int64, _c_int, _c_int64, _c_int64, _c_void_p, _c_void_p],
     "gfst_heev": [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "gfst_exact_block_score": [

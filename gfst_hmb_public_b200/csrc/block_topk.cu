@@ -20,6 +20,12 @@ extern "C" int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_stream
                          top_idx, stream);
 }
 
+extern "C" int gfst_debug_bounded_wait(int64_t cycles, cudaStream_t stream) {
+  GFST_REQUIRE(cycles >= 1 && cycles <= 2000000000LL, GFST_ERR_ARG, "cycles=%lld outside [1, 2e9]",
+               (long long)cycles);
+  return gfst::launch_bounded_wait_probe((long long)cycles, stream);
+}
+
 extern "C" int gfst_check_device_errors(int clear) {
   unsigned int v = 0, w = 0;
   int st = gfst::read_device_error(clear, &v);

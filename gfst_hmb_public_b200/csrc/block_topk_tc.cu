@@ -348,6 +348,22 @@ int make_bf16_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int 
   return GFST_OK;
 }
 
+// One thread waits on an mbarrier that nothing arrives at, for at most
+// `budget` clock cycles, and gives up the way the pipelines' waits do: the
+// sticky word records GFST_ERR_TIMEOUT and the kernel returns.
+__global__ void bounded_wait_probe_kernel(long long budget) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_init_fence();
+  if (!mbar_wait_for(&bar, 0, budget)) atomicExch(&g_device_error, (unsigned)GFST_ERR_TIMEOUT);
+}
+
+int launch_bounded_wait_probe(long long budget, cudaStream_t stream) {
+  bounded_wait_probe_kernel<<<1, 32, 0, stream>>>(budget);
+  return check_launch("bounded_wait_probe_kernel");
+}
+
 int read_device_error(int clear, unsigned int* value) {
   unsigned int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));

@@ -368,6 +368,15 @@ GFST_API int gfst_topk_merge(const float* scores, const int32_t* idx, int64_t ro
  * recorded status, and clears the word when `clear` is non-zero.            */
 GFST_API int gfst_check_device_errors(int clear);
 
+/* ---- failure-path probe ------------------------------------------------------
+ * Launches one CTA that waits on an mbarrier nothing arrives at, for at most
+ * `cycles` SM clock cycles (1 <= cycles <= 2e9, about a second at B200
+ * clocks), then gives up exactly as a pipeline wait does: GFST_ERR_TIMEOUT is
+ * recorded for gfst_check_device_errors and the kernel returns, leaving the
+ * context usable.  For testing the failure path without a fault; no
+ * counterpart in the reference.                                              */
+GFST_API int gfst_debug_bounded_wait(int64_t cycles, cudaStream_t stream);
+
 /* ---- exact-token readout ------------------------------------------------------
  * For every stream s and query q, over the tokens of the k blocks top_idx[s,q,:]
  * (entries < 0 or >= n_slots are skipped; a block listed twice counts once):

@@ -120,6 +120,8 @@ def test_segmented_and_block_score_host_rejects():
     assert lib.gfst_exact_block_materialize(fake, 10, 4, 5, 4, fake, None) == 1
     assert lib.gfst_exact_block_materialize(fake, 10, 4, 5, 11, fake, None) == 1
     assert lib.gfst_exact_block_materialize(None, 10, 4, 3, 3, None, None) == 0
+    assert lib.gfst_debug_bounded_wait(0, None) == 1
+    assert lib.gfst_debug_bounded_wait(3_000_000_000, None) == 1
 
 
 def test_python_ops_reject_cpu_tensors():

@@ -1,0 +1,31 @@
+"""The failure path of the in-kernel waits, exercised without a fault: a wait on
+an mbarrier that nothing completes gives up after its cycle budget, the
+sticky device error word reports GFST_ERR_TIMEOUT to the host, reading it
+clears it, and the context keeps running kernels afterwards."""
+import pytest
+import torch
+
+from gfst_hmb_public_b200 import _native, retrieval
+
+pytestmark = pytest.mark.gpu
+
+GFST_ERR_TIMEOUT = 6
+
+
+def test_bounded_wait_gives_up_and_context_stays_usable(cuda_device):
+    lib = _native.load()
+    assert lib.gfst_check_device_errors(1) == 0
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    with torch.cuda.device(cuda_device):
+        assert lib.gfst_debug_bounded_wait(2_000_000, stream) == 0  # about a millisecond
+        assert lib.gfst_check_device_errors(0) == GFST_ERR_TIMEOUT
+        assert lib.gfst_check_device_errors(1) == GFST_ERR_TIMEOUT  # read and clear
+        assert lib.gfst_check_device_errors(0) == 0
+    # a tensor-core retrieval launch after the probe still gives the right answer
+    g = torch.Generator().manual_seed(4)
+    Q = torch.randn((2, 64, 128), generator=g).to(torch.bfloat16)
+    K = torch.randn((2, 300, 128), generator=g).to(torch.bfloat16)
+    scores, idx = retrieval.block_topk(Q.to(cuda_device), K.to(cuda_device), 4)
+    ref = torch.topk(Q.float() @ K.float().transpose(1, 2), 4, dim=-1)
+    assert torch.allclose(scores.cpu(), ref.values, rtol=1e-5, atol=1e-4)
+    assert lib.gfst_check_device_errors(1) == 0
