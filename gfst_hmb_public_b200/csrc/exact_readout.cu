@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(kPThreads) exact_readout_pipelined_kernel(
 // warp-level MMA keeps them in registers with no accumulator round trip, and the
 // kernel stays bound by HBM, not by the tensor pipe.
 #ifndef GFST_READOUT_RING_KB
-#define GFST_READOUT_RING_KB 64u
+#define GFST_READOUT_RING_KB 80u
 #endif
 constexpr int kMWarps = 4;
 constexpr int kMThreads = (kMWarps + 1) * 32;
@@ -740,8 +740,9 @@ int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t*
   T* ov = static_cast<T*>(out_V);
   const int64_t n_chunks = (Nq + kQC - 1) / kQC;
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    // tensor-core consumers: a ring of GFST_READOUT_RING_KB (4 stages of 16 KB for
-    // 64 x 128 blocks: two CTAs per SM, with room left for a frame-update CTA)
+    // tensor-core consumers: a ring of GFST_READOUT_RING_KB (5 stages of 16 KB for
+    // 64 x 128 blocks, 112 KB per CTA with the run table: two CTAs per SM, or
+    // one beside a frame-update CTA; 4 stages measured 11 % slower)
     const size_t stage_bytes = (size_t)L * d * 2;
     const bool mma_ok = (d == 64 || d == 128 || d == 256) && L % 16 == 0 && L <= 256 &&
                         (int64_t)NS < (1LL << 21) && S * (int64_t)NS * L < (1LL << 31) &&
