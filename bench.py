@@ -2,27 +2,37 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (per GPU, weak scaling: every rank runs its own batch shard):
-  stream_full -- B=64 batch x H=32 heads = 2048 streams, d=128 x r=32 fp32
-  frames updated per token by a rank-4 u v^T (u, v ~ N(0, 1/128)) then a thin
-  QR (CholeskyQR2 on the tensor cores and FP32 units, Householder fallback;
-  the same Q as Householder to fp32 rounding); bf16 keys / values / queries
-  N(0,1); blocks of L=64
-  tokens in a 512-slot memory ring (full, i.e. the memory of a 32,768-token
-  pass); top-k=16 blocks then exact-token argmax and value fetch.
-  One step = one block (64 tokens) of every stream: 64 frame updates + QRs,
-  64 queries read out, one block committed.  Inputs of a step are 436 MB,
-  larger than L2, and every step re-reads them.
-The metric is tokens/s over all GPUs, a token being one position of one batch
-element through all 32 heads (B*T per second).  Sub-results: the batched-QR
-microbenchmark (65,536 frames of 64 x 8) in frames/s, and the long-memory
-readout (256 streams x 1,048,576-token memories, 1024 needle queries each,
-block ranges sharded over the ranks) in queries/s.
+Headline workload (stream_full): batch 64 x 32 heads = 2048 independent
+streams in total, split by batch over the N ranks (strong scaling: 2048 / N
+streams per GPU).  Per stream: d=128 x r=32 fp32 frames updated per token by a
+rank-4 u v^T (u, v ~ N(0, 1/128)) then a thin QR with R-diagonal-positive signs
+(CholeskyQR2 on the tensor cores and FP32 units, Householder fallback); bf16
+keys / values / queries N(0,1); blocks of L=64 tokens in a 512-slot memory ring
+(full: the memory of a 32,768-token pass); per query the top-16 blocks, then
+the exact-token argmax over those blocks and the open block's prefix, and the
+value row of the winner.  One step = one block (64 tokens) of every stream:
+64 frame updates + QRs, 64 queries read out, one block committed.  A step's
+inputs (436 MB over all ranks) exceed L2 and are re-read every step.
 
-Rank 0 prints one JSON line.  Timing: W warm-up steps, then K steps between a
-barrier + synchronize on both sides, CUDA events on the launching streams, the
-maximum over ranks.  The roofline and per-kernel shares come from CUDA events
-recorded on the stream each kernel is launched on, inside the timed region.
+The metric is tokens/s over all GPUs, a token being one position of one batch
+element through all 32 heads (batch * tokens per second).
+
+Sub-results, each measured in a child process of its own so that no
+measurement runs on a device heap that an earlier one shaped:
+  long_memory  256 streams x 1,048,576-token memories (128 GiB), 1024 needle
+               queries each, top-8 + exact argmax; block ranges sharded over
+               the ranks (queries/s)
+  stream_small the CPU-runnable configuration: 2 x 4 streams, 256 tokens,
+               64 x 8 frames, rank 1, L=16, top-2, fp32 (one GPU)
+  stream_mid   16 x 16 streams, 4096 tokens, 128 x 16 frames, rank 2, L=64,
+               64 blocks, top-4, bf16 (one GPU)
+  batched_qr   65,536 frames of 64 x 8, one QR each (frames/s; one GPU)
+
+Timing: W warm-up steps, then exactly K steps between a barrier + synchronize
+on both sides, CUDA events on the launching stream, the maximum over ranks.
+The timed region contains only the steps: per-step events are created before
+it, SM clocks are sampled by a separate process, and the per-kernel phase
+times come from a separate pass afterwards.  Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
@@ -30,10 +40,12 @@ import argparse
 import json
 import math
 import os
+import signal
+import socket
 import statistics
 import subprocess
 import sys
-import threading
+import tempfile
 import time
 from pathlib import Path
 
@@ -41,13 +53,11 @@ REPO = Path(__file__).resolve().parent
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
-import torch  # noqa: E402
-
 METRIC = "GFST step tokens/s (QR+readout) at 1/2/4/8 B200; batched-QR frames/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
-# stream_full workload
-B_PER_GPU, HEADS, D, R, M, L, SLOTS, K_SEL = 64, 32, 128, 32, 4, 64, 512, 16
+# stream_full workload (totals; the streams are split over the ranks)
+B_TOTAL, HEADS, D, R, M, L, SLOTS, K_SEL = 64, 32, 128, 32, 4, 64, 512, 16
 SEED = 20261201 + 4
 
 
@@ -66,162 +76,431 @@ def fp32_peak_tflops(clock_mhz: float) -> float:
     return 148 * 128 * 2 * clock_mhz * 1e6 / 1e12
 
 
+# ---------------------------------------------------------------------------
+# clock sampling in a separate process
+# ---------------------------------------------------------------------------
+REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+
+
+def clock_sampler_main(bus_id: str, out_path: str, period_ms: float) -> None:
+    """Child-process body: append 'wall_time,sm_mhz,max_mhz,reasons' lines to
+    out_path every period_ms until terminated.  Read-only NVML queries."""
+    import pynvml
+
+    pynvml.nvmlInit()
+    try:
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus_id)
+    except Exception:
+        h = pynvml.nvmlDeviceGetHandleByIndex(0)
+    get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+        getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+    stop = []
+    signal.signal(signal.SIGTERM, lambda *a: stop.append(1))
+    with open(out_path, "w", buffering=1) as f:
+        f.write("ready\n")
+        while not stop:
+            t = time.time()
+            sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+            rs = int(get_reasons(h))
+            f.write(f"{t:.6f},{sm},{mx},{rs}\n")
+            time.sleep(max(0.0, period_ms / 1e3 - (time.time() - t)))
+
+
 class ClockSampler:
-    """SM clock and throttle-reason samples taken while the timed region runs.
+    """SM clock and throttle-reason samples from a child process, kept for the
+    wall-clock window of the timed region.  Nothing runs in the process that
+    launches the kernels."""
 
-    Reads NVML every 10 ms from a thread (nvidia_ml_py), so even a timed
-    region of a few tens of milliseconds gets several samples; nvidia-smi's
-    output reaches a pipe only in blocks, which left short regions with none.
-    Falls back to nvidia-smi when NVML cannot be opened.  Read-only: no clock
-    or power setting is touched."""
+    def __init__(self, device, period_ms: float = 20.0):
+        import torch
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
-                   "hw_thermal_slowdown": 0x40}
-
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
+        props = torch.cuda.get_device_properties(device)
+        self.bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        self.period_ms = period_ms
         self.proc = None
-        self.lines: list[str] = []
-        self._thread = None
-        self._stop = threading.Event()
-        self._nvml = None
-        self._handle = None
-        self.samples: list[tuple[float, float, int]] = []
+        fd, self.path = tempfile.mkstemp(prefix="gfst_clocks_", suffix=".csv")
+        os.close(fd)
 
-    def _open_nvml(self) -> bool:
+    def start(self) -> None:
         try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            handle = None
-            try:
-                props = torch.cuda.get_device_properties(self.gpu_index)
-                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
-                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            except Exception:
-                handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
-            self._nvml, self._handle = pynvml, handle
-            self._sample()  # the device answers; this pre-region sample is dropped
-            self.samples.clear()
-            return True
-        except Exception:
-            self._nvml = None
-            return False
-
-    def _sample(self):
-        nv, h = self._nvml, self._handle
-        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-        get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
-        self.samples.append((float(sm), float(mx), int(get(h))))
-
-    def _poll(self):
-        while not self._stop.wait(0.01):
-            try:
-                self._sample()
-            except Exception:
-                return
-
-    def start(self):
-        if self._open_nvml():
-            self._thread = threading.Thread(target=self._poll, daemon=True)
-            self._thread.start()
-            return
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen([sys.executable, str(Path(__file__).resolve()), "--clock-sampler", self.bus,
+                                          self.path, str(self.period_ms)], stdout=subprocess.DEVNULL,
+                                         stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
             return
-        self._thread = threading.Thread(target=self._read, daemon=True)
-        self._thread.start()
+        t0 = time.time()
+        while time.time() - t0 < 20.0:  # wait until NVML answers in the child
+            try:
+                if Path(self.path).read_text().count("\n") >= 2:
+                    return
+            except Exception:
+                pass
+            if self.proc.poll() is not None:
+                return
+            time.sleep(0.05)
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self) -> dict | None:
-        if self._nvml is not None:
-            self._stop.set()
-            if self._thread:
-                self._thread.join(timeout=2)
-            if not self.samples:  # a region shorter than one period: sample once now
-                try:
-                    self._sample()
-                except Exception:
-                    pass
-            if not self.samples:
-                return None
-            reasons = sorted(n for n, bit in self.REASON_BITS.items() if any(r & bit for _, _, r in self.samples))
-            return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
-                    "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons,
-                    "samples": len(self.samples), "source": "nvml"}
+    def stop(self, t0: float, t1: float) -> dict | None:
         if self.proc is None:
             return None
         self.proc.terminate()
         try:
-            self.proc.wait(timeout=5)
+            self.proc.wait(timeout=10)
         except Exception:
             self.proc.kill()
-        if self._thread:
-            self._thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
+        rows = []
+        try:
+            for ln in Path(self.path).read_text().splitlines()[1:]:
+                p = ln.split(",")
+                if len(p) == 4:
+                    rows.append((float(p[0]), float(p[1]), float(p[2]), int(p[3])))
+        except Exception:
+            rows = []
+        try:
+            os.unlink(self.path)
+        except Exception:
+            pass
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm), "source": "nvidia-smi"}
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        how = "inside the timed region"
+        if not inside:  # a region shorter than one period: the sample nearest its middle
+            mid = 0.5 * (t0 + t1)
+            inside = [min(rows, key=lambda r: abs(r[0] - mid))]
+            how = "nearest sample to the timed region"
+        reasons = sorted(n for n, bit in REASON_BITS.items() if any(r[3] & bit for r in inside))
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": reasons, "samples": len(inside), "source": f"nvml in a child process, {how}",
+                "period_ms": self.period_ms}
 
 
 # ---------------------------------------------------------------------------
-# our implementation
+# helpers
 # ---------------------------------------------------------------------------
-def make_inputs(S, device, seed):
-    from gfst_hmb_public_b200 import workloads as wl
+def _dist():
+    import torch.distributed as dist
 
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    std = 1.0 / math.sqrt(D)
-    A = torch.randn((S, L, D, M), generator=g, device=device) * std
-    Bm = torch.randn((S, L, R, M), generator=g, device=device) * std
-    Kt, Vt, Qt = wl.token_tensors(S, L, D, seed=seed + 1, device=device, dtype=torch.bfloat16)
-    return A, Bm, Kt, Vt, Qt
+    return dist if dist.is_available() and dist.is_initialized() else None
 
 
-def build_step(S, device, seed):
+def barrier() -> None:
+    d = _dist()
+    if d is not None:
+        d.barrier()
+
+
+def max_over_ranks(x: float, device) -> float:
+    d = _dist()
+    if d is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    d.all_reduce(t, op=d.ReduceOp.MAX)
+    return float(t.item())
+
+
+def percentile(xs: list[float], q: float) -> float:
+    s = sorted(xs)
+    if not s:
+        return float("nan")
+    i = min(len(s) - 1, max(0, int(math.ceil(q * len(s))) - 1))
+    return s[i]
+
+
+class PhaseEvents:
+    """CUDA events around each kernel of a step, recorded on the stream the
+    kernel is launched on; the events are created before the pass."""
+
+    NAMES = ("frames", "topk", "readout", "open_block", "commit")
+
+    def __init__(self, n_steps: int):
+        import torch
+
+        self.pool = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                     for _ in range(n_steps * len(self.NAMES) + 8)]
+        self.used = 0
+        self.records = []
+
+    def wrap(self):
+        import torch
+
+        from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
+
+        ev = self
+
+        def timed(fn, name):
+            def inner(*a, **kw):
+                s = torch.cuda.current_stream()
+                e0, e1 = ev.pool[ev.used]
+                ev.used += 1
+                e0.record(s)
+                out = fn(*a, **kw)
+                e1.record(s)
+                ev.records.append((name, e0, e1))
+                return out
+            return inner
+
+        self._orig = (gfst.stream_frames, retrieval.block_topk, readout.exact_readout, readout.open_block_readout,
+                      memory.block_commit_mean)
+        gfst.stream_frames = timed(gfst.stream_frames, "frames")
+        retrieval.block_topk = timed(retrieval.block_topk, "topk")
+        readout.exact_readout = timed(readout.exact_readout, "readout")
+        readout.open_block_readout = timed(readout.open_block_readout, "open_block")
+        memory.block_commit_mean = timed(memory.block_commit_mean, "commit")
+
+    def unwrap(self):
+        from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
+
+        (gfst.stream_frames, retrieval.block_topk, readout.exact_readout, readout.open_block_readout,
+         memory.block_commit_mean) = self._orig
+
+    def summary(self) -> dict:
+        out: dict[str, list[float]] = {}
+        for name, e0, e1 in self.records:
+            out.setdefault(name, []).append(e0.elapsed_time(e1))
+        return {k: sum(v) / len(v) for k, v in out.items()}
+
+
+# ---------------------------------------------------------------------------
+# streaming workloads
+# ---------------------------------------------------------------------------
+def build_step(S, d, r, block_len, n_slots, k, dtype, device, seed, fill_slots):
+    import torch
+
     from gfst_hmb_public_b200 import gfst, step as stp
 
-    st = stp.StreamingStep(S, d=D, r=R, block_len=L, n_slots=SLOTS, k=K_SEL, dtype=torch.bfloat16, device=device)
+    st = stp.StreamingStep(S, d=d, r=r, block_len=block_len, n_slots=n_slots, k=k, dtype=dtype, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(seed + 7)
-    U0 = torch.randn((S, D, R), generator=g, device=device)
+    U0 = torch.randn((S, d, r), generator=g, device=device)
     st.set_frames(gfst.frame_update_qr(U0, sign_mode="r_diag_positive"))
-    # fill the memory ring: the state after a 32,768-token pass
-    for b in range(SLOTS):
-        Kb = torch.randn((S, L, D), generator=g, device=device).to(torch.bfloat16)
-        Vb = torch.randn((S, L, D), generator=g, device=device).to(torch.bfloat16)
+    for _ in range(fill_slots):
+        Kb = torch.randn((S, block_len, d), generator=g, device=device).to(dtype)
+        Vb = torch.randn((S, block_len, d), generator=g, device=device).to(dtype)
         st.memory.commit(Kb, Vb)
     torch.cuda.synchronize(device)
     return st
 
 
+def step_inputs(S, T, d, r, m, dtype, device, seed):
+    """A [S, T, d, m], B [S, T, r, m] fp32 (N(0, 1/d)); K, V, Q [S, T, d] N(0,1)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    std = 1.0 / math.sqrt(d)
+    A = torch.randn((S, T, d, m), generator=g, device=device) * std
+    Bm = torch.randn((S, T, r, m), generator=g, device=device) * std
+    K, V, Q = (torch.randn((S, T, d), generator=g, device=device).to(dtype).contiguous() for _ in range(3))
+    return A, Bm, K, V, Q
+
+
+def unique_selected_blocks(sel) -> int:
+    """Distinct blocks each stream's step selects (over all its queries)."""
+    import torch
+
+    uniq = 0
+    for s0 in range(0, sel.shape[0], 256):
+        blk = sel[s0:s0 + 256].reshape(sel[s0:s0 + 256].shape[0], -1)
+        srt = torch.sort(blk, dim=1).values
+        valid = srt >= 0
+        first = torch.ones_like(valid)
+        first[:, 1:] = srt[:, 1:] != srt[:, :-1]
+        uniq += int((first & valid).sum().item())
+    return uniq
+
+
+def run_stream_full(args, rank, world, device) -> dict:
+    import torch
+
+    from gfst_hmb_public_b200 import _native
+    from gfst_hmb_public_b200.step import HostPipeline
+
+    if B_TOTAL % world:
+        raise SystemExit(f"batch {B_TOTAL} does not split over {world} ranks")
+    b_local = B_TOTAL // world
+    S = b_local * HEADS
+    st = build_step(S, D, R, L, SLOTS, K_SEL, torch.bfloat16, device, SEED + 1000 * rank, SLOTS)
+    A, Bm, Kt, Vt, Qt = step_inputs(S, L, D, R, M, torch.bfloat16, device, SEED + 1000 * rank + 1)
+
+    for _ in range(args.warmup):
+        st.step(A, Bm, Kt, Vt, Qt)
+    torch.cuda.synchronize(device)
+    _native.check_device_errors()
+
+    # ---- headline: exactly K steps, nothing else in the region -------------
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    sampler = ClockSampler(device)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize(device)
+    w0 = time.time()
+    evs[0].record()
+    for i in range(args.steps):
+        out = st.step(A, Bm, Kt, Vt, Qt)
+        evs[i + 1].record()
+    torch.cuda.synchronize(device)
+    w1 = time.time()
+    barrier()
+    clocks = sampler.stop(w0, w1)
+    _native.check_device_errors()
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    ms = max_over_ranks(evs[0].elapsed_time(evs[-1]) / args.steps, device)
+    med = max_over_ranks(statistics.median(per_step), device)
+    p90 = max_over_ranks(percentile(per_step, 0.9), device)
+    sel = out.top_idx
+
+    # ---- per-kernel phase times: a separate pass ---------------------------
+    n_phase = max(3, min(args.steps, 10))
+    phases = PhaseEvents(n_phase)
+    phases.wrap()
+    try:
+        for _ in range(n_phase):
+            st.step(A, Bm, Kt, Vt, Qt)
+        torch.cuda.synchronize(device)
+    finally:
+        phases.unwrap()
+    phase_ms = phases.summary()
+
+    # ---- end to end with host buffers ---------------------------------------
+    e2e_steps = max(3, min(args.steps, 6))
+    host_in = [t.cpu().pin_memory() for t in (A, Bm, Kt, Vt, Qt)]
+    host_out = [(torch.empty((S, L), dtype=torch.int32).pin_memory(),
+                 torch.empty((S, L), dtype=torch.float32).pin_memory(),
+                 torch.empty((S, L, D), dtype=torch.bfloat16).pin_memory()) for _ in range(2)]
+    pipe = HostPipeline(st, (A, Bm, Kt, Vt, Qt))
+    pipe.run([host_in] * 2, host_out[:2])  # warm-up
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0.record()
+    pipe.run([host_in] * e2e_steps, [host_out[i % 2] for i in range(e2e_steps)])
+    e1.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    _native.check_device_errors()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, device)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+    uniq = unique_selected_blocks(sel)
+    res = {"ms": ms, "median": med, "p90": p90, "per_step": per_step, "phase_ms": phase_ms, "clocks": clocks,
+           "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h, "uniq": uniq, "S": S, "b_local": b_local,
+           "launches": 5 * args.steps}
+    del st, A, Bm, Kt, Vt, Qt, host_in, host_out, pipe, out, sel
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_stream_pass(spec, device, repeats: int = 3) -> dict:
+    """One full pass of a streaming configuration (spec.tokens tokens from an
+    empty memory, one block per step), timed `repeats` times after one warm-up
+    pass; every pass starts from the same frames and an empty memory."""
+    import torch
+
+    from gfst_hmb_public_b200 import _native, gfst, step as stp
+
+    S, T, Lb = spec.streams, spec.tokens, spec.block_len
+    n_steps = T // Lb
+    A, Bm, Kt, Vt, Qt = step_inputs(S, T, spec.d, spec.r, spec.m, spec.memory_dtype, device, spec.seed)
+    g = torch.Generator(device=device)
+    g.manual_seed(spec.seed + 7)
+    U0 = gfst.frame_update_qr(torch.randn((S, spec.d, spec.r), generator=g, device=device),
+                              sign_mode="r_diag_positive")
+    blocks = [tuple(t[:, i * Lb:(i + 1) * Lb].contiguous() for t in (A, Bm, Kt, Vt, Qt)) for i in range(n_steps)]
+    st = stp.StreamingStep(S, d=spec.d, r=spec.r, block_len=Lb, n_slots=spec.n_blocks, k=spec.k,
+                           dtype=spec.memory_dtype, device=device)
+
+    def one_pass(phases=None):
+        st.reset()
+        st.set_frames(U0)
+        for blk in blocks:
+            st.step(*blk)
+
+    one_pass()
+    torch.cuda.synchronize(device)
+    times = []
+    for _ in range(repeats):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        e0.record()
+        one_pass()
+        e1.record()
+        torch.cuda.synchronize(device)
+        times.append(e0.elapsed_time(e1))
+    phases = PhaseEvents(n_steps)
+    phases.wrap()
+    try:
+        one_pass()
+        torch.cuda.synchronize(device)
+    finally:
+        phases.unwrap()
+    _native.check_device_errors()
+    ms = statistics.median(times)
+    ph = {k: round(v * n_steps, 4) for k, v in phases.summary().items()}
+    return {"tokens_per_s": round(spec.batch * T / (ms / 1e3), 1), "ms_per_pass": round(ms, 4),
+            "steps_per_pass": n_steps, "kernel_ms_per_pass": ph, "passes": repeats}
+
+
+def run_extras(device) -> dict:
+    """The one-GPU sub-results: stream_small, stream_mid, batched_qr."""
+    import torch
+
+    from gfst_hmb_public_b200 import gfst, workloads as wl
+
+    peaks, peak_src = load_peaks()
+    hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    out = {}
+    sm = wl.STREAM_SMALL
+    r = run_stream_pass(sm, device, repeats=5)
+    r["workload"] = ("stream_small: 2 batch x 4 heads, 256 tokens, frames 64x8 fp32 rank-1 + QR per token, "
+                     "fp32 memory of 16-token blocks, top-2 + exact argmax (incl. the open block); one pass "
+                     "from an empty memory")
+    out["stream_small"] = r
+    mid = wl.STREAM_MID
+    r = run_stream_pass(mid, device, repeats=3)
+    r["workload"] = ("stream_mid: 16 batch x 16 heads = 256 streams, 4096 tokens, frames 128x16 fp32 rank-2 + QR "
+                     "per token, bf16 memory of 64 blocks x 64 tokens, top-4 + exact argmax (incl. the open "
+                     "block); one pass from an empty memory")
+    # frames roofline: the unfused per-token byte contract (read U, A, B; write U)
+    S, T = mid.streams, mid.tokens
+    fb = S * T * (2 * mid.d * mid.r * 4 + (mid.d + mid.r) * mid.m * 4)
+    fr_ms = r["kernel_ms_per_pass"].get("frames")
+    if fr_ms:
+        r["frames_unfused_gbs"] = round(fb / (fr_ms / 1e3) / 1e9, 1)
+        r["frames_tflops"] = round(S * T * (4.0 * mid.d * mid.r ** 2 + 2.0 * mid.d * mid.r * mid.m)
+                                   / (fr_ms / 1e3) / 1e12, 2)
+    out["stream_mid"] = r
+
+    spec = wl.BATCHED_QR
+    xq = wl.batched_qr_inputs(spec["n"], spec["d"], spec["r"], seed=spec["seed"], device=device)
+    oq = torch.empty_like(xq)
+    for _ in range(5):
+        gfst.frame_update_qr(xq, sign_mode="r_diag_positive", out=oq)
+    torch.cuda.synchronize(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+    for q0, q1 in evs:
+        flush.zero_()  # evict L2 between launches
+        q0.record()
+        gfst.frame_update_qr(xq, sign_mode="r_diag_positive", out=oq)
+        q1.record()
+    torch.cuda.synchronize(device)
+    qr_ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+    qr_gbs = 2 * xq.numel() * 4 / (qr_ms / 1e3) / 1e9
+    out["batched_qr"] = {
+        "value": round(spec["n"] / (qr_ms / 1e3), 1), "unit": "frames/s", "ms": round(qr_ms, 4),
+        "workload": "65,536 frames 64x8 fp32, column j x 10^(-j/2), 1% near-collinear pairs; L2 flushed",
+        "roofline": {"bound": "hbm", "achieved": round(qr_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(qr_gbs / hbm_peak, 4), "peak_source": peak_src}}
+    return out
+
+
+# ---------------------------------------------------------------------------
+# long-memory readout (block-range sharded over the ranks)
+# ---------------------------------------------------------------------------
 def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int = 2) -> dict | None:
     """Long-memory readout: B=8 x H=32 = 256 streams, each with a 1,048,576-token
     memory (8192 blocks of 128 tokens, d=128, bf16 keys and values: 128 GiB),
@@ -230,10 +509,11 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
     with N ranks every rank holds a block range of every stream (16 GiB at
     N=8) and the readout is the block-sharded exchange (sharding.sharded_readout).
     A step is one pass of all 262,144 queries.  Returns rank 0's sub-result."""
-    import torch.distributed as dist
+    import torch
 
-    from gfst_hmb_public_b200 import readout, retrieval, sharding, workloads as wl
+    from gfst_hmb_public_b200 import _native, readout, retrieval, sharding, workloads as wl
 
+    dist = _dist()
     spec = wl.LONG_MEMORY
     S, Lb, d, nq, k = spec.batch * spec.heads, spec.block_len, spec.d, spec.n_queries, spec.k
     nb = spec.memory_tokens // Lb
@@ -255,7 +535,7 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
     own = (nb_idx >= shard.lo) & (nb_idx < shard.hi)
     loc = torch.where(own, nb_idx - shard.lo, torch.zeros_like(nb_idx))
     keys = pool_K[torch.arange(S, device=device)[:, None], loc, pos].float() * own.unsqueeze(-1)
-    if world > 1:
+    if dist is not None:
         dist.all_reduce(keys)
     Q = (keys + noise).to(bf).contiguous()
     del keys, noise, loc, own
@@ -263,14 +543,16 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
 
     def one_pass(times=None):
         if world == 1:
-            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-            e[0].record()
-            _, top_i = retrieval.block_topk(Q, summary, k)
-            e[1].record()
-            tok, _, _ = readout.exact_readout(Q, pool_K, pool_V, top_i)
-            e[2].record()
             if times is not None:
-                times.append(e)
+                e = times.pop()
+                e[0].record()
+            _, top_i = retrieval.block_topk(Q, summary, k)
+            if times is not None:
+                e[1].record()
+            tok, _, _ = readout.exact_readout(Q, pool_K, pool_V, top_i)
+            if times is not None:
+                e[2].record()
+                times.insert(0, e)
             return tok, top_i
         tok, _, _, top_i, _ = sharding.sharded_readout(Q, summary, pool_K, pool_V, k, shard)
         return tok, top_i
@@ -278,23 +560,18 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
     for _ in range(warmup):
         one_pass()
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
+    times = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    times: list = []
+    barrier()
+    torch.cuda.synchronize(device)
     t0.record()
     for _ in range(steps):
-        tok, top_i = one_pass(times)
+        tok, top_i = one_pass(times if world == 1 else None)
     t1.record()
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    ms = t0.elapsed_time(t1) / steps
-    if world > 1:
-        tt = torch.tensor([ms], device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+    barrier()
+    _native.check_device_errors()
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, device)
     hit = float((tok == needle).float().mean().item())
     res = None
     if rank == 0:
@@ -308,10 +585,10 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
                "needle_recall_note": "share of queries whose winning token is the needle; the mean-of-keys block "
                                      "summary puts the needle's block in the top-8 for about 2% of queries at L=128",
                "steps": steps, "warmup": warmup}
-        if times:
+        if world == 1:
             tk = statistics.mean(e[0].elapsed_time(e[1]) for e in times)
             ro = statistics.mean(e[1].elapsed_time(e[2]) for e in times)
-            srt = torch.sort(top_i.reshape(S, -1, 64 * k)[:, :, :], dim=-1).values
+            srt = torch.sort(top_i.reshape(S, -1, 64 * k), dim=-1).values
             uniq = int((srt[..., 1:] != srt[..., :-1]).sum().item() + srt.shape[0] * srt.shape[1])
             ro_bytes = uniq * Lb * d * 2 + S * nq * (d * 2 * 2 + k * 4 + 8)
             res["kernel_ms"] = {"topk": round(tk, 4), "readout": round(ro, 4)}
@@ -322,180 +599,123 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
     return res
 
 
-class PhaseEvents:
-    """CUDA events around each kernel of a step, on the stream that launches it."""
-
-    def __init__(self):
-        self.records = []
-
-    def wrap(self, st):
-        from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
-
-        ev = self
-
-        def timed(stream_of, fn, name):
-            def inner(*a, **kw):
-                s = stream_of()
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(s)
-                out = fn(*a, **kw)
-                e1.record(s)
-                ev.records.append((name, e0, e1))
-                return out
-            return inner
-
-        cur = lambda: torch.cuda.current_stream()  # noqa: E731 -- the side stream inside step()
-        self._orig = (gfst.stream_frames, retrieval.block_topk, readout.exact_readout, memory.block_commit_mean)
-        gfst.stream_frames = timed(cur, gfst.stream_frames, "frames")
-        retrieval.block_topk = timed(cur, retrieval.block_topk, "topk")
-        readout.exact_readout = timed(cur, readout.exact_readout, "readout")
-        memory.block_commit_mean = timed(cur, memory.block_commit_mean, "commit")
-
-    def unwrap(self):
-        from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
-
-        gfst.stream_frames, retrieval.block_topk, readout.exact_readout, memory.block_commit_mean = self._orig
-
-    def summary(self) -> dict:
-        out: dict[str, list[float]] = {}
-        for name, e0, e1 in self.records:
-            out.setdefault(name, []).append(e0.elapsed_time(e1))
-        return {k: sum(v) / len(v) for k, v in out.items()}
+# ---------------------------------------------------------------------------
+# child processes for the sub-results
+# ---------------------------------------------------------------------------
+def _free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
-def run_ours(args, rank, world, device) -> dict | None:
+def run_child(part: str, rank: int, world: int, local_rank: int, port: int | None, timeout_s: float) -> dict | None:
+    """Run `bench.py --part <part>` as a child process with the same rank
+    layout (its own process group on `port` when world > 1); returns its JSON."""
+    fd, out_path = tempfile.mkstemp(prefix=f"gfst_{part}_", suffix=".json")
+    os.close(fd)
+    env = dict(os.environ)
+    env.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(local_rank),
+                "MASTER_ADDR": "127.0.0.1"})
+    if port is not None:
+        env["MASTER_PORT"] = str(port)
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--part", part, "--part-out", out_path]
+    try:
+        rc = subprocess.run(cmd, env=env, timeout=timeout_s, stdout=sys.stderr, stderr=sys.stderr).returncode
+    except subprocess.TimeoutExpired:
+        rc = -9
+    try:
+        txt = Path(out_path).read_text()
+        os.unlink(out_path)
+    except Exception:
+        txt = ""
+    if rc != 0:
+        return {"error": f"child process for {part} exited with {rc}"}
+    try:
+        return json.loads(txt) if txt.strip() else None
+    except Exception:
+        return {"error": f"child process for {part} wrote no result"}
+
+
+def part_main(args) -> None:
+    import datetime
+
+    import torch
     import torch.distributed as dist
 
-    from gfst_hmb_public_b200 import gfst, workloads as wl
-
-    # long-memory readout sub-result first: its 128 GiB of memory is allocated
-    # on a fresh device heap (large pages) and released before the streaming
-    # state is built
-    long_memory = None
-    if not args.no_long_memory:
-        long_memory = run_long_memory(rank, world, device)
-
-    S = B_PER_GPU * HEADS
-    st = build_step(S, device, SEED + 1000 * rank)
-    A, Bm, Kt, Vt, Qt = make_inputs(S, device, SEED + 1000 * rank + 1)
-
-    def barrier():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        if args.part == "long_memory":
+            res = run_long_memory(rank, world, device)
+        elif args.part == "extras":
+            res = run_extras(device) if rank == 0 else None
+        else:
+            raise SystemExit(f"unknown part {args.part}")
+    finally:
         if world > 1:
             dist.barrier()
+            dist.destroy_process_group()
+    if res is not None and args.part_out:
+        Path(args.part_out).write_text(json.dumps(res))
 
-    for _ in range(args.warmup):
-        st.step(A, Bm, Kt, Vt, Qt)
-    torch.cuda.synchronize(device)
 
-    phases = PhaseEvents()
-    phases.wrap(st)
-    sampler = ClockSampler(device.index if device.index is not None else 0)
-    barrier()
-    torch.cuda.synchronize(device)
-    sampler.start()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        out = st.step(A, Bm, Kt, Vt, Qt)
-    t1.record()
-    torch.cuda.synchronize(device)
-    barrier()
-    clocks = sampler.stop()
-    phases.unwrap()
-    ms = t0.elapsed_time(t1) / args.steps
+# ---------------------------------------------------------------------------
+# our implementation: the headline line
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank, device) -> dict | None:
+    import torch
+
+    dist = _dist()
+    # sub-results first, each in a child process, before this process
+    # allocates anything large
+    port = None
     if world > 1:
-        tt = torch.tensor([ms], device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    phase_ms = phases.summary()
-    launches = 4 * args.steps
+        box = [_free_port() if rank == 0 else 0]
+        dist.broadcast_object_list(box, src=0)
+        port = int(box[0])
+    long_memory = None
+    if not args.no_long_memory:
+        barrier()
+        long_memory = run_child("long_memory", rank, world, local_rank, port, 900)
+        barrier()
+    extras = None
+    if world == 1 and not args.no_extras:
+        extras = run_child("extras", rank, world, local_rank, None, 900)
 
-    # end to end with host buffers: every step's inputs start in pinned host
-    # memory and its per-token results end there (HostPipeline overlaps the
-    # copies of step i+1 with the kernels of step i)
-    from gfst_hmb_public_b200.step import HostPipeline
-
-    e2e_steps = max(3, min(args.steps, 6))
-    host_in = [t.cpu().pin_memory() for t in (A, Bm, Kt, Vt, Qt)]
-    host_out = [(torch.empty((S, L), dtype=torch.int32).pin_memory(),
-                 torch.empty((S, L), dtype=torch.float32).pin_memory(),
-                 torch.empty((S, L, D), dtype=torch.bfloat16).pin_memory()) for _ in range(2)]
-    pipe = HostPipeline(st, (A, Bm, Kt, Vt, Qt))
-    pipe.run([host_in] * 2, host_out[:2])  # warm-up
-    torch.cuda.synchronize(device)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    pipe.run([host_in] * e2e_steps, [host_out[i % 2] for i in range(e2e_steps)])
-    e1.record()
-    torch.cuda.synchronize(device)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
-    h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
-    del host_in, pipe
-
-    # batched-QR microbenchmark (65,536 frames of 64 x 8, one QR each)
-    spec = wl.BATCHED_QR
-    xq = wl.batched_qr_inputs(spec["n"], spec["d"], spec["r"], seed=spec["seed"], device=device)
-    oq = torch.empty_like(xq)
-    for _ in range(5):
-        gfst.frame_update_qr(xq, sign_mode="r_diag_positive", out=oq)
-    torch.cuda.synchronize(device)
-    q0 = torch.cuda.Event(enable_timing=True)
-    q1 = torch.cuda.Event(enable_timing=True)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    qr_ms = []
-    for _ in range(10):
-        flush.zero_()  # evict L2 between launches
-        q0.record()
-        gfst.frame_update_qr(xq, sign_mode="r_diag_positive", out=oq)
-        q1.record()
-        torch.cuda.synchronize(device)
-        qr_ms.append(q0.elapsed_time(q1))
-    qr_ms_med = statistics.median(qr_ms)
-    qr_numel = xq.numel()
-    del flush, xq, oq
-
+    r = run_stream_full(args, rank, world, device)
     if rank != 0:
         return None
 
     peaks, peak_src = load_peaks()
     hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-    tokens_per_step = B_PER_GPU * L
-    value = world * tokens_per_step / (ms / 1e3)
-    e2e_value = world * tokens_per_step / (e2e_ms / 1e3)
+    S, ms, phase_ms = r["S"], r["ms"], r["phase_ms"]
+    tokens_per_step = B_TOTAL * L
+    value = tokens_per_step / (ms / 1e3)
+    e2e_value = tokens_per_step / (r["e2e_ms"] / 1e3)
 
-    # algorithmic bytes per launch:
-    #   frames  -- unfused per-token contract: read U, A, B and write U
-    #   readout -- unique key blocks selected by the step's 64 queries per stream,
-    #              plus queries, selections and the value rows written back
-    #   topk    -- summaries of every slot + queries (tensor-core GEMM, 2*d flops each pair)
-    #   commit  -- read K, V of the block; write them and the summary
-    sel = out.top_idx
-    uniq = 0
-    for s0 in range(0, S, 256):
-        blk = sel[s0:s0 + 256].reshape(sel[s0:s0 + 256].shape[0], -1)
-        srt = torch.sort(blk, dim=1).values
-        uniq += int((srt[:, 1:] != srt[:, :-1]).sum().item() + srt.shape[0])
+    # algorithmic bytes per launch (rank 0's shard):
+    #   frames     -- unfused per-token contract: read U, A, B and write U
+    #   readout    -- distinct key blocks selected by the step's queries, plus
+    #                 queries, selections, results and value rows
+    #   open_block -- the open block's keys, queries, results and value rows
+    #   topk       -- summaries of every slot + queries (2*d flops per pair)
+    #   commit     -- read K, V of the block; write them and the summary
     frames_bytes = S * L * (2 * D * R * 4 + (D * M + R * M) * 4)
-    readout_bytes = uniq * L * D * 2 + S * L * (D * 2 + K_SEL * 4 + D * 2 + 8)
+    readout_bytes = r["uniq"] * L * D * 2 + S * L * (D * 2 + K_SEL * 4 + D * 2 + 8)
+    open_bytes = S * L * (D * 2 * 2 + 8 + 8 + D * 2)
     commit_bytes = S * L * D * 2 * 2 * 2 + S * D * 2
     topk_flops = 2.0 * S * L * SLOTS * D
     shares = {k: v / sum(phase_ms.values()) for k, v in phase_ms.items()}
     dominant = max(phase_ms, key=phase_ms.get)
-    per_kernel = {
-        "frames": {"bytes": frames_bytes, "ms": phase_ms.get("frames")},
-        "readout": {"bytes": readout_bytes, "ms": phase_ms.get("readout")},
-        "commit": {"bytes": commit_bytes, "ms": phase_ms.get("commit")},
-    }
+    per_kernel = {"frames": frames_bytes, "readout": readout_bytes, "open_block": open_bytes,
+                  "commit": commit_bytes}
+    names = {"frames": "frame_stream", "readout": "exact_readout", "open_block": "open_block_readout",
+             "commit": "block_commit", "topk": "block_topk_tc"}
     traffic = None
     tp = REPO / "profiles" / "traffic.json"
     if tp.exists():
@@ -506,37 +726,37 @@ def run_ours(args, rank, world, device) -> dict | None:
     if dominant == "topk":
         ach = topk_flops / (phase_ms["topk"] / 1e3) / 1e12
         peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
-        roof = {"kernel": "block_topk_tc", "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
+        roof = {"kernel": names[dominant], "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
                 "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": traffic}
     else:
-        kb = per_kernel[dominant]
-        ach = kb["bytes"] / (kb["ms"] / 1e3) / 1e9
-        roof = {"kernel": {"frames": "frame_stream", "readout": "exact_readout", "commit": "block_commit"}[dominant],
-                "bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(ach / hbm_peak, 4), "traffic": traffic}
+        ach = per_kernel[dominant] / (phase_ms[dominant] / 1e3) / 1e9
+        roof = {"kernel": names[dominant], "bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak,
+                "unit": "GB/s", "frac": round(ach / hbm_peak, 4), "traffic": traffic}
+    clocks = r["clocks"]
     sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
     # frame work unit: the Householder flop count of a d x r thin QR plus the
     # rank-m update (4 d r^2 + 2 d r m per token), whatever algorithm runs
     frames_flops = S * L * (4.0 * D * R * R + 2.0 * D * R * M)
     fr_tflops = frames_flops / (phase_ms["frames"] / 1e3) / 1e12
     roof["peak_source"] = peak_src
+    roof["per_launch_units"] = f"rank 0's {S} streams x {L} tokens"
     roof["frames_fp32"] = {"achieved_tflops": round(fr_tflops, 2),
                            "peak_tflops_at_clock": round(fp32_peak_tflops(sm_mhz), 1),
                            "frac": round(fr_tflops / fp32_peak_tflops(sm_mhz), 4)}
+    if "readout" in phase_ms:
+        rb = readout_bytes / (phase_ms["readout"] / 1e3) / 1e9
+        roof["readout_hbm"] = {"achieved_gbs": round(rb, 1), "frac": round(rb / hbm_peak, 4)}
+    if "topk" in phase_ms:
+        tf = topk_flops / (phase_ms["topk"] / 1e3) / 1e12
+        roof["topk_tensor"] = {"achieved_tflops": round(tf, 2),
+                               "frac_of_bf16_peak": round(tf / float(peaks.get("bf16_tflops", 1590.0)), 4)}
     roof["kernel_ms"] = {k: round(v, 4) for k, v in phase_ms.items()}
     roof["kernel_share"] = {k: round(v, 3) for k, v in shares.items()}
-    roof["readout_unique_block_frac"] = round(uniq / (S * SLOTS), 3)
+    roof["phase_pass"] = "per-kernel times from a separate pass of the same steps (events on each kernel's stream)"
+    roof["readout_unique_block_frac"] = round(r["uniq"] / (S * SLOTS), 3)
 
-    qr_bytes = 2 * qr_numel * 4
-    qr_gbs = qr_bytes / (qr_ms_med / 1e3) / 1e9
-    batched_qr = {"value": round(spec["n"] / (qr_ms_med / 1e3), 1), "unit": "frames/s", "ms": round(qr_ms_med, 4),
-                  "workload": "65,536 frames 64x8 fp32, column j x 10^(-j/2), 1% near-collinear pairs; L2 flushed",
-                  "roofline": {"bound": "hbm", "achieved": round(qr_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                               "frac": round(qr_gbs / hbm_peak, 4), "peak_source": peak_src}}
-
-    cpu = cpu_baseline_sample(rank, world) if (world == 1 and not args.no_cpu_baseline) else None
-
-    return {
+    cpu = cpu_baseline_sample() if (world == 1 and not args.no_cpu_baseline) else None
+    res = {
         "metric": METRIC,
         "value": round(value, 1),
         "unit": "tokens/s",
@@ -544,88 +764,136 @@ def run_ours(args, rank, world, device) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
+        "step_ms": {"median": round(r["median"], 4), "p90": round(r["p90"], 4),
+                    "min": round(min(r["per_step"]), 4), "max": round(max(r["per_step"]), 4)},
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32 frames / bf16 memory (fp32 accumulate)",
         "data": "synthetic (seeded; no dataset for this path)",
         "config": {
-            "workload": f"stream_full: per GPU {B_PER_GPU} batch x {HEADS} heads = {S} streams; frames {D}x{R} fp32, "
-                        f"rank-{M} update + thin QR (R-diag-positive; CholeskyQR2, Householder fallback) per token; bf16 memory of "
-                        f"{SLOTS} blocks x {L} tokens (full ring); top-{K_SEL} blocks + exact-token argmax; "
-                        f"step = one {L}-token block",
-            "global_batch": B_PER_GPU * world,
+            "workload": f"stream_full: {B_TOTAL} batch x {HEADS} heads = {B_TOTAL * HEADS} streams in total, "
+                        f"{S} per GPU; frames {D}x{R} fp32, rank-{M} update + thin QR (R-diag-positive; "
+                        f"CholeskyQR2, Householder fallback) per token; bf16 memory of {SLOTS} blocks x {L} tokens "
+                        f"(full ring); top-{K_SEL} blocks + exact-token argmax over them and the open block's "
+                        f"prefix; step = one {L}-token block of every stream",
+            "global_batch": B_TOTAL,
             "heads": HEADS,
-            "tokens_per_step_per_gpu": tokens_per_step,
+            "tokens_per_step": tokens_per_step,
             "streams_per_gpu": S,
-            "parallelism": f"dp{world} (streams sharded by batch, no collectives on the data path)",
-            "l2": "step inputs 436 MB > 126 MB L2, re-read every step",
+            "parallelism": f"dp{world} (batch split over ranks, no collectives on the data path)",
+            "l2": "step inputs 436 MB in total (> 126 MB L2), re-read every step",
         },
         "roofline": roof,
         "cpu_baseline": cpu,
-        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "ms_per_step": round(r["e2e_ms"], 3),
+                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
                 "path": "HostPipeline.run: each step's inputs copied from pinned host memory, its results copied "
-                        "back; copies of step i+1 overlap the kernels of step i"},
-        "gpu_launches": launches,
+                        "back; copies of step i+1 overlap the kernels of step i (per rank)"},
+        "gpu_launches": r["launches"],
         "clocks": clocks,
-        "batched_qr": batched_qr,
         "long_memory": long_memory,
     }
+    if extras:
+        res.update({k: v for k, v in extras.items()})
+    return res
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline / reference arm: the oracle restatement of the reference's CPU
-# path, timed on the host cores
+# CPU baseline / reference arm: the reference's own CPU path on the host cores
 # ---------------------------------------------------------------------------
-def cpu_reference_step(n_streams: int, seed: int, threads: int) -> tuple[float, int]:
-    """One 64-token block for ``n_streams`` streams through the oracle
-    (torch.linalg.qr per token, exact scoring, top-k, exact readout) against a
-    full 512-block memory.  Returns (seconds, tokens)."""
-    import numpy as np
+def _reference_modules():
+    """(gfst, retrieval) of the reference from its offline install, or None."""
+    try:
+        from oracle import reference_import
 
-    from oracle import gfst_oracle as go
+        if reference_import.find_reference() is None:
+            return None
+        gfst = reference_import.load("gfst")
+        retrieval = reference_import.load("retrieval")
+        return gfst, retrieval
+    except Exception:
+        return None
+
+
+def cpu_reference_step(n_streams: int, seed: int, threads: int, ref) -> tuple[float, int]:
+    """One 64-token block of ``n_streams`` streams against a full 512-block
+    memory on the host cores.  With ``ref`` = the reference's own modules: the
+    candidate U + A B^T then gfst.canonical_qr_batched per token (gfst.py:26-32),
+    FaissGpuRetriever.exact_topk per query (retrieval.py:165-172), and the exact
+    readout as _score_block_tokens computes it with an identity projection
+    (tokens of the selected blocks and the open block's prefix, K @ q, argmax;
+    modeling.py:599-657, 2948-2963).  Without it: the oracle restatement.
+    Returns (seconds, tokens), tokens = batch positions through all heads."""
+    import torch
 
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(seed)
     std = 1.0 / math.sqrt(D)
-    U0 = torch.linalg.qr(torch.randn((n_streams, D, R), generator=g))[0].numpy()
-    A = (torch.randn((n_streams, L, D, M), generator=g) * std).numpy()
-    Bm = (torch.randn((n_streams, L, R, M), generator=g) * std).numpy()
-    pool = torch.randn((n_streams, SLOTS, L, D), generator=g).to(torch.bfloat16).float().numpy()
-    summary = go.block_commit_mean(pool, bf16=True)
-    Q = torch.randn((n_streams, L, D), generator=g).to(torch.bfloat16).float().numpy()
-    Kb = torch.randn((n_streams, L, D), generator=g).to(torch.bfloat16).float().numpy()
+    U0 = torch.linalg.qr(torch.randn((n_streams, D, R), generator=g))[0]
+    A = torch.randn((n_streams, L, D, M), generator=g) * std
+    Bm = torch.randn((n_streams, L, R, M), generator=g) * std
+    pool = torch.randn((n_streams, SLOTS, L, D), generator=g).to(torch.bfloat16).float()
+    summary = pool.mean(2).to(torch.bfloat16).float()
+    Q = torch.randn((n_streams, L, D), generator=g).to(torch.bfloat16).float()
+    Kb = torch.randn((n_streams, L, D), generator=g).to(torch.bfloat16).float()
+    if ref is not None:
+        rgfst, rret = ref
+        t0 = time.perf_counter()
+        U = U0
+        for t in range(L):
+            cand = U + torch.matmul(A[:, t], Bm[:, t].transpose(-1, -2))
+            U = rgfst.canonical_qr_batched(cand, eps_sign=1e-8)
+        for s in range(n_streams):
+            for t in range(L):
+                idx, _ = rret.FaissGpuRetriever.exact_topk(summary[s], Q[s, t], K_SEL)
+                keys = torch.cat((pool[s, idx].reshape(-1, D), Kb[s, :t + 1] if t < L - 1 else Kb[s, :0]))
+                scores = keys @ Q[s, t]
+                int(torch.argmax(scores))
+        _ = Kb.mean(1)  # the block's summary key at commit
+        dt = time.perf_counter() - t0
+        return dt, L * n_streams // HEADS
+    from oracle import gfst_oracle as go
+
+    np_U0, np_A, np_B = U0.numpy(), A.numpy(), Bm.numpy()
     t0 = time.perf_counter()
-    go.stream_frames(U0, A, Bm, 1.0, 1e-8, go.SIGN_R_DIAG_POSITIVE)
-    _, top_i, _ = go.block_topk(Q, summary, K_SEL)
-    go.exact_readout(Q, pool, pool, top_i)
-    go.block_commit_mean(Kb, bf16=True)
+    go.stream_frames(np_U0, np_A, np_B, 1.0, 1e-8, go.SIGN_R_DIAG_POSITIVE)
+    _, top_i, _ = go.block_topk(Q.numpy(), summary.numpy(), K_SEL)
+    go.exact_readout(Q.numpy(), pool.numpy(), pool.numpy(), top_i)
+    go.block_commit_mean(Kb.numpy(), bf16=True)
     dt = time.perf_counter() - t0
     return dt, L * n_streams // HEADS
 
 
-def cpu_baseline_sample(rank: int, world: int) -> dict:
+def cpu_baseline_sample() -> dict:
     threads = os.cpu_count() or 1
-    dt, tokens = cpu_reference_step(HEADS, SEED + 99, threads)
-    return {"value": round(tokens / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"one batch element ({HEADS} heads) x {L} tokens of the same workload through the oracle "
-                      f"restatement (torch.linalg.qr per token, exact scores, top-k, readout) in {dt:.2f} s"}
+    ref = _reference_modules()
+    cpu_reference_step(HEADS, SEED + 98, threads, ref)  # warm-up
+    dt, tokens = cpu_reference_step(HEADS, SEED + 99, threads, ref)
+    kind = "reference" if ref is not None else "port"
+    what = ("the reference's own canonical_qr_batched per token, FaissGpuRetriever.exact_topk per query and the "
+            "exact readout with torch" if ref is not None else
+            "the oracle restatement (torch.linalg.qr per token, exact scores, top-k, readout)")
+    return {"value": round(tokens / dt, 2), "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"one batch element ({HEADS} heads) x {L} tokens of the same workload through {what} "
+                      f"in {dt:.2f} s"}
 
 
 def run_reference(args, rank, world) -> dict | None:
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
+    ref = _reference_modules()
     for _ in range(max(0, min(args.warmup, 1))):
-        cpu_reference_step(HEADS, SEED + 98, threads)
+        cpu_reference_step(HEADS, SEED + 98, threads, ref)
     times, tokens = [], 0
     for i in range(args.steps):
-        dt, tok = cpu_reference_step(HEADS, SEED + 100 + i, threads)
+        dt, tok = cpu_reference_step(HEADS, SEED + 100 + i, threads, ref)
         times.append(dt)
         tokens = tok
     per_step = sum(times) / len(times)
     value = tokens / per_step
+    kind = "reference" if ref is not None else "port"
     return {
         "metric": METRIC,
         "value": round(value, 2),
@@ -635,21 +903,26 @@ def run_reference(args, rank, world) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": round(per_step * 1e3, 2),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32 frames / bf16-valued memory (fp32 compute)",
         "data": "synthetic (seeded; no dataset for this path)",
         "impl": "reference",
         "config": {"workload": "stream_full (same per-stream shapes); each step a bounded sample of one batch "
                                f"element ({HEADS} heads) x {L} tokens on the host cores",
-                   "global_batch": B_PER_GPU * world, "parallelism": "host cores of rank 0"},
-        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{HEADS} streams x {L} tokens per step"},
+                   "global_batch": B_TOTAL, "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{HEADS} streams x {L} tokens per step"
+                                   + (" through the reference's own gfst / retrieval modules" if ref else
+                                      " through the oracle restatement")},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
 def main() -> None:
+    if len(sys.argv) >= 2 and sys.argv[1] == "--clock-sampler":
+        clock_sampler_main(sys.argv[2], sys.argv[3], float(sys.argv[4]))
+        return
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=20)
@@ -657,7 +930,13 @@ def main() -> None:
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core baseline sample")
     parser.add_argument("--no-long-memory", action="store_true", help="skip the long-memory readout sub-result")
+    parser.add_argument("--no-extras", action="store_true", help="skip the one-GPU sub-results")
+    parser.add_argument("--part", default=None, help=argparse.SUPPRESS)
+    parser.add_argument("--part-out", default=None, help=argparse.SUPPRESS)
     args = parser.parse_args()
+    if args.part:
+        part_main(args)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
@@ -679,14 +958,15 @@ def main() -> None:
 
     import datetime
 
+    import torch
     import torch.distributed as dist
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
-        res = run_ours(args, rank, world, device)
+        res = run_ours(args, rank, world, local_rank, device)
     finally:
         if world > 1:
             dist.barrier()

@@ -90,6 +90,10 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
     ],
+    "gfst_open_block_readout": [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_int64, _c_int,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+    ],
     "gfst_segmented_max": [_c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p],
     "gfst_segmented_logsumexp_occurrence": [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p, _c_void_p,
@@ -153,6 +157,21 @@ def call(name: str, *args) -> None:
     """Invoke entry point ``name`` and raise on a non-OK status."""
     fn = getattr(load(), name)
     check(fn(*args), name)
+
+
+def check_device_errors(clear: bool = True) -> None:
+    """Raise RuntimeError when a kernel recorded a device-side failure since
+    the last check: a bounded in-kernel wait that gave up (GFST_ERR_TIMEOUT) or
+    an eigensolver that did not converge (GFST_ERR_NUMERIC).  Synchronises the
+    current device first, so work enqueued on any stream before the call is
+    covered; the recorded status is cleared unless ``clear`` is False.  Call it
+    at a point where the host waits anyway (the end of a pass, before results
+    are used); outputs of a launch that recorded a failure are not valid."""
+    status = int(load().gfst_check_device_errors(1 if clear else 0))
+    if status != GFST_OK:
+        lib = load()
+        raise RuntimeError(f"device-side failure: {lib.gfst_status_string(status).decode()} (status {status}): "
+                           f"{lib.gfst_last_error().decode()}")
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -28,20 +28,7 @@
 namespace gfst {
 
 // sticky GFST_ERR_NUMERIC report of the eigen commit
-__device__ unsigned int g_commit_error = 0;
-
-int read_commit_error(int clear, unsigned int* value) {
-  unsigned int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_commit_error, sizeof(v));
-  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the commit error word: %s", cudaGetErrorString(e));
-  if (clear && v != 0) {
-    const unsigned int zero = 0;
-    e = cudaMemcpyToSymbol(g_commit_error, &zero, sizeof(zero));
-    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "clearing the commit error word: %s", cudaGetErrorString(e));
-  }
-  *value = v;
-  return GFST_OK;
-}
+GFST_DEFINE_ERROR_WORD(g_commit_error, read_commit_error, "commit")
 
 namespace {
 

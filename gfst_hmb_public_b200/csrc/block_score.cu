@@ -21,21 +21,8 @@
 
 namespace gfst {
 
-__device__ unsigned int g_score_error = 0;  // sticky GFST_ERR_TIMEOUT report of the tensor-core kernel
-
-int read_score_error(int clear, unsigned int* value) {
-  unsigned int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_score_error, sizeof(v));
-  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the block score error word: %s", cudaGetErrorString(e));
-  if (clear && v != 0) {
-    const unsigned int zero = 0;
-    e = cudaMemcpyToSymbol(g_score_error, &zero, sizeof(zero));
-    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "clearing the block score error word: %s",
-                 cudaGetErrorString(e));
-  }
-  *value = v;
-  return GFST_OK;
-}
+// sticky GFST_ERR_TIMEOUT report of the tensor-core block-score kernel
+GFST_DEFINE_ERROR_WORD(g_score_error, read_score_error, "block score")
 
 namespace {
 

@@ -27,6 +27,9 @@ extern "C" int gfst_debug_bounded_wait(int64_t cycles, cudaStream_t stream) {
 }
 
 extern "C" int gfst_check_device_errors(int clear) {
+  // every stream of the current device, the library's non-blocking ones included
+  const cudaError_t se = cudaDeviceSynchronize();
+  GFST_REQUIRE(se == cudaSuccess, GFST_ERR_DEVICE, "cudaDeviceSynchronize: %s", cudaGetErrorString(se));
   unsigned int v = 0, w = 0;
   int st = gfst::read_device_error(clear, &v);
   if (st != GFST_OK) return st;

@@ -25,7 +25,8 @@
 
 namespace gfst {
 
-__device__ unsigned int g_device_error = 0;  // sticky GFST_ERR_TIMEOUT report
+// sticky GFST_ERR_TIMEOUT report of the tensor-core retrieval and the wait probe
+GFST_DEFINE_ERROR_WORD(g_device_error, read_device_error, "retrieval")
 
 namespace {
 
@@ -364,17 +365,5 @@ int launch_bounded_wait_probe(long long budget, cudaStream_t stream) {
   return check_launch("bounded_wait_probe_kernel");
 }
 
-int read_device_error(int clear, unsigned int* value) {
-  unsigned int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
-  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the device error word: %s", cudaGetErrorString(e));
-  if (clear && v != 0) {
-    const unsigned int zero = 0;
-    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
-    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "clearing the device error word: %s", cudaGetErrorString(e));
-  }
-  *value = v;
-  return GFST_OK;
-}
 
 }  // namespace gfst

@@ -24,20 +24,7 @@
 namespace gfst {
 
 // sticky GFST_ERR_TIMEOUT report of the pipelined readout's bounded waits
-__device__ unsigned int g_readout_error = 0;
-
-int read_readout_error(int clear, unsigned int* value) {
-  unsigned int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_readout_error, sizeof(v));
-  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the readout error word: %s", cudaGetErrorString(e));
-  if (clear && v != 0) {
-    const unsigned int zero = 0;
-    e = cudaMemcpyToSymbol(g_readout_error, &zero, sizeof(zero));
-    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "clearing the readout error word: %s", cudaGetErrorString(e));
-  }
-  *value = v;
-  return GFST_OK;
-}
+GFST_DEFINE_ERROR_WORD(g_readout_error, read_readout_error, "readout")
 
 namespace {
 

@@ -28,6 +28,34 @@ int check_launch(const char* what);
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------------------
+// sticky device error words
+// ---------------------------------------------------------------------------
+// One word per translation unit: kernels record a status with atomicExch; the
+// host reads it (and clears it when asked) in one atomic step through a
+// one-thread kernel on the legacy default stream, whose result lands in a
+// snapshot word that the following cudaMemcpyFromSymbol reads.  Callers
+// synchronise the device first (gfst_check_device_errors does), so the word
+// holds every report of work enqueued before the call.
+#define GFST_DEFINE_ERROR_WORD(word, reader, what)                                                         \
+  __device__ unsigned int word = 0;                                                                       \
+  __device__ unsigned int word##_snapshot = 0;                                                            \
+  __global__ void word##_take(int clear) {                                                                \
+    word##_snapshot = clear ? atomicExch(&word, 0u) : atomicOr(&word, 0u);                                \
+  }                                                                                                        \
+  int reader(int clear, unsigned int* value) {                                                             \
+    word##_take<<<1, 1, 0, cudaStreamLegacy>>>(clear);                                                     \
+    cudaError_t e = cudaGetLastError();                                                                    \
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the " what " error word: %s",                \
+                 cudaGetErrorString(e));                                                                   \
+    unsigned int v = 0;                                                                                    \
+    e = cudaMemcpyFromSymbol(&v, word##_snapshot, sizeof(v));                                              \
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "reading the " what " error word: %s",                \
+                 cudaGetErrorString(e));                                                                   \
+    *value = v;                                                                                            \
+    return GFST_OK;                                                                                        \
+  }
+
+// ---------------------------------------------------------------------------
 // compile-time helpers usable in device code
 // ---------------------------------------------------------------------------
 template <int V>

@@ -91,6 +91,12 @@ class BlockMemory:
     def mark_mutated(self) -> None:
         self.state_version += 1
 
+    def reset(self) -> None:
+        """Forget every committed block (the pools keep their bytes; nothing
+        reads a slot before a commit writes it again)."""
+        self.blocks_committed = 0
+        self.mark_mutated()
+
     def slot_block_index(self) -> torch.Tensor:
         """Block index (position in the stream / L) held by each slot, -1 for empty."""
         idx = torch.full((self.n_slots,), -1, dtype=torch.int64)

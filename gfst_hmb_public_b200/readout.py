@@ -47,6 +47,58 @@ def exact_readout(Q: torch.Tensor, pool_K: torch.Tensor, pool_V: torch.Tensor | 
     return best_tok, best_score, out_V
 
 
+def open_block_readout(Q: torch.Tensor, K_open: torch.Tensor, V_open: torch.Tensor | None, best_tok: torch.Tensor,
+                       best_score: torch.Tensor, out_V: torch.Tensor | None, *, open_base: int,
+                       open_len: torch.Tensor | None = None) -> None:
+    """Merge the readout over the open block's prefix into a committed-block
+    result, in place (the current block appended to the retrieved blocks with
+    its prefix length, modeling.py:2948-2963; the token is appended to the exact
+    store before its own retrieval, modeling.py:3807 vs 3853).
+
+    Q [S, Nq, d]; K_open [S, L_open, d]; V_open [S, L_open, dv] or None;
+    best_tok int32 / best_score f32 [S, Nq] and out_V [S, Nq, dv] as
+    exact_readout returns them.  Query q scores open positions [0, n) with
+    n = open_len[s, q] ([S, Nq] int32), or by default n = q + 1 while
+    q < L_open - 1 and n = 0 from q = L_open - 1 on (the reference closes the
+    block in the exact store at its last token, and its summary becomes
+    retrievable only after that token's retrieval).  The best open position p
+    (token index open_base + p) replaces the result when it ranks first in
+    (score descending, token index ascending)."""
+    nat.require_cuda(Q, K_open, V_open, best_tok, best_score, out_V, open_len, what="open_block_readout")
+    if Q.ndim != 3 or K_open.ndim != 3 or K_open.shape[0] != Q.shape[0] or K_open.shape[2] != Q.shape[2]:
+        raise ValueError("open_block_readout expects Q [S,Nq,d], K_open [S,L_open,d]")
+    S, Nq, d = Q.shape
+    Lo = K_open.shape[1]
+    if tuple(best_tok.shape) != (S, Nq) or tuple(best_score.shape) != (S, Nq):
+        raise ValueError("open_block_readout: best_tok / best_score must be [S, Nq]")
+    if best_tok.dtype != torch.int32 or best_score.dtype != torch.float32:
+        raise RuntimeError("open_block_readout: best_tok must be int32 and best_score float32")
+    if (V_open is None) != (out_V is None):
+        raise ValueError("open_block_readout: V_open and out_V go together")
+    dv = 0
+    if V_open is not None:
+        dv = V_open.shape[-1]
+        if tuple(V_open.shape) != (S, Lo, dv) or tuple(out_V.shape) != (S, Nq, dv):
+            raise ValueError("open_block_readout: V_open / out_V shapes do not match")
+        if V_open.dtype != Q.dtype or out_V.dtype != Q.dtype:
+            raise RuntimeError("open_block_readout: Q, K_open, V_open and out_V must share a dtype")
+    if K_open.dtype != Q.dtype:
+        raise RuntimeError("open_block_readout: Q and K_open must share a dtype")
+    for t in (best_tok, best_score, out_V):
+        if t is not None and not t.is_contiguous():
+            raise ValueError("open_block_readout: outputs must be contiguous")
+    if open_len is not None:
+        if tuple(open_len.shape) != (S, Nq):
+            raise ValueError("open_block_readout: open_len must be [S, Nq]")
+        open_len = open_len.to(torch.int32).contiguous()
+    Q, K_open = Q.contiguous(), K_open.contiguous()
+    V_open = V_open.contiguous() if V_open is not None else None
+    with torch.cuda.device(Q.device):
+        nat.call("gfst_open_block_readout", nat.ptr(Q), nat.ptr(K_open), nat.ptr(V_open), nat.ptr(open_len), S, Nq,
+                 Lo, d, dv, int(open_base), nat.dtype_code(Q.dtype, "open_block_readout"), nat.ptr(best_tok),
+                 nat.ptr(best_score), nat.ptr(out_V), nat.stream_of(Q))
+
+
 def exact_readout_collapse(Q: torch.Tensor, pool_K: torch.Tensor, token_ids: torch.Tensor, top_idx: torch.Tensor):
     """The readout with the reference's log-sum-exp collapse of duplicate token
     ids (perf.py:164-229 collapse_logsumexp_scores_and_occurrence, then the

@@ -6,16 +6,22 @@ One step consumes one block of L tokens for every (batch, head) stream:
            held in registers across the block (gfst_frame_stream);
 * readout  for each of the L queries: score every committed block summary
            (tcgen05 GEMM + top-k), then score the tokens of the k selected
-           blocks and return the best token and its value row;
+           blocks and of the step's own block up to the query's position, and
+           return the best token and its value row;
 * commit   the block's keys and values go into the memory ring and its summary
            key (mean of the keys) into the summary table.
 
 The frame update and the readout are independent within a step, so they run on
 two CUDA streams: the frame kernel is FP32-ALU bound and the readout is HBM
 bound, and the two overlap on the SMs.  The commit follows the readout on the
-memory stream (the step's queries see the memory as it was before the step, as
-in the reference, where the block summary is appended after retrieval;
-modeling.py:3618-3632 of pkhairkh/gfst-hmb-public).
+memory stream.  What a query at position p of the step's block sees is what the
+reference's query of that token sees (pkhairkh/gfst-hmb-public): the committed
+blocks (a block summary is appended after the retrieval of the block's last
+token, modeling.py:3618-3632) and, since each token is appended to the exact
+store before its own retrieval (modeling.py:3807 vs 3853), positions [0, p] of
+its own block while p < L - 1 (modeling.py:2948-2963); at p = L - 1 the exact
+store has already closed the block (state.py:749-815), so that query sees the
+committed blocks only.
 
 Reference loop being replaced (pkhairkh/gfst-hmb-public): the per-token
 ``for token: for batch:`` loop of GfstHmbSublayer (src/gfst_hmb_mpuc/modeling.py:
@@ -33,10 +39,16 @@ from . import gfst, memory, readout, retrieval
 
 @dataclass
 class StepOutputs:
-    best_tok: torch.Tensor    # [S, L] int32, token index b * L + p of the best token (-1: none)
+    """Per-query results of one step.  best_tok is the token index slot * L + p
+    of the best token in the memory ring, or open_base + p for position p of
+    the step's own block (open_base = n_slots * L; that block is committed to
+    ``slot`` at the end of the step), or -1 when nothing was valid."""
+    best_tok: torch.Tensor    # [S, L] int32
     best_score: torch.Tensor  # [S, L] float32
     value: torch.Tensor       # [S, L, dv] memory dtype
     top_idx: torch.Tensor     # [S, L, k] int32 selected block slots
+    open_base: int = 0
+    slot: int = -1
 
 
 class StreamingStep:
@@ -56,6 +68,15 @@ class StreamingStep:
 
     def set_frames(self, U0: torch.Tensor) -> None:
         self.U.copy_(U0)
+
+    def reset(self) -> None:
+        """Empty the memory ring (the frames are left as they are)."""
+        self.memory.reset()
+
+    @property
+    def open_base(self) -> int:
+        """Token index of position 0 of the step's own block in StepOutputs.best_tok."""
+        return self.n_slots * self.block_len
 
     def step(self, A: torch.Tensor, B: torch.Tensor, K: torch.Tensor, V: torch.Tensor, Q: torch.Tensor,
              *, out: StepOutputs | None = None) -> StepOutputs:
@@ -79,18 +100,20 @@ class StreamingStep:
                 best_tok = torch.full((S, L), -1, dtype=torch.int32, device=self.device)
                 best_score = torch.full((S, L), float("-inf"), dtype=torch.float32, device=self.device)
                 value = torch.zeros((S, L, V.shape[-1]), dtype=V.dtype, device=self.device)
-            self.memory.commit(K, V)
+            readout.open_block_readout(Q, K, V, best_tok, best_score, value, open_base=self.open_base)
+            slot = self.memory.commit(K, V)
         cur.wait_stream(self.frames_stream)
         cur.wait_stream(self.memory_stream)
         # tensors produced on side streams are consumed on the current stream
         for t in (best_tok, best_score, value, top_i, self.U):
             t.record_stream(cur)
-        result = StepOutputs(best_tok, best_score, value, top_i)
+        result = StepOutputs(best_tok, best_score, value, top_i, self.open_base, slot)
         if out is not None:
             out.best_tok.copy_(best_tok)
             out.best_score.copy_(best_score)
             out.value.copy_(value)
             out.top_idx.copy_(top_i)
+            out.open_base, out.slot = self.open_base, slot
             return out
         return result
 
@@ -113,6 +136,7 @@ class HostPipeline:
         self.download = torch.cuda.Stream(dev)
         self.ready = [torch.cuda.Event() for _ in range(2)]
         self.free = [torch.cuda.Event() for _ in range(2)]
+        self.done = [torch.cuda.Event() for _ in range(2)]
         for e in self.free:
             e.record(torch.cuda.current_stream(dev))
 
@@ -140,9 +164,8 @@ class HostPipeline:
             cur.wait_event(self.ready[b])
             out = self.step_obj.step(*self.buffers[b])
             self.free[b].record(cur)
-            done = torch.cuda.Event()
-            done.record(cur)
-            self.download.wait_event(done)
+            self.done[b].record(cur)
+            self.download.wait_event(self.done[b])
             with torch.cuda.stream(self.download):
                 for h, d in zip(host_outputs_per_step[i], (out.best_tok, out.best_score, out.value)):
                     h.copy_(d, non_blocking=True)

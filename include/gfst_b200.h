@@ -41,6 +41,9 @@
  *                             src/gfst_hmb_mpuc/retrieval.py:136-172
  *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
  *                             src/gfst_hmb_mpuc/modeling.py:599-657, 1151-1169
+ *   gfst_open_block_readout <- the current (open) block appended to the retrieved blocks
+ *                             with its prefix length, modeling.py:2948-2963 (token appended
+ *                             first, modeling.py:3807 / state.py:651-815, retrieval at :3853)
  *   gfst_segmented_max     <- runtime_backends segmented_max_by_group(scores, inverse, group_count)
  *                             src/gfst_hmb_mpuc/csrc/sm120_stub.cu:16-40, 150-172, called by
  *                             perf.collapse_max_scores_by_group perf.py:136-161
@@ -394,6 +397,34 @@ GFST_API int gfst_exact_readout(const void* Q, const void* pool_K, const void* p
                        int n_slots, int L, int d, int dv, int k, int dtype,
                        int32_t* best_tok, float* best_score, void* out_V,
                        cudaStream_t stream);
+
+/* ---- open-block readout ------------------------------------------------------
+ * The exact readout over the prefix of the block still being written, merged
+ * into a result over the committed blocks (gfst_exact_readout's outputs, in
+ * place).  Replaces the current-block part of the reference's readout
+ * (modeling.py:2948-2963: the open block and its prefix length are appended to
+ * the retrieved blocks; the token is appended to the exact store,
+ * modeling.py:3807 / state.py:651-815, before its own retrieval at :3853).
+ * For every stream s and query q with n = open_len(s, q) > 0:
+ *   score(p) = Q[s,q,:] . K_open[s,p,:] for p in [0, n)        (fp32 accumulate)
+ *   the best open position (score descending, position ascending; NaN never
+ *   wins) has token index open_base + p; it replaces (best_tok, best_score,
+ *   out_V) of (s, q) when best_tok[s,q] < 0 or it ranks first in (score
+ *   descending, token index ascending); out_V[s,q,:] = V_open[s,p,:].
+ * open_len: [n_streams, n_queries] int32 (clamped to [0, L_open]), or NULL for
+ *   the streaming rule: query q sees positions [0, q] while q < L_open - 1 and
+ *   none from q = L_open - 1 on (the reference closes a block in the exact
+ *   store at its last token, before that token's retrieval, and appends its
+ *   summary only after it).
+ * Q: [n_streams, n_queries, d]; K_open: [n_streams, L_open, d]; V_open:
+ * [n_streams, L_open, dv] (may be NULL together with out_V); best_tok,
+ * best_score: [n_streams, n_queries]; out_V: [n_streams, n_queries, dv].
+ * dtype (GFST_F32 or GFST_BF16) applies to Q, K_open, V_open, out_V.
+ * Limits: d a multiple of 4, d <= 256; open_base + L_open < 2^31.         */
+GFST_API int gfst_open_block_readout(const void* Q, const void* K_open, const void* V_open,
+                            const int32_t* open_len, int64_t n_streams, int n_queries, int L_open,
+                            int d, int dv, int64_t open_base, int dtype, int32_t* best_tok,
+                            float* best_score, void* out_V, cudaStream_t stream);
 
 /* ---- segmented reductions over group ids -------------------------------------
  * inverse[i] in [0, group_count) names element i's group (elements outside

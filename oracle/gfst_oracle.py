@@ -534,16 +534,23 @@ def block_topk(Q: np.ndarray, Ksum: np.ndarray, k: int):
 # ---------------------------------------------------------------------------
 # exact-token readout
 # ---------------------------------------------------------------------------
-def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, top_idx: np.ndarray):
+def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, top_idx: np.ndarray,
+                  open_K: np.ndarray | None = None, open_V: np.ndarray | None = None,
+                  open_len: np.ndarray | None = None, open_base: int = 0):
     """modeling.py:599-657 (_score_block_tokens: token score = key . query) and
     modeling.py:1151-1169 (best token = first of the scores sorted descending),
     with token index b*L + p and the total order (score desc, index asc); NaN
     scores never win and a block listed twice counts once.
     Q [S,Nq,d]; pool_K [S,NB,L,d]; pool_V [S,NB,L,dv]; top_idx [S,Nq,k] int.
+    Optionally the open block (modeling.py:2948-2963: the current block is
+    appended to the retrieved blocks with its prefix length): open_K [S,Lo,d],
+    open_V [S,Lo,dv], open_len [S,Nq] (positions [0, n) of the open block are
+    candidates too, with token index open_base + p).
     Returns (best_tok int32 [S,Nq], best_score f32 [S,Nq], out_V [S,Nq,dv] or None,
     margin_ok bool [S,Nq] -- False when the runner-up is within 1e-3 relative)."""
     S, Nq, _ = Q.shape
     L = pool_K.shape[2]
+    NB = pool_K.shape[1]
     best_tok = np.full((S, Nq), -1, np.int32)
     best_score = np.full((S, Nq), -np.inf, np.float32)
     margin_ok = np.ones((S, Nq), bool)
@@ -551,12 +558,17 @@ def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, 
     out_V = np.zeros((S, Nq, dv), np.float32) if pool_V is not None else None
     for s in range(S):
         for q in range(Nq):
-            blocks = [int(b) for b in top_idx[s, q] if b >= 0]
-            blocks = sorted(set(blocks))
-            if not blocks:
+            blocks = sorted({int(b) for b in top_idx[s, q] if 0 <= b < NB})
+            key_parts = [pool_K[s, b] for b in blocks]
+            tok_parts = [b * L + np.arange(L) for b in blocks]
+            n_open = 0 if open_K is None else int(min(max(int(open_len[s, q]), 0), open_K.shape[1]))
+            if n_open > 0:
+                key_parts.append(open_K[s, :n_open])
+                tok_parts.append(open_base + np.arange(n_open))
+            if not key_parts:
                 continue
-            keys = np.concatenate([pool_K[s, b] for b in blocks], axis=0).astype(np.float64)
-            toks = np.concatenate([b * L + np.arange(L) for b in blocks])
+            keys = np.concatenate(key_parts, axis=0).astype(np.float64)
+            toks = np.concatenate(tok_parts)
             sc = keys @ np.asarray(Q[s, q], np.float64)
             keep = ~np.isnan(sc)  # NaN scores never win
             if not keep.any():
@@ -570,5 +582,83 @@ def exact_readout(Q: np.ndarray, pool_K: np.ndarray, pool_V: np.ndarray | None, 
                 s1, s2 = sc[order[0]], sc[order[1]]
                 margin_ok[s, q] = abs(s1 - s2) > 1e-3 * max(abs(s1), 1e-30)
             if pool_V is not None:
-                out_V[s, q] = pool_V[s, toks[w] // L, toks[w] % L]
+                tw = int(toks[w])
+                out_V[s, q] = open_V[s, tw - open_base] if tw >= open_base and n_open > 0 else \
+                    pool_V[s, tw // L, tw % L]
     return best_tok, best_score, out_V, margin_ok
+
+
+def streaming_open_len(n_queries: int, block_len: int) -> np.ndarray:
+    """Open-block prefix each query of a block sees (modeling.py:2948-2963 with
+    the exact-store append at modeling.py:3807 before the retrieval at :3853):
+    query p sees positions [0, p] while p < L - 1; at p = L - 1 append_exact_token
+    has already closed the block (state.py:749-815) and its summary is appended
+    only after the retrieval (modeling.py:3632), so that query sees none."""
+    p = np.arange(n_queries)
+    return np.where(p < block_len - 1, p + 1, 0).astype(np.int32)
+
+
+def streaming_pass(U0, A, B, K, V, Q, *, block_len: int, n_slots: int, k: int, memory_bf16: bool,
+                   sign_mode: int = SIGN_R_DIAG_POSITIVE, eps_sign: float = 1e-8):
+    """The streaming step composed token by token in the reference's order
+    (GfstHmbSublayer, modeling.py:3590-3640 and 3790-3870), with the
+    benchmark's simplifications (update U + A B^T, mean-of-keys block summary,
+    identity within-block projection, token keys / values / queries given):
+
+      for each token t (position p = t mod L of its block):
+        1. frame update + thin QR (modeling.py:3600-3607; gfst.py:26-46, 115-140)
+        2. append the token to the open block of the exact store
+           (modeling.py:3807; state.py:651-815); at p = L - 1 the block closes
+        3. retrieval: top-k over the committed summaries (modeling.py:3853 ->
+           2714-2920; retrieval.py:165-172)
+        4. readout: the tokens of the selected blocks and positions [0, p] of the
+           open block while p < L - 1 (modeling.py:2948-2963, 599-657, 1151-1169)
+        5. at p = L - 1, after the retrieval, the block's summary is appended
+           (modeling.py:3632 -> 3401-3571) and the block joins the memory.
+
+    The memory holds the last n_slots committed blocks, block b in slot
+    b mod n_slots (the reference keeps every block; both agree while fewer than
+    n_slots + 1 blocks are committed).  Committed token index = slot * L + p;
+    open-block position p = n_slots * L + p.
+    U0 [S,d,r]; A [S,T,d,m]; B [S,T,r,m]; K, V, Q [S,T,d] float32 (bf16-valued
+    when memory_bf16).  Returns a dict of per-token arrays: frames [S,T,d,r],
+    top_idx [S,T,k], top_ok [S,T], best_tok [S,T], best_score [S,T], value
+    [S,T,dv], read_ok [S,T]."""
+    U = np.array(U0, np.float32, copy=True)
+    A, B = np.asarray(A, np.float32), np.asarray(B, np.float32)
+    K, V, Q = (np.asarray(x, np.float32) for x in (K, V, Q))
+    S, T, d, _ = A.shape
+    L = int(block_len)
+    dv = V.shape[-1]
+    pool_K = np.zeros((S, n_slots, L, d), np.float32)
+    pool_V = np.zeros((S, n_slots, L, dv), np.float32)
+    summary = np.zeros((S, n_slots, d), np.float32)
+    open_K = np.zeros((S, L, d), np.float32)
+    open_V = np.zeros((S, L, dv), np.float32)
+    committed = 0
+    out = {"frames": np.zeros((S, T) + U.shape[1:], np.float32),
+           "top_idx": np.full((S, T, k), -1, np.int32), "top_ok": np.ones((S, T), bool),
+           "best_tok": np.full((S, T), -1, np.int32), "best_score": np.full((S, T), -np.inf, np.float32),
+           "value": np.zeros((S, T, dv), np.float32), "read_ok": np.ones((S, T), bool)}
+    for t in range(T):
+        p = t % L
+        U = qr_reference(frame_candidate(U, A[:, t], B[:, t]), eps_sign, sign_mode)
+        out["frames"][:, t] = U
+        open_K[:, p], open_V[:, p] = K[:, t], V[:, t]
+        n_open = p + 1 if p < L - 1 else 0
+        n_valid = min(committed, n_slots)
+        top_i = np.full((S, 1, k), -1, np.int32)
+        if n_valid > 0:
+            _, top_i, ok = block_topk(Q[:, t:t + 1], summary[:, :n_valid], k)
+            out["top_ok"][:, t] = ok[:, 0]
+        out["top_idx"][:, t] = top_i[:, 0]
+        bt, bs, bv, rok = exact_readout(Q[:, t:t + 1], pool_K, pool_V, top_i, open_K, open_V,
+                                        np.full((S, 1), n_open, np.int32), n_slots * L)
+        out["best_tok"][:, t], out["best_score"][:, t] = bt[:, 0], bs[:, 0]
+        out["value"][:, t], out["read_ok"][:, t] = bv[:, 0], rok[:, 0]
+        if p == L - 1:
+            slot = committed % n_slots
+            pool_K[:, slot], pool_V[:, slot] = open_K, open_V
+            summary[:, slot] = block_commit_mean(open_K, memory_bf16)
+            committed += 1
+    return out

@@ -1,14 +1,17 @@
 """Generate the golden vectors in tests/golden/*.npz from the reference's own code.
 
-Run in the build container only (it needs the read-only reference checkout):
+Run where a copy of the reference exists: its offline install under
+``baseline/_ref`` (found by default) or a source checkout named with
+``--reference <checkout root>`` or ``$GFST_REFERENCE_SRC``:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <checkout root>]
 
 The reference package cannot be imported as shipped (its __init__ pulls in
-modules that were left out of the public release), so this script registers
-namespace modules pointing into the reference's source tree, plus a stub for
-the missing sm120 runtime loader whose accelerated ops report "unavailable",
-which sends the reference down its own torch code paths.  Nothing is copied.
+modules that were left out of the public release), so
+``oracle.reference_import`` registers namespace modules pointing into the
+reference's tree, plus a stub for the missing sm120 runtime loader whose
+accelerated ops report "unavailable", which sends the reference down its own
+torch code paths.  Nothing is copied.
 
 Every fixture stores the inputs and the reference outputs.  The CPU tests pin
 the oracle against them; the GPU tests pin the kernels against the oracle.
@@ -28,45 +31,13 @@ OUT = Path(__file__).resolve().parent
 REPO = OUT.parents[1]
 
 
-def install_reference(root: Path):
-    src = root / "src" / "gfst_hmb_mpuc"
-    pkg = types.ModuleType("gfst_hmb_mpuc")
-    pkg.__path__ = [str(src)]
-    sys.modules["gfst_hmb_mpuc"] = pkg
-    for sub in ("diagnostics", "training"):
-        m = types.ModuleType(f"gfst_hmb_mpuc.{sub}")
-        m.__path__ = [str(src / sub)]
-        sys.modules[f"gfst_hmb_mpuc.{sub}"] = m
-    # runtime_backends: the public release lacks sm120.py; every accelerated op
-    # reports unavailable so callers take their native torch branch
-    rb = types.ModuleType("gfst_hmb_mpuc.runtime_backends")
-    rb.__path__ = [str(src / "runtime_backends")]
-    sm = types.ModuleType("gfst_hmb_mpuc.runtime_backends.sm120")
+def install_reference(pkg_dir: Path):
+    """Register the reference package found at ``pkg_dir`` with the
+    "unavailable" sm120 stub (oracle.reference_import)."""
+    sys.path.insert(0, str(REPO))
+    from oracle import reference_import
 
-    def _none(*args, **kwargs):
-        return None
-
-    def _false(*args, **kwargs):
-        return False
-
-    for name in ("exact_block_score", "exact_block_materialize", "gfst_block_commit", "gfst_heev",
-                 "gfst_reference_block_average", "gfst_reference_global_sketch", "gfst_local_qr",
-                 "gfst_global_sketch", "gfst_canonical_summary_from_eigpairs", "gfst_summary_from_sketch",
-                 "gfst_summary_from_sketch_batched", "load_sm120_extension", "load_mathdx_extension",
-                 "mathdx_extension_dependency_report", "mathdx_runtime_dependency_report", "mpuc_recurrent_scan",
-                 "segmented_logsumexp_occurrence", "segmented_max_by_group"):
-        setattr(sm, name, _none)
-    for name in ("exact_readout_score_available", "experimental_canonical_summary_enabled",
-                 "mathdx_extension_available", "mpuc_recurrent_scan_available", "segmented_reduction_available",
-                 "sm120_exact_math_kernels_available"):
-        setattr(sm, name, _false)
-    sys.modules["gfst_hmb_mpuc.runtime_backends.sm120"] = sm
-    for name in dir(sm):
-        if not name.startswith("_"):
-            setattr(rb, name, getattr(sm, name))
-    rb.sm120 = sm
-    sys.modules["gfst_hmb_mpuc.runtime_backends"] = rb
-    return importlib
+    return reference_import.install(pkg_dir)
 
 
 def batched_qr_inputs(n, d, r, seed):
@@ -78,9 +49,16 @@ def batched_qr_inputs(n, d, r, seed):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=None,
+                        help="root of a reference source checkout (default: baseline/_ref or $GFST_REFERENCE_SRC)")
     args = parser.parse_args()
-    install_reference(Path(args.reference))
+    sys.path.insert(0, str(REPO))
+    from oracle import reference_import
+
+    pkg_dir = (Path(args.reference) / "src" / "gfst_hmb_mpuc") if args.reference else reference_import.find_reference()
+    if pkg_dir is None or not (pkg_dir / "gfst.py").is_file():
+        raise SystemExit("no copy of the reference: pass --reference <checkout root> or install it under baseline/_ref")
+    install_reference(pkg_dir)
     gfst = importlib.import_module("gfst_hmb_mpuc.gfst")
     retrieval = importlib.import_module("gfst_hmb_mpuc.retrieval")
     hh = importlib.import_module("gfst_hmb_mpuc.diagnostics.temp_local_qr_householder_vs_mgs_dataset")
@@ -438,6 +416,27 @@ def make_centroid_fixture(modeling, state_mod) -> None:
                 out[f"q{ci}_{key}"] = diag[key].numpy()
             out[f"q{ci}_confidence"] = np.float32(diag["confidence"])
     np.savez(OUT / "centroid_path.npz", **out)
+
+    # 13. the exact store's open block as the readout sees it: after each
+    #     append_exact_token (state.py:651-815), the current block id and its
+    #     prefix length (current_exact_block_id / current_exact_block_length,
+    #     state.py:817-825), which modeling.py:2948-2963 appends to the
+    #     retrieved blocks, and how many blocks the store has completed
+    st_mod = importlib.import_module("gfst_hmb_mpuc.state")
+    store_out = {}
+    for L_open in (16, 64):
+        state = st_mod.GfstDecodeState(num_layers=1, batch_size=1)
+        ids, prefixes, completed = [], [], []
+        for t in range(3 * L_open + 5):
+            state.append_exact_token(batch_idx=0, absolute_position=t, token_id=1000 + t, block_len=L_open)
+            bid = state.current_exact_block_id(0, L_open)
+            ids.append(-1 if bid is None else int(bid))
+            prefixes.append(int(state.current_exact_block_length(0)))
+            completed.append(len(state.samples[0].exact_store.completed_blocks))
+        store_out[f"L{L_open}_block_id"] = np.array(ids, np.int32)
+        store_out[f"L{L_open}_prefix"] = np.array(prefixes, np.int32)
+        store_out[f"L{L_open}_completed"] = np.array(completed, np.int32)
+    np.savez(OUT / "exact_store_open_block.npz", **store_out)
 
 
 if __name__ == "__main__":

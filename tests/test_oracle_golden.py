@@ -235,3 +235,50 @@ def test_centroid_candidates_match_reference():
                     "selection_margin", "selected_cells_per_head"):
             assert np.array_equal(diag[key], z[f"q{ci}_{key}"]), key
         assert np.float32(diag["confidence"]) == z[f"q{ci}_confidence"]
+
+
+def test_open_block_rule_matches_reference_exact_store():
+    """The open-block prefix a query sees is what the reference's own exact
+    store reports after the token's append (current_exact_block_length,
+    state.py:817-825): p + 1 while p < L - 1, none at the block's last token."""
+    z = load("exact_store_open_block.npz")
+    for L in (16, 64):
+        prefix = z[f"L{L}_prefix"]
+        T = prefix.shape[0]
+        rule = np.array([go.streaming_open_len(L, L)[t % L] for t in range(T)])
+        assert np.array_equal(rule, prefix)
+        # the block id is the current block while it is open, and blocks are
+        # completed at their last token (before that token's retrieval)
+        t = np.arange(T)
+        assert np.array_equal(z[f"L{L}_block_id"], np.where(prefix > 0, t // L, -1))
+        assert np.array_equal(z[f"L{L}_completed"], (t + 1) // L)
+
+
+def test_streaming_pass_composition():
+    """The token-by-token oracle step: its frames are the per-token stream, its
+    memory is the committed blocks with mean-key summaries, and a query sees the
+    committed blocks plus its open prefix."""
+    g = torch.Generator().manual_seed(3)
+    S, T, d, r, m, L, n_slots, k = 2, 48, 16, 4, 1, 8, 3, 2
+    U0 = go.qr_reference(torch.randn((S, d, r), generator=g).numpy(), sign_mode=go.SIGN_R_DIAG_POSITIVE)
+    A = (torch.randn((S, T, d, m), generator=g) / 4).numpy()
+    B = (torch.randn((S, T, r, m), generator=g) / 4).numpy()
+    K, V, Q = (torch.randn((S, T, d), generator=g).numpy() for _ in range(3))
+    out = go.streaming_pass(U0, A, B, K, V, Q, block_len=L, n_slots=n_slots, k=k, memory_bf16=False)
+    Uf, _ = go.stream_frames(U0, A, B, 1.0, 1e-8, go.SIGN_R_DIAG_POSITIVE)
+    assert np.array_equal(out["frames"][:, -1], Uf)
+    # first block: no committed memory, the open prefix only
+    assert (out["top_idx"][:, :L] == -1).all()
+    for p in range(L - 1):
+        keys = K[:, :p + 1]
+        best = np.argmax(np.einsum("spd,sd->sp", keys.astype(np.float64), Q[:, p].astype(np.float64)), axis=1)
+        ok = out["read_ok"][:, p]
+        assert np.array_equal(out["best_tok"][ok, p], (n_slots * L + best)[ok])
+    assert (out["best_tok"][:, L - 1] == -1).all()  # closed block, nothing committed yet
+    # tokens of block 4 (blocks 0..3 committed, slot of block 3 = 0 after the wrap)
+    t = 4 * L + 2
+    summ = np.stack([go.block_commit_mean(K[:, b * L:(b + 1) * L], False) for b in (3, 1, 2)], axis=1)
+    _, ref_i, ok = go.block_topk(Q[:, t:t + 1], summ, k)
+    ok = ok[:, 0]
+    slot_of = np.array([0, 1, 2])  # summ columns are slots 0, 1, 2
+    assert np.array_equal(out["top_idx"][ok, t], slot_of[ref_i[ok, 0]])
