@@ -554,8 +554,11 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
                 e[2].record()
                 times.insert(0, e)
             return tok, top_i
-        tok, _, _, top_i, _ = sharding.sharded_readout(Q, summary, pool_K, pool_V, k, shard)
+        tok, _, _, top_i, _ = sharding.sharded_readout(Q, summary, pool_K, pool_V, k, shard,
+                                                       value_layout="stream_shard", timings=phase)
         return tok, top_i
+
+    phase = None
 
     for _ in range(warmup):
         one_pass()
@@ -573,6 +576,13 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
     _native.check_device_errors()
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, device)
     hit = float((tok == needle).float().mean().item())
+    phase_ms = None
+    if world > 1:  # per-phase times of the exchange, from a separate pass
+        phase = {}
+        for _ in range(2):
+            one_pass()
+        phase_ms = {name: max_over_ranks(v / 2, device) for name, v in sorted(phase.items())}
+        phase = None
     res = None
     if rank == 0:
         res = {"workload": "long_memory: 8 batch x 32 heads = 256 streams, 1,048,576-token memory per stream "
@@ -585,6 +595,9 @@ def run_long_memory(rank: int, world: int, device, steps: int = 3, warmup: int =
                "needle_recall_note": "share of queries whose winning token is the needle; the mean-of-keys block "
                                      "summary puts the needle's block in the top-8 for about 2% of queries at L=128",
                "steps": steps, "warmup": warmup}
+        if phase_ms:
+            res["phase_ms_max_over_ranks"] = {k2: round(v, 4) for k2, v in phase_ms.items()}
+            res["value_layout"] = "stream_shard (each rank receives the winners' value rows of its own streams)"
         if world == 1:
             tk = statistics.mean(e[0].elapsed_time(e[1]) for e in times)
             ro = statistics.mean(e[1].elapsed_time(e[2]) for e in times)

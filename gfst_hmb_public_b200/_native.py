@@ -94,6 +94,11 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_int64, _c_int,
         _c_void_p, _c_void_p, _c_void_p, _c_void_p,
     ],
+    "gfst_exact_topk_workspace_bytes": [_c_int64, _c_int],
+    "gfst_exact_topk": [
+        _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+        ctypes.c_size_t, _c_void_p,
+    ],
     "gfst_segmented_max": [_c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p],
     "gfst_segmented_logsumexp_occurrence": [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p, _c_void_p,
@@ -107,6 +112,7 @@ _SIGNATURES: dict[str, list] = {
     ],
 }
 _RESTYPES = {
+    "gfst_exact_topk_workspace_bytes": ctypes.c_size_t,
     "gfst_status_string": ctypes.c_char_p,
     "gfst_last_error": ctypes.c_char_p,
 }

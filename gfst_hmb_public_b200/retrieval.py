@@ -103,20 +103,41 @@ class BlockRetriever:
 
     @staticmethod
     def exact_topk(keys_tensor: torch.Tensor, query_tensor: torch.Tensor, top_k: int):
-        """retrieval.py:165-172: scores = keys @ q (row 0 of a 2-D query), top-k."""
-        nat.require_cuda(keys_tensor, query_tensor, what="exact_topk")
-        q = query_tensor if query_tensor.ndim == 1 else query_tensor[0]
-        count = int(keys_tensor.shape[0])
-        k = min(int(top_k), count)
-        if k <= 0:
-            return (torch.empty(0, device=q.device, dtype=torch.long),
-                    torch.empty(0, device=q.device, dtype=torch.float32))
-        if k > 32:
-            raise RuntimeError(f"exact_topk selects at most 32 blocks per query (got top_k={top_k})")
-        dtype = keys_tensor.dtype if keys_tensor.dtype in (torch.float32, torch.bfloat16) else torch.float32
-        keys = keys_tensor.to(dtype).contiguous().unsqueeze(0)
-        scores, idx = block_topk(q.to(dtype).reshape(1, 1, -1), keys, k)
-        return idx.reshape(-1).to(torch.long), scores.reshape(-1)
+        """retrieval.py:165-172: scores = keys @ q (row 0 of a 2-D query), the
+        best min(top_k, count) of them, as (indices int64, scores float32).
+        bfloat16 keys score as the reference's bf16 matmul returns them (the
+        fp32 sum rounded to bf16); equal scores rank the lower index first.
+        Keys of other dtypes are scored in float32."""
+        return exact_topk(keys_tensor, query_tensor, top_k)
+
+
+def exact_topk(keys_tensor: torch.Tensor, query_tensor: torch.Tensor, top_k: int):
+    """One query against a bank of keys, any top_k (gfst_exact_topk); see
+    BlockRetriever.exact_topk."""
+    nat.require_cuda(keys_tensor, query_tensor, what="exact_topk")
+    if keys_tensor.ndim != 2:
+        raise ValueError(f"exact_topk expects keys [count, d], got {tuple(keys_tensor.shape)}")
+    q = query_tensor if query_tensor.ndim == 1 else query_tensor[0]
+    if q.numel() != keys_tensor.shape[1]:
+        raise ValueError(f"exact_topk: query of {q.numel()} values for keys of width {keys_tensor.shape[1]}")
+    count = int(keys_tensor.shape[0])
+    k = min(int(top_k), count)
+    if k <= 0:
+        return (torch.empty(0, device=q.device, dtype=torch.long),
+                torch.empty(0, device=q.device, dtype=torch.float32))
+    dtype = keys_tensor.dtype if keys_tensor.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    keys = keys_tensor.to(dtype).contiguous()
+    q = q.to(dtype).contiguous()
+    lib = nat.load()
+    ws_bytes = int(lib.gfst_exact_topk_workspace_bytes(count, k))
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=q.device) if ws_bytes else None
+    scores = torch.empty((k,), dtype=torch.float32, device=q.device)
+    idx = torch.empty((k,), dtype=torch.int64, device=q.device)
+    with torch.cuda.device(q.device):
+        nat.call("gfst_exact_topk", nat.ptr(keys), nat.ptr(q), count, int(keys.shape[1]), k,
+                 nat.dtype_code(dtype, "exact_topk"), 1, nat.ptr(scores), nat.ptr(idx), nat.ptr(ws), ws_bytes,
+                 nat.stream_of(q))
+    return idx, scores
 
 
 # the reference's class name, for drop-in imports

@@ -34,6 +34,7 @@ from dataclasses import dataclass
 
 import torch
 
+from . import _native as nat
 from . import gfst, memory, readout, retrieval
 
 
@@ -56,10 +57,14 @@ class StreamingStep:
 
     def __init__(self, n_streams: int, *, d: int, r: int, block_len: int, n_slots: int, k: int,
                  dtype: torch.dtype = torch.bfloat16, device="cuda", sign_mode="r_diag_positive",
-                 eps_sign: float = 1e-8):
+                 eps_sign: float = 1e-8, check_errors: bool = False):
+        """check_errors: after every step, wait for it and raise RuntimeError if
+        a kernel recorded a device-side failure (a bounded wait that gave up);
+        a debugging aid -- it makes every step synchronous."""
         self.n_streams, self.d, self.r, self.block_len, self.n_slots, self.k = n_streams, d, r, block_len, n_slots, k
         self.sign_mode = sign_mode
         self.eps_sign = eps_sign
+        self.check_errors = check_errors
         self.device = torch.device(device)
         self.U = torch.zeros((n_streams, d, r), dtype=torch.float32, device=self.device)
         self.memory = memory.BlockMemory(n_streams, n_slots, block_len, d, d, dtype=dtype, device=self.device)
@@ -107,6 +112,8 @@ class StreamingStep:
         # tensors produced on side streams are consumed on the current stream
         for t in (best_tok, best_score, value, top_i, self.U):
             t.record_stream(cur)
+        if self.check_errors:
+            nat.check_device_errors()
         result = StepOutputs(best_tok, best_score, value, top_i, self.open_base, slot)
         if out is not None:
             out.best_tok.copy_(best_tok)
@@ -172,3 +179,9 @@ class HostPipeline:
                 for t in (out.best_tok, out.best_score, out.value):
                     t.record_stream(self.download)
         cur.wait_stream(self.download)
+
+    def drain(self) -> None:
+        """Wait for every enqueued step and its copies; raise RuntimeError if a
+        kernel recorded a device-side failure (its results are then invalid)."""
+        torch.cuda.synchronize(self.step_obj.device)
+        nat.check_device_errors()

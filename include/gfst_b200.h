@@ -39,6 +39,8 @@
  *                             modeling.py:1151-1169 (duplicate token ids collapsed)
  *   gfst_block_topk        <- FaissGpuRetriever.search / exact_topk
  *                             src/gfst_hmb_mpuc/retrieval.py:136-172
+ *   gfst_exact_topk        <- FaissGpuRetriever.exact_topk (one query, any k)
+ *                             src/gfst_hmb_mpuc/retrieval.py:165-172
  *   gfst_exact_readout     <- ExactRecallReadout._score_block_tokens + top-1 select
  *                             src/gfst_hmb_mpuc/modeling.py:599-657, 1151-1169
  *   gfst_open_block_readout <- the current (open) block appended to the retrieved blocks
@@ -352,6 +354,24 @@ GFST_API int gfst_centroid_readout(const float* Q, const float* query_heads, con
 GFST_API int gfst_block_topk(const void* Q, const void* Ksum, int64_t n_streams, int n_queries,
                     int n_blocks, int n_blocks_stride, int d, int k, int dtype,
                     float* top_scores, int32_t* top_idx, cudaStream_t stream);
+
+/* ---- exact top-k of one query, any k -----------------------------------------
+ * scores[i] = keys[i,:] . query (fp32 accumulate; with dtype GFST_BF16 and
+ * round_scores != 0 each score is rounded to bf16, as the reference's bf16
+ * `keys @ q` returns it); out_scores[0..k) / out_idx[0..k) = the k best in the
+ * total order (score descending, index ascending; NaN ranks last, -0 == +0).
+ * keys: [count, d] (16-byte aligned), query: [d], same dtype (GFST_F32 or
+ * GFST_BF16).  Replaces FaissGpuRetriever.exact_topk
+ * src/gfst_hmb_mpuc/retrieval.py:165-172 (torch.topk over keys @ q), which is
+ * also the oracle the reference's tests compare FAISS search against.
+ * Banks of more than 16,384 keys need a caller-provided workspace of
+ * gfst_exact_topk_workspace_bytes(count, k) bytes (8-byte aligned; 0 bytes
+ * below that size) and k <= 8192.  Limits: 1 <= k <= count < 2^32, d <= 1024,
+ * d a multiple of 4 (fp32) or 8 (bf16).                                     */
+GFST_API size_t gfst_exact_topk_workspace_bytes(int64_t count, int k);
+GFST_API int gfst_exact_topk(const void* keys, const void* query, int64_t count, int d, int k, int dtype,
+                    int round_scores, float* out_scores, int64_t* out_idx, void* workspace,
+                    size_t workspace_bytes, cudaStream_t stream);
 
 /* ---- candidate merge ----------------------------------------------------------
  * For every row: the k best of the row's n_cand (score, index) candidates in the

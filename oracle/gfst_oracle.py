@@ -531,6 +531,45 @@ def block_topk(Q: np.ndarray, Ksum: np.ndarray, k: int):
     return top_sc, top_idx, margin_ok
 
 
+def exact_topk(keys: np.ndarray, query: np.ndarray, k: int, round_bf16: bool = False):
+    """retrieval.py:165-172 (FaissGpuRetriever.exact_topk): scores = keys @ q,
+    the best min(k, count) as (indices int64, scores float32), in the total
+    order (score desc, index asc; NaN last).  round_bf16: the scores of a bf16
+    bank, which the reference's bf16 matmul returns rounded to bf16 (here the
+    float64 dot rounded to float32, then to bf16)."""
+    sc = np.asarray(keys, np.float64) @ np.asarray(query, np.float64)
+    sc = sc.astype(np.float32)
+    if round_bf16:
+        sc = to_bf16_f32(sc)
+    key = np.where(np.isnan(sc), -np.inf, sc).astype(np.float64)
+    nan_last = np.isnan(sc).astype(np.int8)
+    idx = np.arange(sc.shape[0])
+    order = np.lexsort((idx, -key, nan_last))
+    kk = min(int(k), sc.shape[0])
+    return order[:kk].astype(np.int64), sc[order[:kk]]
+
+
+def same_topk_up_to_ties(idx_a, sc_a, idx_b, sc_b, all_scores) -> bool:
+    """Two top-k answers agree when their score lists are equal and, for every
+    score value, the same keys were chosen -- except at the k-th score, where
+    any keys of that score are a valid completion (the reference's torch.topk
+    orders equal scores arbitrarily)."""
+    sc_a, sc_b = np.asarray(sc_a, np.float32), np.asarray(sc_b, np.float32)
+    if sc_a.shape != sc_b.shape or not np.array_equal(sc_a, sc_b, equal_nan=True):
+        return False
+    if sc_a.size == 0:
+        return True
+    kth = sc_a[-1]
+    inner = sc_a != kth
+    if set(np.asarray(idx_a)[inner].tolist()) != set(np.asarray(idx_b)[inner].tolist()):
+        return False
+    all_scores = np.asarray(all_scores, np.float32)
+    for ia, ib in zip(np.asarray(idx_a)[~inner], np.asarray(idx_b)[~inner]):
+        if all_scores[int(ia)] != kth or all_scores[int(ib)] != kth:
+            return False
+    return True
+
+
 # ---------------------------------------------------------------------------
 # exact-token readout
 # ---------------------------------------------------------------------------

@@ -309,6 +309,7 @@ def main() -> None:
     out["n_cases"] = np.array(len(cases))
     np.savez(OUT / "block_commit_eig_cases.npz", **out)
     make_centroid_fixture(modeling, state_mod)
+    make_store_and_topk_fixtures()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
@@ -417,6 +418,11 @@ def make_centroid_fixture(modeling, state_mod) -> None:
             out[f"q{ci}_confidence"] = np.float32(diag["confidence"])
     np.savez(OUT / "centroid_path.npz", **out)
 
+
+
+def make_store_and_topk_fixtures() -> None:
+    """The exact store's open block and exact_topk on bf16 banks."""
+    retrieval = importlib.import_module("gfst_hmb_mpuc.retrieval")
     # 13. the exact store's open block as the readout sees it: after each
     #     append_exact_token (state.py:651-815), the current block id and its
     #     prefix length (current_exact_block_id / current_exact_block_length,
@@ -437,6 +443,24 @@ def make_centroid_fixture(modeling, state_mod) -> None:
         store_out[f"L{L_open}_prefix"] = np.array(prefixes, np.int32)
         store_out[f"L{L_open}_completed"] = np.array(completed, np.int32)
     np.savez(OUT / "exact_store_open_block.npz", **store_out)
+
+    # 14. exact_topk (retrieval.py:165-172) on bf16 banks: the reference ranks
+    #     the bf16 result of keys @ q, so equal scores are common; and any k
+    g = torch.Generator().manual_seed(14)
+    topk_out = {}
+    for ci, (count, d, k) in enumerate(((300, 64, 50), (4000, 64, 40), (17000, 32, 64), (77, 32, 77))):
+        # multiples of 1/8 in [-2, 2): every partial sum is exact in float32,
+        # so the bf16 rounding of a score does not depend on the summation order
+        keys = (torch.randint(-16, 16, (count, d), generator=g) / 8.0).to(torch.bfloat16)
+        q = (torch.randint(-16, 16, (d,), generator=g) / 8.0).to(torch.bfloat16)
+        idx, sc = retrieval.FaissGpuRetriever.exact_topk(keys, q, k)
+        topk_out[f"c{ci}_keys"] = keys.view(torch.int16).numpy()
+        topk_out[f"c{ci}_query"] = q.view(torch.int16).numpy()
+        topk_out[f"c{ci}_k"] = np.array(k)
+        topk_out[f"c{ci}_idx"] = idx.numpy()
+        topk_out[f"c{ci}_scores"] = sc.numpy()
+        topk_out[f"c{ci}_all_scores"] = (keys @ q).float().numpy()
+    np.savez(OUT / "retrieval_exact_topk_bf16.npz", **topk_out)
 
 
 if __name__ == "__main__":

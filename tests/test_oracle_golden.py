@@ -282,3 +282,20 @@ def test_streaming_pass_composition():
     ok = ok[:, 0]
     slot_of = np.array([0, 1, 2])  # summ columns are slots 0, 1, 2
     assert np.array_equal(out["top_idx"][ok, t], slot_of[ref_i[ok, 0]])
+
+
+def test_exact_topk_bf16_matches_reference():
+    """exact_topk on bf16 banks (the reference ranks the bf16 result of
+    keys @ q): the oracle's rounded scores equal the reference's, and the
+    chosen keys agree up to the order of equal scores."""
+    z = load("retrieval_exact_topk_bf16.npz")
+    for c in range(4):
+        keys = torch.from_numpy(z[f"c{c}_keys"]).view(torch.bfloat16).float().numpy()
+        q = torch.from_numpy(z[f"c{c}_query"]).view(torch.bfloat16).float().numpy()
+        k = int(z[f"c{c}_k"])
+        idx, sc = go.exact_topk(keys, q, k, round_bf16=True)
+        assert go.same_topk_up_to_ties(idx, sc, z[f"c{c}_idx"], z[f"c{c}_scores"], z[f"c{c}_all_scores"])
+        # ties are resolved toward the lower index
+        for j in range(1, k):
+            if sc[j] == sc[j - 1]:
+                assert idx[j] > idx[j - 1]

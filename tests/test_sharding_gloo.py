@@ -27,10 +27,11 @@ class OracleOps:
     """The oracle in place of the kernels (CPU tensors in and out)."""
 
     @staticmethod
-    def block_topk(Q, Ksum, k):
+    def block_topk(Q, Ksum, k, n_blocks=None):
         from oracle import gfst_oracle as go
 
-        s, i, _ = go.block_topk(Q.numpy(), Ksum.numpy(), k)
+        nb = Ksum.shape[1] if n_blocks is None else n_blocks
+        s, i, _ = go.block_topk(Q.numpy(), Ksum[:, :nb].numpy(), k)
         return torch.from_numpy(s), torch.from_numpy(i)
 
     @staticmethod
@@ -62,7 +63,7 @@ def _free_port():
 
 def _data():
     g = torch.Generator().manual_seed(5)
-    S, NB, L, d, Nq, k = 2, 12, 8, 16, 6, 3
+    S, NB, L, d, Nq, k = 3, 12, 8, 16, 6, 3
     pool = torch.randn((S, NB, L, d), generator=g)
     vals = torch.randn((S, NB, L, d), generator=g)
     Q = torch.randn((S, Nq, d), generator=g)
@@ -70,31 +71,61 @@ def _data():
     return pool, vals, Q, summary, k
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, n_committed, layout):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         pool, vals, Q, summary, k = _data()
+        if n_committed is not None:  # slots past the committed blocks hold nothing (zeros)
+            pool[:, n_committed:] = 0
+            vals[:, n_committed:] = 0
+            summary[:, n_committed:] = 0
         shard = sharding.BlockRange(rank, world, pool.shape[1])
         sl = slice(shard.lo, shard.hi)
+        n_valid = None if n_committed is None else max(0, min(n_committed, shard.hi) - shard.lo)
         res = sharding.sharded_readout(Q, summary[:, sl].contiguous(), pool[:, sl].contiguous(),
-                                       vals[:, sl].contiguous(), k, shard, ops=OracleOps)
+                                       vals[:, sl].contiguous(), k, shard, ops=OracleOps, n_valid=n_valid,
+                                       value_layout=layout)
         torch.save([t for t in res], f"{out_path}.{rank}")
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_block_range_sharded_readout_equals_unsharded(tmp_path, world):
+@pytest.mark.parametrize("world,n_committed,layout", [(2, None, "replicated"), (2, None, "stream_shard"),
+                                                      (2, 7, "replicated"), (3, 5, "stream_shard")])
+def test_block_range_sharded_readout_equals_unsharded(tmp_path, world, n_committed, layout):
     out = str(tmp_path / "res")
-    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), out, n_committed, layout), nprocs=world,
+                       start_method="spawn")
     pool, vals, Q, summary, k = _data()
-    ref_ts, ref_ti = OracleOps.block_topk(Q, summary, k)
+    nb = pool.shape[1] if n_committed is None else n_committed
+    ref_ts, ref_ti = OracleOps.block_topk(Q, summary, k, n_blocks=nb)
     ref_t, ref_s, ref_v = OracleOps.exact_readout(Q, pool, vals, ref_ti)
+    S = Q.shape[0]
     for r in range(world):
         best_t, best_s, value, top_i, top_s = torch.load(f"{out}.{r}")
         assert torch.equal(top_i.to(torch.int32), ref_ti.to(torch.int32))
         assert torch.equal(best_t.to(torch.int32), ref_t.to(torch.int32))
         assert torch.allclose(best_s, ref_s)
-        assert torch.equal(value, ref_v)
+        if layout == "replicated":
+            assert torch.equal(value, ref_v)
+        else:
+            lo, hi = sharding.stream_shard(S, r, world)
+            assert torch.equal(value, ref_v[lo:hi])
+
+
+def test_owner_of_matches_block_ranges():
+    for n_blocks in (1, 5, 12, 8192, 8195):
+        for world in (1, 2, 3, 8):
+            L = 4
+            tok = torch.arange(-1, n_blocks * L)
+            own = sharding._owner_of(tok, L, n_blocks, world)
+            assert own[0] == -1
+            for r in range(world):
+                br = sharding.BlockRange(r, world, n_blocks)
+                sel = own[1:] == r
+                blocks = torch.unique(tok[1:][sel] // L)
+                assert blocks.numel() == br.size
+                if br.size:
+                    assert int(blocks.min()) == br.lo and int(blocks.max()) == br.hi - 1
