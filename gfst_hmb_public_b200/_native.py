@@ -99,6 +99,9 @@ _SIGNATURES: dict[str, list] = {
         _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
         ctypes.c_size_t, _c_void_p,
     ],
+    "gfst_exact_topk_noalloc": [
+        _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+    ],
     "gfst_segmented_max": [_c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p],
     "gfst_segmented_logsumexp_occurrence": [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int64, _c_void_p, _c_void_p, _c_void_p,

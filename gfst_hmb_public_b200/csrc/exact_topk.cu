@@ -16,7 +16,14 @@
 // scores and keeps its best min(k, kTile) keys in a workspace buffer; merge
 // passes sort tiles of those candidates until one tile remains (k <= kTile/2,
 // so every pass shrinks the candidate count by at least half).
+#include <mutex>
+
 #include "gfst_common.cuh"
+
+// Scratch of gfst_exact_topk_noalloc: the tournament's two candidate buffers
+// for banks of more than one tile, 1 MiB, shared by every call on a device.
+constexpr long long kNoAllocScratchKeys = 131072;
+static __device__ __align__(256) unsigned long long g_exact_topk_scratch[kNoAllocScratchKeys];
 
 namespace gfst {
 namespace {
@@ -238,4 +245,50 @@ extern "C" int gfst_exact_topk(const void* keys, const void* query, int64_t coun
   }
   set_last_error("unsupported dtype %d", dtype);
   return GFST_ERR_DTYPE;
+}
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (cudaGetSymbolAddress with that device current) and cached.
+int scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+  GFST_REQUIRE(dev >= 0 && dev < kMaxDevices, GFST_ERR_DEVICE, "device ordinal %d above %d", dev, kMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_address[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_exact_topk_scratch);
+    GFST_REQUIRE(e == cudaSuccess && p != nullptr, GFST_ERR_DEVICE, "cudaGetSymbolAddress of the top-k scratch: %s",
+                 cudaGetErrorString(e));
+    g_scratch_address[dev] = p;
+  }
+  *out = g_scratch_address[dev];
+  return GFST_OK;
+}
+
+}  // namespace
+
+extern "C" int gfst_exact_topk_noalloc(const void* keys, const void* query, int64_t count, int d, int k, int dtype,
+                                       int round_scores, float* out_scores, int64_t* out_idx, cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(count >= 1 && k >= 1 && k <= count, GFST_ERR_ARG, "need 1 <= k <= count (count=%lld k=%d)",
+               (long long)count, k);
+  const size_t need = gfst_exact_topk_workspace_bytes(count, k);
+  const size_t have = (size_t)kNoAllocScratchKeys * sizeof(unsigned long long);
+  GFST_REQUIRE(need <= have, GFST_ERR_SHAPE,
+               "count=%lld with k=%d needs %zu bytes of scratch, above the %zu-byte static scratch of "
+               "gfst_exact_topk_noalloc (2 * ceil(count / 16384) * k must be <= %lld); use gfst_exact_topk with a "
+               "caller-provided workspace", (long long)count, k, need, have, kNoAllocScratchKeys);
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int st = scratch_address(&scratch);
+    if (st != GFST_OK) return st;
+  }
+  return gfst_exact_topk(keys, query, count, d, k, dtype, round_scores, out_scores, out_idx, scratch, need, stream);
 }

@@ -373,6 +373,26 @@ GFST_API int gfst_exact_topk(const void* keys, const void* query, int64_t count,
                     int round_scores, float* out_scores, int64_t* out_idx, void* workspace,
                     size_t workspace_bytes, cudaStream_t stream);
 
+/* ---- exact top-k without allocation -------------------------------------------
+ * No counterpart in the reference.  gfst_exact_topk with its workspace taken
+ * from a static 1 MiB device array instead of the caller: for callers that
+ * cannot allocate device memory per call -- a host whose device memory is
+ * reserved up front by its own pool allocator (a raw cudaMalloc would go
+ * around that pool and fails once the pool holds the free memory), or a
+ * latency-bound loop that cannot take the device-wide synchronisation that
+ * cudaFree implies.  The caller still passes keys, query and outputs.
+ * Limit: 2 * ceil(count / 16384) * k <= 131072 (the workspace of
+ * gfst_exact_topk must fit in 1 MiB); larger requests return GFST_ERR_SHAPE.
+ * Every device that loads the library holds the 1 MiB until the process
+ * exits.  The first call on a device looks up the array's device address
+ * (once per device); make that first call before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race (serialise
+ * them on one stream); nothing in it has to start at zero, since every pass
+ * writes the candidates the next one reads.  Same results as gfst_exact_topk. */
+GFST_API int gfst_exact_topk_noalloc(const void* keys, const void* query, int64_t count, int d, int k,
+                            int dtype, int round_scores, float* out_scores, int64_t* out_idx,
+                            cudaStream_t stream);
+
 /* ---- candidate merge ----------------------------------------------------------
  * For every row: the k best of the row's n_cand (score, index) candidates in the
  * total order (score descending, index ascending); candidates with index < 0,
