@@ -7,6 +7,7 @@ Each case builds seeded inputs on cuda:0, launches its kernel ``repeat`` times
 the last launch.  CASE is one of:
 
   frames      streaming pass of 64 tokens, 128x32 frames, rank-4 updates
+  frames_mid  streaming pass of 64 tokens, 128x16 frames, rank-2 updates (default 256 streams)
   batched_qr  one update+QR launch over 65,536 frames of 64x8
   topk        tensor-core score + top-16 of 64 queries over 512 summaries per stream
   topk_long   tensor-core score + top-8 of 1024 queries over 8192 summaries per stream
@@ -51,25 +52,26 @@ def _timed(fn, repeat: int, batch: int = 1) -> float:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("case", choices=["frames", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
+    parser.add_argument("case", choices=["frames", "frames_mid", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
                                          "readout_long", "commit_eig", "block_tracker", "centroid_commit",
                                          "centroid_readout", "segmented", "block_score", "heev"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     parser.add_argument("--batch", type=int, default=1, help="calls per timed round (segmented, block_score)")
-    parser.add_argument("--qr-method", default="auto", choices=["auto", "householder", "cholesky2"],
-                        help="QR of the frames case")
+    parser.add_argument("--qr-method", default="auto", choices=["auto", "householder", "cholesky2", "cholesky2_split"],
+                        help="QR of the frames cases")
     args = parser.parse_args()
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
     g.manual_seed(20261201)
     bf = torch.bfloat16
 
-    if args.case == "frames":
-        S = args.streams or 2048
-        U = gfst.frame_update_qr(torch.randn((S, 128, 32), generator=g, device=dev), sign_mode="r_diag_positive")
-        A = torch.randn((S, 64, 128, 4), generator=g, device=dev) / math.sqrt(128)
-        B = torch.randn((S, 64, 32, 4), generator=g, device=dev) / math.sqrt(128)
+    if args.case in ("frames", "frames_mid"):
+        S = args.streams or (2048 if args.case == "frames" else 256)
+        r, m = (32, 4) if args.case == "frames" else (16, 2)
+        U = gfst.frame_update_qr(torch.randn((S, 128, r), generator=g, device=dev), sign_mode="r_diag_positive")
+        A = torch.randn((S, 64, 128, m), generator=g, device=dev) / math.sqrt(128)
+        B = torch.randn((S, 64, r, m), generator=g, device=dev) / math.sqrt(128)
         ms = _timed(lambda: gfst.stream_frames(U, A, B, sign_mode="r_diag_positive", qr_method=args.qr_method),
                     args.repeat)
         units = f"{S * 64 / ms / 1e3:.2f} M frame-tokens/s"

@@ -69,7 +69,8 @@ extern "C" int gfst_frame_stream_ex(float* U, const float* A, const float* B, fl
   using namespace gfst;
   int st = check_frame_args(n_frames, d, r, m, sign_mode);
   if (st != GFST_OK) return st;
-  GFST_REQUIRE(qr_method == GFST_QR_AUTO || qr_method == GFST_QR_HOUSEHOLDER || qr_method == GFST_QR_CHOLESKY2,
+  GFST_REQUIRE(qr_method == GFST_QR_AUTO || qr_method == GFST_QR_HOUSEHOLDER || qr_method == GFST_QR_CHOLESKY2 ||
+                   qr_method == GFST_QR_CHOLESKY2_SPLIT,
                GFST_ERR_ARG, "unknown qr_method %d", qr_method);
   GFST_REQUIRE(T >= 0, GFST_ERR_ARG, "T must be >= 0 (got %d)", T);
   GFST_REQUIRE(m >= 1, GFST_ERR_SHAPE, "streaming needs an update rank m >= 1");

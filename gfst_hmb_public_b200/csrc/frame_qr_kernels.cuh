@@ -9,6 +9,7 @@
 //   src/gfst_hmb_mpuc/modeling.py:2299-2423  per-token largest-level tracker update
 #pragma once
 #include "frame_chol.cuh"
+#include "frame_chol_mw.cuh"
 #include "frame_qr.cuh"
 #include "frame_qr_launch.h"
 
@@ -185,6 +186,65 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
 }
 
 // ---------------------------------------------------------------------------
+// streaming with CholeskyQR2, one frame per CTA split over d/32 warps
+// (frame_chol_mw.cuh): for batches that leave most SMs idle with one frame
+// per warp.  Each warp stages its own 32 rows of A_t and all of B_t.
+// ---------------------------------------------------------------------------
+template <int DMAX, int RMAX>
+__global__ void __launch_bounds__(DMAX, 2)
+    frame_stream_chol_mw_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
+                                float beta, int64_t n_frames, int T, int d, int r, int m, float eps_sign,
+                                int sign_mode, float* __restrict__ frames_out, int out_every, bool vec4) {
+  using MW = FrameCholMW<DMAX, RMAX>;
+  extern __shared__ __align__(16) unsigned char mw_smem[];
+  typename MW::Smem& sm = *reinterpret_cast<typename MW::Smem*>(mw_smem);
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int row = 32 * w + lane;
+  const int64_t f = blockIdx.x;
+  const int a_rows = max(0, min(32, d - 32 * w));
+  const int a_elems = a_rows * m, b_elems = r * m;
+  const int stage_elems = 32 * m + b_elems;  // a multiple of 4 (r * m is, host-checked)
+  float* stage = reinterpret_cast<float*>(mw_smem + sizeof(typename MW::Smem)) + (size_t)w * 2 * stage_elems;
+  const size_t frame_elems = (size_t)d * r;
+  const float* Af = A + f * (size_t)T * d * m + (size_t)32 * w * m;
+  const float* Bf = B + f * (size_t)T * b_elems;
+
+  auto issue = [&](int tok) {
+    if (tok < T) {
+      float* dst = stage + (tok & 1) * stage_elems;
+      const float* srcA = Af + (size_t)tok * d * m;
+      const float* srcB = Bf + (size_t)tok * b_elems;
+      for (int c = lane; c < a_elems / 4; c += 32) cp_async16(dst + 4 * c, srcA + 4 * c);
+      for (int c = lane; c < b_elems / 4; c += 32) cp_async16(dst + 32 * m + 4 * c, srcB + 4 * c);
+    }
+    cp_async_commit();
+  };
+
+  float fr[RMAX];
+  MW::load(fr, U + f * frame_elems, row, d, r, vec4);
+  issue(0);
+  for (int tok = 0; tok < T; ++tok) {
+    issue(tok + 1);
+    cp_async_wait_all_but_one();
+    __syncwarp();
+    const float* sA = stage + (tok & 1) * stage_elems;
+    if (beta != 1.f) {
+#pragma unroll
+      for (int c = 0; c < RMAX; ++c) fr[c] *= beta;
+    }
+    if (row < d) MW::rank_update(fr, sA + lane * m, sA + 32 * m, r, m);
+    MW::qr(fr, sm, w, lane, eps_sign, sign_mode, r);
+    if (frames_out != nullptr && ((tok + 1) % out_every) == 0) {
+      const int64_t snap = (tok + 1) / out_every - 1;
+      MW::store(fr, frames_out + (snap * n_frames + f) * frame_elems, row, d, r, vec4);
+    }
+    __syncwarp();  // every lane is done with this stage buffer before it is refilled
+  }
+  MW::store(fr, U + f * frame_elems, row, d, r, vec4);
+}
+
+// ---------------------------------------------------------------------------
 // launchers (host)
 // ---------------------------------------------------------------------------
 
@@ -219,17 +279,44 @@ int launch_stream_chol(float* U, const float* A, const float* B, float beta, int
   return check_launch("frame_stream_chol_kernel");
 }
 
+template <int DMAX, int RMAX>
+int launch_stream_chol_mw(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r,
+                          int m, float eps_sign, int sign_mode, float* frames_out, int out_every,
+                          cudaStream_t stream) {
+  using MW = FrameCholMW<DMAX, RMAX>;
+  GFST_REQUIRE(n <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many frames: %lld", (long long)n);
+  const bool vec4 = (r % 4 == 0) && aligned16(U) && (frames_out == nullptr || aligned16(frames_out));
+  const size_t smem = sizeof(typename MW::Smem) + (size_t)MW::W * 2 * (size_t)(32 * m + r * m) * sizeof(float);
+  auto kern = frame_stream_chol_mw_kernel<DMAX, RMAX>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  kern<<<(unsigned)n, DMAX, smem, stream>>>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode, frames_out,
+                                            out_every, vec4);
+  return check_launch("frame_stream_chol_mw_kernel");
+}
+
+// Frames below which the automatic choice splits each frame over d/32 warps:
+// one frame per warp then leaves most SMs idle and runs each frame's
+// dependency chain on one warp.  Measured on B200, 64 tokens of 128 x 32
+// frames with rank-4 updates: 256 frames 0.74 ms split against 1.00 ms one
+// per warp, 512 frames 1.40 against 1.07 ms.
+constexpr int64_t kSplitFramesBelow = 384;
+
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
                   float eps_sign, int sign_mode, float* frames_out, int out_every, int qr_method,
                   cudaStream_t stream) {
   constexpr bool kChol = (DMAX == 64 || DMAX == 128) && (RMAX == 16 || RMAX == 32) && RG == 8 && CG == 4;
   if constexpr (kChol) {
+    const bool split = qr_method == GFST_QR_CHOLESKY2_SPLIT || (qr_method == GFST_QR_AUTO && n < kSplitFramesBelow);
+    if (split)
+      return launch_stream_chol_mw<DMAX, RMAX>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode, frames_out,
+                                               out_every, stream);
     if (qr_method != GFST_QR_HOUSEHOLDER)
       return launch_stream_chol<DMAX, RMAX>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode, frames_out,
                                             out_every, stream);
   } else {
-    GFST_REQUIRE(qr_method != GFST_QR_CHOLESKY2, GFST_ERR_SHAPE,
+    GFST_REQUIRE(qr_method != GFST_QR_CHOLESKY2 && qr_method != GFST_QR_CHOLESKY2_SPLIT, GFST_ERR_SHAPE,
                  "CholeskyQR2 streaming covers d in (32, 128] with 8 < r <= 32 (d=%d r=%d)", d, r);
   }
   constexpr int GPW = 32 / (RG * CG);

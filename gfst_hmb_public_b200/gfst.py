@@ -123,7 +123,7 @@ def gfst_local_qr(candidate_matrices: torch.Tensor, eps_sign: float) -> torch.Te
     return canonical_qr_batched(candidate_matrices, eps_sign=float(eps_sign))
 
 
-_QR_METHODS = {"auto": 0, "householder": 1, "cholesky2": 2}
+_QR_METHODS = {"auto": 0, "householder": 1, "cholesky2": 2, "cholesky2_split": 3}
 
 
 def stream_frames(
@@ -142,9 +142,12 @@ def stream_frames(
     U: [F, d, r] float32, updated in place.  A: [F, T, d, m]; B: [F, T, r, m].
     With ``out_every > 0`` the frames after tokens out_every-1, 2*out_every-1, ...
     are returned as [T // out_every, F, d, r]; otherwise returns None.
-    ``qr_method``: "auto" (CholeskyQR2 for 32 < d <= 128 and 8 < r <= 32,
-    Householder otherwise), "householder" or "cholesky2" (a frame whose Gram
-    pivots fail the conditioning test falls back to Householder for that token).
+    ``qr_method``: "auto" (CholeskyQR2 for 32 < d <= 128 and 8 < r <= 32 --
+    below 384 frames with each frame split over d/32 warps -- Householder
+    otherwise), "householder", "cholesky2" (one frame per warp) or
+    "cholesky2_split" (one frame per CTA of d/32 warps); with CholeskyQR2 a
+    frame whose Gram pivots fail the conditioning test falls back to
+    Householder for that token.
     """
     nat.require_cuda(U, A, B, what="stream_frames")
     if U.ndim != 3 or A.ndim != 4 or B.ndim != 4:

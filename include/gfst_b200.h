@@ -105,7 +105,8 @@ enum gfst_sign_mode {
 
 /* QR algorithm of the streaming frame pass (gfst_frame_stream_ex). */
 enum gfst_qr_method {
-  /* CholeskyQR2 for 32 < d <= 128 with 8 < r <= 32, Householder otherwise. */
+  /* CholeskyQR2 for 32 < d <= 128 with 8 < r <= 32 (split over warps below
+   * 384 frames), Householder otherwise. */
   GFST_QR_AUTO = 0,
   /* LAPACK-order Householder (geqrf/orgqr) for every token. */
   GFST_QR_HOUSEHOLDER = 1,
@@ -113,7 +114,11 @@ enum gfst_qr_method {
    * a frame whose pivot R_jj^2 falls below 1e-2 * G_jj (or is not finite)
    * takes the Householder path for that token.  Same Q as Householder with
    * R_jj > 0 to fp32 rounding; shapes outside the AUTO range are rejected. */
-  GFST_QR_CHOLESKY2 = 2
+  GFST_QR_CHOLESKY2 = 2,
+  /* GFST_QR_CHOLESKY2 with each frame split over d/32 warps (a CTA per frame):
+   * shorter per-token latency for batches too small to fill the GPU with one
+   * frame per warp.  AUTO takes it below 384 frames. */
+  GFST_QR_CHOLESKY2_SPLIT = 3
 };
 
 /* Element types of key / value / query / summary buffers. */

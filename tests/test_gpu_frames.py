@@ -133,7 +133,7 @@ def test_stream_small_trajectory(cuda_device, sign_mode):
         _check_frames(snaps[i], ref_snaps[i])
 
 
-@pytest.mark.parametrize("qr_method", ["householder", "cholesky2"])
+@pytest.mark.parametrize("qr_method", ["householder", "cholesky2", "cholesky2_split"])
 @pytest.mark.parametrize("d,r,m,T", [(128, 16, 2, 256), (128, 32, 4, 96), (64, 32, 4, 64), (64, 16, 4, 64)])
 def test_stream_mid_and_full_frames(cuda_device, d, r, m, T, qr_method):
     F = 12
@@ -145,9 +145,10 @@ def test_stream_mid_and_full_frames(cuda_device, d, r, m, T, qr_method):
     _check_frames(U, ref)
 
 
+@pytest.mark.parametrize("qr_method", ["cholesky2", "cholesky2_split"])
 @pytest.mark.parametrize("sign_mode", MODES)
 @pytest.mark.parametrize("d,r,m", [(128, 32, 4), (100, 24, 4), (40, 12, 2)])
-def test_stream_cholesky2_sign_modes_and_padding(cuda_device, d, r, m, sign_mode):
+def test_stream_cholesky2_sign_modes_and_padding(cuda_device, d, r, m, sign_mode, qr_method):
     # padded rows (d < 64 or 128) and columns (r < 16 or 32) go through the
     # same Gram / Cholesky / solve with unit columns in R
     F, T = 10, 48
@@ -155,15 +156,16 @@ def test_stream_cholesky2_sign_modes_and_padding(cuda_device, d, r, m, sign_mode
     A, B = wl.stream_update_factors(F, T, d, r, m, seed=d + 7 * r)
     U = U0.to(cuda_device).clone()
     snaps = gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), sign_mode=sign_mode, out_every=16,
-                               qr_method="cholesky2")
+                               qr_method=qr_method)
     ref_final, ref_snaps = go.stream_frames(U0.numpy(), A.numpy(), B.numpy(), 1.0, 1e-8, sign_mode, 16)
     _check_frames(U, ref_final)
     for i in range(snaps.shape[0]):
         _check_frames(snaps[i], ref_snaps[i])
 
 
+@pytest.mark.parametrize("qr_method", ["cholesky2", "cholesky2_split"])
 @pytest.mark.parametrize("sign_mode", MODES)
-def test_stream_cholesky2_falls_back_on_zero_columns(cuda_device, sign_mode):
+def test_stream_cholesky2_falls_back_on_zero_columns(cuda_device, sign_mode, qr_method):
     # U = 0 and B = [I_m; 0]: the frame is [A, 0, ..., 0], whose zero columns
     # fail the pivot test; Householder then gives LAPACK's answer (trailing
     # columns = the reflectors applied to unit vectors)
@@ -173,7 +175,7 @@ def test_stream_cholesky2_falls_back_on_zero_columns(cuda_device, sign_mode):
     B = torch.zeros((F, 1, r, m))
     B[:, 0, :m, :] = torch.eye(m)
     U = torch.zeros((F, d, r), device=cuda_device)
-    gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), sign_mode=sign_mode, qr_method="cholesky2")
+    gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), sign_mode=sign_mode, qr_method=qr_method)
     ref, _ = go.stream_frames(np.zeros((F, d, r), np.float32), A.numpy(), B.numpy(), 1.0, 1e-8, sign_mode)
     q = U.cpu().numpy()
     assert np.isfinite(q).all()
@@ -181,8 +183,9 @@ def test_stream_cholesky2_falls_back_on_zero_columns(cuda_device, sign_mode):
     assert np.abs(q - ref).max() <= 1e-5
 
 
+@pytest.mark.parametrize("qr_method", ["cholesky2", "cholesky2_split"])
 @pytest.mark.parametrize("beta", [0.03, 0.05, 0.1])
-def test_stream_cholesky2_mixed_conditioning(cuda_device, beta):
+def test_stream_cholesky2_mixed_conditioning(cuda_device, beta, qr_method):
     # a shrunken frame plus a rank-4 update: relative pivots around the 1e-2
     # test, so tokens and frames go either way; every token must still match
     F, d, r, m, T = 16, 128, 32, 4, 24
@@ -191,7 +194,7 @@ def test_stream_cholesky2_mixed_conditioning(cuda_device, beta):
     A = A * 2.0
     U = U0.to(cuda_device).clone()
     gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), beta=beta, sign_mode="r_diag_positive",
-                       qr_method="cholesky2")
+                       qr_method=qr_method)
     ref, _ = go.stream_frames(U0.numpy(), A.numpy(), B.numpy(), beta, 1e-8, go.SIGN_R_DIAG_POSITIVE)
     _check_frames(U, ref)
 
@@ -212,6 +215,27 @@ def test_stream_matches_repeated_single_steps(cuda_device):
     W = U0.clone()
     gfst.stream_frames(W, A, B, qr_method="cholesky2")
     assert (W - V).abs().max().item() <= 1e-5
+    X = U0.clone()
+    gfst.stream_frames(X, A, B, qr_method="cholesky2_split")
+    assert (X - V).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("d,r,m", [(128, 32, 4), (128, 16, 2)])
+def test_split_and_single_warp_cholesky2_agree(cuda_device, d, r, m):
+    # the split kernel sums the Gram in four row blocks: the same factor to fp32
+    # rounding as the one-warp kernel, over many frames and tokens; and it is
+    # deterministic
+    F, T = 300, 64
+    U0 = wl.random_orthonormal_frames(F, d, r, seed=5).to(cuda_device)
+    A, B = wl.stream_update_factors(F, T, d, r, m, seed=6, device="cpu")
+    A, B = A.to(cuda_device), B.to(cuda_device)
+    one, split, again = U0.clone(), U0.clone(), U0.clone()
+    gfst.stream_frames(one, A, B, sign_mode="r_diag_positive", qr_method="cholesky2")
+    gfst.stream_frames(split, A, B, sign_mode="r_diag_positive", qr_method="cholesky2_split")
+    gfst.stream_frames(again, A, B, sign_mode="r_diag_positive", qr_method="cholesky2_split")
+    assert torch.equal(split, again)
+    assert (split - one).abs().max().item() <= 1e-5
+    assert go.orthogonality_error(split.cpu().numpy()).max() <= ORTH_TOL
 
 
 def test_stream_cholesky2_rejects_other_shapes(cuda_device):
@@ -220,6 +244,8 @@ def test_stream_cholesky2_rejects_other_shapes(cuda_device):
     B = torch.zeros((2, 1, 8, 4), device=cuda_device)
     with pytest.raises(RuntimeError):
         gfst.stream_frames(U, A, B, qr_method="cholesky2")
+    with pytest.raises(RuntimeError):
+        gfst.stream_frames(U, A, B, qr_method="cholesky2_split")
 
 
 def test_cpu_tensors_rejected():
