@@ -621,16 +621,25 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def child_env(rank: int, world: int, local_rank: int, port: int | None) -> dict:
+    """Environment of a sub-result child: the parent's rank layout and a
+    rendezvous of its own on `port`.  torchrun's agent variables are dropped:
+    with TORCHELASTIC_USE_AGENT_STORE set, rank 0 would connect to the agent's
+    store as a client instead of hosting the children's store."""
+    env = {k: v for k, v in os.environ.items() if not k.startswith("TORCHELASTIC_")}
+    env.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(local_rank),
+                "MASTER_ADDR": "127.0.0.1"})
+    if port is not None:
+        env["MASTER_PORT"] = str(port)
+    return env
+
+
 def run_child(part: str, rank: int, world: int, local_rank: int, port: int | None, timeout_s: float) -> dict | None:
     """Run `bench.py --part <part>` as a child process with the same rank
     layout (its own process group on `port` when world > 1); returns its JSON."""
     fd, out_path = tempfile.mkstemp(prefix=f"gfst_{part}_", suffix=".json")
     os.close(fd)
-    env = dict(os.environ)
-    env.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(local_rank),
-                "MASTER_ADDR": "127.0.0.1"})
-    if port is not None:
-        env["MASTER_PORT"] = str(port)
+    env = child_env(rank, world, local_rank, port)
     cmd = [sys.executable, str(Path(__file__).resolve()), "--part", part, "--part-out", out_path]
     try:
         rc = subprocess.run(cmd, env=env, timeout=timeout_s, stdout=sys.stderr, stderr=sys.stderr).returncode

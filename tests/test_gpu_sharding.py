@@ -83,7 +83,7 @@ def test_block_range_sharded_readout_two_ranks(cuda_device, tmp_path):
         assert torch.equal(value, ref_v.cpu())
 
 
-def _nccl_worker(rank, world, port, out_path):
+def _nccl_worker(rank, world, port, out_path, layout, n_committed):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -94,11 +94,20 @@ def _nccl_worker(rank, world, port, out_path):
                             device_id=dev)
     try:
         pool, vals, Q, summary, k = _data(dev)
+        if n_committed is not None:
+            pool[:, n_committed:] = 0
+            vals[:, n_committed:] = 0
+            summary[:, n_committed:] = 0
         shard = sharding.BlockRange(rank, world, pool.shape[1])
         sl = slice(shard.lo, shard.hi)
+        n_valid = None if n_committed is None else max(0, min(n_committed, shard.hi) - shard.lo)
+        timings = {}
         res = sharding.sharded_readout(Q, summary[:, sl].contiguous(), pool[:, sl].contiguous(),
-                                       vals[:, sl].contiguous(), k, shard)
+                                       vals[:, sl].contiguous(), k, shard, n_valid=n_valid, value_layout=layout,
+                                       timings=timings)
         torch.cuda.synchronize(dev)
+        assert set(timings) == {"local_topk", "gather_candidates", "merge", "readout", "gather_winners",
+                                "value_exchange"}
         torch.save([t.cpu() for t in res], f"{out_path}.{rank}")
         dist.barrier()
     finally:
@@ -106,19 +115,28 @@ def _nccl_worker(rank, world, port, out_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_block_range_sharded_readout_nccl_two_gpus(cuda_device, tmp_path):
-    # one rank per GPU over NCCL: all-gather of candidates and winners, all-reduce
-    # of the owner's value row; equal to the single-GPU readout bit for bit
+@pytest.mark.parametrize("layout,n_committed", [("replicated", None), ("stream_shard", None), ("replicated", 27)])
+def test_block_range_sharded_readout_nccl_two_gpus(cuda_device, tmp_path, layout, n_committed):
+    # one rank per GPU over NCCL: all-gather of candidates and winners, then the
+    # winners' value rows from their owners; equal to the single-GPU readout bit
+    # for bit (on a part-filled memory: the readout of its committed blocks)
     world = 2
     out = str(tmp_path / "nccl")
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), out, layout, n_committed), nprocs=world,
+                       start_method="spawn")
     pool, vals, Q, summary, k = _data(cuda_device)
-    ref_s, ref_i = retrieval.block_topk(Q, summary, k)
+    nb = pool.shape[1] if n_committed is None else n_committed
+    ref_s, ref_i = retrieval.block_topk(Q, summary, k, n_blocks=nb)
     ref_t, ref_bs, ref_v = readout.exact_readout(Q, pool, vals, ref_i)
+    S = Q.shape[0]
     for r in range(world):
         best_t, best_s, value, top_i, top_s = torch.load(f"{out}.{r}")
         assert torch.equal(top_i, ref_i.cpu())
         assert torch.equal(top_s, ref_s.cpu())
         assert torch.equal(best_t, ref_t.cpu())
         assert torch.equal(best_s, ref_bs.cpu())
-        assert torch.equal(value, ref_v.cpu())
+        if layout == "replicated":
+            assert torch.equal(value, ref_v.cpu())
+        else:
+            lo, hi = sharding.stream_shard(S, r, world)
+            assert torch.equal(value, ref_v.cpu()[lo:hi])
