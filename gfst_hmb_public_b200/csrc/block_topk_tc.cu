@@ -87,6 +87,10 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 2)
   const int64_t s = blockIdx.y;
   const int q0 = blockIdx.x * BM;
   const int n_tiles = (n_blocks + BN - 1) / BN;
+  // epilogue warps whose 32 rows hold queries (a stream with fewer than 128
+  // queries leaves the upper lane quadrants empty: they take no part)
+  const int active_quads = min(4, max(1, (n_queries - q0 + 31) / 32));
+  const int active_epi = active_quads * (kEpiWarps / 4);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 2)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], kEpiWarps);
+      mbar_init(&tempty[i], active_epi);
     }
     mbar_init(afull, 1);
     mbar_init(done, 1);
@@ -171,7 +175,8 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 2)
     const int quad = warp & 3, half = warp >> 2;
     TopK<KCAP> top;
     top.init();
-    for (int i = 0; i < n_tiles; ++i) {
+    const int my_tiles = quad < active_quads ? n_tiles : 0;  // empty quadrants skip the tiles
+    for (int i = 0; i < my_tiles; ++i) {
       const int acc = i & 1;
       // one lane waits and the warp follows its verdict, so the .sync.aligned
       // TMEM loads below always run with the whole warp
@@ -208,13 +213,14 @@ __global__ void __launch_bounds__(TcWarps<EPW>::kThreads, 2)
         top.write(top_scores + ((size_t)s * n_queries + q) * k, top_idx + ((size_t)s * n_queries + q) * k, k);
     } else {
       // merge the two halves of each row through shared memory (the B ring is
-      // idle once every tile has been consumed; after a timeout nothing is merged)
+      // idle once a warp has consumed every tile; the warps of empty quadrants
+      // consumed none and write nothing; after a timeout nothing is merged)
       const int row = quad * 32 + lane;
       const int q = q0 + row;
       float* ms = reinterpret_cast<float*>(sB);                 // [2][BM][KCAP]
       int* mi = reinterpret_cast<int*>(sB + 2 * BM * KCAP * 4);  // [2][BM][KCAP]
       const bool merge = *abort_flag == 0;
-      if (merge) {
+      if (merge && quad < active_quads) {
   #pragma unroll
         for (int j = 0; j < KCAP; ++j) {
           ms[(half * BM + row) * KCAP + j] = top.s[j];
