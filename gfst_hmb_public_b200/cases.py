@@ -22,6 +22,8 @@ the last launch.  CASE is one of:
   segmented   log-sum-exp collapse of one candidate list (--streams = elements, default 2048)
   block_score block token scores through a 128 x 128 bf16 projection (--streams = tokens, default 65536)
   heev        batched symmetric eigendecomposition of 64 x 64 float64 matrices (--streams = matrices, default 2048)
+  open_block  open-block readout merge of 64 queries over a 64-token open block per stream (bf16, d=128)
+  exact_topk  one query against a bf16 bank (--streams = keys, default 8192; top-16)
 """
 from __future__ import annotations
 
@@ -54,7 +56,8 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("case", choices=["frames", "frames_mid", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
                                          "readout_long", "commit_eig", "block_tracker", "centroid_commit",
-                                         "centroid_readout", "segmented", "block_score", "heev"])
+                                         "centroid_readout", "segmented", "block_score", "heev", "open_block",
+                                         "exact_topk"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     parser.add_argument("--batch", type=int, default=1, help="calls per timed round (segmented, block_score)")
@@ -170,6 +173,22 @@ def main() -> None:
         x = torch.randn((S, 64, 64), generator=g, device=dev)
         ms = _timed(lambda: tr.step(x), args.repeat)
         units = f"{S * 64 / ms / 1e3:.2f} M tokens/s"
+    elif args.case == "open_block":
+        S = args.streams or 2048
+        Q = torch.randn((S, 64, 128), generator=g, device=dev).to(bf)
+        Ko = torch.randn((S, 64, 128), generator=g, device=dev).to(bf)
+        Vo = torch.randn((S, 64, 128), generator=g, device=dev).to(bf)
+        bt = torch.full((S, 64), -1, dtype=torch.int32, device=dev)
+        bs = torch.full((S, 64), float("-inf"), device=dev)
+        ov = torch.zeros((S, 64, 128), dtype=bf, device=dev)
+        ms = _timed(lambda: readout.open_block_readout(Q, Ko, Vo, bt, bs, ov, open_base=512 * 64), args.repeat)
+        units = f"{S * 64 * 128 * 2 * 2 / ms / 1e6:.0f} GB/s of queries and open keys"
+    elif args.case == "exact_topk":
+        n = args.streams or 8192
+        keys = torch.randn((n, 128), generator=g, device=dev).to(bf)
+        q = torch.randn((128,), generator=g, device=dev).to(bf)
+        ms = _timed(lambda: retrieval.exact_topk(keys, q, 16), args.repeat, args.batch)
+        units = f"{n * 128 * 2 / ms / 1e6:.0f} GB/s of keys"
     else:  # commit
         S = args.streams or 2048
         mem = memory.BlockMemory(S, 4, 64, 128, dtype=bf, device=dev)
