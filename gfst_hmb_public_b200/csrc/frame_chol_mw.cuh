@@ -15,10 +15,13 @@
 //     column-major copy stays inside the warp: the chunk swizzle only permutes
 //     4-row chunks within a 32-row block), the partial Grams meet in shared
 //     memory and every warp adds them in the same fixed order (deterministic);
-//   * every warp then runs the same Cholesky on the same sums, so no warp
-//     waits for another's R and all warps take the same fallback decision.
-// Two CTA barriers per pass (partials written / partials read).  The
-// Householder fallback runs on warp 0 over the whole matrix.
+//   * warp 0 adds the partials and runs the 32-step Cholesky (or takes the
+//     first-order correction) while the other warps wait at the barrier that
+//     publishes its decision and R; every warp then solves (or corrects) its
+//     own rows.  Two CTA barriers per pass (partials written / R published).
+// The frame row is not live across the Cholesky (it waits in the shared copy),
+// and the Householder fallback keeps its matrix in shared memory (one row per
+// thread), so the kernel fits in 128 registers: four frame CTAs per SM.
 #pragma once
 
 #include "frame_chol.cuh"
@@ -31,16 +34,20 @@ struct FrameCholMW {
   static_assert(RMAX == 16 || RMAX == 32, "Gram tiles of FrameChol");
   static constexpr int W = DMAX / 32;   // warps per frame
   static constexpr int GS = RMAX + 4;   // Gram row stride (floats)
-  using One = FrameChol<DMAX, RMAX>;    // swizzled layout, TF32 helpers, Householder layout
-  using HH = typename One::HH;
+  using One = FrameChol<DMAX, RMAX>;    // swizzled layout, TF32 helpers
   using Row = float[RMAX];              // this lane's row of the frame
 
   struct __align__(16) Smem {
     float mt[RMAX * DMAX];              // column-major, chunk-swizzled copy of the pass input
-    float part[W][RMAX * GS];           // warp w's partial Gram; then its R (or G) rows
-    typename HH::Smem hh;               // Householder scratch (warp 0)
+    float part[W][RMAX * GS];           // warp w's partial Gram
+    float area[RMAX * GS];              // warp 0's R rows (or the Gram rows for the correction)
+    float red2[W][RMAX];                // Householder fallback: per-warp column sums
+    float red[W];                       // Householder fallback: per-warp scalar sums
+    float tau[RMAX], beta[RMAX];        // Householder fallback: reflector scales, R diagonal
     uint32_t sign_bits[W][2];           // first-significant search: found / negative bits
+    int action;                         // warp 0's decision for the pass (kSolve / kCorrect / kFallback)
   };
+  static constexpr int kSolve = 0, kCorrect = 1, kFallback = 2;
 
   __device__ static __forceinline__ void write_mt(const Row& f, Smem& sm, int row) {
 #pragma unroll
@@ -223,26 +230,89 @@ struct FrameCholMW {
     });
   }
 
-  // Householder QR (sign rule included) of the whole matrix in mt, by warp 0,
-  // written back to mt.  Called by every thread of the CTA.
-  __device__ static __forceinline__ void householder(Smem& sm, int w, int lane, float eps_sign, int sign_mode,
-                                                     int r) {
-    __syncthreads();  // every warp's rows are in mt; nobody reads mt until the second barrier
-    if (w == 0) {
-      const int rg = lane & 7, cg = lane >> 3;
-      typename HH::Frame a;
+  __device__ static __forceinline__ float warp_sum(float x) {
 #pragma unroll
-      for (int s = 0; s < DMAX / 8; ++s)
-#pragma unroll
-        for (int c = 0; c < RMAX / 4; ++c) HH::set(a, s, c, sm.mt[One::mt_at(cg + 4 * c, rg + 8 * s)]);
-      __syncwarp();
-      HH::qr(a, lane, lane, sm.hh, eps_sign, sign_mode, r);
-#pragma unroll
-      for (int s = 0; s < DMAX / 8; ++s)
-#pragma unroll
-        for (int c = 0; c < RMAX / 4; ++c) sm.mt[One::mt_at(cg + 4 * c, rg + 8 * s)] = HH::get(a, s, c);
-    }
+    for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+  }
+
+  // Sum of x over the CTA (every thread gets it).
+  __device__ static __forceinline__ float block_sum(float x, Smem& sm, int w, int lane) {
+    x = warp_sum(x);
+    if (lane == 0) sm.red[w] = x;
     __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int v = 0; v < W; ++v) s += sm.red[v];
+    __syncthreads();  // red is free again
+    return s;
+  }
+
+  // w_j = sum over rows of v * A[row][j] for j in (k, r) into red2 (warp sums;
+  // the caller adds the W warps' entries after a barrier).
+  __device__ static __forceinline__ void column_dots(Smem& sm, float v, int k, int r, int row, int w, int lane) {
+    for (int j = k + 1; j < r; ++j) {
+      const float c = warp_sum(v * sm.mt[One::mt_at(j, row)]);
+      if (lane == 0) sm.red2[w][j] = c;
+    }
+  }
+  __device__ static __forceinline__ void column_update(Smem& sm, float tv, int k, int r, int row) {
+    for (int j = k + 1; j < r; ++j) {
+      float wj = 0.f;
+#pragma unroll
+      for (int v = 0; v < W; ++v) wj += sm.red2[v][j];
+      sm.mt[One::mt_at(j, row)] -= tv * wj;
+    }
+  }
+
+  // Householder QR of the matrix in mt -- LAPACK's sgeqr2 then sorg2r, with the
+  // formulas of FrameQR (slarfg: xnorm == 0 gives tau = 0 and beta = alpha;
+  // else beta = -sign(alpha) sqrt(alpha^2 + xnorm^2), tau = (beta - alpha) /
+  // beta, v = x / (alpha - beta)) -- one row per thread, the matrix kept in
+  // shared memory; the R-diagonal rule applied (the first-significant rule is
+  // the caller's).  The fallback for frames whose Gram fails the pivot test:
+  // written to hold few registers, not for speed.  Called by every thread of
+  // the CTA after the pass input is in mt; the thin Q replaces it.
+  __device__ static void householder(Smem& sm, int w, int lane, int r, int sign_mode) {
+    const int row = 32 * w + lane;
+#pragma unroll 1
+    for (int k = 0; k < r; ++k) {
+      const float xk = sm.mt[One::mt_at(k, row)];
+      const float ssq = block_sum(row > k ? xk * xk : 0.f, sm, w, lane);
+      const float alpha = sm.mt[One::mt_at(k, k)];
+      float beta = alpha, tau = 0.f, scale = 0.f;
+      if (ssq != 0.f) {
+        const float nrm = sqrtf(fmaf(alpha, alpha, ssq));
+        beta = alpha >= 0.f ? -nrm : nrm;
+        tau = (beta - alpha) / beta;
+        scale = 1.f / (alpha - beta);
+      }
+      const float v = row > k ? xk * scale : (row == k ? 1.f : 0.f);
+      if (row == 0) {
+        sm.tau[k] = tau;
+        sm.beta[k] = beta;
+      }
+      column_dots(sm, v, k, r, row, w, lane);
+      __syncthreads();  // dots written; alpha and column k read by everyone
+      if (row > k) sm.mt[One::mt_at(k, row)] = v;
+      if (row == k) sm.mt[One::mt_at(k, k)] = beta;
+      column_update(sm, tau * v, k, r, row);
+      __syncthreads();  // red2 free, the trailing columns updated
+    }
+#pragma unroll 1
+    for (int i = r - 1; i >= 0; --i) {
+      const float vi = row > i ? sm.mt[One::mt_at(i, row)] : (row == i ? 1.f : 0.f);
+      const float tau = sm.tau[i];
+      column_dots(sm, vi, i, r, row, w, lane);
+      __syncthreads();
+      column_update(sm, tau * vi, i, r, row);
+      sm.mt[One::mt_at(i, row)] = row > i ? -tau * vi : (row == i ? 1.f - tau : 0.f);
+      __syncthreads();
+    }
+    if (sign_mode == GFST_SIGN_R_DIAG_POSITIVE) {
+      for (int k = 0; k < r; ++k)
+        if (sm.beta[k] < 0.f) sm.mt[One::mt_at(k, row)] = -sm.mt[One::mt_at(k, row)];
+    }
   }
 
   // Reference sign rule (gfst.py:35-46) across the warps: the first row of each
@@ -274,39 +344,49 @@ struct FrameCholMW {
       if ((flip >> c) & 1u) f[c] = -f[c];
   }
 
-  // In place: f (this lane's row) <- the row of the sign-fixed thin Q.
+  // In place: f (this lane's row) <- the row of the sign-fixed thin Q.  Warp 0
+  // adds the partial Grams and runs the Cholesky (or decides on the
+  // first-order correction) while the other warps wait at the barrier that
+  // publishes its decision and R.
   __device__ static __forceinline__ void qr(Row& f, Smem& sm, int w, int lane, float eps_sign, int sign_mode,
                                             int r) {
     const int row = 32 * w + lane;
-    float* area = sm.part[w];
 #pragma unroll 1
     for (int ps = 0; ps < 2; ++ps) {
       write_mt(f, sm, row);
       __syncwarp();
       gram_partial(sm, w, lane);
-      __syncthreads();  // every partial is written
-      Row g;
-      sum_partials(g, sm, lane);
-      __syncthreads();  // every partial is read: the areas are free
-      if (ps == 1 && gram_defect(g, lane, r) <= kFirstOrderTol) {
-        if (lane < RMAX) {
+      __syncthreads();  // every partial is written; everyone is done with the last area
+      if (w == 0) {
+        Row g;
+        sum_partials(g, sm, lane);
+        int action;
+        if (ps == 1 && gram_defect(g, lane, r) <= kFirstOrderTol) {
+          if (lane < RMAX) {
 #pragma unroll
-          for (int q = 0; q < RMAX; q += 4)
-            *reinterpret_cast<float4*>(area + lane * GS + q) = make_float4(g[q], g[q + 1], g[q + 2], g[q + 3]);
+            for (int q = 0; q < RMAX; q += 4)
+              *reinterpret_cast<float4*>(sm.area + lane * GS + q) = make_float4(g[q], g[q + 1], g[q + 2], g[q + 3]);
+          }
+          action = kCorrect;
+        } else {
+          action = __all_sync(0xffffffffu, cholesky(g, sm.area, lane, r)) ? kSolve : kFallback;
         }
-        __syncwarp();
-        correct(f, area);
+        if (lane == 0) sm.action = action;
+      }
+      __syncthreads();  // the decision and R (or G) are published; the partials are free
+      const int action = sm.action;
+      if (action == kCorrect) {
+        correct(f, sm.area);
         break;
       }
-      const bool ok = __all_sync(0xffffffffu, cholesky(g, area, lane, r));
-      __syncwarp();
-      if (!ok) {  // the same on every warp: the same sums, the same code
-        householder(sm, w, lane, eps_sign, sign_mode, r);
+      if (action == kFallback) {
+        householder(sm, w, lane, r, sign_mode);
         read_mt(f, sm, row);
+        if (sign_mode == GFST_SIGN_FIRST_SIGNIFICANT) first_significant(f, sm, w, lane, eps_sign);
         return;
       }
-      read_mt(f, sm, row);  // the row waits in mt across the Cholesky
-      solve(f, area);
+      read_mt(f, sm, row);  // the row waited in mt across the Cholesky
+      solve(f, sm.area);
     }
     if (sign_mode == GFST_SIGN_FIRST_SIGNIFICANT) first_significant(f, sm, w, lane, eps_sign);
   }

@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
 // per warp.  Each warp stages its own 32 rows of A_t and all of B_t.
 // ---------------------------------------------------------------------------
 template <int DMAX, int RMAX>
-__global__ void __launch_bounds__(DMAX, 2)
+__global__ void __launch_bounds__(DMAX, 512 / DMAX)
     frame_stream_chol_mw_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
                                 float beta, int64_t n_frames, int T, int d, int r, int m, float eps_sign,
                                 int sign_mode, float* __restrict__ frames_out, int out_every, bool vec4) {
