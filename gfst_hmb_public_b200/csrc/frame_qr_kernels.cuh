@@ -10,6 +10,7 @@
 #pragma once
 #include "frame_chol.cuh"
 #include "frame_chol_mw.cuh"
+#include "frame_chol_small.cuh"
 #include "frame_qr.cuh"
 #include "frame_qr_launch.h"
 
@@ -24,6 +25,13 @@ template <int DMAX, int RMAX, int RG, int CG>
 constexpr int min_blocks() {
   return (DMAX / RG) * (RMAX / CG) >= 128 ? 2 : 4;
 }
+
+// Classes whose QR takes CholeskyQR2 in the Householder kernels' lane layout
+// (frame_chol_small.cuh, with the Householder code as its fallback): up to 8
+// columns, 9 to 128 rows.  The one-step kernel always takes it; the streaming
+// kernel unless GFST_QR_HOUSEHOLDER is asked for.
+template <int DMAX, int RMAX, int CG>
+constexpr bool kCholSmall = RMAX == 8 && CG == 1 && DMAX >= 32 && DMAX <= 128;
 
 // ---------------------------------------------------------------------------
 // one step: Uout = QR(beta * U + A B^T)
@@ -51,7 +59,11 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>())
   QR::load(a, U + fs * frame_elems, t, d, r, valid, vec4);
   if (beta != 1.f) QR::scale(a, beta);
   if (m > 0 && valid) QR::rank_update(a, A + fs * (size_t)d * m, B + fs * (size_t)r * m, t, d, r, m);
-  QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
+  if constexpr (kCholSmall<DMAX, RMAX, CG>) {
+    FrameCholSmall<DMAX, RG>::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r, valid);
+  } else {
+    QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
+  }
   QR::store(a, Uout + fs * frame_elems, t, d, r, valid, vec4);
 }
 
@@ -73,7 +85,7 @@ template <int DMAX, int RMAX, int RG, int CG, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>()))
     frame_stream_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B, float beta,
                         int64_t n_frames, int T, int d, int r, int m, float eps_sign, int sign_mode,
-                        float* __restrict__ frames_out, int out_every, bool vec4) {
+                        float* __restrict__ frames_out, int out_every, bool vec4, bool chol) {
   using QR = FrameQR<DMAX, RMAX, RG, CG>;
   constexpr int TPF = QR::TPF;
   constexpr int GPW = 32 / TPF;
@@ -117,7 +129,15 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<DMAX, RMAX, RG, CG>())
     const float* sA = my_stage + (tok & 1) * tok_elems;
     if (beta != 1.f) QR::scale(a, beta);
     if (valid) QR::rank_update(a, sA, sA + a_elems, t, d, r, m);
-    QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
+    if constexpr (kCholSmall<DMAX, RMAX, CG>) {
+      if (chol) {
+        FrameCholSmall<DMAX, RG>::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r, valid);
+      } else {
+        QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
+      }
+    } else {
+      QR::qr(a, lane, t, qsm[g], eps_sign, sign_mode, r);
+    }
     if (frames_out != nullptr && ((tok + 1) % out_every) == 0) {
       const int64_t snap = (tok + 1) / out_every - 1;
       QR::store(a, frames_out + (snap * n_frames + fs) * frame_elems, t, d, r, valid, vec4);
@@ -315,10 +335,14 @@ int launch_stream(float* U, const float* A, const float* B, float beta, int64_t 
     if (qr_method != GFST_QR_HOUSEHOLDER)
       return launch_stream_chol<DMAX, RMAX>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode, frames_out,
                                             out_every, stream);
+  } else if constexpr (kCholSmall<DMAX, RMAX, CG>) {
+    GFST_REQUIRE(qr_method != GFST_QR_CHOLESKY2_SPLIT, GFST_ERR_SHAPE,
+                 "the split CholeskyQR2 kernel covers d in (32, 128] with 8 < r <= 32 (d=%d r=%d)", d, r);
   } else {
     GFST_REQUIRE(qr_method != GFST_QR_CHOLESKY2 && qr_method != GFST_QR_CHOLESKY2_SPLIT, GFST_ERR_SHAPE,
-                 "CholeskyQR2 streaming covers d in (32, 128] with 8 < r <= 32 (d=%d r=%d)", d, r);
+                 "CholeskyQR2 streaming covers d in (8, 128] with r <= 32 (d=%d r=%d)", d, r);
   }
+  const bool chol_small = kCholSmall<DMAX, RMAX, CG> && qr_method != GFST_QR_HOUSEHOLDER;
   constexpr int GPW = 32 / (RG * CG);
   const int64_t per_block = kWarps * GPW;
   const int64_t blocks = (n + per_block - 1) / per_block;
@@ -332,7 +356,7 @@ int launch_stream(float* U, const float* A, const float* B, float beta, int64_t 
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
   kern<<<(unsigned)blocks, kWarps * 32, smem, stream>>>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode,
-                                                         frames_out, out_every, vec4);
+                                                         frames_out, out_every, vec4, chol_small);
   return check_launch("frame_stream_kernel");
 }
 

@@ -14,7 +14,8 @@ int launch_update(const float* U, const float* A, const float* B, float beta, fl
                   int m, float eps_sign, int sign_mode, cudaStream_t stream);
 
 // qr_method: GFST_QR_AUTO (CholeskyQR2 where the class has it, else
-// Householder), GFST_QR_HOUSEHOLDER or GFST_QR_CHOLESKY2.
+// Householder), GFST_QR_HOUSEHOLDER, GFST_QR_CHOLESKY2 or
+// GFST_QR_CHOLESKY2_SPLIT (classes with 8 < r <= 32 only).
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
                   float eps_sign, int sign_mode, float* frames_out, int out_every, int qr_method,

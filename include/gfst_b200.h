@@ -106,14 +106,16 @@ enum gfst_sign_mode {
 /* QR algorithm of the streaming frame pass (gfst_frame_stream_ex). */
 enum gfst_qr_method {
   /* CholeskyQR2 for 32 < d <= 128 with 8 < r <= 32 (split over warps below
-   * 384 frames), Householder otherwise. */
+   * 384 frames) and for 8 < d <= 128 with r <= 8, Householder otherwise. */
   GFST_QR_AUTO = 0,
   /* LAPACK-order Householder (geqrf/orgqr) for every token. */
   GFST_QR_HOUSEHOLDER = 1,
   /* Two Cholesky QR passes per token (G = C^T C = R^T R, C <- C R^{-1});
    * a frame whose pivot R_jj^2 falls below 1e-2 * G_jj (or is not finite)
    * takes the Householder path for that token.  Same Q as Householder with
-   * R_jj > 0 to fp32 rounding; shapes outside the AUTO range are rejected. */
+   * R_jj > 0 to fp32 rounding; shapes outside the AUTO range are rejected.
+   * With r <= 8 a frame is split over 8 or 16 lanes and a failed pivot test
+   * sends the frames of the whole warp (2 or 4) through Householder. */
   GFST_QR_CHOLESKY2 = 2,
   /* GFST_QR_CHOLESKY2 with each frame split over d/32 warps (a CTA per frame):
    * shorter per-token latency for batches too small to fill the GPU with one
@@ -132,11 +134,14 @@ GFST_API int gfst_abi_version(void);
  * (empty string if none). */
 GFST_API const char* gfst_last_error(void);
 
-/* ---- frames: rank-m update + Householder thin QR ---------------------- *
+/* ---- frames: rank-m update + thin QR ----------------------------------- *
  * For every frame f in [0, n_frames):
  *     C   = beta * U[f] + A[f] * B[f]^T        (U: d x r, A: d x m, B: r x m)
  *     Q   = thin Q of Householder QR(C) (LAPACK geqrf/orgqr order), sign-fixed
  *     Uout[f] = Q                               (d x r)
+ * Frames of 8 < d <= 128 rows and r <= 8 columns take CholeskyQR2 (the same
+ * Q to fp32 rounding; Householder for a warp whose frames fail the pivot
+ * test of GFST_QR_CHOLESKY2).
  * m == 0 is a plain batched QR of U (A and B may be NULL).  U and Uout may alias.
  * Limits: 1 <= r <= d, r <= 32, d <= 128 (d <= 256 when r <= 16), 0 <= m <= 8.
  * fp32 throughout; no fast-math.                                            */

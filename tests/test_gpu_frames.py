@@ -6,6 +6,8 @@ principal-angle distance of every leading-column prefix <= 1e-4, and
 elementwise |Q - Q_oracle| <= 1e-4 (two correct fp32 Householder codes differ by
 up to ~5e-5 on the near-collinear frames).
 """
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -239,13 +241,64 @@ def test_split_and_single_warp_cholesky2_agree(cuda_device, d, r, m):
 
 
 def test_stream_cholesky2_rejects_other_shapes(cuda_device):
-    U = torch.zeros((2, 64, 8), device=cuda_device)
-    A = torch.zeros((2, 1, 64, 4), device=cuda_device)
-    B = torch.zeros((2, 1, 8, 4), device=cuda_device)
-    with pytest.raises(RuntimeError):
-        gfst.stream_frames(U, A, B, qr_method="cholesky2")
-    with pytest.raises(RuntimeError):
-        gfst.stream_frames(U, A, B, qr_method="cholesky2_split")
+    # CholeskyQR2 covers 8 < d <= 128; the split kernel only 8 < r <= 32
+    for d, r, method in ((8, 8, "cholesky2"), (200, 8, "cholesky2"), (64, 8, "cholesky2_split")):
+        U = torch.zeros((2, d, r), device=cuda_device)
+        A = torch.zeros((2, 1, d, 4), device=cuda_device)
+        B = torch.zeros((2, 1, r, 4), device=cuda_device)
+        with pytest.raises(RuntimeError):
+            gfst.stream_frames(U, A, B, qr_method=method)
+
+
+@pytest.mark.parametrize("qr_method", ["householder", "cholesky2", "auto"])
+@pytest.mark.parametrize("sign_mode", MODES)
+@pytest.mark.parametrize("d,r,m", [(64, 8, 1), (40, 5, 4), (128, 8, 2), (20, 4, 1)])
+def test_stream_narrow_frames(cuda_device, d, r, m, sign_mode, qr_method):
+    # frames of <= 8 columns: CholeskyQR2 in the Householder kernel's lane
+    # layout (8 or 16 lanes per frame), padded rows and columns included
+    F, T = 19, 64
+    U0 = wl.random_orthonormal_frames(F, d, r, seed=5 * d + r)
+    A, B = wl.stream_update_factors(F, T, d, r, m, seed=d + 11 * r)
+    U = U0.to(cuda_device).clone()
+    snaps = gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), sign_mode=sign_mode, out_every=16,
+                               qr_method=qr_method)
+    ref_final, ref_snaps = go.stream_frames(U0.numpy(), A.numpy(), B.numpy(), 1.0, 1e-8, sign_mode, 16)
+    _check_frames(U, ref_final)
+    for i in range(snaps.shape[0]):
+        _check_frames(snaps[i], ref_snaps[i])
+
+
+@pytest.mark.parametrize("beta", [0.03, 0.1])
+def test_stream_narrow_frames_mixed_conditioning(cuda_device, beta):
+    # shrunken 64 x 8 frames plus rank-4 updates: pivots around the 1e-2 test,
+    # so some warps take Householder for a token and others CholeskyQR2
+    F, d, r, m, T = 40, 64, 8, 4, 32
+    U0 = wl.random_orthonormal_frames(F, d, r, seed=31)
+    A, B = wl.stream_update_factors(F, T, d, r, m, seed=32)
+    A = A * 2.0
+    U = U0.to(cuda_device).clone()
+    gfst.stream_frames(U, A.to(cuda_device), B.to(cuda_device), beta=beta, sign_mode="r_diag_positive",
+                       qr_method="cholesky2")
+    ref, _ = go.stream_frames(U0.numpy(), A.numpy(), B.numpy(), beta, 1e-8, go.SIGN_R_DIAG_POSITIVE)
+    _check_frames(U, ref)
+
+
+@pytest.mark.parametrize("sign_mode", MODES)
+def test_batched_narrow_qr_near_collinear_and_scaled(cuda_device, sign_mode):
+    # one QR per frame, 64 x 8: columns scaled over 3.5 decades (Cholesky's
+    # error is componentwise in the column scaling) and, in every fifth frame,
+    # a column at cos 0.9999 to the previous one (pivot test fails -> that
+    # warp's frames go through Householder)
+    g = torch.Generator().manual_seed(41)
+    x = torch.randn((400, 64, 8), generator=g) * torch.pow(10.0, -torch.arange(8) / 2.0)
+    for f in range(0, 400, 5):
+        c = x[f, :, 2] / x[f, :, 2].norm()
+        p = torch.randn(64, generator=g)
+        p -= (p @ c) * c
+        p /= p.norm()
+        x[f, :, 3] = 0.9999 * c + math.sqrt(1 - 0.9999 ** 2) * p
+    q = gfst.frame_update_qr(x.to(cuda_device), sign_mode=sign_mode)
+    _check_frames(q, go.qr_reference(x.numpy(), 1e-8, sign_mode))
 
 
 def test_cpu_tensors_rejected():
