@@ -24,6 +24,8 @@ the last launch.  CASE is one of:
   heev        batched symmetric eigendecomposition of 64 x 64 float64 matrices (--streams = matrices, default 2048)
   open_block  open-block readout merge of 64 queries over a 64-token open block per stream (bf16, d=128)
   exact_topk  one query against a bf16 bank (--streams = keys, default 8192; top-16)
+  mpuc_scan   MPUC recurrent scan of a d_model 2048 cell (fast 1024, mid 512, slow 512,
+              bridge rank 128) over 256 tokens (--streams = sequences, default 8)
 """
 from __future__ import annotations
 
@@ -32,7 +34,7 @@ import math
 
 import torch
 
-from . import block_commit, centroid, gfst, memory, readout, retrieval, tracker, workloads as wl
+from . import block_commit, centroid, gfst, memory, mpuc, readout, retrieval, tracker, workloads as wl
 
 
 def _timed(fn, repeat: int, batch: int = 1) -> float:
@@ -57,7 +59,7 @@ def main() -> None:
     parser.add_argument("case", choices=["frames", "frames_mid", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
                                          "readout_long", "commit_eig", "block_tracker", "centroid_commit",
                                          "centroid_readout", "segmented", "block_score", "heev", "open_block",
-                                         "exact_topk"])
+                                         "exact_topk", "mpuc_scan"])
     parser.add_argument("--streams", type=int, default=None)
     parser.add_argument("--repeat", type=int, default=2)
     parser.add_argument("--batch", type=int, default=1, help="calls per timed round (segmented, block_score)")
@@ -189,6 +191,12 @@ def main() -> None:
         q = torch.randn((128,), generator=g, device=dev).to(bf)
         ms = _timed(lambda: retrieval.exact_topk(keys, q, 16), args.repeat, args.batch)
         units = f"{n * 128 * 2 / ms / 1e6:.0f} GB/s of keys"
+    elif args.case == "mpuc_scan":
+        B, T = args.streams or 8, 256
+        cell = wl.mpuc_cell_weights(2048, seed=20261210, device=dev)
+        ins = [torch.randn((B, T, n), generator=g, device=dev) for n in (cell.F, cell.M, cell.S)]
+        ms = _timed(lambda: mpuc.recurrent_scan(cell, *ins), args.repeat)
+        units = f"{ms * 1e3 / T:.2f} us per token, {B * T / ms / 1e3:.3f} M sequence-tokens/s"
     else:  # commit
         S = args.streams or 2048
         mem = memory.BlockMemory(S, 4, 64, 128, dtype=bf, device=dev)

@@ -42,6 +42,9 @@ extern "C" int gfst_check_device_errors(int clear) {
   st = gfst::read_score_error(clear, &w);
   if (st != GFST_OK) return st;
   v = v != 0 ? v : w;
+  st = gfst::read_scan_error(clear, &w);
+  if (st != GFST_OK) return st;
+  v = v != 0 ? v : w;
   if (v != 0) {
     gfst::set_last_error("a kernel gave up a bounded wait (device error word %u)", v);
     return (int)v;

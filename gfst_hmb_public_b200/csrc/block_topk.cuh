@@ -96,6 +96,7 @@ int read_device_error(int clear, unsigned int* value);
 int read_readout_error(int clear, unsigned int* value);  // exact_readout.cu
 int read_commit_error(int clear, unsigned int* value);   // block_commit_eig.cu
 int read_score_error(int clear, unsigned int* value);    // block_score.cu
+int read_scan_error(int clear, unsigned int* value);     // mpuc_scan.cu
 int launch_bounded_wait_probe(long long budget, cudaStream_t stream);  // block_topk_tc.cu
 
 int block_topk_simt(const void* Q, const void* Ksum, int64_t S, int Nq, int NB, int NBs, int d, int k, int dtype,

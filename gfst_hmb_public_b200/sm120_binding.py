@@ -15,9 +15,12 @@ callers to the sm_100a kernels of this package:
 * ``exact_block_materialize``  the packed-store slice (state.py:568)
 * ``segmented_max_by_group`` / ``segmented_logsumexp_occurrence``
                                the readout collapse reductions (perf.py:153, 189)
+* ``mpuc_recurrent_scan``      the MPUC recurrent scan (modeling.py:4424-4430),
+                               for blocks registered with
+                               ``install_mpuc_recurrent_scan``
 
 The operators without a kernel here (the eigenpair-to-summary helpers, the
-extension loaders and reports, the MPUC recurrent scan) return ``None`` or
+extension loaders and reports) return ``None`` or
 ``False``, which the reference's callers treat as "not available" and answer
 with their own torch code, exactly as they do when an sm_120 extension is
 missing.  Every operator given CPU tensors raises RuntimeError (there is no
@@ -25,9 +28,11 @@ CPU path), as the reference's extension checks do.
 """
 from __future__ import annotations
 
+import threading
+
 import torch
 
-from . import block_commit, gfst, memory, readout
+from . import block_commit, gfst, memory, mpuc, readout
 
 
 def _cuda() -> bool:
@@ -56,7 +61,7 @@ def experimental_canonical_summary_enabled() -> bool:
 
 
 def mpuc_recurrent_scan_available() -> bool:
-    return False
+    return _cuda()
 
 
 # ---- operators with a B200 kernel -------------------------------------------
@@ -133,4 +138,51 @@ load_sm120_extension = _unavailable
 load_mathdx_extension = _unavailable
 mathdx_extension_dependency_report = _unavailable
 mathdx_runtime_dependency_report = _unavailable
-mpuc_recurrent_scan = _unavailable
+
+
+# ---- the MPUC recurrent scan -------------------------------------------------
+# The reference calls mpuc_recurrent_scan(normalized, fast_inputs, mid_inputs,
+# slow_inputs) from MpucGfstHmbBlock._forward_sequence (modeling.py:4424-4430)
+# without the cell's weights; install_mpuc_recurrent_scan registers a block so
+# that, while its _forward_sequence runs, the op finds that block's weights.
+_active = threading.local()
+
+
+def mpuc_recurrent_scan(normalized, fast_inputs, mid_inputs, slow_inputs):
+    """runtime_backends.mpuc_recurrent_scan (csrc/sm120_stub.cu:210-224): the
+    outputs, boundary logits and final fast / mid / slow states of
+    _forward_sequence_tensors (modeling.py:4449-4476), the recurrence on the
+    B200 scan kernel and the output projection batched over all tokens.
+    Returns None -- the caller's "not available", after which it runs its own
+    compiled path -- when no block registered with install_mpuc_recurrent_scan
+    is running on this thread."""
+    cell = getattr(_active, "cell", None)
+    if cell is None:
+        return None
+    states, logits, fast, mid, slow = mpuc.recurrent_scan(cell, fast_inputs, mid_inputs, slow_inputs)
+    out = mpuc.output_projection(cell, normalized, states)
+    dt = normalized.dtype
+    return out.to(dt), logits.to(dt), fast.to(dt), mid.to(dt), slow.to(dt)
+
+
+def install_mpuc_recurrent_scan(block) -> "mpuc.MpucCellWeights":
+    """Send ``block``'s recurrent scan (an MpucGfstHmbBlock) through the B200
+    kernel: pack its weights on the current CUDA device (once: re-install after
+    the parameters change), select the reference's own "sm120_cutlass" backend
+    (set_recurrent_kernel_backend, modeling.py:4494-4508) and wrap the block's
+    _forward_sequence so that mpuc_recurrent_scan sees these weights while it
+    runs."""
+    weights = mpuc.MpucCellWeights.from_module(block)
+    inner = block._forward_sequence
+
+    def forward_sequence(normalised):
+        prev = getattr(_active, "cell", None)
+        _active.cell = weights
+        try:
+            return inner(normalised)
+        finally:
+            _active.cell = prev
+
+    block._forward_sequence = forward_sequence
+    block.set_recurrent_kernel_backend("sm120_cutlass")
+    return weights

@@ -140,3 +140,35 @@ def token_tensors(n: int, T: int, d: int, *, seed: int, device="cpu", dtype=torc
     g = _gen(device, seed)
     return [torch.randn((n, T, d), generator=g, device=device, dtype=torch.float32).to(dtype).contiguous()
             for _ in range(count)]
+
+
+def mpuc_cell_weights(hidden: int, *, seed: int, device="cpu"):
+    """Weights of an MPUC cell of width ``hidden`` with the reference's sizes
+    (MpucGfstHmbBlock.__init__, modeling.py:4259-4315 of
+    pkhairkh/gfst-hmb-public: fast H/2, mid H/4, slow the rest, bridge and
+    semantic rank max(64, H/16), boundary hidden max(8, H/16)) and nn.Linear's
+    default scale (uniform in +-1/sqrt(fan_in)), as an mpuc.MpucCellWeights."""
+    from .mpuc import MpucCellWeights
+
+    g = _gen("cpu", seed)
+    H = int(hidden)
+    F, M = H // 2, H // 4
+    S = H - F - M
+    C = SR = max(64, H // 16)
+    BH = max(8, H // 16)
+
+    def lin(o, i):
+        return (torch.rand((o, i), generator=g) * 2 - 1) / math.sqrt(i)
+
+    def bias(o, i):
+        return (torch.rand((o,), generator=g) * 2 - 1) / math.sqrt(i)
+
+    w = {"fast_gate_w": lin(F, F), "fast_gate_b": bias(F, F), "fast_cand_w": lin(F, F), "fast_cand_b": bias(F, F),
+         "mid_gate_w": lin(M, M), "mid_gate_b": bias(M, M), "mid_cand_w": lin(M, M), "mid_cand_b": bias(M, M),
+         "slow_gate_w": lin(S, S), "slow_gate_b": bias(S, S), "slow_cand_w": lin(S, S), "slow_cand_b": bias(S, S),
+         "fm_down": lin(C, M), "fm_up": lin(F, C), "fs_down": lin(C, S), "fs_up": lin(F, C),
+         "mf_down": lin(C, F), "mf_up": lin(M, C), "ms_down": lin(C, S), "ms_up": lin(M, C),
+         "sf_down": lin(C, F), "sf_up": lin(S, C), "sm_down": lin(C, M), "sm_up": lin(S, C),
+         "bnd_w1": lin(BH, 4), "bnd_b1": bias(BH, 4), "bnd_w2": lin(1, BH), "bnd_b2": bias(1, BH),
+         "sem_in": lin(SR, H), "sem_cond": lin(SR, M + S), "sem_out": lin(H, SR), "fusion": lin(H, H)}
+    return MpucCellWeights(w, device)

@@ -522,6 +522,54 @@ GFST_API int gfst_heev(const void* matrices, int64_t batch, int d, int dtype, vo
 GFST_API int gfst_exact_block_materialize(const void* packed, int64_t n_elements, int elem_size, int64_t start,
                        int64_t end, void* out, cudaStream_t stream);
 
+/* ---- MPUC recurrent scan ------------------------------------------------------
+ * The token loop of MpucGfstHmbBlock._forward_sequence_tensors
+ * (src/gfst_hmb_mpuc/modeling.py:4449-4476; cell _token_step 4363-4411,
+ * _update_band 4343-4356, bridges up(silu(down(x))) 4182-4183).  Replaces the
+ * reference's native mpuc_recurrent_scan_forward(normalized, fast_inputs,
+ * mid_inputs, slow_inputs) (csrc/sm120_stub.cu:210-224, caller
+ * modeling.py:4424), which takes no weights and returns zeros: this entry
+ * point takes the cell's weights.  Widths: fast F, mid M, slow S, bridge rank
+ * C, boundary MLP hidden width Bh.  Weights are fp32 in nn.Linear layout
+ * ([out, in] row-major, 16-byte aligned matrices):                           */
+typedef struct gfst_mpuc_weights {
+  const float *fast_gate_w, *fast_gate_b, *fast_cand_w, *fast_cand_b; /* [F, F], [F]     */
+  const float *mid_gate_w, *mid_gate_b, *mid_cand_w, *mid_cand_b;     /* [M, M], [M]     */
+  const float *slow_gate_w, *slow_gate_b, *slow_cand_w, *slow_cand_b; /* [S, S], [S]     */
+  const float *fm_down, *fm_up; /* fast_from_mid:  [C, M], [F, C]                      */
+  const float *fs_down, *fs_up; /* fast_from_slow: [C, S], [F, C]                      */
+  const float *mf_down, *mf_up; /* mid_from_fast:  [C, F], [M, C]                      */
+  const float *ms_down, *ms_up; /* mid_from_slow:  [C, S], [M, C]                      */
+  const float *sf_down, *sf_up; /* slow_from_fast: [C, F], [S, C]                      */
+  const float *sm_down, *sm_up; /* slow_from_mid:  [C, M], [S, C]                      */
+  const float *bnd_w1, *bnd_b1, *bnd_w2, *bnd_b2; /* boundary MLP: [Bh, 4], [Bh], [1, Bh], [1] */
+} gfst_mpuc_weights;
+
+/* Workspace bytes gfst_mpuc_recurrent_scan needs for this batch and widths. */
+GFST_API int gfst_mpuc_scan_workspace_bytes(int64_t batch, int fast_dim, int mid_dim, int slow_dim,
+                                            int cross_rank, size_t* bytes);
+
+/* For each batch element b and token t in order (fp32 throughout):
+ *   the recurrence of _token_step on fast_in [batch, T, F], mid_in
+ *   [batch, T, M], slow_in [batch, T, S] (the three branch outputs);
+ *   states_out [batch, T, F + M + S] = (fast, mid, slow) after token t;
+ *   boundary_out [batch, T] = the boundary logit of token t.
+ * fast_state [batch, F], mid_state [batch, M], slow_state [batch, S] hold the
+ * states before the first token on entry (zeros for a new sequence, as
+ * _forward_sequence_tensors starts) and after the last on return.  The output
+ * projection (fusion_proj + semantic residual) is not applied: it does not
+ * feed back and is one batched product over all tokens.  workspace: at least
+ * gfst_mpuc_scan_workspace_bytes (16-byte aligned); it also carries the grid
+ * barrier, so concurrent calls need separate workspaces.  One cooperative
+ * launch (one CTA per SM) per 8 batch elements.  Limits: F, M, S, C multiples
+ * of 4; max(F, M + S, 2 C) <= 6144; T <= 2^20.                               */
+GFST_API int gfst_mpuc_recurrent_scan(const gfst_mpuc_weights* weights, int fast_dim, int mid_dim,
+                                      int slow_dim, int cross_rank, int boundary_hidden,
+                                      const float* fast_in, const float* mid_in, const float* slow_in,
+                                      int64_t batch, int T, float* states_out, float* boundary_out,
+                                      float* fast_state, float* mid_state, float* slow_state,
+                                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -111,3 +111,53 @@ def load(module: str, pkg_dir: Path | str | None = None, backend: types.ModuleTy
         raise FileNotFoundError("no copy of the reference package (baseline/_ref or $GFST_REFERENCE_SRC)")
     install(pkg_dir, backend)
     return importlib.import_module(f"gfst_hmb_mpuc.{module}")
+
+
+def reference_mpuc_cell(modeling, hidden: int, seed: int):
+    """A reference MpucGfstHmbBlock that holds only its recurrent cell: the
+    submodules that _forward_sequence / _forward_sequence_tensors use
+    (modeling.py:4417-4476), built with the reference's own constructors and
+    sizes (MpucGfstHmbBlock.__init__, modeling.py:4259-4315: fast = H/2,
+    mid = H/4, slow = the rest, cross and semantic rank max(64, H/16),
+    boundary hidden max(8, H/16), branch specs (3, 1), (5, 2), (9, 4)), with
+    nn.Linear's default initialisation under torch.manual_seed(seed).  The
+    GFST sublayer is left out (the cell never touches it)."""
+    import torch
+
+    nn = torch.nn
+    cls = modeling.MpucGfstHmbBlock
+    torch.manual_seed(seed)
+    blk = cls.__new__(cls)
+    nn.Module.__init__(blk)
+    H = int(hidden)
+    blk.hidden_size = H
+    blk.fast_dim, blk.mid_dim = H // 2, H // 4
+    blk.slow_dim = H - blk.fast_dim - blk.mid_dim
+    blk.cross_rank = max(64, H // 16)
+    blk.semantic_rank = max(64, H // 16)
+    F, M, S, C = blk.fast_dim, blk.mid_dim, blk.slow_dim, blk.cross_rank
+    br = modeling._CausalDepthwiseBranch
+    blk.fast_branch = br(H, F, kernel_size=3, dilation=1)
+    blk.mid_branch = br(H, M, kernel_size=5, dilation=2)
+    blk.slow_branch = br(H, S, kernel_size=9, dilation=4)
+    lr = modeling._LowRankBridge
+    blk.fast_from_mid, blk.fast_from_slow = lr(M, F, C), lr(S, F, C)
+    blk.mid_from_fast, blk.mid_from_slow = lr(F, M, C), lr(S, M, C)
+    blk.slow_from_fast, blk.slow_from_mid = lr(F, S, C), lr(M, S, C)
+    blk.fast_gate_proj, blk.fast_cand_proj = nn.Linear(F, F), nn.Linear(F, F)
+    blk.mid_gate_proj, blk.mid_cand_proj = nn.Linear(M, M), nn.Linear(M, M)
+    blk.slow_gate_proj, blk.slow_cand_proj = nn.Linear(S, S), nn.Linear(S, S)
+    bh = max(8, H // 16)
+    blk.boundary_mlp = nn.Sequential(nn.Linear(4, bh), nn.SiLU(), nn.Linear(bh, 1))
+    blk.semantic_in = nn.Linear(H, blk.semantic_rank, bias=False)
+    blk.semantic_cond = nn.Linear(M + S, blk.semantic_rank, bias=False)
+    blk.semantic_out = nn.Linear(blk.semantic_rank, H, bias=False)
+    blk.fusion_proj = nn.Linear(H, H, bias=False)
+    blk.recurrent_kernel_backend = "native"
+    blk.recurrent_compile_mode = "max-autotune-no-cudagraphs"
+    blk.runtime_profiler_mode = "off"
+    blk._runtime_profile_recorder = None
+    blk._compiled_forward_sequence_impl = None
+    blk.last_forward_stats = None
+    blk.last_boundary_logits = None
+    return blk

@@ -51,6 +51,7 @@ def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=None,
                         help="root of a reference source checkout (default: baseline/_ref or $GFST_REFERENCE_SRC)")
+    parser.add_argument("--only", choices=["mpuc"], default=None, help="write one fixture only")
     args = parser.parse_args()
     sys.path.insert(0, str(REPO))
     from oracle import reference_import
@@ -58,6 +59,10 @@ def main() -> None:
     pkg_dir = (Path(args.reference) / "src" / "gfst_hmb_mpuc") if args.reference else reference_import.find_reference()
     if pkg_dir is None or not (pkg_dir / "gfst.py").is_file():
         raise SystemExit("no copy of the reference: pass --reference <checkout root> or install it under baseline/_ref")
+    if args.only == "mpuc":
+        install_reference(pkg_dir)
+        make_mpuc_fixture(importlib.import_module("gfst_hmb_mpuc.modeling"))
+        return
     install_reference(pkg_dir)
     gfst = importlib.import_module("gfst_hmb_mpuc.gfst")
     retrieval = importlib.import_module("gfst_hmb_mpuc.retrieval")
@@ -310,6 +315,7 @@ def main() -> None:
     np.savez(OUT / "block_commit_eig_cases.npz", **out)
     make_centroid_fixture(modeling, state_mod)
     make_store_and_topk_fixtures()
+    make_mpuc_fixture(modeling)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
@@ -462,6 +468,38 @@ def make_store_and_topk_fixtures() -> None:
         topk_out[f"c{ci}_all_scores"] = (keys @ q).float().numpy()
     np.savez(OUT / "retrieval_exact_topk_bf16.npz", **topk_out)
 
+
+
+def make_mpuc_fixture(modeling) -> None:
+    """13. The MPUC recurrent cell: MpucGfstHmbBlock._forward_sequence_tensors
+    (modeling.py:4449-4476) with _token_step / _update_band /
+    _semantic_residual (4343-4411), called on a block that holds only the
+    cell (oracle.reference_import.reference_mpuc_cell: the reference's own
+    constructors and sizes, nn.Linear's default initialisation under a fixed
+    seed).  Stored: the branch outputs the scan consumes, the normalised
+    tokens, every weight, and the reference's five outputs."""
+    sys.path.insert(0, str(REPO))
+    from oracle import mpuc_oracle, reference_import
+
+    cls = modeling.MpucGfstHmbBlock
+    out = {}
+    for tag, H, B, T, seed in (("h64", 64, 3, 40, 901), ("h128", 128, 2, 24, 902)):
+        blk = reference_import.reference_mpuc_cell(modeling, H, seed)
+        g = torch.Generator().manual_seed(seed + 1)
+        normalised = torch.randn((B, T, H), generator=g)
+        with torch.no_grad():
+            fin = blk.fast_branch.forward_sequence(normalised)
+            mid_in = blk.mid_branch.forward_sequence(normalised)
+            sin = blk.slow_branch.forward_sequence(normalised)
+            outs = cls._forward_sequence_tensors(blk, normalised)
+        params = dict(blk.named_parameters())
+        for short, full in mpuc_oracle.WEIGHT_NAMES.items():
+            out[f"{tag}_{short}"] = params[full].detach().numpy()
+        out[f"{tag}_normalised"] = normalised.numpy()
+        out[f"{tag}_fast_in"], out[f"{tag}_mid_in"], out[f"{tag}_slow_in"] = fin.numpy(), mid_in.numpy(), sin.numpy()
+        for name, v in zip(("outputs", "boundary_logits", "fast", "mid", "slow"), outs):
+            out[f"{tag}_{name}"] = v.detach().numpy()
+    np.savez(OUT / "mpuc_scan.npz", tags=np.array(["h64", "h128"]), **out)
 
 if __name__ == "__main__":
     main()

@@ -72,8 +72,20 @@ def test_host_validation_rejects_without_launching():
     buf = (ctypes.c_float * 4096)()
     p = ctypes.cast(buf, ctypes.c_void_p)
     assert lib.gfst_frame_stream_ex(None, None, None, 1.0, 4, 8, 64, 8, 4, 1e-8, 0, None, 0, 7, None) == 1
-    assert lib.gfst_frame_stream_ex(p, p, p, 1.0, 4, 8, 64, 8, 4, 1e-8, 0, None, 0, 2, None) == 2
+    assert lib.gfst_frame_stream_ex(p, p, p, 1.0, 4, 8, 64, 8, 4, 1e-8, 0, None, 0, 3, None) == 2
     assert b"CholeskyQR2" in lib.gfst_last_error()
+    assert lib.gfst_frame_stream_ex(p, p, p, 1.0, 4, 8, 8, 8, 4, 1e-8, 0, None, 0, 2, None) == 2
+    assert b"CholeskyQR2" in lib.gfst_last_error()
+    # MPUC scan: widths not multiples of 4, stage too wide, no workspace (the
+    # call returns before touching the device)
+    from gfst_hmb_public_b200 import mpuc
+
+    wts = mpuc._WeightsC(**{n: ctypes.cast(buf, ctypes.c_void_p).value for n, _ in mpuc.WEIGHT_FIELDS})
+    wp = ctypes.addressof(wts)
+    assert lib.gfst_mpuc_recurrent_scan(wp, 30, 16, 16, 64, 8, p, p, p, 2, 4, p, p, p, p, p, p, 4096, None) == 2
+    assert lib.gfst_mpuc_recurrent_scan(wp, 8192, 16, 16, 64, 8, p, p, p, 2, 4, p, p, p, p, p, p, 4096, None) == 2
+    assert lib.gfst_mpuc_recurrent_scan(None, 32, 16, 16, 64, 8, p, p, p, 2, 4, p, p, p, p, p, p, 4096, None) == 1
+    assert lib.gfst_mpuc_recurrent_scan(wp, 32, 16, 16, 64, 8, p, p, p, 0, 4, p, p, p, p, p, p, 0, None) == 0
     # centroid cell write: L * W too large, too many cells, null buffers, empty
     assert lib.gfst_centroid_cell_commit(None, None, None, None, 4, 512, 4, 16, 32, 16, None, None, None, None,
                                          None, None) == 2

@@ -157,3 +157,41 @@ def test_block_commit_replay_candidate_is_clean(cuda_device, ref):
             # only the device-formed projectors are past 1e-8
             assert max(deltas.values()) > clean
             assert max(summary["average_projector_max_abs"], summary["reduced_mean_max_abs"]) <= clean
+
+
+def test_reference_mpuc_block_runs_the_scan_kernel(cuda_device, ref):
+    # the reference's own MpucGfstHmbBlock._forward_sequence with its
+    # "sm120_cutlass" backend calls runtime_backends.mpuc_recurrent_scan
+    # (modeling.py:4424-4430); registered with install_mpuc_recurrent_scan,
+    # that is the B200 scan, and it gives what the reference's own
+    # _forward_sequence_tensors gives on the CPU
+    modeling = ref.import_module("gfst_hmb_mpuc.modeling")
+    blk = reference_import.reference_mpuc_cell(modeling, 128, 31)
+    g = torch.Generator().manual_seed(32)
+    normalised = torch.randn((3, 20, 128), generator=g)
+    with torch.no_grad():
+        want = modeling.MpucGfstHmbBlock._forward_sequence_tensors(blk, normalised)
+    blk = blk.to(cuda_device)
+    # no block registered: "not available", the caller keeps its own path
+    assert sm120_binding.mpuc_recurrent_scan(normalised.to(cuda_device), None, None, None) is None
+    sm120_binding.install_mpuc_recurrent_scan(blk)
+    assert blk.recurrent_kernel_backend == "sm120_cutlass"
+    calls = []
+    inner = sm120_binding.mpuc.recurrent_scan
+
+    def counting(*a, **k):
+        calls.append(1)
+        return inner(*a, **k)
+
+    sm120_binding.mpuc.recurrent_scan = counting
+    try:
+        with torch.no_grad():
+            outputs, logits, cache = blk._forward_sequence(normalised.to(cuda_device))
+    finally:
+        sm120_binding.mpuc.recurrent_scan = inner
+    assert calls, "the reference's call site did not reach the B200 scan"
+    for got, exp in ((outputs, want[0]), (logits, want[1]), (cache.fast_state, want[2]), (cache.mid_state, want[3]),
+                     (cache.slow_state, want[4])):
+        got = got.cpu().numpy()
+        exp = exp.numpy()
+        assert np.abs(got - exp).max() <= 1e-4 * max(1.0, float(np.abs(exp).max()))

@@ -299,3 +299,25 @@ def test_exact_topk_bf16_matches_reference():
         for j in range(1, k):
             if sc[j] == sc[j - 1]:
                 assert idx[j] > idx[j - 1]
+
+
+def mpuc_case(z, tag):
+    from oracle import mpuc_oracle as mo
+
+    w = {k: z[f"{tag}_{k}"] for k in mo.WEIGHT_NAMES}
+    return w, z[f"{tag}_normalised"], z[f"{tag}_fast_in"], z[f"{tag}_mid_in"], z[f"{tag}_slow_in"]
+
+
+def test_mpuc_scan_oracle_matches_reference():
+    # the reference's own _forward_sequence_tensors (modeling.py:4449-4476) on
+    # two cell sizes; float32 matmuls sum in a different order -> 1e-5
+    from oracle import mpuc_oracle as mo
+
+    z = load("mpuc_scan.npz")
+    for tag in z["tags"]:
+        w, x, fin, mid, sin = mpuc_case(z, str(tag))
+        got = mo.forward_sequence_tensors(w, x, fin, mid, sin)
+        for name, v in zip(("outputs", "boundary_logits", "fast", "mid", "slow"), got):
+            ref = z[f"{tag}_{name}"]
+            assert v.shape == ref.shape, name
+            assert np.abs(v - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max()), (tag, name)
