@@ -27,6 +27,9 @@ measurement runs on a device heap that an earlier one shaped:
   stream_mid   16 x 16 streams, 4096 tokens, 128 x 16 frames, rank 2, L=64,
                64 blocks, top-4, bf16 (one GPU)
   batched_qr   65,536 frames of 64 x 8, one QR each (frames/s; one GPU)
+  mpuc_scan    the MPUC recurrent scan at d_model 2048, 8 sequences x 256 tokens
+               (sequence-tokens/s; one GPU), with the reference's own torch path
+               on this GPU and on the host cores beside it
 
 Timing: W warm-up steps, then exactly K steps between a barrier + synchronize
 on both sides, CUDA events on the launching stream, the maximum over ranks.
@@ -445,7 +448,7 @@ def run_stream_pass(spec, device, repeats: int = 3) -> dict:
 
 
 def run_extras(device) -> dict:
-    """The one-GPU sub-results: stream_small, stream_mid, batched_qr."""
+    """The one-GPU sub-results: stream_small, stream_mid, batched_qr, mpuc_scan."""
     import torch
 
     from gfst_hmb_public_b200 import gfst, workloads as wl
@@ -495,7 +498,98 @@ def run_extras(device) -> dict:
         "workload": "65,536 frames 64x8 fp32, column j x 10^(-j/2), 1% near-collinear pairs; L2 flushed",
         "roofline": {"bound": "hbm", "achieved": round(qr_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(qr_gbs / hbm_peak, 4), "peak_source": peak_src}}
+    out["mpuc_scan"] = run_mpuc_scan(device)
     return out
+
+
+def run_mpuc_scan(device, B: int = 8, T: int = 256, H: int = 2048) -> dict:
+    """The MPUC recurrent scan at the reference model's width (d_model 2048:
+    fast 1024, mid 512, slow 512, bridge rank 128): B sequences x T tokens.
+    The cell comes from the reference's own constructors when a copy of the
+    reference is present (else the same sizes and initial scale).  Timed: the
+    scan kernel alone, and the whole _forward_sequence_tensors replacement
+    (branches, scan, output projection).  Beside it: the reference's own
+    _forward_sequence_tensors (torch, token by token) on this GPU over the
+    first 32 tokens, and on the host cores over the first 64."""
+    import torch
+
+    from gfst_hmb_public_b200 import mpuc, workloads as wl
+
+    modeling = None
+    try:
+        from oracle import reference_import
+
+        if reference_import.find_reference() is not None:
+            modeling = reference_import.load("modeling")
+    except Exception:
+        modeling = None
+    g = torch.Generator().manual_seed(SEED + 50)
+    normalised = torch.randn((B, T, H), generator=g)
+    res = {"workload": f"MPUC recurrent cell, d_model {H} (fast {H // 2}, mid {H // 4}, slow {H // 4}, bridge rank "
+                       f"{max(64, H // 16)}), {B} sequences x {T} tokens, fp32",
+           "unit": "sequence-tokens/s"}
+    if modeling is not None:
+        blk = reference_import.reference_mpuc_cell(modeling, H, SEED + 51).to(device)
+        cell = mpuc.MpucCellWeights.from_module(blk, device=device)
+    else:
+        blk = None
+        cell = wl.mpuc_cell_weights(H, seed=SEED + 51, device=device)
+    x = normalised.to(device)
+    if blk is not None:
+        with torch.no_grad():
+            ins = [blk.fast_branch.forward_sequence(x), blk.mid_branch.forward_sequence(x),
+                   blk.slow_branch.forward_sequence(x)]
+    else:
+        ins = [torch.randn((B, T, n), generator=g).to(device) for n in (cell.F, cell.M, cell.S)]
+
+    def timed(fn, reps=3):
+        fn()
+        torch.cuda.synchronize(device)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            best = min(best, e0.elapsed_time(e1))
+        return best
+
+    scan_ms = timed(lambda: mpuc.recurrent_scan(cell, *ins))
+    res["value"] = round(B * T / (scan_ms / 1e3), 1)
+    res["scan_ms"] = round(scan_ms, 3)
+    res["us_per_token"] = round(scan_ms * 1e3 / T, 2)
+    w_floats = 2 * (cell.F ** 2 + cell.M ** 2 + cell.S ** 2) + 4 * cell.C * cell.hidden
+    res["roofline"] = {"bound": "latency",
+                       "note": "nine dependent grid-wide stages per token (one cooperative launch, bounded grid "
+                               f"barriers); the {w_floats} recurrent weights ({w_floats * 4 / 1e6:.1f} MB fp32) "
+                               "are re-read from L2 every token",
+                       "weight_gbs_from_l2": round(w_floats * 4 / (scan_ms / 1e3 / T) / 1e9, 1)}
+    if blk is not None:
+        with torch.no_grad():
+            full_ms = timed(lambda: mpuc.forward_sequence_tensors(blk, x, cell), reps=2)
+            res["forward_sequence_ms"] = round(full_ms, 3)
+            Tr = 32
+            xr = x[:, :Tr].contiguous()
+            ref_ms = timed(lambda: modeling.MpucGfstHmbBlock._forward_sequence_tensors(blk, xr), reps=1)
+        res["reference_torch_cuda"] = {"value": round(B * Tr / (ref_ms / 1e3), 1), "unit": "sequence-tokens/s",
+                                       "sample": f"the reference's own _forward_sequence_tensors on this GPU "
+                                                 f"(torch, token by token), {B} x {Tr} tokens"}
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        blk_cpu = reference_import.reference_mpuc_cell(modeling, H, SEED + 51)
+        Tc = 64
+        xc = normalised[:, :Tc].contiguous()
+        with torch.no_grad():
+            modeling.MpucGfstHmbBlock._forward_sequence_tensors(blk_cpu, xc[:, :2])
+            t0 = time.perf_counter()
+            modeling.MpucGfstHmbBlock._forward_sequence_tensors(blk_cpu, xc)
+            dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": round(B * Tc / dt, 1), "unit": "sequence-tokens/s", "cores": threads,
+                               "kind": "reference",
+                               "sample": f"the reference's own _forward_sequence_tensors on the host cores, "
+                                         f"{B} x {Tc} tokens in {dt:.2f} s"}
+    return res
 
 
 # ---------------------------------------------------------------------------
