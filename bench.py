@@ -443,7 +443,24 @@ def run_stream_pass(spec, device, repeats: int = 3) -> dict:
     _native.check_device_errors()
     ms = statistics.median(times)
     ph = {k: round(v * n_steps, 4) for k, v in phases.summary().items()}
-    return {"tokens_per_s": round(spec.batch * T / (ms / 1e3), 1), "ms_per_pass": round(ms, 4),
+    # the same pass captured once as a CUDA graph (step.StreamingPass) and replayed
+    sp = stp.StreamingPass(st, U0, blocks)
+    gtimes = []
+    for _ in range(repeats):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        e0.record()
+        sp.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        gtimes.append(e0.elapsed_time(e1))
+    _native.check_device_errors()
+    gms = statistics.median(gtimes)
+    del sp
+    return {"tokens_per_s": round(spec.batch * T / (gms / 1e3), 1), "ms_per_pass": round(gms, 4),
+            "method": "one pass captured as a CUDA graph (step.StreamingPass), replayed",
+            "eager": {"tokens_per_s": round(spec.batch * T / (ms / 1e3), 1), "ms_per_pass": round(ms, 4),
+                      "method": "StreamingStep.step per block from Python"},
             "steps_per_pass": n_steps, "kernel_ms_per_pass": ph, "passes": repeats}
 
 

@@ -110,8 +110,10 @@ class StreamingStep:
         cur.wait_stream(self.frames_stream)
         cur.wait_stream(self.memory_stream)
         # tensors produced on side streams are consumed on the current stream
-        for t in (best_tok, best_score, value, top_i, self.U):
-            t.record_stream(cur)
+        # (under CUDA-graph capture the graph's private pool keeps them instead)
+        if not torch.cuda.is_current_stream_capturing():
+            for t in (best_tok, best_score, value, top_i, self.U):
+                t.record_stream(cur)
         if self.check_errors:
             nat.check_device_errors()
         result = StepOutputs(best_tok, best_score, value, top_i, self.open_base, slot)
@@ -123,6 +125,50 @@ class StreamingStep:
             out.open_base, out.slot = self.open_base, slot
             return out
         return result
+
+
+class StreamingPass:
+    """A whole streaming pass captured once as a CUDA graph and replayed.
+
+    The pass is: empty the memory ring, load the frames ``U0``, then one
+    ``StreamingStep.step`` per block of ``blocks`` (each an (A, B, K, V, Q)
+    tuple of device tensors, as ``step`` takes them).  At small batches the
+    pass is a chain of short kernels whose launch cost exceeds their run time;
+    replaying the captured graph launches them all at once.  The input tensors
+    (``U0`` and every block) are read in place on each replay: copy new data
+    into them, not new tensors.  ``outputs[i]`` holds block i's StepOutputs
+    after each replay (the same tensors every time).  The capture follows one
+    eager pass (which allocates and configures every kernel); the step must
+    not synchronise (``check_errors`` off).
+    """
+
+    def __init__(self, step: StreamingStep, U0: torch.Tensor, blocks):
+        if step.check_errors:
+            raise ValueError("StreamingPass: a step with check_errors=True synchronises and cannot be captured")
+        self.step_obj = step
+        self.U0 = U0
+        self.blocks = [tuple(b) for b in blocks]
+        dev = step.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            self._run()                       # eager: allocations, kernel attributes
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.outputs = self._run()
+
+    def _run(self):
+        st = self.step_obj
+        st.reset()
+        st.set_frames(self.U0)
+        return [st.step(*blk) for blk in self.blocks]
+
+    def replay(self) -> list:
+        """Run the pass again on the current stream; returns ``outputs``."""
+        self.graph.replay()
+        return self.outputs
 
 
 class HostPipeline:

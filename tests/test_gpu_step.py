@@ -55,3 +55,42 @@ def test_host_pipeline_matches_device_steps(cuda_device):
     # the frames are still orthonormal after five 64-token blocks
     eye = torch.eye(r)
     assert (st.U.cpu().transpose(1, 2) @ st.U.cpu() - eye).abs().max() < 1e-5
+
+
+@pytest.mark.parametrize("shape", ["small_fp32", "mid_bf16"])
+def test_graph_captured_pass_matches_eager_pass(cuda_device, shape):
+    # a whole pass (empty ring -> frames -> one step per block) captured once
+    # as a CUDA graph and replayed twice gives, bit for bit, what the eager
+    # pass gives; the ring wraps in the bf16 case (6 blocks into 4 slots)
+    from gfst_hmb_public_b200.step import StreamingPass
+
+    if shape == "small_fp32":
+        S, d, r, m, L, n_slots, k, n_blk, dt = 8, 64, 8, 1, 16, 16, 2, 5, torch.float32
+    else:
+        S, d, r, m, L, n_slots, k, n_blk, dt = 10, 128, 16, 2, 64, 4, 3, 6, torch.bfloat16
+    g = torch.Generator().manual_seed(55)
+    blocks = []
+    for _ in range(n_blk):
+        A = torch.randn((S, L, d, m), generator=g) / d ** 0.5
+        B = torch.randn((S, L, r, m), generator=g) / d ** 0.5
+        K, V, Q = (torch.randn((S, L, d), generator=g).to(dt) for _ in range(3))
+        blocks.append(tuple(t.to(cuda_device) for t in (A, B, K, V, Q)))
+    U0 = wl.random_orthonormal_frames(S, d, r, seed=56, device=cuda_device)
+
+    eager = StreamingStep(S, d=d, r=r, block_len=L, n_slots=n_slots, k=k, dtype=dt, device=cuda_device)
+    eager.set_frames(U0)
+    want = []
+    for blk in blocks:
+        o = eager.step(*blk)
+        want.append([t.clone() for t in (o.best_tok, o.best_score, o.value, o.top_idx)])
+    torch.cuda.synchronize()
+
+    st = StreamingStep(S, d=d, r=r, block_len=L, n_slots=n_slots, k=k, dtype=dt, device=cuda_device)
+    sp = StreamingPass(st, U0, blocks)
+    for _ in range(2):
+        outs = sp.replay()
+        torch.cuda.synchronize()
+        for o, w in zip(outs, want):
+            for got, exp in zip((o.best_tok, o.best_score, o.value, o.top_idx), w):
+                assert torch.equal(got, exp)
+        assert torch.equal(st.U, eager.U)
