@@ -192,49 +192,62 @@ def sharded_readout(Q: torch.Tensor, summary: torch.Tensor, pool_K: torch.Tensor
 
 def _exchange_replicated(bv: torch.Tensor, owner: torch.Tensor, mine: torch.Tensor, world: int, group):
     """Every rank ends with every winner's value row: each owner contributes its
-    rows (query order) padded to the largest owner's count; one all-gather."""
-    dv = bv.shape[-1]
-    counts = [int(c) for c in torch.bincount(owner[owner >= 0].reshape(-1), minlength=world).tolist()]
+    rows (query order) padded to the largest owner's count; one all-gather.
+    The per-owner counts come to the host in one copy (the collective's size)."""
+    S, Nq, dv = bv.shape
+    own_flat = owner.reshape(-1)
+    key = torch.where(own_flat >= 0, own_flat, torch.full_like(own_flat, world))
+    counts = torch.bincount(key, minlength=world + 1)[:world].tolist()  # the one host sync
     width = max(max(counts), 1)
+    mine_flat = mine.reshape(-1)
+    n_mine = counts[dist.get_rank(group)]
+    # this rank's rows in query order: a stable sort puts them first
+    order = torch.argsort((~mine_flat).to(torch.int8), stable=True)[:n_mine]
     send = torch.zeros((width, dv), dtype=bv.dtype, device=bv.device)
-    rows = bv[mine]
-    send[:rows.shape[0]] = rows
+    send[:n_mine] = bv.reshape(S * Nq, dv)[order]
     parts = torch.empty((world, width, dv), dtype=bv.dtype, device=bv.device)
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(parts, send, group=group)
     else:  # gloo has no all_gather_into_tensor
         dist.all_gather(list(parts.unbind(0)), send, group=group)
-    value = torch.zeros_like(bv)
+    # row j of owner r's part is owner r's j-th winner in query order
+    by_owner = torch.argsort(key, stable=True)
+    starts = [0]
+    for c in counts:
+        starts.append(starts[-1] + c)
+    value = torch.zeros((S * Nq, dv), dtype=bv.dtype, device=bv.device)
     for r in range(world):
         if counts[r]:
-            value[owner == r] = parts[r, :counts[r]]
-    return value
+            value[by_owner[starts[r]:starts[r + 1]]] = parts[r, :counts[r]]
+    return value.reshape(S, Nq, dv)
 
 
 def _exchange_to_stream_shards(bv: torch.Tensor, owner: torch.Tensor, mine: torch.Tensor, rank: int, world: int,
                                group):
     """Each rank ends with the value rows of its stream shard: owners send each
-    row to the rank of the query's stream with one all-to-all."""
+    row to the rank of the query's stream with one all-to-all.  Split sizes are
+    counted on the device and reach the host in one copy; rows are placed by
+    index (stable sorts keep query order inside each source)."""
     S, Nq, dv = bv.shape
     dest = torch.empty((S,), dtype=torch.int64, device=bv.device)
     spans = [stream_shard(S, r, world) for r in range(world)]
-    for r, (lo, hi) in enumerate(spans):
-        dest[lo:hi] = r
-    dest_q = dest[:, None].expand(S, Nq)
-    # rows this rank sends, grouped by destination rank (query order inside)
-    in_counts = [int((mine & (dest_q == r)).sum()) for r in range(world)]
-    order = torch.argsort(torch.where(mine, dest_q, torch.full_like(dest_q, world)).reshape(-1), stable=True)
-    n_send = sum(in_counts)
-    send = bv.reshape(S * Nq, dv)[order[:n_send]].contiguous()
+    for r, (lo_r, hi_r) in enumerate(spans):
+        dest[lo_r:hi_r] = r
+    dest_q = dest[:, None].expand(S, Nq).reshape(-1)
+    send_key = torch.where(mine.reshape(-1), dest_q, torch.full_like(dest_q, world))
     lo, hi = spans[rank]
-    my_owner = owner[lo:hi]
-    out_counts = [int((my_owner == src).sum()) for src in range(world)]
-    recv = torch.empty((sum(out_counts), dv), dtype=bv.dtype, device=bv.device)
+    my_owner = owner[lo:hi].reshape(-1)
+    recv_key = torch.where(my_owner >= 0, my_owner, torch.full_like(my_owner, world))
+    counts = torch.cat((torch.bincount(send_key, minlength=world + 1)[:world],
+                        torch.bincount(recv_key, minlength=world + 1)[:world])).tolist()  # the one host sync
+    in_counts, out_counts = counts[:world], counts[world:]
+    n_send, n_recv = sum(in_counts), sum(out_counts)
+    order = torch.argsort(send_key, stable=True)[:n_send]
+    send = bv.reshape(S * Nq, dv)[order].contiguous()
+    recv = torch.empty((n_recv, dv), dtype=bv.dtype, device=bv.device)
     dist.all_to_all_single(recv, send, output_split_sizes=out_counts, input_split_sizes=in_counts, group=group)
-    value = torch.zeros((hi - lo, Nq, dv), dtype=bv.dtype, device=bv.device)
-    off = 0
-    for src in range(world):
-        if out_counts[src]:
-            value[my_owner == src] = recv[off:off + out_counts[src]]
-        off += out_counts[src]
-    return value
+    # recv holds source 0's rows, then source 1's, ..., each in query order
+    place = torch.argsort(recv_key, stable=True)[:n_recv]
+    value = torch.zeros(((hi - lo) * Nq, dv), dtype=bv.dtype, device=bv.device)
+    value[place] = recv
+    return value.reshape(hi - lo, Nq, dv)
