@@ -113,6 +113,11 @@ _SIGNATURES: dict[str, list] = {
     "gfst_exact_block_score": [
         _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
     ],
+    "gfst_block_commit_i8": [_c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_void_p],
+    "gfst_exact_readout_i8": [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int,
+        _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+    ],
     "gfst_mpuc_scan_workspace_bytes": [_c_int64, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_size_t)],
     "gfst_mpuc_recurrent_scan": [
         _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int64, _c_int,

@@ -12,6 +12,7 @@ the last launch.  CASE is one of:
   topk        tensor-core score + top-16 of 64 queries over 512 summaries per stream
   topk_long   tensor-core score + top-8 of 1024 queries over 8192 summaries per stream
   readout     exact-token readout of 64 queries x 16 blocks of 64 tokens per stream
+  readout_i8  the same readout with the int8 first look (int8 key copies + side data)
   commit      one 64-token block commit per stream
   tracker     64 tokens of the local tracker (d=64, flag dims 8/16/32, nested levels + features)
   readout_long  exact-token readout of 1024 queries x 8 blocks of 128 tokens per stream out of 8192 blocks
@@ -56,7 +57,8 @@ def _timed(fn, repeat: int, batch: int = 1) -> float:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("case", choices=["frames", "frames_mid", "batched_qr", "topk", "topk_long", "readout", "commit", "tracker",
+    parser.add_argument("case", choices=["frames", "frames_mid", "batched_qr", "topk", "topk_long", "readout", "readout_i8",
+                                         "commit", "tracker",
                                          "readout_long", "commit_eig", "block_tracker", "centroid_commit",
                                          "centroid_readout", "segmented", "block_score", "heev", "open_block",
                                          "exact_topk", "mpuc_scan"])
@@ -98,6 +100,17 @@ def main() -> None:
         sel = torch.randint(0, 512, (S, 64, 16), generator=g, device=dev, dtype=torch.int32)
         ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel), args.repeat)
         units = f"{S * 64 * 16 * 64 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bytes"
+    elif args.case == "readout_i8":
+        S = args.streams or 1024
+        pool = torch.randn((S, 512, 64, 128), generator=g, device=dev).to(bf)
+        pool8 = torch.empty((S, 512, 64, 128), dtype=torch.int8, device=dev)
+        meta = torch.empty((S, 512, 64 + 4), dtype=torch.float32, device=dev)
+        for b in range(512):
+            memory.block_commit_i8(pool[:, b], pool8, meta, b)
+        Q = torch.randn((S, 64, 128), generator=g, device=dev).to(bf)
+        sel = torch.randint(0, 512, (S, 64, 16), generator=g, device=dev, dtype=torch.int32)
+        ms = _timed(lambda: readout.exact_readout(Q, pool, pool, sel, k8=(pool8, meta)), args.repeat)
+        units = f"{S * 64 * 16 * 64 * 128 * 2 / ms / 1e6:.0f} GB/s per-query bf16 bytes"
     elif args.case == "readout_long":
         S = args.streams or 16
         pool = torch.randn((S, 8192, 128, 128), generator=g, device=dev, dtype=bf)

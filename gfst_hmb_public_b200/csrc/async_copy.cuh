@@ -80,5 +80,8 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // 2-D bf16 tensor map of a row-major [rows, d] matrix: box of 64 columns
 // (one 128-byte swizzle row) x box_rows rows, 128-byte swizzle.
 int make_bf16_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int box_rows);
+// 2-D byte tensor map of a row-major [rows, row_bytes] matrix: box of 128
+// bytes x box_rows rows, 128-byte swizzle.
+int make_u8_map(CUtensorMap* map, const void* base, uint64_t rows, int row_bytes, int box_rows);
 
 }  // namespace gfst

@@ -355,6 +355,20 @@ int make_bf16_map(CUtensorMap* map, const void* base, uint64_t rows, int d, int 
   return GFST_OK;
 }
 
+int make_u8_map(CUtensorMap* map, const void* base, uint64_t rows, int row_bytes, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  GFST_REQUIRE(enc != nullptr, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  GFST_REQUIRE(r == CUDA_SUCCESS, GFST_ERR_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GFST_OK;
+}
+
 // One thread waits on an mbarrier that nothing arrives at, for at most
 // `budget` clock cycles, and gives up the way the pipelines' waits do: the
 // sticky word records GFST_ERR_TIMEOUT and the kernel returns.

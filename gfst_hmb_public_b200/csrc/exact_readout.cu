@@ -712,6 +712,433 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_mma_kernel(
                                best_tok, best_score, out_V);
 }
 
+// ---- exact readout with an int8 first look (bf16 pools, d = 128 * NB8) ----
+// The committed keys also exist as int8 copies k8 = round(k / s_k) with a
+// per-token scale s_k = max|k| / 127 (gfst_block_commit_i8), and per block
+// E >= max |k - s_k k8|_2 and N >= max |k|_2 over its tokens.  The kernel
+// streams those copies (L d + 4 L + 16 bytes per block instead of 2 L d),
+// quantises each query the same way (s_q, q8, e_q >= |q - s_q q8|_2,
+// n_q >= |q|_2) and takes the integer products q8 . k8 on the tensor cores
+// (mma.sync m16n8k32, exact int32 sums).  For every (query, token) pair of a
+// block the fp32 score S of the exact readout then lies within A +- b with
+//     A = s_q s_k (q8 . k8),
+//     b = n_q E + e_q (N + E) + slack n_q N  (+ 2^-20 of the largest |A| + b)
+// (q.k - q^.k^ = q.(k - k^) + (q - q^).k^ and Cauchy-Schwarz; slack covers the
+// fp32 rounding of A and of any fp32 evaluation of S).  Each query keeps
+// LB = max(A - b) over its tokens and a list of the tokens whose A + b reached
+// the LB current when they were scored; the argmax of S (and every token tied
+// with it) has A + b >= S_max >= LB, so it is on the list.  The listed tokens
+// with A + b >= the final LB are re-scored exactly from the bf16 keys, and the
+// best in the total order (score descending, token ascending; NaN never wins)
+// is the result: the same token the exact readout picks.  A query whose list
+// overflows, or whose own values are not finite or all zero, and any block
+// holding a key with a non-finite value (E = inf), is scored in full from the
+// bf16 keys instead.
+constexpr int kCandCap = 32;
+
+__device__ __forceinline__ void mma_i8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// order-preserving float -> uint (NaN -> 0, the smallest)
+__device__ __forceinline__ uint32_t ord_u32(float x) {
+  uint32_t u = __float_as_uint(x);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return x != x ? 0u : u;
+}
+__device__ __forceinline__ float ord_f32(uint32_t u) {
+  u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+  return __uint_as_float(u);
+}
+
+// fp32 dot of one bf16 key row and one bf16 query row (d / 8 16-byte chunks)
+__device__ __forceinline__ float bf16_row_dot(const __nv_bfloat16* __restrict__ kr, const __nv_bfloat16* __restrict__ qr,
+                                              int d) {
+  const uint4* k4 = reinterpret_cast<const uint4*>(kr);
+  const uint4* q4 = reinterpret_cast<const uint4*>(qr);
+  float acc = 0.f;
+  for (int c = 0; c < d / 8; ++c) {
+    const uint4 kv = __ldg(k4 + c), qv = __ldg(q4 + c);
+    acc = fmaf(bf16_lo(kv.x), bf16_lo(qv.x), acc);
+    acc = fmaf(bf16_hi(kv.x), bf16_hi(qv.x), acc);
+    acc = fmaf(bf16_lo(kv.y), bf16_lo(qv.y), acc);
+    acc = fmaf(bf16_hi(kv.y), bf16_hi(qv.y), acc);
+    acc = fmaf(bf16_lo(kv.z), bf16_lo(qv.z), acc);
+    acc = fmaf(bf16_hi(kv.z), bf16_hi(qv.z), acc);
+    acc = fmaf(bf16_lo(kv.w), bf16_lo(qv.w), acc);
+    acc = fmaf(bf16_hi(kv.w), bf16_hi(qv.w), acc);
+  }
+  return acc;
+}
+
+template <int NB8>
+__global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
+    const __grid_constant__ CUtensorMap tmK8, const __nv_bfloat16* __restrict__ Q,
+    const __nv_bfloat16* __restrict__ pool_K, const float* __restrict__ k8_scale,
+    const __nv_bfloat16* __restrict__ pool_V, const int32_t* __restrict__ top_idx, int n_queries, int n_chunks,
+    int n_slots, int L, int dv, int k, int n_stages, float slack, int32_t* __restrict__ best_tok,
+    float* __restrict__ best_score, __nv_bfloat16* __restrict__ out_V) {
+  constexpr int D = NB8 * 128;  // key width = int8 bytes per key row
+  constexpr int KSTEPS = D / 32;
+  extern __shared__ uint8_t dyn_raw[];
+  __shared__ RunTable rt;
+  __shared__ unsigned long long best[kQC];
+  __shared__ uint32_t lbk[kQC];
+  __shared__ int ccount[kQC];
+  __shared__ uint2 cand[kQC][kCandCap];
+  __shared__ float4 qstat[kQC];  // s_q, e_q, n_q, 1 = score in full
+  __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ int stage_run[kMaxStages];
+  __shared__ int abort_s, issued_s;
+  volatile int* abort_v = &abort_s;
+  volatile int* stage_run_v = stage_run;
+
+  const uint32_t key_bytes = (uint32_t)L * D;
+  const uint32_t side_bytes = (uint32_t)(L + 4) * 4u;  // scales, then E, N, 0, 0
+  // stages 1024-byte aligned (the swizzle atom)
+  const uint32_t stage_bytes = (key_bytes + side_bytes + 1023u) & ~1023u;
+  const uint32_t raw = smem_u32(dyn_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* dyn = dyn_raw + (base - raw);
+  uint8_t* qs = dyn + (size_t)n_stages * stage_bytes;  // [kQC][D] int8, chunk-swizzled
+  uint8_t* zrow = qs + kQC * D;
+  const uint32_t qs_u = base + n_stages * stage_bytes;
+  const uint32_t zrow_u = qs_u + kQC * D;
+  const int64_t s = blockIdx.x / n_chunks;
+  const int q0 = (int)(blockIdx.x % n_chunks) * kQC;
+  const int nq = min(kQC, n_queries - q0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const __nv_bfloat16* Qc = Q + ((size_t)s * n_queries + q0) * D;
+
+  for (int q = tid; q < kQC; q += kMThreads) {
+    best[q] = 0ull;
+    lbk[q] = ord_u32(-INFINITY);
+    ccount[q] = 0;
+  }
+  for (int e = tid; e < D / 16; e += kMThreads) reinterpret_cast<uint4*>(zrow)[e] = make_uint4(0, 0, 0, 0);
+  // the chunk's bf16 queries into the (still idle) ring, one coalesced copy
+  __nv_bfloat16* qbf = reinterpret_cast<__nv_bfloat16*>(dyn);
+  for (int e = tid; e < nq * D / 8; e += kMThreads)
+    reinterpret_cast<uint4*>(qbf)[e] = __ldg(reinterpret_cast<const uint4*>(Qc) + e);
+  __syncthreads();
+  // quantise them: one warp per query, D / 32 values per lane
+  for (int q = warp; q < kQC; q += kMWarps + 1) {
+    constexpr int PL = D / 32;
+    float v[PL];
+    float mx = 0.f, nn = 0.f;
+    bool bad = q >= nq;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      v[i] = q < nq ? bf16_to_f32(qbf[q * D + lane * PL + i]) : 0.f;
+      mx = fmaxf(mx, fabsf(v[i]));
+      nn = fmaf(v[i], v[i], nn);
+      bad = bad || !(fabsf(v[i]) <= 3.0e38f);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      nn += __shfl_xor_sync(0xffffffffu, nn, o);
+    }
+    bad = __any_sync(0xffffffffu, bad) || !(mx > 0.f);
+    const float sq = bad ? 0.f : mx / 127.f;
+    const float inv = bad ? 0.f : 127.f / mx;
+    float ee = 0.f;
+    uint32_t packed[PL / 4];
+#pragma unroll
+    for (int i = 0; i < PL / 4; ++i) packed[i] = 0u;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int q8 = bad ? 0 : max(-127, min(127, __float2int_rn(v[i] * inv)));
+      const float r = v[i] - sq * (float)q8;
+      ee = fmaf(r, r, ee);
+      packed[i >> 2] |= ((uint32_t)(q8 & 0xff)) << (8 * (i & 3));
+    }
+    // bytes [lane PL, lane PL + PL) of the row, 4 at a time: chunk c, swizzled
+#pragma unroll
+    for (int w = 0; w < PL / 4; ++w) {
+      const int byte0 = lane * PL + 4 * w;
+      const int c = byte0 >> 4;
+      const int pos = (c & ~7) | ((c ^ q) & 7);
+      *reinterpret_cast<uint32_t*>(qs + q * D + pos * 16 + (byte0 & 15)) = packed[w];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ee += __shfl_xor_sync(0xffffffffu, ee, o);
+    if (lane == 0) {
+      const float n_q = sqrtf(nn) * (1.f + 1.f / 1024.f);
+      const float e_q = sqrtf(ee) * (1.f + 1.f / 1024.f) + n_q * (1.f / 1048576.f);
+      qstat[q] = make_float4(sq, e_q, n_q, bad ? 1.f : 0.f);
+    }
+  }
+  if (tid == 0) {
+    for (int i = 0; i < n_stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      stage_run[i] = -1;
+    }
+    abort_s = 0;
+    issued_s = 0;
+    mbar_init_fence();
+  }
+  build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
+  const int n_runs = rt.n_runs;
+  // (build_runs ends with a CTA barrier: the ring's bf16 query copy is dead)
+
+  if (warp == kMWarps) {
+    if (lane == 0) {
+      // the generic-proxy writes of the query copy precede the ring's copies
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      int r = 0;
+      for (; r < n_runs; ++r) {
+        const int st = r % n_stages;
+        if (!mbar_wait(&empty[st], ((r / n_stages) & 1) ^ 1)) {
+          *abort_v = 1;
+          break;
+        }
+        if (*abort_v) break;
+        const int b = (int)(rt.keys[rt.run_start[r]] >> 11);
+        const int64_t blk = (int64_t)s * n_slots + b;
+        stage_run_v[st] = r;
+        mbar_arrive_expect_tx(&full[st], key_bytes + side_bytes);
+        uint8_t* sb = dyn + (size_t)st * stage_bytes;
+#pragma unroll
+        for (int kb = 0; kb < NB8; ++kb)
+          tma_load_2d(sb + (size_t)kb * L * 128, &tmK8, &full[st], kb * 128, (int)(blk * L));
+        bulk_load(sb + key_bytes, k8_scale + blk * (L + 4), side_bytes, &full[st]);
+      }
+      issued_s = r;
+    }
+  } else {
+    const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int a_hi = lane >> 4;
+    const int bcol = lane & 7;
+    const int nt = L / 16;
+    uint32_t aoff[KSTEPS];
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+      aoff[kk] = (uint32_t)((kk >> 2) * L * 128) + (uint32_t)((((2 * kk + a_hi) & 7) ^ (lane & 7)) << 4);
+    for (int r = warp; r < n_runs; r += kMWarps) {
+      const int st = r % n_stages;
+      if (!wait_stage(stage_run_v, full, abort_v, st, r, n_stages)) break;
+      const int p0 = rt.run_start[r], p1 = rt.run_start[r + 1];
+      const int b = (int)(rt.keys[p0] >> 11);
+      const uint32_t abase = base + st * stage_bytes + a_row * 128;
+      const float* sk = reinterpret_cast<const float*>(dyn + (size_t)st * stage_bytes + key_bytes);
+      const float E = sk[L], N = sk[L + 1];
+      if (!(E <= 3.0e38f)) {
+        // a key of this block has a non-finite value: its queries are scored in full
+        for (int pp = p0 + lane; pp < p1; pp += 32) qstat[rt.keys[pp] & 2047u].w = 1.f;
+      } else {
+        for (int g0 = p0; g0 < p1; g0 += 8) {
+          const int pn = g0 + bcol;
+          const int qn = pn < p1 ? (int)(rt.keys[pn] & 2047u) : -1;
+          uint32_t bq[KSTEPS][2];
+#pragma unroll
+          for (int kk = 0; kk < KSTEPS; kk += 2) {
+            const int c = 2 * kk + (lane >> 3);
+            const uint32_t addr =
+                qn >= 0 ? qs_u + qn * D + (uint32_t)(((c & ~7) | ((c ^ qn) & 7)) << 4) : zrow_u + (uint32_t)(c << 4);
+            ldsm_x4(addr, bq[kk][0], bq[kk][1], bq[kk + 1][0], bq[kk + 1][1]);
+          }
+          // this lane's two query columns (pairs g0 + 2 (lane % 4) and + 1):
+          // scale s_q and the block's bound b
+          int qc[2];
+          float sq[2], bq_[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int pj = g0 + 2 * (lane & 3) + j;
+            qc[j] = pj < p1 ? (int)(rt.keys[pj] & 2047u) : -1;
+            const float4 st4 = qc[j] >= 0 ? qstat[qc[j]] : make_float4(0.f, 0.f, 0.f, 1.f);
+            sq[j] = st4.x;
+            float bb = fmaf(st4.z, E, st4.y * (N + E)) + slack * st4.z * N;
+            bb += (bb + (st4.z + st4.y) * (N + E)) * (1.f / 1048576.f);
+            bq_[j] = bb;
+          }
+          float amax[2] = {-INFINITY, -INFINITY};
+          float av[4][4];  // A of the 16 (token, query) pairs this lane holds
+          for (int t = 0; t < nt; t += 4) {
+            const int tn = min(4, nt - t);  // 16-row tiles of this group (the last may hold fewer)
+            int acc[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0;
+#pragma unroll
+            for (int kk = 0; kk < KSTEPS; ++kk) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                if (u < tn) {
+                  uint32_t a0, a1, a2, a3;
+                  ldsm_x4(abase + (uint32_t)((t + u) * 16 * 128) + aoff[kk], a0, a1, a2, a3);
+                  mma_i8_16832(acc[u], a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int row = (t + u) * 16 + (lane >> 2);
+              const float s0 = u < tn ? sk[row] : 0.f, s1 = u < tn ? sk[row + 8] : 0.f;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = e & 1;
+                const float a = u < tn ? (float)acc[u][e] * ((e & 2) ? s1 : s0) * sq[j] : -INFINITY;
+                av[u][e] = a;
+                amax[j] = fmaxf(amax[j], a);
+              }
+            }
+            // LB of each column: max over the 8 lanes that hold it, then over the CTA
+            float lbc[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              float m = amax[j];
+#pragma unroll
+              for (int o = 4; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+              if ((lane >> 2) == 0 && qc[j] >= 0) atomicMax(&lbk[qc[j]], ord_u32(m - bq_[j]));
+            }
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              lbc[j] = qc[j] >= 0 ? ord_f32(*(volatile uint32_t*)&lbk[qc[j]]) - bq_[j] : INFINITY;
+            // candidates: A >= LB - b, i.e. A + b >= LB
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = e & 1;
+                if (av[u][e] >= lbc[j]) {
+                  const int row = (t + u) * 16 + (lane >> 2) + ((e & 2) ? 8 : 0);
+                  const int slot = atomicAdd(&ccount[qc[j]], 1);
+                  if (slot < kCandCap)
+                    cand[qc[j]][slot] = make_uint2((uint32_t)(b * L + row), __float_as_uint(av[u][e] + bq_[j]));
+                }
+              }
+            }
+            amax[0] = amax[1] = -INFINITY;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+  }
+  __syncthreads();
+  if (tid == kMWarps * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
+  // exact re-score: one warp per query, one lane per listed token (or every
+  // token of the selected blocks for a query scored in full)
+  if (!*abort_v) {
+    for (int ql = warp; ql < nq; ql += kMWarps + 1) {
+      const __nv_bfloat16* qrow = Qc + (size_t)ql * D;
+      const int cnt = ccount[ql];
+      const bool in_full = qstat[ql].w != 0.f || cnt > kCandCap;
+      float bs = __int_as_float(0x7fc00000);
+      int bi = 0x7fffffff;
+      if (!in_full) {
+        const float lb = ord_f32(lbk[ql]);
+        if (lane < cnt) {
+          const uint2 c = cand[ql][lane];
+          if (__uint_as_float(c.y) >= lb) {
+            const int tok = (int)c.x;
+            bs = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, qrow, D);
+            bi = tok;
+          }
+        }
+      } else {
+        const int32_t* sel = top_idx + ((size_t)s * n_queries + q0 + ql) * k;
+        for (int j = 0; j < k; ++j) {
+          const int b = __ldg(sel + j);
+          if (b < 0 || b >= n_slots) continue;
+          for (int p = lane; p < L; p += 32) {
+            const int tok = b * L + p;
+            const float v = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, qrow, D);
+            if (better(v, tok, bs, bi)) {
+              bs = v;
+              bi = tok;
+            }
+          }
+        }
+      }
+      warp_best(bs, bi);
+      if (lane == 0) best[ql] = (bi != 0x7fffffff && bs == bs) ? pack_best(bs, bi) : 0ull;
+    }
+  }
+  __syncthreads();
+  write_outputs<__nv_bfloat16>(best, nq, kMWarps + 1, (int64_t)s * n_queries + q0, L, n_slots, dv, s, pool_V,
+                               best_tok, best_score, out_V);
+}
+
+// int8 copy of one committed block per stream: one CTA per stream, a warp per
+// token row (D / 32 values per lane).  Per token the scale s = max|k| / 127;
+// per block E >= max |k - s k8|_2 and N >= max |k|_2 (fp32 norms rounded up by
+// a relative 2^-10, plus 2^-20 of N on E; +inf for a non-finite key) follow
+// the L scales in k8_scale [.., L + 4] as (E, N, 0, 0).
+template <int PL>
+__global__ void __launch_bounds__(256) block_commit_i8_kernel(const __nv_bfloat16* __restrict__ K,
+                                                              int8_t* __restrict__ pool_K8,
+                                                              float* __restrict__ k8_scale, int n_slots, int slot,
+                                                              int L) {
+  constexpr int D = PL * 32;
+  __shared__ float red_e[8], red_n[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t s = blockIdx.x;
+  const int64_t blk = s * n_slots + slot;
+  float emax = 0.f, nmax = 0.f;
+  for (int p = warp; p < L; p += 8) {
+    const __nv_bfloat16* src = K + (s * L + p) * D;
+    float v[PL];
+    float mx = 0.f, nn = 0.f;
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      v[i] = bf16_to_f32(src[lane * PL + i]);
+      mx = fmaxf(mx, fabsf(v[i]));
+      nn = fmaf(v[i], v[i], nn);
+      bad = bad || !(fabsf(v[i]) <= 3.0e38f);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      nn += __shfl_xor_sync(0xffffffffu, nn, o);
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    const float sk = (bad || !(mx > 0.f)) ? 0.f : mx / 127.f;
+    const float inv = sk > 0.f ? 127.f / mx : 0.f;
+    int8_t* dst = pool_K8 + (blk * L + p) * D + lane * PL;
+    float ee = 0.f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int q8 = sk > 0.f ? max(-127, min(127, __float2int_rn(v[i] * inv))) : 0;
+      const float r = v[i] - sk * (float)q8;
+      ee = fmaf(r, r, ee);
+      dst[i] = (int8_t)q8;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ee += __shfl_xor_sync(0xffffffffu, ee, o);
+    const float n_k = bad ? INFINITY : sqrtf(nn) * (1.f + 1.f / 1024.f);
+    const float e_k = bad ? INFINITY : sqrtf(ee) * (1.f + 1.f / 1024.f) + n_k * (1.f / 1048576.f);
+    emax = fmaxf(emax, e_k);
+    nmax = fmaxf(nmax, n_k);
+    if (lane == 0) k8_scale[blk * (L + 4) + p] = sk;
+  }
+  if (lane == 0) {
+    red_e[warp] = emax;
+    red_n[warp] = nmax;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) {
+      emax = fmaxf(emax, red_e[w]);
+      nmax = fmaxf(nmax, red_n[w]);
+    }
+    // fmaxf drops NaN: a non-finite key already gave +inf
+    float* tail = k8_scale + blk * (L + 4) + L;
+    tail[0] = emax;
+    tail[1] = nmax;
+    tail[2] = 0.f;
+    tail[3] = 0.f;
+  }
+}
+
 template <typename T>
 int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t* top_idx, int64_t S, int Nq,
            int NS, int L, int d, int dv, int k, int32_t* best_tok, float* best_score, void* out_V,
@@ -799,6 +1226,44 @@ int launch(const void* Q, const void* pool_K, const void* pool_V, const int32_t*
   return check_launch("exact_readout_kernel");
 }
 
+// int8 first look: bf16 pools, d = 128 or 256, L % 16 == 0, L <= 256
+int launch_i8(const void* Q, const void* pool_K, const int8_t* pool_K8, const float* k8_scale, const void* pool_V,
+              const int32_t* top_idx, int64_t S, int Nq, int NS, int L, int d, int dv, int k, int32_t* best_tok,
+              float* best_score, void* out_V, cudaStream_t stream) {
+  const int64_t n_chunks = (Nq + kQC - 1) / kQC;
+  GFST_REQUIRE(S * n_chunks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many query chunks");
+  const size_t stage_bytes = ((size_t)L * d + (size_t)(L + 4) * 4 + 1023) & ~(size_t)1023;
+  // about 64 KB of ring: two CTAs per SM with the run table and candidate lists
+  int n_stages = (int)((64u * 1024u) / stage_bytes);
+  n_stages = n_stages < 2 ? 2 : (n_stages > kMaxStages ? kMaxStages : n_stages);
+  // the ring holds the chunk's bf16 queries before the pipeline starts
+  while ((size_t)n_stages * stage_bytes < (size_t)kQC * d * 2) ++n_stages;
+  const size_t dyn = 1024 + (size_t)n_stages * stage_bytes + (size_t)(kQC + 1) * d;
+  CUtensorMap tm;
+  const int st = make_u8_map(&tm, pool_K8, (uint64_t)S * NS * L, d, L);
+  if (st != GFST_OK) return st;
+  // fp32 rounding of A and of an fp32 evaluation of the exact score: 2 d + 16 units of 2^-24
+  const float slack = (float)(2 * d + 16) / 16777216.f;
+  const unsigned grid = (unsigned)(S * n_chunks);
+  cudaError_t e = cudaSuccess;
+#define GFST_READOUT_I8(NB)                                                                                       \
+  {                                                                                                               \
+    auto kern = exact_readout_i8_kernel<NB>;                                                                      \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);                        \
+    GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));          \
+    kern<<<grid, kMThreads, dyn, stream>>>(tm, static_cast<const __nv_bfloat16*>(Q),                               \
+                                           static_cast<const __nv_bfloat16*>(pool_K),                             \
+                                           k8_scale,                                                              \
+                                           static_cast<const __nv_bfloat16*>(pool_V), top_idx, Nq, (int)n_chunks, \
+                                           NS, L, dv, k, n_stages, slack, best_tok, best_score,                  \
+                                           static_cast<__nv_bfloat16*>(out_V));                                   \
+    return check_launch("exact_readout_i8_kernel");                                                                \
+  }
+  if (d == 128) GFST_READOUT_I8(1)
+  GFST_READOUT_I8(2)
+#undef GFST_READOUT_I8
+}
+
 }  // namespace
 }  // namespace gfst
 
@@ -824,4 +1289,45 @@ extern "C" int gfst_exact_readout(const void* Q, const void* pool_K, const void*
                                  best_score, out_V, stream);
   set_last_error("unsupported dtype %d", dtype);
   return GFST_ERR_DTYPE;
+}
+
+extern "C" int gfst_block_commit_i8(const void* K, int8_t* pool_K8, float* k8_scale, int64_t n_streams, int n_slots,
+                                    int slot, int L, int d, cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(n_streams >= 0 && n_slots >= 1 && L >= 1, GFST_ERR_ARG, "bad sizes");
+  GFST_REQUIRE(slot >= 0 && slot < n_slots, GFST_ERR_ARG, "slot %d outside [0, %d)", slot, n_slots);
+  GFST_REQUIRE(d == 128 || d == 256, GFST_ERR_SHAPE, "int8 key copies cover d = 128 or 256 (d=%d)", d);
+  GFST_REQUIRE(n_streams <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many streams");
+  if (n_streams == 0) return GFST_OK;
+  GFST_REQUIRE(K && pool_K8 && k8_scale, GFST_ERR_ARG, "null buffer");
+  if (d == 128)
+    block_commit_i8_kernel<4><<<(unsigned)n_streams, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(K), pool_K8,
+                                                                       k8_scale, n_slots, slot, L);
+  else
+    block_commit_i8_kernel<8><<<(unsigned)n_streams, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(K), pool_K8,
+                                                                       k8_scale, n_slots, slot, L);
+  return check_launch("block_commit_i8_kernel");
+}
+
+extern "C" int gfst_exact_readout_i8(const void* Q, const void* pool_K, const int8_t* pool_K8, const float* k8_scale,
+                                     const void* pool_V, const int32_t* top_idx, int64_t n_streams, int n_queries,
+                                     int n_slots, int L, int d, int dv, int k, int32_t* best_tok, float* best_score,
+                                     void* out_V, cudaStream_t stream) {
+  using namespace gfst;
+  GFST_REQUIRE(n_streams >= 0 && n_queries >= 0 && n_slots >= 1 && L >= 1, GFST_ERR_ARG, "bad sizes");
+  GFST_REQUIRE(k >= 1 && k <= 32, GFST_ERR_SHAPE, "k=%d outside [1, 32]", k);
+  GFST_REQUIRE(d == 128 || d == 256, GFST_ERR_SHAPE, "the int8 first look covers d = 128 or 256 (d=%d)", d);
+  GFST_REQUIRE(L % 16 == 0 && L <= 256, GFST_ERR_SHAPE, "the int8 first look needs L %% 16 == 0 and L <= 256 (L=%d)",
+               L);
+  GFST_REQUIRE(dv % 8 == 0, GFST_ERR_ALIGN, "dv=%d must be a multiple of 8", dv);
+  GFST_REQUIRE((pool_V == nullptr) == (out_V == nullptr), GFST_ERR_ARG, "pool_V and out_V go together");
+  GFST_REQUIRE((int64_t)n_slots < (1LL << 21) && n_streams * (int64_t)n_slots * L < (1LL << 31), GFST_ERR_SHAPE,
+               "token index overflows");
+  if (n_streams == 0 || n_queries == 0) return GFST_OK;
+  GFST_REQUIRE(Q && pool_K && pool_K8 && k8_scale && top_idx && best_tok && best_score, GFST_ERR_ARG, "null buffer");
+  GFST_REQUIRE(aligned16(Q) && aligned16(pool_K) && aligned16(pool_K8) && aligned16(k8_scale) && aligned16(pool_V) &&
+                   aligned16(out_V),
+               GFST_ERR_ALIGN, "buffers must be 16-byte aligned");
+  return launch_i8(Q, pool_K, pool_K8, k8_scale, pool_V, top_idx, n_streams, n_queries, n_slots, L, d, dv, k,
+                   best_tok, best_score, out_V, stream);
 }

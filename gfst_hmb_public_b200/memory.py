@@ -51,23 +51,59 @@ def block_commit_mean(K: torch.Tensor, V: torch.Tensor | None, pool_K: torch.Ten
                  nat.stream_of(K))
 
 
+def block_commit_i8(K: torch.Tensor, pool_K8: torch.Tensor, k8_scale: torch.Tensor, slot: int) -> None:
+    """Write the int8 copy of block K [S, L, d] (bf16, d = 128 or 256) into
+    ``slot`` of pool_K8 [S, n_slots, L, d] int8, with the per-token scales and
+    the block's error / key norm bounds in k8_scale [S, n_slots, L + 4]
+    float32 (gfst_block_commit_i8): the side data that lets exact_readout bound
+    exact scores from the int8 copies."""
+    nat.require_cuda(K, pool_K8, k8_scale, what="block_commit_i8")
+    S, L, d = K.shape
+    n_slots = pool_K8.shape[1]
+    if K.dtype != torch.bfloat16 or pool_K8.dtype != torch.int8 or k8_scale.dtype != torch.float32:
+        raise RuntimeError("block_commit_i8: bf16 keys, int8 copies, float32 side data")
+    if tuple(pool_K8.shape) != (S, n_slots, L, d) or tuple(k8_scale.shape) != (S, n_slots, L + 4):
+        raise ValueError("block_commit_i8: shape mismatch")
+    if not (pool_K8.is_contiguous() and k8_scale.is_contiguous()):
+        raise ValueError("block_commit_i8: int8 copies and side data must be contiguous")
+    K = K.contiguous()
+    with torch.cuda.device(K.device):
+        nat.call("gfst_block_commit_i8", nat.ptr(K), nat.ptr(pool_K8), nat.ptr(k8_scale), S, n_slots, int(slot), L, d,
+                 nat.stream_of(K))
+
+
 class BlockMemory:
-    """Ring of ``n_slots`` committed blocks per stream (keys, values, summaries)."""
+    """Ring of ``n_slots`` committed blocks per stream (keys, values, summaries).
+
+    ``int8_keys``: also keep an int8 copy of every key with its side data
+    (``pool_K8``, ``k8_scale``; block_commit_i8), which exact_readout streams in
+    place of the bf16 keys (bf16 memories, d = 128 or 256)."""
 
     def __init__(self, n_streams: int, n_slots: int, block_len: int, d: int, dv: int | None = None, *,
-                 dtype: torch.dtype = torch.bfloat16, device="cuda"):
+                 dtype: torch.dtype = torch.bfloat16, device="cuda", int8_keys: bool = False):
         dv = d if dv is None else dv
         self.n_streams, self.n_slots, self.block_len, self.d, self.dv = n_streams, n_slots, block_len, d, dv
         self.dtype = dtype
         self.pool_K = torch.zeros((n_streams, n_slots, block_len, d), dtype=dtype, device=device)
         self.pool_V = torch.zeros((n_streams, n_slots, block_len, dv), dtype=dtype, device=device)
         self.summary = torch.zeros((n_streams, n_slots, d), dtype=dtype, device=device)
+        self.pool_K8 = self.k8_scale = None
+        if int8_keys:
+            if dtype != torch.bfloat16 or d not in (128, 256):
+                raise ValueError("BlockMemory: int8 key copies need bf16 keys with d = 128 or 256")
+            self.pool_K8 = torch.zeros((n_streams, n_slots, block_len, d), dtype=torch.int8, device=device)
+            self.k8_scale = torch.zeros((n_streams, n_slots, block_len + 4), dtype=torch.float32, device=device)
         self.blocks_committed = 0      # total blocks ever committed
         self.state_version = 0         # bumped on every mutation (retrieval caches key on it)
 
     @property
     def device(self) -> torch.device:
         return self.pool_K.device
+
+    @property
+    def k8(self) -> tuple | None:
+        """(pool_K8, k8_scale) for exact_readout, or None without int8 copies."""
+        return None if self.pool_K8 is None else (self.pool_K8, self.k8_scale)
 
     @property
     def n_valid(self) -> int:
@@ -84,6 +120,8 @@ class BlockMemory:
         """Commit one block per stream; returns the slot written."""
         slot = self.next_slot()
         block_commit_mean(K, V, self.pool_K, self.pool_V if V is not None else None, self.summary, slot)
+        if self.pool_K8 is not None:
+            block_commit_i8(K, self.pool_K8, self.k8_scale, slot)
         self.blocks_committed += 1
         self.mark_mutated()
         return slot

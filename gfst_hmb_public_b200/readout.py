@@ -17,11 +17,19 @@ import torch
 from . import _native as nat
 
 
-def exact_readout(Q: torch.Tensor, pool_K: torch.Tensor, pool_V: torch.Tensor | None, top_idx: torch.Tensor):
+def exact_readout(Q: torch.Tensor, pool_K: torch.Tensor, pool_V: torch.Tensor | None, top_idx: torch.Tensor,
+                  *, k8: tuple | None = None):
     """Q [S, Nq, d]; pool_K [S, n_slots, L, d]; pool_V [S, n_slots, L, dv] or None;
     top_idx [S, Nq, k] int32 (entries < 0 skipped).
     Returns (best_tok int32 [S,Nq] (-1 if nothing valid), best_score f32 [S,Nq],
-    out_V [S,Nq,dv] or None)."""
+    out_V [S,Nq,dv] or None).
+
+    ``k8`` = (pool_K8 int8 [S, n_slots, L, d], k8_scale float32 [S, n_slots, L + 4]),
+    the int8 copies of the keys written by ``block_commit_i8`` (BlockMemory with
+    ``int8_keys=True``): the kernel then streams the int8 copies, bounds every
+    token's exact score from them and re-scores only the tokens the bound does
+    not rule out from the bf16 keys -- the same best token and score, about
+    half the bytes (bf16 pools, d = 128 or 256, L % 16 == 0, L <= 256)."""
     nat.require_cuda(Q, pool_K, pool_V, top_idx, what="exact_readout")
     if Q.ndim != 3 or pool_K.ndim != 4 or top_idx.ndim != 3:
         raise ValueError("exact_readout expects Q [S,Nq,d], pool_K [S,slots,L,d], top_idx [S,Nq,k]")
@@ -40,6 +48,21 @@ def exact_readout(Q: torch.Tensor, pool_K: torch.Tensor, pool_V: torch.Tensor | 
     best_tok = torch.empty((S, Nq), dtype=torch.int32, device=Q.device)
     best_score = torch.empty((S, Nq), dtype=torch.float32, device=Q.device)
     out_V = torch.empty((S, Nq, dv), dtype=Q.dtype, device=Q.device) if pool_V is not None else None
+    if k8 is not None:
+        pool_K8, k8_scale = k8
+        nat.require_cuda(pool_K8, k8_scale, what="exact_readout")
+        if Q.dtype != torch.bfloat16:
+            raise RuntimeError("exact_readout: the int8 first look needs bf16 pools")
+        if tuple(pool_K8.shape) != tuple(pool_K.shape) or pool_K8.dtype != torch.int8 or \
+                tuple(k8_scale.shape) != (S, n_slots, L + 4) or k8_scale.dtype != torch.float32:
+            raise ValueError("exact_readout: k8 must be (int8 [S, slots, L, d], float32 [S, slots, L + 4])")
+        if not (pool_K8.is_contiguous() and k8_scale.is_contiguous()):
+            raise ValueError("exact_readout: int8 copies must be contiguous")
+        with torch.cuda.device(Q.device):
+            nat.call("gfst_exact_readout_i8", nat.ptr(Q), nat.ptr(pool_K), nat.ptr(pool_K8), nat.ptr(k8_scale),
+                     nat.ptr(pool_V), nat.ptr(top_idx), S, Nq, n_slots, L, d, dv, k, nat.ptr(best_tok),
+                     nat.ptr(best_score), nat.ptr(out_V), nat.stream_of(Q))
+        return best_tok, best_score, out_V
     with torch.cuda.device(Q.device):
         nat.call("gfst_exact_readout", nat.ptr(Q), nat.ptr(pool_K), nat.ptr(pool_V), nat.ptr(top_idx), S, Nq,
                  n_slots, L, d, dv, k, nat.dtype_code(Q.dtype, "exact_readout"), nat.ptr(best_tok),

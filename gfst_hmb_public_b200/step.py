@@ -57,17 +57,24 @@ class StreamingStep:
 
     def __init__(self, n_streams: int, *, d: int, r: int, block_len: int, n_slots: int, k: int,
                  dtype: torch.dtype = torch.bfloat16, device="cuda", sign_mode="r_diag_positive",
-                 eps_sign: float = 1e-8, check_errors: bool = False):
+                 eps_sign: float = 1e-8, check_errors: bool = False, int8_keys: bool | None = None):
         """check_errors: after every step, wait for it and raise RuntimeError if
         a kernel recorded a device-side failure (a bounded wait that gave up);
-        a debugging aid -- it makes every step synchronous."""
+        a debugging aid -- it makes every step synchronous.
+        int8_keys: keep int8 copies of the committed keys and read them out
+        with the int8 first look (exact_readout's ``k8``: the same results from
+        about half the bytes); default on for bf16 memories with d = 128 or
+        256 and 16 | L <= 256."""
         self.n_streams, self.d, self.r, self.block_len, self.n_slots, self.k = n_streams, d, r, block_len, n_slots, k
         self.sign_mode = sign_mode
         self.eps_sign = eps_sign
         self.check_errors = check_errors
         self.device = torch.device(device)
         self.U = torch.zeros((n_streams, d, r), dtype=torch.float32, device=self.device)
-        self.memory = memory.BlockMemory(n_streams, n_slots, block_len, d, d, dtype=dtype, device=self.device)
+        if int8_keys is None:
+            int8_keys = dtype == torch.bfloat16 and d in (128, 256) and block_len % 16 == 0 and block_len <= 256
+        self.memory = memory.BlockMemory(n_streams, n_slots, block_len, d, d, dtype=dtype, device=self.device,
+                                         int8_keys=int8_keys)
         self.frames_stream = torch.cuda.Stream(self.device)
         self.memory_stream = torch.cuda.Stream(self.device)
 
@@ -98,7 +105,8 @@ class StreamingStep:
             n_valid = self.memory.n_valid
             if n_valid > 0:
                 top_s, top_i = retrieval.block_topk(Q, self.memory.summary, self.k, n_blocks=n_valid)
-                best_tok, best_score, value = readout.exact_readout(Q, self.memory.pool_K, self.memory.pool_V, top_i)
+                best_tok, best_score, value = readout.exact_readout(Q, self.memory.pool_K, self.memory.pool_V, top_i,
+                                                                    k8=self.memory.k8)
             else:
                 S, L = Q.shape[0], Q.shape[1]
                 top_i = torch.full((S, L, self.k), -1, dtype=torch.int32, device=self.device)

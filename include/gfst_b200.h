@@ -522,6 +522,30 @@ GFST_API int gfst_heev(const void* matrices, int64_t batch, int d, int dtype, vo
 GFST_API int gfst_exact_block_materialize(const void* packed, int64_t n_elements, int elem_size, int64_t start,
                        int64_t end, void* out, cudaStream_t stream);
 
+/* ---- exact readout with an int8 first look ---------------------------------
+ * gfst_block_commit_i8 writes the int8 copy of one bf16 block per stream
+ * (K [n_streams, L, d]) into slot `slot` of pool_K8 [n_streams, n_slots, L, d]
+ * int8, and into k8_scale [n_streams, n_slots, L + 4] float32 the per-token
+ * scales s (k8 = round(k / s), s = max|k| / 127) followed by the block's
+ * (E, N, 0, 0): E >= max |k - s k8|_2 and N >= max |k|_2 over its tokens
+ * (rounded up; +inf when a key has a non-finite value).
+ * gfst_exact_readout_i8 returns what gfst_exact_readout returns for bf16
+ * pools (same arguments, plus pool_K8 and k8_scale of every committed slot):
+ * it streams the int8 copies, bounds each (query, token) score by A +- b from
+ * the exact integer product of the int8 values and the error norms, and
+ * re-scores from pool_K only the tokens whose upper bound reaches the best
+ * lower bound of their query (a query with more than 32 such tokens, with
+ * non-finite or all-zero values, or selecting a block with a non-finite key,
+ * is scored in full).  No reference counterpart: a B200 path for the readout
+ * of modeling.py:599-657, 1151-1169.
+ * Limits: d = 128 or 256; L % 16 == 0, L <= 256; k <= 32.                   */
+GFST_API int gfst_block_commit_i8(const void* K, int8_t* pool_K8, float* k8_scale, int64_t n_streams, int n_slots,
+                                  int slot, int L, int d, cudaStream_t stream);
+GFST_API int gfst_exact_readout_i8(const void* Q, const void* pool_K, const int8_t* pool_K8, const float* k8_scale,
+                                   const void* pool_V, const int32_t* top_idx, int64_t n_streams, int n_queries,
+                                   int n_slots, int L, int d, int dv, int k, int32_t* best_tok, float* best_score,
+                                   void* out_V, cudaStream_t stream);
+
 /* ---- MPUC recurrent scan ------------------------------------------------------
  * The token loop of MpucGfstHmbBlock._forward_sequence_tensors
  * (src/gfst_hmb_mpuc/modeling.py:4449-4476; cell _token_step 4363-4411,
