@@ -299,6 +299,60 @@ __device__ __forceinline__ void build_runs(RunTable& rt, uint16_t* run_of, const
   __syncthreads();
 }
 
+// build_runs by a counting sort over the block indices (n_slots <= the
+// histogram's size, hist: n_slots ints of scratch shared memory): the keys
+// come out grouped by block in ascending block order; inside a block their
+// order is the order the scatter's atomics happen to take, which nothing
+// downstream depends on (every query's result is order-free).  Three CTA
+// barriers instead of the bitonic sort's log^2.
+template <int NT>
+__device__ __forceinline__ void build_runs_counting(RunTable& rt, int* hist, const int32_t* __restrict__ sel,
+                                                    int n_pairs, int k, int n_slots) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < n_slots; i += NT) hist[i] = 0;
+  __syncthreads();
+  for (int e = tid; e < n_pairs; e += NT) {
+    const int b = __ldg(sel + e);
+    if (b >= 0 && b < n_slots) atomicAdd(&hist[b], 1);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    // exclusive scans of the counts (key offsets) and of the non-empty bins (run indices)
+    int base_e = 0, base_r = 0;
+    for (int c0 = 0; c0 < n_slots; c0 += 32) {
+      const int i = c0 + tid;
+      const int cnt = i < n_slots ? hist[i] : 0;
+      int ie = cnt, ir = cnt > 0 ? 1 : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int ye = __shfl_up_sync(0xffffffffu, ie, o), yr = __shfl_up_sync(0xffffffffu, ir, o);
+        if (tid >= o) {
+          ie += ye;
+          ir += yr;
+        }
+      }
+      const int ex = base_e + ie - cnt, rx = base_r + ir - (cnt > 0 ? 1 : 0);
+      if (i < n_slots) {
+        hist[i] = ex;
+        if (cnt > 0) rt.run_start[rx] = (uint16_t)ex;
+      }
+      base_e += __shfl_sync(0xffffffffu, ie, 31);
+      base_r += __shfl_sync(0xffffffffu, ir, 31);
+    }
+    if (tid == 0) {
+      rt.n_runs = base_r;
+      rt.n_valid = base_e;
+      rt.run_start[base_r] = (uint16_t)base_e;
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < n_pairs; e += NT) {
+    const int b = __ldg(sel + e);
+    if (b >= 0 && b < n_slots) rt.keys[atomicAdd(&hist[b], 1)] = ((uint32_t)b << 11) | (uint32_t)(e / k);
+  }
+  __syncthreads();
+}
+
 // Consumer side of the ring: wait until stage st holds run r.  Lane 0 waits;
 // the verdict is broadcast.  false: give up (timeout or another warp aborted).
 __device__ __forceinline__ bool wait_stage(volatile int* stage_run, uint64_t* full, volatile int* abort_flag,
@@ -883,9 +937,14 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
     issued_s = 0;
     mbar_init_fence();
   }
-  build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
+  if (n_slots <= kCandCap * kQC * 2)  // the candidate lists (unused until the scoring) hold the histogram
+    build_runs_counting<kMThreads>(rt, reinterpret_cast<int*>(&cand[0][0]),
+                                   top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
+  else
+    build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k,
+                                        n_slots);
   const int n_runs = rt.n_runs;
-  // (build_runs ends with a CTA barrier: the ring's bf16 query copy is dead)
+  // (the builders end with a CTA barrier: the ring's bf16 query copy is dead)
 
   if (warp == kMWarps) {
     if (lane == 0) {
@@ -1024,37 +1083,87 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
   }
   __syncthreads();
   if (tid == kMWarps * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
-  // exact re-score: one warp per query, one lane per listed token (or every
-  // token of the selected blocks for a query scored in full)
+  // exact re-score of the surviving candidates, flattened over the chunk: the
+  // (query, token) pairs with A + b >= the query's final LB are listed in the
+  // (now idle) run table, one thread per pair computes the fp32 score from
+  // the bf16 rows, and one thread per query takes the best of its pairs in
+  // the total order.  Queries scored in full take a warp each afterwards.
+  int* pair_off = reinterpret_cast<int*>(rt.run_start);     // [kQC + 1]
+  uint32_t* pair_tok = rt.keys;                             // [<= kQC * kCandCap]
+  float* pair_score = reinterpret_cast<float*>(dyn);        // the idle ring
   if (!*abort_v) {
-    for (int ql = warp; ql < nq; ql += kMWarps + 1) {
-      const __nv_bfloat16* qrow = Qc + (size_t)ql * D;
-      const int cnt = ccount[ql];
-      const bool in_full = qstat[ql].w != 0.f || cnt > kCandCap;
+    if (warp == 0) {
+      int n_keep[2], ex[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int q = lane + 32 * h;
+        n_keep[h] = 0;
+        if (q < nq && qstat[q].w == 0.f && ccount[q] <= kCandCap) {
+          const float lb = ord_f32(lbk[q]);
+          for (int j = 0; j < ccount[q]; ++j) n_keep[h] += __uint_as_float(cand[q][j].y) >= lb ? 1 : 0;
+        }
+      }
+      int base = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        int incl = n_keep[h];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        ex[h] = base + incl - n_keep[h];
+        base += __shfl_sync(0xffffffffu, incl, 31);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int q = lane + 32 * h;
+        pair_off[q] = ex[h];
+        if (n_keep[h] > 0) {
+          const float lb = ord_f32(lbk[q]);
+          int w = ex[h];
+          for (int j = 0; j < ccount[q]; ++j)
+            if (__uint_as_float(cand[q][j].y) >= lb) pair_tok[w++] = ((uint32_t)q << 24) | cand[q][j].x;
+        }
+      }
+      if (lane == 0) pair_off[kQC] = base;
+    }
+    __syncthreads();
+    const int n_pairs = pair_off[kQC];
+    for (int p = tid; p < n_pairs; p += kMThreads) {
+      const uint32_t e = pair_tok[p];
+      const int q = (int)(e >> 24), tok = (int)(e & 0xffffffu);
+      pair_score[p] = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, Qc + (size_t)q * D, D);
+    }
+    __syncthreads();
+    if (tid < nq) {
       float bs = __int_as_float(0x7fc00000);
       int bi = 0x7fffffff;
-      if (!in_full) {
-        const float lb = ord_f32(lbk[ql]);
-        if (lane < cnt) {
-          const uint2 c = cand[ql][lane];
-          if (__uint_as_float(c.y) >= lb) {
-            const int tok = (int)c.x;
-            bs = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, qrow, D);
-            bi = tok;
-          }
+      for (int p = pair_off[tid]; p < pair_off[tid + 1]; ++p) {
+        const int tok = (int)(pair_tok[p] & 0xffffffu);
+        if (better(pair_score[p], tok, bs, bi)) {
+          bs = pair_score[p];
+          bi = tok;
         }
-      } else {
-        const int32_t* sel = top_idx + ((size_t)s * n_queries + q0 + ql) * k;
-        for (int j = 0; j < k; ++j) {
-          const int b = __ldg(sel + j);
-          if (b < 0 || b >= n_slots) continue;
-          for (int p = lane; p < L; p += 32) {
-            const int tok = b * L + p;
-            const float v = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, qrow, D);
-            if (better(v, tok, bs, bi)) {
-              bs = v;
-              bi = tok;
-            }
+      }
+      best[tid] = (bi != 0x7fffffff && bs == bs) ? pack_best(bs, bi) : 0ull;
+    }
+    // queries scored in full: a warp each, lanes over the tokens of each selected block
+    for (int ql = warp; ql < nq; ql += kMWarps + 1) {
+      if (!(qstat[ql].w != 0.f || ccount[ql] > kCandCap)) continue;
+      const __nv_bfloat16* qrow = Qc + (size_t)ql * D;
+      float bs = __int_as_float(0x7fc00000);
+      int bi = 0x7fffffff;
+      const int32_t* sel = top_idx + ((size_t)s * n_queries + q0 + ql) * k;
+      for (int j = 0; j < k; ++j) {
+        const int b = __ldg(sel + j);
+        if (b < 0 || b >= n_slots) continue;
+        for (int p = lane; p < L; p += 32) {
+          const int tok = b * L + p;
+          const float v = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, qrow, D);
+          if (better(v, tok, bs, bi)) {
+            bs = v;
+            bi = tok;
           }
         }
       }
@@ -1063,8 +1172,28 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
     }
   }
   __syncthreads();
-  write_outputs<__nv_bfloat16>(best, nq, kMWarps + 1, (int64_t)s * n_queries + q0, L, n_slots, dv, s, pool_V,
-                               best_tok, best_score, out_V);
+  // outputs, flattened: the value rows move as 16-byte chunks over all threads
+  const int64_t sq0 = (int64_t)s * n_queries + q0;
+  if (tid < nq) {
+    const unsigned long long key = best[tid];
+    const bool found = key != 0ull;
+    best_tok[sq0 + tid] = found ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : -1;
+    best_score[sq0 + tid] = found ? unpack_score(key) : -INFINITY;
+  }
+  if (out_V != nullptr) {
+    const int vv = dv / 8;
+    for (int e = tid; e < nq * vv; e += kMThreads) {
+      const int ql = e / vv, c = e - ql * vv;
+      const unsigned long long key = best[ql];
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (key != 0ull) {
+        const int tok = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+        const int bb = tok / L, p = tok % L;
+        v = __ldg(reinterpret_cast<const uint4*>(pool_V + (((size_t)s * n_slots + bb) * L + p) * dv) + c);
+      }
+      reinterpret_cast<uint4*>(out_V + (sq0 + ql) * dv)[c] = v;
+    }
+  }
 }
 
 // int8 copy of one committed block per stream: one CTA per stream, a warp per
@@ -1321,8 +1450,8 @@ extern "C" int gfst_exact_readout_i8(const void* Q, const void* pool_K, const in
                L);
   GFST_REQUIRE(dv % 8 == 0, GFST_ERR_ALIGN, "dv=%d must be a multiple of 8", dv);
   GFST_REQUIRE((pool_V == nullptr) == (out_V == nullptr), GFST_ERR_ARG, "pool_V and out_V go together");
-  GFST_REQUIRE((int64_t)n_slots < (1LL << 21) && n_streams * (int64_t)n_slots * L < (1LL << 31), GFST_ERR_SHAPE,
-               "token index overflows");
+  GFST_REQUIRE((int64_t)n_slots * L < (1LL << 24) && n_streams * (int64_t)n_slots * L < (1LL << 31), GFST_ERR_SHAPE,
+               "the int8 first look needs n_slots * L < 2^24 (token index)");
   if (n_streams == 0 || n_queries == 0) return GFST_OK;
   GFST_REQUIRE(Q && pool_K && pool_K8 && k8_scale && top_idx && best_tok && best_score, GFST_ERR_ARG, "null buffer");
   GFST_REQUIRE(aligned16(Q) && aligned16(pool_K) && aligned16(pool_K8) && aligned16(k8_scale) && aligned16(pool_V) &&

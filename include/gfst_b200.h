@@ -538,7 +538,7 @@ GFST_API int gfst_exact_block_materialize(const void* packed, int64_t n_elements
  * non-finite or all-zero values, or selecting a block with a non-finite key,
  * is scored in full).  No reference counterpart: a B200 path for the readout
  * of modeling.py:599-657, 1151-1169.
- * Limits: d = 128 or 256; L % 16 == 0, L <= 256; k <= 32.                   */
+ * Limits: d = 128 or 256; L % 16 == 0, L <= 256; k <= 32; n_slots L < 2^24. */
 GFST_API int gfst_block_commit_i8(const void* K, int8_t* pool_K8, float* k8_scale, int64_t n_streams, int n_slots,
                                   int slot, int L, int d, cudaStream_t stream);
 GFST_API int gfst_exact_readout_i8(const void* Q, const void* pool_K, const int8_t* pool_K8, const float* k8_scale,
