@@ -33,9 +33,14 @@ measurement runs on a device heap that an earlier one shaped:
 
 Timing: W warm-up steps, then exactly K steps between a barrier + synchronize
 on both sides, CUDA events on the launching stream, the maximum over ranks.
-The timed region contains only the steps: per-step events are created before
-it, SM clocks are sampled by a separate process, and the per-kernel phase
-times come from a separate pass afterwards.  Rank 0 prints one JSON line.
+The K steps go through StreamingStep.run (the frame chain and the memory chain
+of consecutive blocks on two streams, joined at the end; per-block events on
+both streams give the per-step median and p90); the same steps joined one by
+one (StreamingStep.step) are timed after it as `joined_ms_per_step`.  The
+timed region contains only the steps: the events are created before it, SM
+clocks are sampled by a separate process, and the per-kernel times come from a
+separate pass afterwards in which the step's two streams are one, so that
+each kernel is timed alone.  Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
@@ -216,7 +221,7 @@ class PhaseEvents:
     """CUDA events around each kernel of a step, recorded on the stream the
     kernel is launched on; the events are created before the pass."""
 
-    NAMES = ("frames", "topk", "readout", "open_block", "commit")
+    NAMES = ("frames", "topk", "readout", "open_block", "commit", "commit_i8")
 
     def __init__(self, n_steps: int):
         import torch
@@ -246,18 +251,19 @@ class PhaseEvents:
             return inner
 
         self._orig = (gfst.stream_frames, retrieval.block_topk, readout.exact_readout, readout.open_block_readout,
-                      memory.block_commit_mean)
+                      memory.block_commit_mean, memory.block_commit_i8)
         gfst.stream_frames = timed(gfst.stream_frames, "frames")
         retrieval.block_topk = timed(retrieval.block_topk, "topk")
         readout.exact_readout = timed(readout.exact_readout, "readout")
         readout.open_block_readout = timed(readout.open_block_readout, "open_block")
         memory.block_commit_mean = timed(memory.block_commit_mean, "commit")
+        memory.block_commit_i8 = timed(memory.block_commit_i8, "commit_i8")
 
     def unwrap(self):
         from gfst_hmb_public_b200 import gfst, memory, readout, retrieval
 
         (gfst.stream_frames, retrieval.block_topk, readout.exact_readout, readout.open_block_readout,
-         memory.block_commit_mean) = self._orig
+         memory.block_commit_mean, memory.block_commit_i8) = self._orig
 
     def summary(self) -> dict:
         out: dict[str, list[float]] = {}
@@ -328,43 +334,64 @@ def run_stream_full(args, rank, world, device) -> dict:
     st = build_step(S, D, R, L, SLOTS, K_SEL, torch.bfloat16, device, SEED + 1000 * rank, SLOTS)
     A, Bm, Kt, Vt, Qt = step_inputs(S, L, D, R, M, torch.bfloat16, device, SEED + 1000 * rank + 1)
 
-    for _ in range(args.warmup):
-        st.step(A, Bm, Kt, Vt, Qt)
+    block = (A, Bm, Kt, Vt, Qt)
+    st.run([block] * args.warmup)
     torch.cuda.synchronize(device)
     _native.check_device_errors()
 
-    # ---- headline: exactly K steps, nothing else in the region -------------
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    # ---- headline: exactly K steps through StreamingStep.run, nothing else
+    # in the region (the per-block events are created before it) -------------
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    blk_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
     sampler = ClockSampler(device)
     sampler.start()
     barrier()
     torch.cuda.synchronize(device)
     w0 = time.time()
-    evs[0].record()
-    for i in range(args.steps):
-        out = st.step(A, Bm, Kt, Vt, Qt)
-        evs[i + 1].record()
+    start.record()
+    outs = st.run([block] * args.steps, block_events=blk_evs)
+    end.record()
     torch.cuda.synchronize(device)
     w1 = time.time()
     barrier()
     clocks = sampler.stop(w0, w1)
     _native.check_device_errors()
-    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
-    ms = max_over_ranks(evs[0].elapsed_time(evs[-1]) / args.steps, device)
+    # block i is done when both its frame and its memory work are
+    done_at = [max(start.elapsed_time(ef), start.elapsed_time(em)) for ef, em in blk_evs]
+    per_step = [done_at[0]] + [done_at[i] - done_at[i - 1] for i in range(1, args.steps)]
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, device)
     med = max_over_ranks(statistics.median(per_step), device)
     p90 = max_over_ranks(percentile(per_step, 0.9), device)
-    sel = out.top_idx
+    sel = outs[-1].top_idx
+    del outs
 
-    # ---- per-kernel phase times: a separate pass ---------------------------
+    # ---- the same steps joined one by one (StreamingStep.step) -------------
+    j0, j1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_joined = max(3, min(args.steps, 10))
+    barrier()
+    torch.cuda.synchronize(device)
+    j0.record()
+    for _ in range(n_joined):
+        st.step(*block)
+    j1.record()
+    torch.cuda.synchronize(device)
+    joined_ms = max_over_ranks(j0.elapsed_time(j1) / n_joined, device)
+
+    # ---- per-kernel times: a separate pass with both of the step's streams
+    # replaced by one, so that each kernel's events time it alone ------------
     n_phase = max(3, min(args.steps, 10))
     phases = PhaseEvents(n_phase)
+    saved_streams = (st.frames_stream, st.memory_stream)
+    st.frames_stream = st.memory_stream = torch.cuda.current_stream(device)
     phases.wrap()
     try:
         for _ in range(n_phase):
-            st.step(A, Bm, Kt, Vt, Qt)
+            st.step(*block)
         torch.cuda.synchronize(device)
     finally:
         phases.unwrap()
+        st.frames_stream, st.memory_stream = saved_streams
     phase_ms = phases.summary()
 
     # ---- end to end with host buffers ---------------------------------------
@@ -389,10 +416,11 @@ def run_stream_full(args, rank, world, device) -> dict:
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out[0])
     uniq = unique_selected_blocks(sel)
+    int8 = st.memory.k8 is not None
     res = {"ms": ms, "median": med, "p90": p90, "per_step": per_step, "phase_ms": phase_ms, "clocks": clocks,
            "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h, "uniq": uniq, "S": S, "b_local": b_local,
-           "launches": 5 * args.steps}
-    del st, A, Bm, Kt, Vt, Qt, host_in, host_out, pipe, out, sel
+           "joined_ms": joined_ms, "int8_keys": int8, "launches": (6 if int8 else 5) * args.steps}
+    del st, A, Bm, Kt, Vt, Qt, host_in, host_out, pipe, sel
     torch.cuda.empty_cache()
     return res
 
@@ -831,62 +859,67 @@ def run_ours(args, rank, world, local_rank, device) -> dict | None:
     value = tokens_per_step / (ms / 1e3)
     e2e_value = tokens_per_step / (r["e2e_ms"] / 1e3)
 
-    # algorithmic bytes per launch (rank 0's shard):
-    #   frames     -- unfused per-token contract: read U, A, B and write U
-    #   readout    -- distinct key blocks selected by the step's queries, plus
-    #                 queries, selections, results and value rows
+    # algorithmic work per launch (rank 0's shard), per kernel:
+    #   frames     -- the Householder flop count of a d x r thin QR plus the
+    #                 rank-m update, 4 d r^2 + 2 d r m per frame-token, whatever
+    #                 algorithm runs; bound by the FP32 units (no tensor-core or
+    #                 HBM bound applies: the frame stays on chip for the block)
+    #   readout    -- int8 first look: the int8 keys and per-token side data of
+    #                 every distinct selected block, plus queries, selections,
+    #                 results and value rows (the bf16 rows of the few tokens it
+    #                 re-scores are not counted); bf16 readout: the bf16 keys
     #   open_block -- the open block's keys, queries, results and value rows
-    #   topk       -- summaries of every slot + queries (2*d flops per pair)
+    #   topk       -- summaries of every slot against every query (2 d flops per pair)
     #   commit     -- read K, V of the block; write them and the summary
-    frames_bytes = S * L * (2 * D * R * 4 + (D * M + R * M) * 4)
-    readout_bytes = r["uniq"] * L * D * 2 + S * L * (D * 2 + K_SEL * 4 + D * 2 + 8)
+    #   commit_i8  -- read K of the block; write its int8 copy and side data
+    int8 = bool(r.get("int8_keys"))
+    key_block_bytes = L * D + (L + 4) * 4 if int8 else L * D * 2
+    readout_bytes = r["uniq"] * key_block_bytes + S * L * (D * 2 + K_SEL * 4 + D * 2 + 8)
     open_bytes = S * L * (D * 2 * 2 + 8 + 8 + D * 2)
     commit_bytes = S * L * D * 2 * 2 * 2 + S * D * 2
+    commit_i8_bytes = S * (L * D * 2 + L * D + (L + 4) * 4)
     topk_flops = 2.0 * S * L * SLOTS * D
-    shares = {k: v / sum(phase_ms.values()) for k, v in phase_ms.items()}
+    frames_flops = S * L * (4.0 * D * R * R + 2.0 * D * R * M)
+    clocks = r["clocks"]
+    sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
+    bf16_peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    fp32_peak = fp32_peak_tflops(sm_mhz)
+    names = {"frames": "frame_stream_chol_kernel", "readout": "exact_readout_i8_kernel" if int8 else
+             "exact_readout_mma_kernel", "open_block": "open_block_readout_kernel", "commit": "block_commit_kernel",
+             "commit_i8": "block_commit_i8_kernel", "topk": "block_topk_tc_kernel"}
+    work = {"frames": ("fp32", frames_flops / 1e12, "TFLOP/s", fp32_peak),
+            "topk": ("tensor", topk_flops / 1e12, "TFLOP/s", bf16_peak),
+            "readout": ("hbm", readout_bytes / 1e9, "GB/s", hbm_peak),
+            "open_block": ("hbm", open_bytes / 1e9, "GB/s", hbm_peak),
+            "commit": ("hbm", commit_bytes / 1e9, "GB/s", hbm_peak),
+            "commit_i8": ("hbm", commit_i8_bytes / 1e9, "GB/s", hbm_peak)}
+    total_ms = sum(phase_ms.values())
+    kernels = {}
+    for k, v in phase_ms.items():
+        bound, amount, unit, peak = work[k]
+        ach = amount / (v / 1e3)
+        kernels[k] = {"kernel": names[k], "ms": round(v, 4), "share": round(v / total_ms, 3), "bound": bound,
+                      "achieved": round(ach, 2), "unit": unit, "peak": round(peak, 1),
+                      "frac": round(ach / peak, 4)}
     dominant = max(phase_ms, key=phase_ms.get)
-    per_kernel = {"frames": frames_bytes, "readout": readout_bytes, "open_block": open_bytes,
-                  "commit": commit_bytes}
-    names = {"frames": "frame_stream", "readout": "exact_readout", "open_block": "open_block_readout",
-             "commit": "block_commit", "topk": "block_topk_tc"}
     traffic = None
     tp = REPO / "profiles" / "traffic.json"
     if tp.exists():
         try:
-            traffic = json.loads(tp.read_text()).get(dominant)
+            traffic = json.loads(tp.read_text()).get(names[dominant])  # keyed by kernel name
         except Exception:
             traffic = None
-    if dominant == "topk":
-        ach = topk_flops / (phase_ms["topk"] / 1e3) / 1e12
-        peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
-        roof = {"kernel": names[dominant], "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
-                "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": traffic}
-    else:
-        ach = per_kernel[dominant] / (phase_ms[dominant] / 1e3) / 1e9
-        roof = {"kernel": names[dominant], "bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak,
-                "unit": "GB/s", "frac": round(ach / hbm_peak, 4), "traffic": traffic}
-    clocks = r["clocks"]
-    sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
-    # frame work unit: the Householder flop count of a d x r thin QR plus the
-    # rank-m update (4 d r^2 + 2 d r m per token), whatever algorithm runs
-    frames_flops = S * L * (4.0 * D * R * R + 2.0 * D * R * M)
-    fr_tflops = frames_flops / (phase_ms["frames"] / 1e3) / 1e12
-    roof["peak_source"] = peak_src
+    dk = kernels[dominant]
+    roof = {"kernel": dk["kernel"], "bound": dk["bound"], "achieved": dk["achieved"], "peak": dk["peak"],
+            "unit": dk["unit"], "frac": dk["frac"], "traffic": traffic}
+    roof["peak_source"] = (f"derived: 148 SMs x 128 FP32 lanes x 2 flops x the sampled {sm_mhz:.0f} MHz (no FP32 "
+                           f"figure among the measured peaks)" if dk["bound"] == "fp32" else peak_src)
     roof["per_launch_units"] = f"rank 0's {S} streams x {L} tokens"
-    roof["frames_fp32"] = {"achieved_tflops": round(fr_tflops, 2),
-                           "peak_tflops_at_clock": round(fp32_peak_tflops(sm_mhz), 1),
-                           "frac": round(fr_tflops / fp32_peak_tflops(sm_mhz), 4)}
-    if "readout" in phase_ms:
-        rb = readout_bytes / (phase_ms["readout"] / 1e3) / 1e9
-        roof["readout_hbm"] = {"achieved_gbs": round(rb, 1), "frac": round(rb / hbm_peak, 4)}
-    if "topk" in phase_ms:
-        tf = topk_flops / (phase_ms["topk"] / 1e3) / 1e12
-        roof["topk_tensor"] = {"achieved_tflops": round(tf, 2),
-                               "frac_of_bf16_peak": round(tf / float(peaks.get("bf16_tflops", 1590.0)), 4)}
-    roof["kernel_ms"] = {k: round(v, 4) for k, v in phase_ms.items()}
-    roof["kernel_share"] = {k: round(v, 3) for k, v in shares.items()}
-    roof["phase_pass"] = "per-kernel times from a separate pass of the same steps (events on each kernel's stream)"
+    roof["kernels"] = kernels
+    roof["phase_pass"] = ("per-kernel times from a separate pass of the same steps with the step's two streams "
+                          "replaced by one (each kernel timed alone by CUDA events on its stream)")
     roof["readout_unique_block_frac"] = round(r["uniq"] / (S * SLOTS), 3)
+    roof["readout_int8_first_look"] = int8
 
     cpu = cpu_baseline_sample() if (world == 1 and not args.no_cpu_baseline) else None
     res = {
@@ -897,6 +930,7 @@ def run_ours(args, rank, world, local_rank, device) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
+        "joined_ms_per_step": round(r["joined_ms"], 4),
         "step_ms": {"median": round(r["median"], 4), "p90": round(r["p90"], 4),
                     "min": round(min(r["per_step"]), 4), "max": round(max(r["per_step"]), 4)},
         "higher_is_better": True,
@@ -916,6 +950,8 @@ def run_ours(args, rank, world, local_rank, device) -> dict | None:
             "streams_per_gpu": S,
             "parallelism": f"dp{world} (batch split over ranks, no collectives on the data path)",
             "l2": "step inputs 436 MB in total (> 126 MB L2), re-read every step",
+            "timed_path": "StreamingStep.run over the K blocks (frame chain and memory chain on two streams, "
+                          "joined at the end)",
         },
         "roofline": roof,
         "cpu_baseline": cpu,

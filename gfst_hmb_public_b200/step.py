@@ -90,6 +90,37 @@ class StreamingStep:
         """Token index of position 0 of the step's own block in StepOutputs.best_tok."""
         return self.n_slots * self.block_len
 
+    def _memory_work(self, K: torch.Tensor, V: torch.Tensor, Q: torch.Tensor) -> StepOutputs:
+        """Top-k, readout, open block and commit of one block, enqueued on the
+        current stream (the memory stream)."""
+        n_valid = self.memory.n_valid
+        if n_valid > 0:
+            top_s, top_i = retrieval.block_topk(Q, self.memory.summary, self.k, n_blocks=n_valid)
+            best_tok, best_score, value = readout.exact_readout(Q, self.memory.pool_K, self.memory.pool_V, top_i,
+                                                                k8=self.memory.k8)
+        else:
+            S, L = Q.shape[0], Q.shape[1]
+            top_i = torch.full((S, L, self.k), -1, dtype=torch.int32, device=self.device)
+            best_tok = torch.full((S, L), -1, dtype=torch.int32, device=self.device)
+            best_score = torch.full((S, L), float("-inf"), dtype=torch.float32, device=self.device)
+            value = torch.zeros((S, L, V.shape[-1]), dtype=V.dtype, device=self.device)
+        readout.open_block_readout(Q, K, V, best_tok, best_score, value, open_base=self.open_base)
+        slot = self.memory.commit(K, V)
+        return StepOutputs(best_tok, best_score, value, top_i, self.open_base, slot)
+
+    def _join(self, cur, results) -> None:
+        cur.wait_stream(self.frames_stream)
+        cur.wait_stream(self.memory_stream)
+        # tensors produced on side streams are consumed on the current stream
+        # (under CUDA-graph capture the graph's private pool keeps them instead)
+        if not torch.cuda.is_current_stream_capturing():
+            self.U.record_stream(cur)
+            for res in results:
+                for t in (res.best_tok, res.best_score, res.value, res.top_idx):
+                    t.record_stream(cur)
+        if self.check_errors:
+            nat.check_device_errors()
+
     def step(self, A: torch.Tensor, B: torch.Tensor, K: torch.Tensor, V: torch.Tensor, Q: torch.Tensor,
              *, out: StepOutputs | None = None) -> StepOutputs:
         """A [S, L, d, m], B [S, L, r, m] fp32 update factors; K, V, Q [S, L, d]
@@ -102,45 +133,58 @@ class StreamingStep:
         with torch.cuda.stream(self.frames_stream):
             gfst.stream_frames(self.U, A, B, eps_sign=self.eps_sign, sign_mode=self.sign_mode)
         with torch.cuda.stream(self.memory_stream):
-            n_valid = self.memory.n_valid
-            if n_valid > 0:
-                top_s, top_i = retrieval.block_topk(Q, self.memory.summary, self.k, n_blocks=n_valid)
-                best_tok, best_score, value = readout.exact_readout(Q, self.memory.pool_K, self.memory.pool_V, top_i,
-                                                                    k8=self.memory.k8)
-            else:
-                S, L = Q.shape[0], Q.shape[1]
-                top_i = torch.full((S, L, self.k), -1, dtype=torch.int32, device=self.device)
-                best_tok = torch.full((S, L), -1, dtype=torch.int32, device=self.device)
-                best_score = torch.full((S, L), float("-inf"), dtype=torch.float32, device=self.device)
-                value = torch.zeros((S, L, V.shape[-1]), dtype=V.dtype, device=self.device)
-            readout.open_block_readout(Q, K, V, best_tok, best_score, value, open_base=self.open_base)
-            slot = self.memory.commit(K, V)
-        cur.wait_stream(self.frames_stream)
-        cur.wait_stream(self.memory_stream)
-        # tensors produced on side streams are consumed on the current stream
-        # (under CUDA-graph capture the graph's private pool keeps them instead)
-        if not torch.cuda.is_current_stream_capturing():
-            for t in (best_tok, best_score, value, top_i, self.U):
-                t.record_stream(cur)
-        if self.check_errors:
-            nat.check_device_errors()
-        result = StepOutputs(best_tok, best_score, value, top_i, self.open_base, slot)
+            result = self._memory_work(K, V, Q)
+        self._join(cur, (result,))
         if out is not None:
-            out.best_tok.copy_(best_tok)
-            out.best_score.copy_(best_score)
-            out.value.copy_(value)
-            out.top_idx.copy_(top_i)
-            out.open_base, out.slot = self.open_base, slot
+            out.best_tok.copy_(result.best_tok)
+            out.best_score.copy_(result.best_score)
+            out.value.copy_(result.value)
+            out.top_idx.copy_(result.top_idx)
+            out.open_base, out.slot = result.open_base, result.slot
             return out
         return result
+
+    def run(self, blocks, *, block_events=None) -> list:
+        """Several consecutive blocks in one call: ``blocks`` is a sequence of
+        (A, B, K, V, Q) tuples as ``step`` takes them; returns one StepOutputs
+        per block, the same values consecutive ``step`` calls return.
+        ``block_events``, if given, holds one (frames_event, memory_event) pair
+        of CUDA events per block, recorded on the two streams after that
+        block's work (block i is done when both have completed).
+
+        The frames of a block depend only on the frames of the block before,
+        and its top-k, readout and commit only on the memory the blocks before
+        committed, so the two chains run on their own streams with no join
+        between blocks: the frame kernel of block i+1 may run beside the
+        readout of block i (on B200, 20 blocks of 64 tokens with 512-block
+        rings: 4.55 against 4.79 ms per block at 2048 streams, 1.03 against
+        1.18 ms at 256).  The current stream waits for both chains at the end."""
+        blocks = [tuple(b) for b in blocks]
+        cur = torch.cuda.current_stream(self.device)
+        self.frames_stream.wait_stream(cur)
+        self.memory_stream.wait_stream(cur)
+        if block_events is not None and len(block_events) < len(blocks):
+            raise ValueError("block_events: one (frames, memory) event pair per block")
+        results = []
+        for i, (A, B, K, V, Q) in enumerate(blocks):
+            with torch.cuda.stream(self.frames_stream):
+                gfst.stream_frames(self.U, A, B, eps_sign=self.eps_sign, sign_mode=self.sign_mode)
+                if block_events is not None:
+                    block_events[i][0].record(self.frames_stream)
+            with torch.cuda.stream(self.memory_stream):
+                results.append(self._memory_work(K, V, Q))
+                if block_events is not None:
+                    block_events[i][1].record(self.memory_stream)
+        self._join(cur, results)
+        return results
 
 
 class StreamingPass:
     """A whole streaming pass captured once as a CUDA graph and replayed.
 
-    The pass is: empty the memory ring, load the frames ``U0``, then one
-    ``StreamingStep.step`` per block of ``blocks`` (each an (A, B, K, V, Q)
-    tuple of device tensors, as ``step`` takes them).  At small batches the
+    The pass is: empty the memory ring, load the frames ``U0``, then
+    ``StreamingStep.run`` over ``blocks`` (each an (A, B, K, V, Q) tuple of
+    device tensors, as ``step`` takes them).  At small batches the
     pass is a chain of short kernels whose launch cost exceeds their run time;
     replaying the captured graph launches them all at once.  The input tensors
     (``U0`` and every block) are read in place on each replay: copy new data
@@ -171,7 +215,7 @@ class StreamingPass:
         st = self.step_obj
         st.reset()
         st.set_frames(self.U0)
-        return [st.step(*blk) for blk in self.blocks]
+        return st.run(self.blocks)
 
     def replay(self) -> list:
         """Run the pass again on the current stream; returns ``outputs``."""

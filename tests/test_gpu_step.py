@@ -94,3 +94,35 @@ def test_graph_captured_pass_matches_eager_pass(cuda_device, shape):
             for got, exp in zip((o.best_tok, o.best_score, o.value, o.top_idx), w):
                 assert torch.equal(got, exp)
         assert torch.equal(st.U, eager.U)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_multi_block_run_matches_consecutive_steps(cuda_device, dt):
+    # StreamingStep.run enqueues the frame chain and the memory chain of
+    # several blocks on their own streams with no join between blocks; its
+    # results equal those of one step() per block, bit for bit, through a
+    # ring wrap (7 blocks into 4 slots) and a second call that continues
+    S, d, r, m, L, n_slots, k = 9, 128, 32, 4, 64, 4, 3
+    g = torch.Generator().manual_seed(71)
+    blocks = []
+    for _ in range(7):
+        A = torch.randn((S, L, d, m), generator=g) / d ** 0.5
+        B = torch.randn((S, L, r, m), generator=g) / d ** 0.5
+        K, V, Q = (torch.randn((S, L, d), generator=g).to(dt) for _ in range(3))
+        blocks.append(tuple(t.to(cuda_device) for t in (A, B, K, V, Q)))
+    U0 = wl.random_orthonormal_frames(S, d, r, seed=72, device=cuda_device)
+    a = StreamingStep(S, d=d, r=r, block_len=L, n_slots=n_slots, k=k, dtype=dt, device=cuda_device)
+    b = StreamingStep(S, d=d, r=r, block_len=L, n_slots=n_slots, k=k, dtype=dt, device=cuda_device)
+    a.set_frames(U0)
+    b.set_frames(U0)
+    want = [a.step(*blk) for blk in blocks]
+    got = b.run(blocks[:5]) + b.run(blocks[5:])
+    torch.cuda.synchronize()
+    assert len(got) == len(want)
+    for o, w in zip(got, want):
+        for x, y in zip((o.best_tok, o.best_score, o.value, o.top_idx), (w.best_tok, w.best_score, w.value,
+                                                                          w.top_idx)):
+            assert torch.equal(x, y)
+        assert o.slot == w.slot and o.open_base == w.open_base
+    assert torch.equal(a.U, b.U)
+    assert b.run([]) == []
