@@ -789,6 +789,8 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_mma_kernel(
 // holding a key with a non-finite value (E = inf), is scored in full from the
 // bf16 keys instead.
 constexpr int kCandCap = 32;
+constexpr int kMaxStagesI8 = 16;  // ring stages of the int8 readout
+constexpr int kI8Warps = 8;       // its consumer warps (plus one TMA warp)
 
 __device__ __forceinline__ void mma_i8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
@@ -829,14 +831,15 @@ __device__ __forceinline__ float bf16_row_dot(const __nv_bfloat16* __restrict__ 
   return acc;
 }
 
-template <int NB8>
-__global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
+template <int NB8, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
     const __grid_constant__ CUtensorMap tmK8, const __nv_bfloat16* __restrict__ Q,
     const __nv_bfloat16* __restrict__ pool_K, const float* __restrict__ k8_scale,
     const __nv_bfloat16* __restrict__ pool_V, const int32_t* __restrict__ top_idx, int n_queries, int n_chunks,
     int n_slots, int L, int dv, int k, int n_stages, float slack, int32_t* __restrict__ best_tok,
     float* __restrict__ best_score, __nv_bfloat16* __restrict__ out_V) {
   constexpr int D = NB8 * 128;  // key width = int8 bytes per key row
+  constexpr int NT = (CW + 1) * 32;  // CW consumer warps + the TMA warp
   constexpr int KSTEPS = D / 32;
   extern __shared__ uint8_t dyn_raw[];
   __shared__ RunTable rt;
@@ -845,22 +848,24 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
   __shared__ int ccount[kQC];
   __shared__ uint2 cand[kQC][kCandCap];
   __shared__ float4 qstat[kQC];  // s_q, e_q, n_q, 1 = score in full
-  __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
-  __shared__ int stage_run[kMaxStages];
+  __shared__ uint64_t full[kMaxStagesI8], empty[kMaxStagesI8];
+  __shared__ int stage_run[kMaxStagesI8];
   __shared__ int abort_s, issued_s;
   volatile int* abort_v = &abort_s;
   volatile int* stage_run_v = stage_run;
 
   const uint32_t key_bytes = (uint32_t)L * D;
-  const uint32_t side_bytes = (uint32_t)(L + 4) * 4u;  // scales, then E, N, 0, 0
-  // stages 1024-byte aligned (the swizzle atom)
-  const uint32_t stage_bytes = (key_bytes + side_bytes + 1023u) & ~1023u;
+  const uint32_t side_bytes = (uint32_t)(L + 4) * 4u;  // scales, then E, N, 0, 0 (a multiple of 16)
+  // key stages 1024-byte aligned (the swizzle atom); the side data in a ring
+  // of its own after them, so that no stage carries alignment padding
+  const uint32_t stage_bytes = (key_bytes + 1023u) & ~1023u;
   const uint32_t raw = smem_u32(dyn_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* dyn = dyn_raw + (base - raw);
-  uint8_t* qs = dyn + (size_t)n_stages * stage_bytes;  // [kQC][D] int8, chunk-swizzled
+  uint8_t* side = dyn + (size_t)n_stages * stage_bytes;        // [n_stages][L + 4] fp32
+  uint8_t* qs = side + (size_t)n_stages * side_bytes;           // [kQC][D] int8, chunk-swizzled
   uint8_t* zrow = qs + kQC * D;
-  const uint32_t qs_u = base + n_stages * stage_bytes;
+  const uint32_t qs_u = base + n_stages * (stage_bytes + side_bytes);
   const uint32_t zrow_u = qs_u + kQC * D;
   const int64_t s = blockIdx.x / n_chunks;
   const int q0 = (int)(blockIdx.x % n_chunks) * kQC;
@@ -868,19 +873,19 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const __nv_bfloat16* Qc = Q + ((size_t)s * n_queries + q0) * D;
 
-  for (int q = tid; q < kQC; q += kMThreads) {
+  for (int q = tid; q < kQC; q += NT) {
     best[q] = 0ull;
     lbk[q] = ord_u32(-INFINITY);
     ccount[q] = 0;
   }
-  for (int e = tid; e < D / 16; e += kMThreads) reinterpret_cast<uint4*>(zrow)[e] = make_uint4(0, 0, 0, 0);
+  for (int e = tid; e < D / 16; e += NT) reinterpret_cast<uint4*>(zrow)[e] = make_uint4(0, 0, 0, 0);
   // the chunk's bf16 queries into the (still idle) ring, one coalesced copy
   __nv_bfloat16* qbf = reinterpret_cast<__nv_bfloat16*>(dyn);
-  for (int e = tid; e < nq * D / 8; e += kMThreads)
+  for (int e = tid; e < nq * D / 8; e += NT)
     reinterpret_cast<uint4*>(qbf)[e] = __ldg(reinterpret_cast<const uint4*>(Qc) + e);
   __syncthreads();
   // quantise them: one warp per query, D / 32 values per lane
-  for (int q = warp; q < kQC; q += kMWarps + 1) {
+  for (int q = warp; q < kQC; q += CW + 1) {
     constexpr int PL = D / 32;
     float v[PL];
     float mx = 0.f, nn = 0.f;
@@ -938,15 +943,15 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
     mbar_init_fence();
   }
   if (n_slots <= kCandCap * kQC * 2)  // the candidate lists (unused until the scoring) hold the histogram
-    build_runs_counting<kMThreads>(rt, reinterpret_cast<int*>(&cand[0][0]),
+    build_runs_counting<NT>(rt, reinterpret_cast<int*>(&cand[0][0]),
                                    top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
   else
-    build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k,
+    build_runs<NT, CW * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k,
                                         n_slots);
   const int n_runs = rt.n_runs;
   // (the builders end with a CTA barrier: the ring's bf16 query copy is dead)
 
-  if (warp == kMWarps) {
+  if (warp == CW) {
     if (lane == 0) {
       // the generic-proxy writes of the query copy precede the ring's copies
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -966,7 +971,7 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
 #pragma unroll
         for (int kb = 0; kb < NB8; ++kb)
           tma_load_2d(sb + (size_t)kb * L * 128, &tmK8, &full[st], kb * 128, (int)(blk * L));
-        bulk_load(sb + key_bytes, k8_scale + blk * (L + 4), side_bytes, &full[st]);
+        bulk_load(side + (size_t)st * side_bytes, k8_scale + blk * (L + 4), side_bytes, &full[st]);
       }
       issued_s = r;
     }
@@ -979,13 +984,13 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk)
       aoff[kk] = (uint32_t)((kk >> 2) * L * 128) + (uint32_t)((((2 * kk + a_hi) & 7) ^ (lane & 7)) << 4);
-    for (int r = warp; r < n_runs; r += kMWarps) {
+    for (int r = warp; r < n_runs; r += CW) {
       const int st = r % n_stages;
       if (!wait_stage(stage_run_v, full, abort_v, st, r, n_stages)) break;
       const int p0 = rt.run_start[r], p1 = rt.run_start[r + 1];
       const int b = (int)(rt.keys[p0] >> 11);
       const uint32_t abase = base + st * stage_bytes + a_row * 128;
-      const float* sk = reinterpret_cast<const float*>(dyn + (size_t)st * stage_bytes + key_bytes);
+      const float* sk = reinterpret_cast<const float*>(side + (size_t)st * side_bytes);
       const float E = sk[L], N = sk[L + 1];
       if (!(E <= 3.0e38f)) {
         // a key of this block has a non-finite value: its queries are scored in full
@@ -1082,7 +1087,7 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
     }
   }
   __syncthreads();
-  if (tid == kMWarps * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
+  if (tid == CW * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
   // exact re-score of the surviving candidates, flattened over the chunk: the
   // (query, token) pairs with A + b >= the query's final LB are listed in the
   // (now idle) run table, one thread per pair computes the fp32 score from
@@ -1130,7 +1135,7 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
     }
     __syncthreads();
     const int n_pairs = pair_off[kQC];
-    for (int p = tid; p < n_pairs; p += kMThreads) {
+    for (int p = tid; p < n_pairs; p += NT) {
       const uint32_t e = pair_tok[p];
       const int q = (int)(e >> 24), tok = (int)(e & 0xffffffu);
       pair_score[p] = bf16_row_dot(pool_K + (((size_t)s * n_slots) * L + tok) * D, Qc + (size_t)q * D, D);
@@ -1149,7 +1154,7 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
       best[tid] = (bi != 0x7fffffff && bs == bs) ? pack_best(bs, bi) : 0ull;
     }
     // queries scored in full: a warp each, lanes over the tokens of each selected block
-    for (int ql = warp; ql < nq; ql += kMWarps + 1) {
+    for (int ql = warp; ql < nq; ql += CW + 1) {
       if (!(qstat[ql].w != 0.f || ccount[ql] > kCandCap)) continue;
       const __nv_bfloat16* qrow = Qc + (size_t)ql * D;
       float bs = __int_as_float(0x7fc00000);
@@ -1182,7 +1187,7 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_i8_kernel(
   }
   if (out_V != nullptr) {
     const int vv = dv / 8;
-    for (int e = tid; e < nq * vv; e += kMThreads) {
+    for (int e = tid; e < nq * vv; e += NT) {
       const int ql = e / vv, c = e - ql * vv;
       const unsigned long long key = best[ql];
       uint4 v = make_uint4(0, 0, 0, 0);
@@ -1361,26 +1366,41 @@ int launch_i8(const void* Q, const void* pool_K, const int8_t* pool_K8, const fl
               float* best_score, void* out_V, cudaStream_t stream) {
   const int64_t n_chunks = (Nq + kQC - 1) / kQC;
   GFST_REQUIRE(S * n_chunks <= 0x7fffffffLL, GFST_ERR_SHAPE, "too many query chunks");
-  const size_t stage_bytes = ((size_t)L * d + (size_t)(L + 4) * 4 + 1023) & ~(size_t)1023;
-  // about 64 KB of ring: two CTAs per SM with the run table and candidate lists
-  int n_stages = (int)((64u * 1024u) / stage_bytes);
-  n_stages = n_stages < 2 ? 2 : (n_stages > kMaxStages ? kMaxStages : n_stages);
+  const size_t stage_bytes = ((size_t)L * d + 1023) & ~(size_t)1023;
+  const size_t side_bytes = (size_t)(L + 4) * 4;
+  const size_t fixed = 1024 + (size_t)(kQC + 1) * d;  // alignment slack, quantised queries, zero row
+  // the ring takes what shared memory leaves beside the kernel's static arrays
+  // at two CTAs per SM (d = 128: 8 stages).  Measured on B200, 2048 streams x
+  // 64 queries x 16 of 512 blocks: two CTAs of 8 consumer warps 1.50 ms, of 4
+  // consumer warps 1.60 ms; one CTA of 8 consumer warps with a 22-stage ring
+  // 2.51 ms -- the consumers' per-block chains, not the bytes in flight, set
+  // the pace, so more CTAs per SM beat a deeper ring.
+  int dev = 0, smem_sm = 0, reserved = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, d == 128 ? (const void*)exact_readout_i8_kernel<1, kI8Warps>
+                                                      : (const void*)exact_readout_i8_kernel<2, kI8Warps>);
+  GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+  const long long budget = (long long)smem_sm / 2 - reserved - (long long)fa.sharedSizeBytes - (long long)fixed;
+  int n_stages = budget > 0 ? (int)(budget / (long long)(stage_bytes + side_bytes)) : 0;
+  n_stages = n_stages < 2 ? 2 : (n_stages > kMaxStagesI8 ? kMaxStagesI8 : n_stages);
   // the ring holds the chunk's bf16 queries before the pipeline starts
   while ((size_t)n_stages * stage_bytes < (size_t)kQC * d * 2) ++n_stages;
-  const size_t dyn = 1024 + (size_t)n_stages * stage_bytes + (size_t)(kQC + 1) * d;
+  const size_t dyn = fixed + (size_t)n_stages * (stage_bytes + side_bytes);
   CUtensorMap tm;
   const int st = make_u8_map(&tm, pool_K8, (uint64_t)S * NS * L, d, L);
   if (st != GFST_OK) return st;
   // fp32 rounding of A and of an fp32 evaluation of the exact score: 2 d + 16 units of 2^-24
   const float slack = (float)(2 * d + 16) / 16777216.f;
   const unsigned grid = (unsigned)(S * n_chunks);
-  cudaError_t e = cudaSuccess;
-#define GFST_READOUT_I8(NB)                                                                                       \
+#define GFST_READOUT_I8(NB, CWV)                                                                                  \
   {                                                                                                               \
-    auto kern = exact_readout_i8_kernel<NB>;                                                                      \
+    auto kern = exact_readout_i8_kernel<NB, CWV>;                                                                 \
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);                        \
     GFST_REQUIRE(e == cudaSuccess, GFST_ERR_DEVICE, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));          \
-    kern<<<grid, kMThreads, dyn, stream>>>(tm, static_cast<const __nv_bfloat16*>(Q),                               \
+    kern<<<grid, (CWV + 1) * 32, dyn, stream>>>(tm, static_cast<const __nv_bfloat16*>(Q),                               \
                                            static_cast<const __nv_bfloat16*>(pool_K),                             \
                                            k8_scale,                                                              \
                                            static_cast<const __nv_bfloat16*>(pool_V), top_idx, Nq, (int)n_chunks, \
@@ -1388,8 +1408,8 @@ int launch_i8(const void* Q, const void* pool_K, const int8_t* pool_K8, const fl
                                            static_cast<__nv_bfloat16*>(out_V));                                   \
     return check_launch("exact_readout_i8_kernel");                                                                \
   }
-  if (d == 128) GFST_READOUT_I8(1)
-  GFST_READOUT_I8(2)
+  if (d == 128) GFST_READOUT_I8(1, kI8Warps)
+  GFST_READOUT_I8(2, kI8Warps)
 #undef GFST_READOUT_I8
 }
 
