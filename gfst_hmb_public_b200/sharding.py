@@ -16,10 +16,14 @@ Two partitions, one process per GPU over ``torch.distributed`` (NCCL on NVLink):
        the winner, identical on every rank;
     5. value exchange: the winner's owner is known on every rank (its block
        range), so only owners send value rows -- either all-gathered
-       ("replicated": every rank gets every row) or sent with one all-to-all
-       to the rank that owns the query's stream ("stream_shard": each rank gets
-       the rows of its own stream shard).  Counts follow from the winners, so
-       no sizes are exchanged.
+       ("replicated": every rank gets every row) or delivered to the rank that
+       owns the query's stream ("stream_shard": each rank gets the rows of its
+       own stream shard).  Counts follow from the winners, so no sizes are
+       exchanged.  For equal stream shards over NCCL the stream-shard delivery
+       is one reduce-scatter: each rank contributes the rows it owns and -0.0
+       elsewhere (x + -0.0 = x for every x, so the sum is the owner's row bit
+       for bit), with no host synchronisation and no sorting; otherwise one
+       all-to-all of the owned rows, split sizes counted on the device.
   The result equals the single-GPU readout: scores of a (query, block) pair do
   not depend on which rank computes them, and the merges use the same total
   order (score descending, index ascending).
@@ -183,6 +187,8 @@ def sharded_readout(Q: torch.Tensor, summary: torch.Tensor, pool_K: torch.Tensor
         mine = owner == rank  # the winner is this rank's own best for that query
         if value_layout == "replicated":
             value = _exchange_replicated(bv, owner, mine, world, group)
+        elif S % world == 0 and dist.get_backend(group) == "nccl":
+            value = _reduce_scatter_to_stream_shards(bv, best_t, mine, rank, world, group)
         else:
             value = _exchange_to_stream_shards(bv, owner, mine, rank, world, group)
     tm.mark("value_exchange")
@@ -220,6 +226,22 @@ def _exchange_replicated(bv: torch.Tensor, owner: torch.Tensor, mine: torch.Tens
         if counts[r]:
             value[by_owner[starts[r]:starts[r + 1]]] = parts[r, :counts[r]]
     return value.reshape(S, Nq, dv)
+
+
+def _reduce_scatter_to_stream_shards(bv: torch.Tensor, best_t: torch.Tensor, mine: torch.Tensor, rank: int,
+                                     world: int, group):
+    """Equal stream shards: the rows this rank owns, -0.0 elsewhere, summed over
+    the ranks by one reduce-scatter along the stream axis.  Exactly one rank
+    owns each found winner and -0.0 is the identity of the addition, so every
+    row arrives bit for bit; rows without a winner come out as +0.0, as the
+    single-GPU readout writes them."""
+    S, Nq, dv = bv.shape
+    contrib = torch.where(mine[..., None], bv, torch.full((), -0.0, dtype=bv.dtype, device=bv.device))
+    value = torch.empty((S // world, Nq, dv), dtype=bv.dtype, device=bv.device)
+    dist.reduce_scatter_tensor(value, contrib.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    lo = rank * (S // world)
+    found = best_t[lo:lo + S // world] >= 0
+    return torch.where(found[..., None], value, torch.zeros((), dtype=bv.dtype, device=bv.device))
 
 
 def _exchange_to_stream_shards(bv: torch.Tensor, owner: torch.Tensor, mine: torch.Tensor, rank: int, world: int,
