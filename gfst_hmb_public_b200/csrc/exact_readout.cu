@@ -850,7 +850,7 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
   __shared__ float4 qstat[kQC];  // s_q, e_q, n_q, 1 = score in full
   __shared__ uint64_t full[kMaxStagesI8], empty[kMaxStagesI8];
   __shared__ int stage_run[kMaxStagesI8];
-  __shared__ int abort_s, issued_s;
+  __shared__ int abort_s, issued_p[4];
   volatile int* abort_v = &abort_s;
   volatile int* stage_run_v = stage_run;
 
@@ -939,7 +939,7 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
       stage_run[i] = -1;
     }
     abort_s = 0;
-    issued_s = 0;
+    issued_p[0] = issued_p[1] = issued_p[2] = issued_p[3] = 0;
     mbar_init_fence();
   }
   if (n_slots <= kCandCap * kQC * 2)  // the candidate lists (unused until the scoring) hold the histogram
@@ -951,12 +951,17 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
   const int n_runs = rt.n_runs;
   // (the builders end with a CTA barrier: the ring's bf16 query copy is dead)
 
+  // producer lanes: lane p issues the runs r = p (mod np) into the stages
+  // r % n_stages, which no other lane touches (np divides n_stages); one
+  // issuing thread spends several hundred cycles per run between its barrier
+  // waits and copies, which held the ring below what the consumers take
+  const int np = n_stages % 4 == 0 ? 4 : (n_stages % 2 == 0 ? 2 : 1);
   if (warp == CW) {
-    if (lane == 0) {
+    if (lane < np) {
       // the generic-proxy writes of the query copy precede the ring's copies
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      int r = 0;
-      for (; r < n_runs; ++r) {
+      int r = lane;
+      for (; r < n_runs; r += np) {
         const int st = r % n_stages;
         if (!mbar_wait(&empty[st], ((r / n_stages) & 1) ^ 1)) {
           *abort_v = 1;
@@ -973,7 +978,7 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
           tma_load_2d(sb + (size_t)kb * L * 128, &tmK8, &full[st], kb * 128, (int)(blk * L));
         bulk_load(side + (size_t)st * side_bytes, k8_scale + blk * (L + 4), side_bytes, &full[st]);
       }
-      issued_s = r;
+      issued_p[lane] = r;
     }
   } else {
     const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
@@ -1046,39 +1051,53 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int j = e & 1;
-                const float a = u < tn ? (float)acc[u][e] * ((e & 2) ? s1 : s0) * sq[j] : -INFINITY;
-                av[u][e] = a;
-                amax[j] = fmaxf(amax[j], a);
+                av[u][e] = u < tn ? (float)acc[u][e] * ((e & 2) ? s1 : s0) * sq[j] : -INFINITY;
               }
             }
-            // LB of each column: max over the 8 lanes that hold it, then over the CTA
+            // column maxima as a tree (fmaxf is exact, so the order is free)
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              amax[j] = fmaxf(fmaxf(fmaxf(av[0][j], av[0][j + 2]), fmaxf(av[1][j], av[1][j + 2])),
+                              fmaxf(fmaxf(av[2][j], av[2][j + 2]), fmaxf(av[3][j], av[3][j + 2])));
+            // LB of each column: max over the 8 lanes that hold it, then over the
+            // CTA.  The atomicMax returns the CTA's LB before this warp's
+            // contribution, so max(old, own) is the LB right after it -- a valid
+            // lower bound without a second read (any LB at or below the final
+            // one prunes correctly; the final filter uses the final LB)
             float lbc[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               float m = amax[j];
 #pragma unroll
               for (int o = 4; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-              if ((lane >> 2) == 0 && qc[j] >= 0) atomicMax(&lbk[qc[j]], ord_u32(m - bq_[j]));
+              const uint32_t own = ord_u32(m - bq_[j]);
+              uint32_t lb = own;
+              if ((lane >> 2) == 0 && qc[j] >= 0) lb = max(atomicMax(&lbk[qc[j]], own), own);
+              lb = __shfl_sync(0xffffffffu, lb, lane & 3);  // lanes t, t + 4, ... hold column 2t + j
+              lbc[j] = qc[j] >= 0 ? ord_f32(lb) - bq_[j] : INFINITY;
             }
-            __syncwarp();
+            // candidates: A >= LB - b, i.e. A + b >= LB; most pairs fail, so
+            // the tests come first as one mask and the appends only run for it
+            uint32_t pass = 0u;
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
-              lbc[j] = qc[j] >= 0 ? ord_f32(*(volatile uint32_t*)&lbk[qc[j]]) - bq_[j] : INFINITY;
-            // candidates: A >= LB - b, i.e. A + b >= LB
+            for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+              for (int e = 0; e < 4; ++e) pass |= (av[u][e] >= lbc[e & 1] ? 1u : 0u) << (4 * u + e);
+            if (pass != 0u) {
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j = e & 1;
-                if (av[u][e] >= lbc[j]) {
-                  const int row = (t + u) * 16 + (lane >> 2) + ((e & 2) ? 8 : 0);
-                  const int slot = atomicAdd(&ccount[qc[j]], 1);
-                  if (slot < kCandCap)
-                    cand[qc[j]][slot] = make_uint2((uint32_t)(b * L + row), __float_as_uint(av[u][e] + bq_[j]));
+              for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = e & 1;
+                  if ((pass >> (4 * u + e)) & 1u) {
+                    const int row = (t + u) * 16 + (lane >> 2) + ((e & 2) ? 8 : 0);
+                    const int slot = atomicAdd(&ccount[qc[j]], 1);
+                    if (slot < kCandCap)
+                      cand[qc[j]][slot] = make_uint2((uint32_t)(b * L + row), __float_as_uint(av[u][e] + bq_[j]));
+                  }
                 }
               }
             }
-            amax[0] = amax[1] = -INFINITY;
           }
         }
       }
@@ -1087,7 +1106,13 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
     }
   }
   __syncthreads();
-  if (tid == CW * 32 && *abort_v) drain_after_abort(full, issued_s, n_stages);
+  if (tid == CW * 32 && *abort_v) {
+    // wait (bounded) for every lane's copies still in flight, then report
+    for (int p = 0; p < np; ++p)
+      for (int r = max(p, issued_p[p] - n_stages); r < issued_p[p]; r += np)
+        mbar_wait(&full[r % n_stages], (r / n_stages) & 1);
+    atomicExch(&g_readout_error, (unsigned)GFST_ERR_TIMEOUT);
+  }
   // exact re-score of the surviving candidates, flattened over the chunk: the
   // (query, token) pairs with A + b >= the query's final LB are listed in the
   // (now idle) run table, one thread per pair computes the fp32 score from
