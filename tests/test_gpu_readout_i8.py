@@ -139,3 +139,29 @@ def test_int8_first_look_in_the_streaming_step(cuda_device):
         Kb, Vb, Qb = (torch.randn((S, L, d), generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(3))
         oa, ob = a.step(A, B, Kb, Vb, Qb), b.step(A, B, Kb, Vb, Qb)
         _check_vs_bf16((oa.best_tok, oa.best_score, oa.value), (ob.best_tok, ob.best_score, ob.value))
+
+
+@pytest.mark.parametrize("L,slots,d", [(16, 48, 128), (128, 24, 128), (256, 12, 128), (16, 4100, 128),
+                                       (128, 10, 256)])
+def test_int8_first_look_block_lengths_and_large_rings(cuda_device, L, slots, d):
+    # every supported block length (16 | L <= 256: one to four 16-row tile
+    # groups per column tile, 2 to 8 ring stages), d = 256 with long blocks,
+    # and a ring of more than 4096 slots (selections grouped by the bitonic
+    # sort instead of the counting sort)
+    S, Nq, k = 2, 70, 6
+    g = torch.Generator().manual_seed(40 + L + slots)
+    mem = memory.BlockMemory(S, slots, L, d, dtype=torch.bfloat16, device=cuda_device, int8_keys=True)
+    K = torch.randn((S, slots, L, d), generator=g).to(torch.bfloat16)
+    V = torch.randn((S, slots, L, d), generator=g).to(torch.bfloat16)
+    for b in range(slots):
+        mem.commit(K[:, b].to(cuda_device), V[:, b].to(cuda_device))
+    Q = torch.randn((S, Nq, d), generator=g).to(torch.bfloat16)
+    sel = torch.stack([torch.stack([torch.randperm(slots, generator=g)[:k] for _ in range(Nq)]) for _ in range(S)])
+    sel = sel.to(torch.int32)
+    if slots > 4096:
+        sel[:, :, 0] = slots - 1 - torch.arange(Nq, dtype=torch.int32)  # blocks beyond the counting sort's range
+    a, b = _both(Q.to(cuda_device), mem, sel.to(cuda_device))
+    _check_vs_bf16(a, b)
+    rt, rs, _, ok = go.exact_readout(Q.float().numpy(), K.float().numpy(), None, sel.numpy())
+    tok = a[0].cpu().numpy()
+    assert np.array_equal(tok[ok], rt[ok])
