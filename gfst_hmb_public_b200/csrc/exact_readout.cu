@@ -655,11 +655,22 @@ __global__ void __launch_bounds__(kMThreads) exact_readout_mma_kernel(
     issued_s = 0;
     mbar_init_fence();
   }
-  build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k, n_slots);
+  // the ring is idle until the pipeline starts: it holds the counting sort's
+  // histogram when the ring has room for one count per slot (three CTA
+  // barriers; the bitonic sort takes log^2 of the pair capacity)
+  const bool counting = (int64_t)n_slots * 4 <= (int64_t)n_stages * stage_bytes;
+  if (counting)
+    build_runs_counting<kMThreads>(rt, reinterpret_cast<int*>(dyn), top_idx + ((size_t)s * n_queries + q0) * k,
+                                   nq * k, k, n_slots);
+  else
+    build_runs<kMThreads, kMWarps * 32>(rt, nullptr, top_idx + ((size_t)s * n_queries + q0) * k, nq * k, k,
+                                        n_slots);
   const int n_runs = rt.n_runs;
 
   if (warp == kMWarps) {
     if (lane == 0) {
+      // generic-proxy writes to the ring (the histogram) precede its copies
+      if (counting) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       int r = 0;
       for (; r < n_runs; ++r) {
         const int st = r % n_stages;
