@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
 // per warp.  Each warp stages its own 32 rows of A_t and all of B_t.
 // ---------------------------------------------------------------------------
 template <int DMAX, int RMAX>
-__global__ void __launch_bounds__(DMAX, 512 / DMAX)
+__global__ void __launch_bounds__(DMAX, 256 / DMAX)
     frame_stream_chol_mw_kernel(float* __restrict__ U, const float* __restrict__ A, const float* __restrict__ B,
                                 float beta, int64_t n_frames, int T, int d, int r, int m, float eps_sign,
                                 int sign_mode, float* __restrict__ frames_out, int out_every, bool vec4) {
@@ -315,12 +315,19 @@ int launch_stream_chol_mw(float* U, const float* A, const float* B, float beta, 
   return check_launch("frame_stream_chol_mw_kernel");
 }
 
-// Frames below which the automatic choice splits each frame over d/32 warps:
-// one frame per warp then leaves most SMs idle and runs each frame's
-// dependency chain on one warp.  Measured on B200, 64 tokens of 128 x 32
-// frames with rank-4 updates: 256 frames 0.74 ms split against 1.00 ms one
-// per warp, 512 frames 1.40 against 1.07 ms.
-constexpr int64_t kSplitFramesBelow = 384;
+// The automatic choice splits each frame over d/32 warps while every split
+// CTA is resident at once (256 / DMAX CTAs per SM by registers: 2 per SM for
+// d = 128, 296 frames on B200): one frame per warp would leave most SMs idle
+// and run each frame's dependency chain on one warp.  Measured on B200, 64
+// tokens of 128 x 32 frames with rank-4 updates: 256 frames 0.66 ms split
+// against 1.00 ms one per warp; past the resident count the split kernel
+// needs a second wave (512 frames: 1.40 against 1.07 ms).
+inline int64_t split_frames_max(int dmax) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return (int64_t)(256 / dmax) * sms;
+}
 
 template <int DMAX, int RMAX, int RG, int CG>
 int launch_stream(float* U, const float* A, const float* B, float beta, int64_t n, int T, int d, int r, int m,
@@ -328,7 +335,8 @@ int launch_stream(float* U, const float* A, const float* B, float beta, int64_t 
                   cudaStream_t stream) {
   constexpr bool kChol = (DMAX == 64 || DMAX == 128) && (RMAX == 16 || RMAX == 32) && RG == 8 && CG == 4;
   if constexpr (kChol) {
-    const bool split = qr_method == GFST_QR_CHOLESKY2_SPLIT || (qr_method == GFST_QR_AUTO && n < kSplitFramesBelow);
+    const bool split =
+        qr_method == GFST_QR_CHOLESKY2_SPLIT || (qr_method == GFST_QR_AUTO && n <= split_frames_max(DMAX));
     if (split)
       return launch_stream_chol_mw<DMAX, RMAX>(U, A, B, beta, n, T, d, r, m, eps_sign, sign_mode, frames_out,
                                                out_every, stream);

@@ -143,7 +143,8 @@ def stream_frames(
     With ``out_every > 0`` the frames after tokens out_every-1, 2*out_every-1, ...
     are returned as [T // out_every, F, d, r]; otherwise returns None.
     ``qr_method``: "auto" (CholeskyQR2 for 32 < d <= 128 and 8 < r <= 32 --
-    below 384 frames with each frame split over d/32 warps -- and for
+    up to 2 frames per SM for d = 128 (4 for d <= 64) with each frame split
+    over d/32 warps -- and for
     8 < d <= 128 with r <= 8; Householder otherwise), "householder",
     "cholesky2" (one frame per warp; 2 or 4 frames per warp with r <= 8) or
     "cholesky2_split" (one frame per CTA of d/32 warps, 8 < r <= 32); with

@@ -105,8 +105,9 @@ enum gfst_sign_mode {
 
 /* QR algorithm of the streaming frame pass (gfst_frame_stream_ex). */
 enum gfst_qr_method {
-  /* CholeskyQR2 for 32 < d <= 128 with 8 < r <= 32 (split over warps below
-   * 384 frames) and for 8 < d <= 128 with r <= 8, Householder otherwise. */
+  /* CholeskyQR2 for 32 < d <= 128 with 8 < r <= 32 (split over warps while
+   * every split CTA is resident: up to 2 frames per SM for d = 128, 4 for
+   * d <= 64) and for 8 < d <= 128 with r <= 8, Householder otherwise. */
   GFST_QR_AUTO = 0,
   /* LAPACK-order Householder (geqrf/orgqr) for every token. */
   GFST_QR_HOUSEHOLDER = 1,
@@ -119,7 +120,8 @@ enum gfst_qr_method {
   GFST_QR_CHOLESKY2 = 2,
   /* GFST_QR_CHOLESKY2 with each frame split over d/32 warps (a CTA per frame):
    * shorter per-token latency for batches too small to fill the GPU with one
-   * frame per warp.  AUTO takes it below 384 frames. */
+   * frame per warp.  AUTO takes it up to 2 frames per SM (d = 128) or 4
+   * (d <= 64): 296 or 592 frames on B200. */
   GFST_QR_CHOLESKY2_SPLIT = 3
 };
 
