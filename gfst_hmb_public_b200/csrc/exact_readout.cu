@@ -1008,6 +1008,12 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
       const uint32_t abase = base + st * stage_bytes + a_row * 128;
       const float* sk = reinterpret_cast<const float*>(side + (size_t)st * side_bytes);
       const float E = sk[L], N = sk[L + 1];
+      // the stage is handed back as soon as its last key tile and scales are
+      // in registers, so the producer refills it while this warp finishes the
+      // block's selection work (with as many stages as consumer warps, a run
+      // and the run CW later share a stage: a warp's next block is requested
+      // only when its current one is released)
+      bool released = false;
       if (!(E <= 3.0e38f)) {
         // a key of this block has a non-finite value: its queries are scored in full
         for (int pp = p0 + lane; pp < p1; pp += 32) qstat[rt.keys[pp] & 2047u].w = 1.f;
@@ -1055,14 +1061,24 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
                 }
               }
             }
+            float sc0[4], sc1[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int row = (t + u) * 16 + (lane >> 2);
-              const float s0 = u < tn ? sk[row] : 0.f, s1 = u < tn ? sk[row + 8] : 0.f;
+              sc0[u] = u < tn ? sk[row] : 0.f;
+              sc1[u] = u < tn ? sk[row + 8] : 0.f;
+            }
+            if (g0 + 8 >= p1 && t + 4 >= nt) {  // the run's last reads of the stage are done
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[st]);
+              released = true;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int j = e & 1;
-                av[u][e] = u < tn ? (float)acc[u][e] * ((e & 2) ? s1 : s0) * sq[j] : -INFINITY;
+                av[u][e] = u < tn ? (float)acc[u][e] * ((e & 2) ? sc1[u] : sc0[u]) * sq[j] : -INFINITY;
               }
             }
             // column maxima as a tree (fmaxf is exact, so the order is free)
@@ -1112,8 +1128,10 @@ __global__ void __launch_bounds__((CW + 1) * 32) exact_readout_i8_kernel(
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
+      if (!released) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
     }
   }
   __syncthreads();
